@@ -1,0 +1,168 @@
+/*
+ * qia_b200.h -- C ABI of the B200 (sm_100a) denoiser hot-path kernels.
+ *
+ * Every function takes plain device pointers, int64 sizes and the caller's
+ * cudaStream_t (passed as void*), queues its kernel(s) on that stream and
+ * returns a status code (QIA_OK == 0). Nothing here allocates device memory,
+ * synchronises the device or aborts the process; the text of the last failure
+ * on the calling host thread is returned by qia_last_error_string().
+ *
+ * Tensor conventions (all contiguous unless a leading dimension is given):
+ *   bf16       : __nv_bfloat16 / torch.bfloat16, row-major.
+ *   MXFP8      : E4M3 codes [padded_rows, K] row-major plus E8M0 scales (one
+ *                byte per 1x32 block along K) in the 128x4 blocked layout:
+ *                byte((r, kb)) = ((r/128)*(K/128) + kb/4)*512 + (r%32)*16
+ *                                + ((r/32)%4)*4 + kb%4,
+ *                rows padded to a multiple of 128 (zeros in the padding).
+ *   attention  : NHD, [batch, seq, heads, head_dim] bf16.
+ *   RoPE freqs : complex64 viewed as float pairs, [seq, head_dim/2, 2] f32.
+ *
+ * Each declaration names the reference interface it replaces
+ * (paths relative to the Qwen-Image-2.1-Accel checkout; WHL: = the pinned
+ * diffusers wheel; SAGE: = the pinned SageAttention source).
+ */
+#ifndef QIA_B200_H_
+#define QIA_B200_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum qia_status {
+  QIA_OK = 0,
+  QIA_ERR_INVALID = 1,      /* bad pointer, size, stride or argument */
+  QIA_ERR_UNSUPPORTED = 2,  /* valid input outside what the kernel implements */
+  QIA_ERR_ALIGNMENT = 3,    /* pointer or leading dimension misaligned */
+  QIA_ERR_CUDA = 4,         /* a CUDA runtime call or launch failed */
+  QIA_ERR_TIMEOUT = 5       /* a bounded device-side wait gave up */
+};
+
+/* Text of the last error raised on this host thread ("" if none). */
+const char* qia_last_error_string(void);
+/* ABI version: bumped whenever a signature changes. */
+int qia_abi_version(void);
+
+/* ---------------------------------------------------------------------------
+ * Normalisation family
+ * ------------------------------------------------------------------------ */
+
+/* LayerNorm (no affine, eps) in PyTorch's CUDA Welford order, rounded to bf16,
+ * times scale[b] (= 1 + s, bf16) -> bf16, plus optional shift[b] -> bf16.
+ * x, out: [rows, dim]; scale, shift: [rows / rows_per_batch, dim]; shift may be
+ * NULL. dim % 512 == 0, dim <= 8192.
+ * Replaces: layer_norm_scale (src/qwen_image_accel/kernels/layernorm.py:58)
+ * and the v1 img_norm1 + _modulate pair (WHL:diffusers/models/transformers/
+ * transformer_qwenimage.py:683-717). */
+int qia_ln_mod(const void* x, const void* scale, const void* shift, void* out,
+               int64_t rows, int64_t dim, int64_t rows_per_batch, float eps,
+               void* stream);
+
+/* qia_ln_mod followed by MXFP8 quantization of the bf16 result, in one pass.
+ * q_values: [padded_rows, dim] e4m3; q_scales: padded_rows*dim/32 bytes.
+ * padded_rows = ceil(rows/128)*128; rows past `rows` are written as zeros.
+ * Replaces: layer_norm_scale_quantize (src/qwen_image_accel/kernels/epilogue.py:304). */
+int qia_ln_mod_quant(const void* x, const void* scale, const void* shift,
+                     void* q_values, void* q_scales, int64_t rows, int64_t dim,
+                     int64_t rows_per_batch, float eps, void* stream);
+
+/* Gated residual: out = bf16(h + bf16(x * gate[b])). h, x, out: [rows, dim];
+ * gate: [rows / rows_per_batch, dim].
+ * Replaces: residual (src/qwen_image_accel/kernels/elementwise.py:26). */
+int qia_gated_residual(const void* h, const void* x, const void* gate, void* out,
+                       int64_t rows, int64_t dim, int64_t rows_per_batch,
+                       void* stream);
+
+/* The benchmark AdaLN composite (one pass):
+ * out = bf16(r + bf16(gate * bf16(bf16(bf16(LN(x)) * scale) + shift))).
+ * scale is the precomputed bf16 (1 + scale) vector, as in qia_ln_mod.
+ * Replaces: the eager r + gate*(norm(x)*(1+scale)+shift) sequence of
+ * WHL:diffusers/models/transformers/transformer_qwenimage.py:741-767. */
+int qia_adaln_residual(const void* x, const void* r, const void* scale,
+                       const void* shift, const void* gate, void* out,
+                       int64_t rows, int64_t dim, int64_t rows_per_batch,
+                       float eps, void* stream);
+
+/* Per-row RMSNorm with bf16 weight, two bf16 rounding points
+ * (normalised -> bf16, * weight -> bf16). x, out: [rows, dim], dim == 128.
+ * Replaces: rms_norm (src/qwen_image_accel/kernels/bf16.py:58). */
+int qia_rms_norm(const void* x, const void* weight, void* out, int64_t rows,
+                 int64_t dim, float eps, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Attention input preparation
+ * ------------------------------------------------------------------------ */
+
+/* Complex RoPE on interleaved pairs in the CUDA complex-FMA order.
+ * q, k, out_q, out_k: [batch, seq, heads, head_dim]; freqs: [seq, head_dim/2, 2].
+ * Replaces: rope_qk (src/qwen_image_accel/kernels/elementwise.py:63). */
+int qia_rope_qk(const void* q, const void* k, const void* freqs, void* out_q,
+                void* out_k, int64_t batch, int64_t seq, int64_t heads,
+                int64_t head_dim, void* stream);
+
+/* Q/K RMSNorm + RoPE + K/V pack after a cached prefix, one launch.
+ * q, k, v: [batch, seq, heads, 128]; cached_k/v: [batch, prefix, heads, 128]
+ * (may be NULL when prefix == 0); out_q: [batch, seq, heads, 128];
+ * out_k/out_v: [batch, prefix + seq, heads, 128].
+ * Replaces: prepare_attention_inputs (src/qwen_image_accel/kernels/attention.py:92). */
+int qia_qknorm_rope_pack(const void* q, const void* k, const void* v,
+                         const void* cached_k, const void* cached_v,
+                         const void* weight_q, const void* weight_k,
+                         const void* freqs, void* out_q, void* out_k,
+                         void* out_v, int64_t batch, int64_t seq,
+                         int64_t prefix, int64_t heads, int64_t head_dim,
+                         float eps_q, float eps_k, void* stream);
+
+/* Joint text+image variant for the dual-stream (v1) block: one segment of the
+ * joint sequence. Reads q/k/v rows of this segment from a projection output
+ * whose rows have leading dimension ld_in (elements; q at column 0, k at
+ * q_cols, v at 2*q_cols where q_cols = heads*head_dim), applies RMSNorm with
+ * this stream's weights and RoPE with this segment's freqs, and writes
+ * [batch, seg_len] rows at sequence offset seq_offset of the joint
+ * [batch, seq_total, heads, head_dim] outputs.
+ * Replaces: the per-stream norm_q/norm_k/norm_added_q/norm_added_k + RoPE +
+ * cat of QwenDoubleStreamAttnProcessor2_0
+ * (WHL:diffusers/models/transformers/transformer_qwenimage.py:540-575). */
+int qia_qknorm_rope_segment(const void* qkv, int64_t ld_in,
+                            const void* weight_q, const void* weight_k,
+                            const void* freqs, void* out_q, void* out_k,
+                            void* out_v, int64_t batch, int64_t seg_len,
+                            int64_t seq_offset, int64_t seq_total,
+                            int64_t heads, int64_t head_dim, float eps_q,
+                            float eps_k, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Feed-forward activations
+ * ------------------------------------------------------------------------ */
+
+/* SwiGLU: out = bf16(bf16(silu(gate)) * value), silu = div.rn(g, 1 + exp(-g)).
+ * Replaces: swiglu (src/qwen_image_accel/kernels/bf16.py:184). */
+int qia_swiglu(const void* gate, const void* value, void* out, int64_t n,
+               void* stream);
+
+/* SwiGLU + MXFP8 quantization. gate, value: [rows, width], width % 128 == 0.
+ * Replaces: swiglu_quantize (src/qwen_image_accel/kernels/epilogue.py:351). */
+int qia_swiglu_quant(const void* gate, const void* value, void* q_values,
+                     void* q_scales, int64_t rows, int64_t width, void* stream);
+
+/* GELU (tanh approximation, PyTorch CUDA formula) on bf16: out = bf16(gelu(x)).
+ * Replaces: F.gelu(approximate="tanh") in the v1 FeedForward
+ * (WHL:diffusers/models/activations.py:81-90). */
+int qia_gelu_tanh(const void* x, void* out, int64_t n, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * MXFP8 quantization
+ * ------------------------------------------------------------------------ */
+
+/* Quantize a bf16 [rows, k] matrix (row stride ld elements) to MXFP8.
+ * k % 128 == 0. Outputs as described at the top of this file.
+ * Replaces: quantize / _mx_quantize_kernel (src/qwen_image_accel/kernels/mxfp8.py:190-226). */
+int qia_mxfp8_quantize(const void* x, int64_t ld, void* q_values, void* q_scales,
+                       int64_t rows, int64_t k, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* QIA_B200_H_ */

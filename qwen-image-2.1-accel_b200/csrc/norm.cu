@@ -1,0 +1,269 @@
+// LayerNorm + AdaLN modulation family and the gated residual.
+//
+// Numerics follow the reference contracts:
+//  * LayerNorm statistics in PyTorch 2.11's vectorised CUDA LayerNorm order
+//    (reference src/qwen_image_accel/kernels/layernorm.py:17-55): 128 threads
+//    per row, each owning the vec4 groups t*4 + j*512 (j < dim/512) and running
+//    one Welford update per element; then five shuffle-down merges inside each
+//    warp and the warp 0+2, 0+1 merges through shared memory, each merge in
+//    cuWelfordCombine's arithmetic; var = m2 / dim, rstd = rsqrtf(var + eps).
+//  * Every eager bf16 tensor boundary is kept as a bf16 rounding point
+//    (normalised, *scale, +shift, *gate, +residual).
+//  * The MXFP8 epilogue quantizes the bf16 result exactly as the standalone
+//    quantizer does (reference kernels/epilogue.py:252-301).
+//
+// HBM layout: rows are contiguous [rows, dim] bf16; one 128-thread CTA per row
+// keeps the row in registers (dim/128 fp32 per thread), so x is read once.
+#include "qia_common.cuh"
+
+namespace qia {
+namespace {
+
+constexpr int kThreads = 128;
+enum Mode { kModBf16 = 0, kModQuant = 1, kAdalnResidual = 2 };
+
+struct Welford {
+  float mean, m2, count;
+};
+
+// cuWelfordCombine(dataB = own, dataA = other) as used by PyTorch's warp and
+// block reductions.
+__device__ __forceinline__ Welford welford_combine(const Welford own, const Welford other) {
+  const float delta = own.mean - other.mean;
+  const float count = other.count + own.count;
+  const float coef = 1.0f / count;
+  const float n_a = other.count * coef;
+  const float n_b = own.count * coef;
+  Welford r;
+  r.mean = __fmaf_rn(n_a, other.mean, __fmul_rn(n_b, own.mean));
+  r.m2 = __fmaf_rn(__fmul_rn(__fmul_rn(delta, delta), other.count), n_b, other.m2 + own.m2);
+  r.count = count;
+  return r;
+}
+
+template <int NV>
+__device__ __forceinline__ void row_stats(const __nv_bfloat16* __restrict__ xrow, bool live,
+                                          float (&v)[NV * 4], float& mean, float& rstd,
+                                          int dim, float eps) {
+  __shared__ float s_stat[4];
+  const int t = threadIdx.x;
+  uint2 raw[NV];
+#pragma unroll
+  for (int j = 0; j < NV; ++j) {
+    raw[j] = live ? __ldg(reinterpret_cast<const uint2*>(xrow + t * 4 + j * 512)) : make_uint2(0u, 0u);
+  }
+  Welford w{0.0f, 0.0f, float(NV * 4)};
+#pragma unroll
+  for (int j = 0; j < NV; ++j) {
+    unpack4(raw[j], &v[j * 4]);
+#pragma unroll
+    for (int ii = 0; ii < 4; ++ii) {
+      const float inv = 1.0f / float(j * 4 + ii + 1);
+      const float x = v[j * 4 + ii];
+      const float delta = x - w.mean;
+      w.mean = __fmaf_rn(delta, inv, w.mean);
+      w.m2 = __fmaf_rn(delta, x - w.mean, w.m2);
+    }
+  }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) {
+    Welford o;
+    o.mean = __shfl_down_sync(0xffffffffu, w.mean, off);
+    o.m2 = __shfl_down_sync(0xffffffffu, w.m2, off);
+    o.count = __shfl_down_sync(0xffffffffu, w.count, off);
+    w = welford_combine(w, o);
+  }
+  __shared__ Welford s_w[2];
+  const int warp = t >> 5, lane = t & 31;
+  // upper half of the warps hands its partial to the lower half (offset 2, then 1)
+  if (lane == 0 && warp >= 2) s_w[warp - 2] = w;
+  __syncthreads();
+  if (lane == 0 && warp < 2) w = welford_combine(w, s_w[warp]);
+  __syncthreads();
+  if (lane == 0 && warp == 1) s_w[0] = w;
+  __syncthreads();
+  if (t == 0) {
+    w = welford_combine(w, s_w[0]);
+    s_stat[0] = w.mean;
+    s_stat[1] = __fdiv_rn(w.m2, float(dim));
+  }
+  __syncthreads();
+  mean = s_stat[0];
+  rstd = rsqrtf(s_stat[1] + eps);
+}
+
+template <int NV, int MODE, bool SHIFT>
+__global__ void __launch_bounds__(kThreads)
+ln_mod_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ resid,
+              const __nv_bfloat16* __restrict__ scale, const __nv_bfloat16* __restrict__ shift,
+              const __nv_bfloat16* __restrict__ gate, __nv_bfloat16* __restrict__ out,
+              uint8_t* __restrict__ q_values, uint8_t* __restrict__ q_scales,
+              int64_t rows, int rows_per_batch, float eps) {
+  constexpr int D = NV * 512;
+  const int64_t row = blockIdx.x;
+  const bool live = row < rows;
+  const int t = threadIdx.x;
+  float v[NV * 4];
+  float mean, rstd;
+  row_stats<NV>(x + row * D, live, v, mean, rstd, D, eps);
+
+  const int64_t vec_row = live ? (row / rows_per_batch) * D : 0;
+#pragma unroll
+  for (int j = 0; j < NV; ++j) {
+    const int c = t * 4 + j * 512;
+    float s[4], y[4];
+    unpack4(__ldg(reinterpret_cast<const uint2*>(scale + vec_row + c)), s);
+    float sh[4];
+    if (SHIFT) unpack4(__ldg(reinterpret_cast<const uint2*>(shift + vec_row + c)), sh);
+#pragma unroll
+    for (int ii = 0; ii < 4; ++ii) {
+      const float nrm = round_bf16(__fmul_rn(rstd, v[j * 4 + ii] - mean));
+      float m = round_bf16(__fmul_rn(nrm, s[ii]));
+      if (SHIFT) m = round_bf16(__fadd_rn(m, sh[ii]));
+      y[ii] = live ? m : 0.0f;
+    }
+    if (MODE == kModBf16) {
+      *reinterpret_cast<uint2*>(out + row * D + c) = pack4(y);
+    } else if (MODE == kAdalnResidual) {
+      float g[4], r[4];
+      unpack4(__ldg(reinterpret_cast<const uint2*>(gate + vec_row + c)), g);
+      unpack4(__ldg(reinterpret_cast<const uint2*>(resid + row * D + c)), r);
+#pragma unroll
+      for (int ii = 0; ii < 4; ++ii) y[ii] = __fadd_rn(r[ii], round_bf16(__fmul_rn(g[ii], y[ii])));
+      *reinterpret_cast<uint2*>(out + row * D + c) = pack4(y);
+    } else {
+      // 32-element MX block = 8 consecutive threads (aligned groups of 8 lanes)
+      float amax = fmaxf(fmaxf(fabsf(y[0]), fabsf(y[1])), fmaxf(fabsf(y[2]), fabsf(y[3])));
+      amax = warp_max_xor(amax, 4);
+      const int e = mx_exponent(amax);
+      const float inv = mx_inverse_scale(e);
+      const uint32_t codes = cvt_e4m3x4(y[0] * inv, y[1] * inv, y[2] * inv, y[3] * inv);
+      *reinterpret_cast<uint32_t*>(q_values + row * D + c) = codes;
+      if ((t & 7) == 0) q_scales[mx_scale_offset(row, c >> 5, D / 128)] = uint8_t(e);
+    }
+  }
+}
+
+template <int MODE, bool SHIFT>
+int launch_ln(int nv, dim3 grid, cudaStream_t st, const void* x, const void* resid, const void* scale,
+              const void* shift, const void* gate, void* out, void* qv, void* qs, int64_t rows,
+              int rows_per_batch, float eps) {
+#define QIA_LN_CASE(N)                                                                                 \
+  case N:                                                                                              \
+    ln_mod_kernel<N, MODE, SHIFT><<<grid, kThreads, 0, st>>>(                                          \
+        (const __nv_bfloat16*)x, (const __nv_bfloat16*)resid, (const __nv_bfloat16*)scale,             \
+        (const __nv_bfloat16*)shift, (const __nv_bfloat16*)gate, (__nv_bfloat16*)out, (uint8_t*)qv,    \
+        (uint8_t*)qs, rows, rows_per_batch, eps);                                                      \
+    break;
+  switch (nv) {
+    QIA_LN_CASE(1) QIA_LN_CASE(2) QIA_LN_CASE(3) QIA_LN_CASE(4) QIA_LN_CASE(5) QIA_LN_CASE(6)
+    QIA_LN_CASE(7) QIA_LN_CASE(8) QIA_LN_CASE(9) QIA_LN_CASE(10) QIA_LN_CASE(11) QIA_LN_CASE(12)
+    QIA_LN_CASE(13) QIA_LN_CASE(14) QIA_LN_CASE(15) QIA_LN_CASE(16)
+    default:
+      return set_error(QIA_ERR_UNSUPPORTED, "layer norm: dim/512 = %d outside [1, 16]", nv);
+  }
+#undef QIA_LN_CASE
+  return check_launch("ln_mod_kernel");
+}
+
+int validate_ln(const void* x, const void* scale, const void* out, int64_t rows, int64_t dim,
+                int64_t rows_per_batch, const char* who) {
+  if (!x || !scale || !out) return set_error(QIA_ERR_INVALID, "%s: null pointer", who);
+  if (rows <= 0 || dim <= 0 || rows_per_batch <= 0)
+    return set_error(QIA_ERR_INVALID, "%s: rows=%lld dim=%lld rows_per_batch=%lld", who, (long long)rows,
+                     (long long)dim, (long long)rows_per_batch);
+  if (dim % 512 != 0 || dim > 8192)
+    return set_error(QIA_ERR_UNSUPPORTED, "%s: dim=%lld must be a multiple of 512 and <= 8192", who,
+                     (long long)dim);
+  if (rows > 0x7fffffffLL) return set_error(QIA_ERR_UNSUPPORTED, "%s: too many rows", who);
+  if (!aligned(x, 8) || !aligned(scale, 8) || !aligned(out, 8))
+    return set_error(QIA_ERR_ALIGNMENT, "%s: pointers must be 8-byte aligned", who);
+  return QIA_OK;
+}
+
+// ---------------------------------------------------------------------------
+// gated residual: out = bf16(h + bf16(x * gate))
+// ---------------------------------------------------------------------------
+__global__ void gated_residual_kernel(const uint4* __restrict__ h, const uint4* __restrict__ x,
+                                      const __nv_bfloat16* __restrict__ gate, uint4* __restrict__ out,
+                                      int64_t n8, int64_t dim, int64_t batch_elems) {
+  for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < n8; i += int64_t(gridDim.x) * blockDim.x) {
+    const int64_t e = i * 8;
+    const int64_t c = e % dim;
+    const int64_t b = e / batch_elems;
+    float fh[8], fx[8], fg[8], o[8];
+    unpack8(__ldg(h + i), fh);
+    unpack8(__ldg(x + i), fx);
+    unpack8(__ldg(reinterpret_cast<const uint4*>(gate + b * dim + c)), fg);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) o[k] = __fadd_rn(fh[k], round_bf16(__fmul_rn(fx[k], fg[k])));
+    out[i] = pack8(o);
+  }
+}
+
+}  // namespace
+}  // namespace qia
+
+using namespace qia;
+
+extern "C" int qia_ln_mod(const void* x, const void* scale, const void* shift, void* out, int64_t rows,
+                          int64_t dim, int64_t rows_per_batch, float eps, void* stream) {
+  int rc = validate_ln(x, scale, out, rows, dim, rows_per_batch, "qia_ln_mod");
+  if (rc) return rc;
+  if (shift && !aligned(shift, 8)) return set_error(QIA_ERR_ALIGNMENT, "qia_ln_mod: shift misaligned");
+  const int nv = int(dim / 512);
+  const dim3 grid{unsigned(rows)};
+  if (shift)
+    return launch_ln<kModBf16, true>(nv, grid, as_stream(stream), x, nullptr, scale, shift, nullptr, out, nullptr,
+                                     nullptr, rows, int(rows_per_batch), eps);
+  return launch_ln<kModBf16, false>(nv, grid, as_stream(stream), x, nullptr, scale, nullptr, nullptr, out, nullptr,
+                                    nullptr, rows, int(rows_per_batch), eps);
+}
+
+extern "C" int qia_ln_mod_quant(const void* x, const void* scale, const void* shift, void* q_values,
+                                void* q_scales, int64_t rows, int64_t dim, int64_t rows_per_batch, float eps,
+                                void* stream) {
+  int rc = validate_ln(x, scale, q_values, rows, dim, rows_per_batch, "qia_ln_mod_quant");
+  if (rc) return rc;
+  if (!q_scales) return set_error(QIA_ERR_INVALID, "qia_ln_mod_quant: null q_scales");
+  if (shift && !aligned(shift, 8)) return set_error(QIA_ERR_ALIGNMENT, "qia_ln_mod_quant: shift misaligned");
+  const int64_t padded = (rows + 127) / 128 * 128;
+  const int nv = int(dim / 512);
+  const dim3 grid{unsigned(padded)};
+  if (shift)
+    return launch_ln<kModQuant, true>(nv, grid, as_stream(stream), x, nullptr, scale, shift, nullptr, nullptr,
+                                      q_values, q_scales, rows, int(rows_per_batch), eps);
+  return launch_ln<kModQuant, false>(nv, grid, as_stream(stream), x, nullptr, scale, nullptr, nullptr, nullptr,
+                                     q_values, q_scales, rows, int(rows_per_batch), eps);
+}
+
+extern "C" int qia_adaln_residual(const void* x, const void* r, const void* scale, const void* shift,
+                                  const void* gate, void* out, int64_t rows, int64_t dim, int64_t rows_per_batch,
+                                  float eps, void* stream) {
+  int rc = validate_ln(x, scale, out, rows, dim, rows_per_batch, "qia_adaln_residual");
+  if (rc) return rc;
+  if (!r || !shift || !gate) return set_error(QIA_ERR_INVALID, "qia_adaln_residual: null r/shift/gate");
+  if (!aligned(r, 8) || !aligned(shift, 8) || !aligned(gate, 8))
+    return set_error(QIA_ERR_ALIGNMENT, "qia_adaln_residual: pointers must be 8-byte aligned");
+  const int nv = int(dim / 512);
+  return launch_ln<kAdalnResidual, true>(nv, dim3(unsigned(rows)), as_stream(stream), x, r, scale, shift, gate,
+                                         out, nullptr, nullptr, rows, int(rows_per_batch), eps);
+}
+
+extern "C" int qia_gated_residual(const void* h, const void* x, const void* gate, void* out, int64_t rows,
+                                  int64_t dim, int64_t rows_per_batch, void* stream) {
+  if (!h || !x || !gate || !out) return set_error(QIA_ERR_INVALID, "qia_gated_residual: null pointer");
+  if (rows <= 0 || dim <= 0 || rows_per_batch <= 0)
+    return set_error(QIA_ERR_INVALID, "qia_gated_residual: bad sizes");
+  if (dim % 8 != 0) return set_error(QIA_ERR_UNSUPPORTED, "qia_gated_residual: dim %% 8 != 0");
+  if (!aligned(h, 16) || !aligned(x, 16) || !aligned(gate, 16) || !aligned(out, 16))
+    return set_error(QIA_ERR_ALIGNMENT, "qia_gated_residual: pointers must be 16-byte aligned");
+  const int64_t n8 = rows * dim / 8;
+  const int threads = 256;
+  int64_t blocks = (n8 + threads - 1) / threads;
+  const int64_t cap = int64_t(sm_count()) * 16;
+  if (blocks > cap) blocks = cap;
+  gated_residual_kernel<<<unsigned(blocks), threads, 0, as_stream(stream)>>>(
+      (const uint4*)h, (const uint4*)x, (const __nv_bfloat16*)gate, (uint4*)out, n8, dim, rows_per_batch * dim);
+  return check_launch("gated_residual_kernel");
+}

@@ -1,0 +1,121 @@
+// Shared helpers for the sm_100a kernels behind the qia_* C ABI.
+//
+// Every entry point validates its arguments on the host, launches on the
+// caller's stream and returns a qia status code; it never aborts and never
+// synchronises. The message of the last failure on the calling host thread is
+// kept in a thread-local buffer (qia_last_error_string).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <cuda_fp8.h>
+#include <stdint.h>
+#include <stdarg.h>
+#include <stdio.h>
+
+#include "../../include/qia_b200.h"
+
+namespace qia {
+
+// Records a formatted message as the thread's last error and returns `code`.
+int set_error(int code, const char* fmt, ...);
+
+// Checks the launch that was just queued; maps a CUDA error to QIA_ERR_CUDA.
+int check_launch(const char* what);
+
+inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
+
+inline bool aligned(const void* p, uintptr_t a) {
+  return (reinterpret_cast<uintptr_t>(p) % a) == 0;
+}
+
+// Number of SMs of the current device (cached per device).
+int sm_count();
+
+// ---------------------------------------------------------------------------
+// Device helpers
+// ---------------------------------------------------------------------------
+
+__device__ __forceinline__ float bf16_to_f32(__nv_bfloat16 v) { return __bfloat162float(v); }
+__device__ __forceinline__ __nv_bfloat16 f32_to_bf16(float v) { return __float2bfloat16_rn(v); }
+// Round an fp32 value through bf16 and back (the eager bf16 tensor boundary).
+__device__ __forceinline__ float round_bf16(float v) { return __bfloat162float(__float2bfloat16_rn(v)); }
+
+__device__ __forceinline__ float bf16_lo(uint32_t packed) { return __uint_as_float(packed << 16); }
+__device__ __forceinline__ float bf16_hi(uint32_t packed) { return __uint_as_float(packed & 0xffff0000u); }
+
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+  __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+
+// Unpack 8 bf16 values held in a uint4 into fp32.
+__device__ __forceinline__ void unpack8(const uint4& v, float* f) {
+  f[0] = bf16_lo(v.x); f[1] = bf16_hi(v.x);
+  f[2] = bf16_lo(v.y); f[3] = bf16_hi(v.y);
+  f[4] = bf16_lo(v.z); f[5] = bf16_hi(v.z);
+  f[6] = bf16_lo(v.w); f[7] = bf16_hi(v.w);
+}
+
+__device__ __forceinline__ uint4 pack8(const float* f) {
+  uint4 v;
+  v.x = pack_bf16x2(f[0], f[1]);
+  v.y = pack_bf16x2(f[2], f[3]);
+  v.z = pack_bf16x2(f[4], f[5]);
+  v.w = pack_bf16x2(f[6], f[7]);
+  return v;
+}
+
+__device__ __forceinline__ void unpack4(const uint2& v, float* f) {
+  f[0] = bf16_lo(v.x); f[1] = bf16_hi(v.x);
+  f[2] = bf16_lo(v.y); f[3] = bf16_hi(v.y);
+}
+
+__device__ __forceinline__ uint2 pack4(const float* f) {
+  uint2 v;
+  v.x = pack_bf16x2(f[0], f[1]);
+  v.y = pack_bf16x2(f[2], f[3]);
+  return v;
+}
+
+// Two fp32 values -> two E4M3 codes (round to nearest even, saturate to +-448),
+// low byte = first value.
+__device__ __forceinline__ uint16_t cvt_e4m3x2(float a, float b) {
+  uint16_t r;
+  asm("cvt.rn.satfinite.e4m3x2.f32 %0, %2, %1;" : "=h"(r) : "f"(a), "f"(b));
+  return r;
+}
+
+__device__ __forceinline__ uint32_t cvt_e4m3x4(float a, float b, float c, float d) {
+  return uint32_t(cvt_e4m3x2(a, b)) | (uint32_t(cvt_e4m3x2(c, d)) << 16);
+}
+
+// MXFP8 (OCP MX, E8M0 scale, 32-element blocks) exponent selection used by the
+// reference quantizer (src/qwen_image_accel/kernels/mxfp8.py:201-209): the
+// smallest power of two 2^(e-127) with amax / 2^(e-127) <= 448, read from the
+// fp32 bits of amax; 0 when the block is all zeros; clamped to [0, 254].
+__device__ __forceinline__ int mx_exponent(float amax) {
+  const uint32_t bits = __float_as_uint(amax);
+  int e = int((bits >> 23) & 0xffu) - 8 + (((bits & 0x7fffffu) > 6291456u) ? 1 : 0);
+  e = e < 0 ? 0 : (e > 254 ? 254 : e);
+  return amax == 0.0f ? 0 : e;
+}
+
+// 2^(127-e) as an exact fp32 bit pattern.
+__device__ __forceinline__ float mx_inverse_scale(int e) {
+  return __uint_as_float(uint32_t(254 - e) << 23);
+}
+
+// Byte offset of the E8M0 scale of (row, k-block) in the 128x4 blocked layout
+// consumed by block-scaled tensor-core MMAs (reference kernels/mxfp8.py:212-215):
+// 512-byte tiles of 128 rows x 4 k-blocks, ordered (row % 32, row / 32 % 4, kb % 4).
+__host__ __device__ __forceinline__ int64_t mx_scale_offset(int64_t row, int64_t kb, int64_t kb_tiles) {
+  return ((row >> 7) * kb_tiles + (kb >> 2)) * 512 + (row & 31) * 16 + ((row >> 5) & 3) * 4 + (kb & 3);
+}
+
+__device__ __forceinline__ float warp_max_xor(float v, int width_mask) {
+  for (int o = width_mask; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+}  // namespace qia

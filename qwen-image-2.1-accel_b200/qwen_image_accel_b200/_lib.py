@@ -1,0 +1,93 @@
+"""ctypes binding of libqia_b200.so (the C ABI declared in include/qia_b200.h).
+
+The library is loaded from this package directory. There is no fallback: if
+the shared library is missing or fails to load, every op raises.
+"""
+from __future__ import annotations
+
+import ctypes
+import threading
+from pathlib import Path
+
+import torch
+
+LIB_PATH = Path(__file__).resolve().parent / "libqia_b200.so"
+
+_P = ctypes.c_void_p
+_I = ctypes.c_int64
+_F = ctypes.c_float
+
+# name -> argument types (all return int status)
+SIGNATURES: dict[str, list] = {
+    "qia_ln_mod": [_P, _P, _P, _P, _I, _I, _I, _F, _P],
+    "qia_ln_mod_quant": [_P, _P, _P, _P, _P, _I, _I, _I, _F, _P],
+    "qia_gated_residual": [_P, _P, _P, _P, _I, _I, _I, _P],
+    "qia_adaln_residual": [_P, _P, _P, _P, _P, _P, _I, _I, _I, _F, _P],
+    "qia_rms_norm": [_P, _P, _P, _I, _I, _F, _P],
+    "qia_rope_qk": [_P, _P, _P, _P, _P, _I, _I, _I, _I, _P],
+    "qia_qknorm_rope_pack": [_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _F, _F, _P],
+    "qia_qknorm_rope_segment": [_P, _I, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _F, _F, _P],
+    "qia_swiglu": [_P, _P, _P, _I, _P],
+    "qia_swiglu_quant": [_P, _P, _P, _P, _I, _I, _P],
+    "qia_gelu_tanh": [_P, _P, _I, _P],
+    "qia_mxfp8_quantize": [_P, _I, _P, _P, _I, _I, _P],
+}
+
+_lock = threading.Lock()
+_lib: ctypes.CDLL | None = None
+
+
+class QiaError(RuntimeError):
+    """A qia_* entry point returned a non-zero status."""
+
+    def __init__(self, name: str, code: int, message: str):
+        super().__init__(f"{name} failed with status {code}: {message}")
+        self.code = code
+
+
+def load() -> ctypes.CDLL:
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is None:
+            if not LIB_PATH.exists():
+                raise RuntimeError(f"{LIB_PATH} is missing: build it with "
+                                   "`python qwen-image-2.1-accel_b200/build.py` (no CPU fallback exists)")
+            lib = ctypes.CDLL(str(LIB_PATH))
+            lib.qia_last_error_string.restype = ctypes.c_char_p
+            lib.qia_last_error_string.argtypes = []
+            lib.qia_abi_version.restype = ctypes.c_int
+            for name, args in SIGNATURES.items():
+                fn = getattr(lib, name)
+                fn.argtypes = args
+                fn.restype = ctypes.c_int
+            _lib = lib
+    return _lib
+
+
+def declared_symbols() -> list[str]:
+    return ["qia_last_error_string", "qia_abi_version", *SIGNATURES]
+
+
+def call(name: str, *args) -> None:
+    """Invoke a qia_* entry point and raise QiaError on a non-zero status."""
+    lib = load()
+    rc = getattr(lib, name)(*args)
+    if rc != 0:
+        msg = lib.qia_last_error_string().decode(errors="replace")
+        raise QiaError(name, rc, msg)
+
+
+def ptr(t: torch.Tensor | None):
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+def stream(device: torch.device | None = None):
+    return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+
+
+def require_cuda(*tensors: torch.Tensor | None) -> None:
+    for t in tensors:
+        if t is not None and not t.is_cuda:
+            raise ValueError("qwen_image_accel_b200 ops run on CUDA tensors only (no CPU path)")

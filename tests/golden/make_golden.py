@@ -1,0 +1,151 @@
+"""Generate the golden fixtures in tests/golden/ from the reference itself.
+
+Runs only where the reference checkout is mounted (it is read, never
+modified). Sources of truth, per fixture:
+
+* mxfp8_quantize.npz -- E8M0 scales from the reference's own Triton kernel
+  `_mx_quantize_kernel` (src/qwen_image_accel/kernels/mxfp8.py:190) run by the
+  Triton interpreter on the CPU; codes from the reference's known-answer rule
+  (tests/gpu/check_mxfp8.py:41-51): x * 2^(127-e) cast with torch's
+  float8_e4m3fn. (The interpreter's own fp8/bf16 casts truncate, so its codes
+  are not used.) Shapes and the outlier pattern follow check_mxfp8.py:59-62.
+* residual.npz -- eager `h + gate * x` in bf16, the oracle of the reference's
+  residual check (tests/gpu/check_fused.py:197-198).
+* ln_mod.npz -- eager bf16 `LayerNorm(x) * (1 + s) + shift` (CPU order; the
+  CUDA-order pin runs on the GPU against torch's CUDA LayerNorm).
+* rope_rms.npz -- Diffusers RMSNorm and apply_rotary_emb_qwen(use_real=False)
+  from the pinned wheel (the oracle of tests/gpu/check_attention_ops.py:264-267),
+  with freqs from QwenEmbedRope for a (1, 4, 4) grid and 16 text tokens.
+* activations.npz -- eager F.silu(g) * v and F.gelu(x, approximate="tanh").
+
+Usage: python tests/golden/make_golden.py [--reference /path/to/checkout]
+"""
+from __future__ import annotations
+
+import argparse
+import os
+import sys
+import tempfile
+import types
+import zipfile
+from pathlib import Path
+
+import numpy as np
+
+OUT = Path(__file__).resolve().parent
+
+
+def _bits(t):
+    import torch
+    return t.contiguous().view(torch.int16).numpy().view(np.uint16).copy()
+
+
+def _import_diffusers(reference: Path):
+    whl = next((reference / "third_party" / "wheels").glob("diffusers-*.whl"))
+    dest = Path(tempfile.mkdtemp(prefix="qia_golden_whl_"))
+    with zipfile.ZipFile(whl) as z:
+        z.extractall(dest)
+    sys.path.insert(0, str(dest))
+    import huggingface_hub
+    import huggingface_hub.errors
+    import huggingface_hub.utils
+    # attributes the pinned wheel imports but the installed hub release lacks
+    for mod, name, val in [(huggingface_hub, "resolve_revision", lambda *a, **k: None),
+                           (huggingface_hub.errors, "RevisionResolutionError",
+                            type("RevisionResolutionError", (Exception,), {})),
+                           (huggingface_hub.utils, "httpx", types.SimpleNamespace())]:
+        if not hasattr(mod, name):
+            setattr(mod, name, val)
+
+
+def make_mxfp8(reference: Path):
+    os.environ["TRITON_INTERPRET"] = "1"
+    sys.path.insert(0, str(reference / "src"))
+    import torch
+    from qwen_image_accel.kernels import mxfp8
+    torch.manual_seed(0)
+    cases = {}
+    for m, k in [(1, 128), (77, 256), (130, 256), (200, 384)]:
+        x = torch.randn(m, k, dtype=torch.bfloat16)
+        x[:, ::64] *= 40
+        if m > 100:
+            x[m // 3] *= 1e-3
+        a = mxfp8.quantize(x)
+        padded = a.values.shape[0]
+        scales = a.scales.view(torch.uint8)
+        # unswizzle the kernel's exponents back to [padded, k/32]
+        e = scales.view(padded // 128, k // 128, 32, 4, 4).permute(0, 3, 2, 1, 4).reshape(padded, k // 32)
+        xp = torch.zeros(padded, k, dtype=torch.bfloat16)
+        xp[:m] = x
+        codes = (xp.float().view(padded, k // 32, 32) * torch.exp2(127 - e.float())[..., None]
+                 ).to(torch.float8_e4m3fn).view(torch.uint8).view(padded, k)
+        cases[f"x_{m}_{k}"] = _bits(x)
+        cases[f"codes_{m}_{k}"] = codes.numpy()
+        cases[f"scales_{m}_{k}"] = scales.numpy().copy()
+    np.savez_compressed(OUT / "mxfp8_quantize.npz", **cases)
+
+
+def make_eager(reference: Path):
+    import torch
+    import torch.nn.functional as F
+    _import_diffusers(reference)
+    from diffusers.models.normalization import RMSNorm
+    from diffusers.models.transformers.transformer_qwenimage import QwenEmbedRope, apply_rotary_emb_qwen
+
+    torch.manual_seed(91)
+    res = {}
+    for b, s, d in [(1, 49, 256), (2, 9, 512)]:
+        h = torch.randn(b, s, d, dtype=torch.bfloat16)
+        x = torch.randn_like(h)
+        g = torch.randn(b, 1, d, dtype=torch.bfloat16).tanh()
+        res[f"h_{b}_{s}_{d}"], res[f"x_{b}_{s}_{d}"], res[f"g_{b}_{s}_{d}"] = _bits(h), _bits(x), _bits(g)
+        res[f"out_{b}_{s}_{d}"] = _bits(h + g * x)
+    np.savez_compressed(OUT / "residual.npz", **res)
+
+    torch.manual_seed(717)
+    ln = {}
+    for b, s, d in [(1, 7, 512), (2, 3, 1536), (1, 2, 3072)]:
+        x = torch.randn(b, s, d, dtype=torch.bfloat16) * 3
+        sc = (1 + 0.1 * torch.randn(b, 1, d)).to(torch.bfloat16)
+        sh = (0.1 * torch.randn(b, 1, d)).to(torch.bfloat16)
+        norm = torch.nn.LayerNorm(d, elementwise_affine=False, eps=1e-6)
+        key = f"{b}_{s}_{d}"
+        ln[f"x_{key}"], ln[f"scale_{key}"], ln[f"shift_{key}"] = _bits(x), _bits(sc), _bits(sh)
+        ln[f"out_{key}"] = _bits(norm(x) * sc + sh)
+        ln[f"noshift_{key}"] = _bits(norm(x) * sc)
+    np.savez_compressed(OUT / "ln_mod.npz", **ln)
+
+    torch.manual_seed(721)
+    rr = {}
+    rope = QwenEmbedRope(theta=10000, axes_dim=[16, 56, 56], scale_rope=True)
+    img_freqs, txt_freqs = rope([(1, 4, 4)], max_txt_seq_len=16, device=torch.device("cpu"))
+    rr["img_freqs"] = torch.view_as_real(img_freqs).numpy().copy()
+    rr["txt_freqs"] = torch.view_as_real(txt_freqs).numpy().copy()
+    nq = RMSNorm(128, eps=1e-6).to(torch.bfloat16)
+    with torch.no_grad():
+        nq.weight.copy_(torch.randn(128))
+    q = torch.randn(2, 16, 3, 128, dtype=torch.bfloat16) * 2
+    with torch.no_grad():
+        normed = nq(q)
+        rot = apply_rotary_emb_qwen(normed, img_freqs, use_real=False)
+    rr["q"], rr["w"], rr["normed"], rr["rotated"] = _bits(q), _bits(nq.weight.data), _bits(normed), _bits(rot)
+    np.savez_compressed(OUT / "rope_rms.npz", **rr)
+
+    torch.manual_seed(5)
+    act = {}
+    g = torch.randn(32, 128, dtype=torch.bfloat16) * 3
+    v = torch.randn(32, 128, dtype=torch.bfloat16)
+    act["g"], act["v"], act["swiglu"] = _bits(g), _bits(v), _bits(F.silu(g) * v)
+    x = torch.randn(32, 128, dtype=torch.bfloat16) * 4
+    act["x"], act["gelu"] = _bits(x), _bits(F.gelu(x, approximate="tanh"))
+    np.savez_compressed(OUT / "activations.npz", **act)
+
+
+if __name__ == "__main__":
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--reference", default="/root/reference")
+    args = ap.parse_args()
+    ref = Path(args.reference)
+    make_mxfp8(ref)   # first: the interpreter flag must precede the first triton import
+    make_eager(ref)
+    print("wrote", sorted(p.name for p in OUT.glob("*.npz")))

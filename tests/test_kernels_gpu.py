@@ -1,0 +1,301 @@
+"""GPU parity of the memory-bound kernels and the MXFP8 quantizer.
+
+Two oracles per op, as in the reference's own GPU checks:
+* the eager CUDA op the reference compares against with torch.equal
+  (tests/gpu/check_layernorm_ops.py, check_fused.py, check_attention_ops.py,
+  check_mx_epilogue.py) -- bit-exact;
+* the CPU oracle (oracle/) on the same seeded inputs -- bit-exact for integer
+  outputs, within one bf16 ulp for bf16 outputs (the oracle uses correctly
+  rounded rsqrt/exp/tanh where the GPU uses CUDA's).
+"""
+import numpy as np
+import pytest
+import torch
+import torch.nn.functional as F
+
+import oracle
+
+pytestmark = pytest.mark.gpu
+
+DEV = "cuda"
+
+
+def bits(t: torch.Tensor) -> np.ndarray:
+    return t.detach().contiguous().cpu().view(torch.int16).numpy().view(np.uint16)
+
+
+def u8(t: torch.Tensor) -> np.ndarray:
+    return t.detach().contiguous().cpu().view(torch.uint8).numpy()
+
+
+def close_bf16(a_bits, b_bits, atol=1e-6):
+    a = a_bits.astype(np.int32)
+    b = b_bits.astype(np.int32)
+    a = np.where(a & 0x8000, -(a & 0x7FFF), a)
+    b = np.where(b & 0x8000, -(b & 0x7FFF), b)
+    fa, fb = oracle.bf16_bits_to_f32(a_bits), oracle.bf16_bits_to_f32(b_bits)
+    return (np.abs(a - b) <= 1) | (np.abs(fa - fb) <= atol)
+
+
+@pytest.fixture(autouse=True)
+def _cuda():
+    if not torch.cuda.is_available():
+        pytest.skip("needs a CUDA device")
+
+
+# ------------------------------------------------------------------ LayerNorm
+@pytest.mark.parametrize("d", [3072, 4096])
+@pytest.mark.parametrize("b,n", [(1, 49), (2, 257), (1, 1024), (1, 4096)])
+@pytest.mark.parametrize("scale", [1e-3, 1.0, 20.0])
+def test_layer_norm_scale_equals_torch_cuda(d, b, n, scale):
+    from qwen_image_accel_b200.kernels.layernorm import layer_norm_scale
+    g = torch.Generator(device=DEV).manual_seed(717)
+    x = torch.randn(b, n, d, device=DEV, dtype=torch.bfloat16, generator=g) * scale
+    s = torch.randn(b, 1, d, device=DEV, dtype=torch.bfloat16, generator=g)
+    sh = torch.randn(b, 1, d, device=DEV, dtype=torch.bfloat16, generator=g) * 0.1
+    norm = torch.nn.LayerNorm(d, eps=1e-6, elementwise_affine=False).to(DEV)
+    assert torch.equal(layer_norm_scale(x, s, norm), norm(x) * s)
+    assert torch.equal(layer_norm_scale(x, s, norm, shift=sh), norm(x) * s + sh)
+
+
+@pytest.mark.parametrize("d", [3072, 4096])
+def test_layer_norm_scale_vs_oracle(d):
+    from qwen_image_accel_b200.kernels.layernorm import layer_norm_scale
+    g = torch.Generator(device=DEV).manual_seed(1)
+    x = torch.randn(2, 37, d, device=DEV, dtype=torch.bfloat16, generator=g) * 3
+    s = 1 + 0.1 * torch.randn(2, 1, d, device=DEV, dtype=torch.bfloat16, generator=g)
+    sh = 0.1 * torch.randn(2, 1, d, device=DEV, dtype=torch.bfloat16, generator=g)
+    norm = torch.nn.LayerNorm(d, eps=1e-6, elementwise_affine=False)
+    y = layer_norm_scale(x, s, norm, shift=sh)
+    ref = oracle.ln_mod(bits(x).reshape(-1, d), bits(s).reshape(2, d), bits(sh).reshape(2, d), 37)
+    ok = close_bf16(bits(y).reshape(-1, d), ref)
+    assert ok.all()
+    assert (bits(y).reshape(-1, d) == ref).mean() > 0.999
+
+
+@pytest.mark.parametrize("d", [3072, 4096])
+@pytest.mark.parametrize("b,n", [(1, 77), (2, 1024), (1, 2400), (2, 4352)])
+def test_ln_quantize_fused_equals_separate(d, b, n):
+    from qwen_image_accel_b200.kernels.epilogue import layer_norm_scale_quantize
+    from qwen_image_accel_b200.kernels.layernorm import layer_norm_scale
+    from qwen_image_accel_b200.kernels.mxfp8 import quantize
+    g = torch.Generator(device=DEV).manual_seed(0)
+    x = torch.randn(b, n, d, device=DEV, dtype=torch.bfloat16, generator=g)
+    x[..., ::512] *= 25
+    s = torch.randn(b, 1, d, device=DEV, dtype=torch.bfloat16, generator=g)
+    sh = torch.randn(b, 1, d, device=DEV, dtype=torch.bfloat16, generator=g)
+    norm = torch.nn.LayerNorm(d, eps=1e-6, elementwise_affine=False)
+    for shift in (None, sh):
+        fused = layer_norm_scale_quantize(x, s, norm, shift=shift)
+        sep = quantize(layer_norm_scale(x, s, norm, shift=shift).reshape(-1, d))
+        assert np.array_equal(u8(fused.values), u8(sep.values))
+        assert np.array_equal(u8(fused.scales), u8(sep.scales))
+        assert fused.rows == b * n and tuple(fused.shape) == (b, n, d)
+
+
+def test_adaln_residual_equals_eager():
+    from qwen_image_accel_b200.kernels.adaln import adaln_residual
+    g = torch.Generator(device=DEV).manual_seed(0)
+    x = torch.randn(1, 4096, 3072, device=DEV, dtype=torch.bfloat16, generator=g)
+    r = torch.randn(1, 4096, 3072, device=DEV, dtype=torch.bfloat16, generator=g)
+    shift = 0.1 * torch.randn(1, 1, 3072, device=DEV, dtype=torch.bfloat16, generator=g)
+    scale = 0.1 * torch.randn(1, 1, 3072, device=DEV, dtype=torch.bfloat16, generator=g)
+    gate = 0.1 * torch.randn(1, 1, 3072, device=DEV, dtype=torch.bfloat16, generator=g)
+    norm = torch.nn.LayerNorm(3072, eps=1e-6, elementwise_affine=False)
+    eager = r + gate * (norm(x) * (1 + scale) + shift)
+    assert torch.equal(adaln_residual(x, r, 1 + scale, shift, gate), eager)
+
+
+# ------------------------------------------------------------------ residual
+@pytest.mark.parametrize("b,s,d", [(1, 49, 4096), (2, 257, 4096), (1, 4096, 4096), (2, 4096, 3072)])
+def test_residual_equals_eager(b, s, d):
+    from qwen_image_accel_b200.kernels.elementwise import residual
+    g = torch.Generator(device=DEV).manual_seed(91)
+    h = torch.randn(b, s, d, device=DEV, dtype=torch.bfloat16, generator=g)
+    v = torch.randn(b, s, d, device=DEV, dtype=torch.bfloat16, generator=g)
+    gate = torch.randn(b, 1, d, device=DEV, dtype=torch.bfloat16, generator=g).tanh()
+    out = residual(h, v, gate)
+    assert torch.equal(out, h + gate * v)
+    if s <= 257:
+        ref = oracle.gated_residual(bits(h).reshape(-1, d), bits(v).reshape(-1, d), bits(gate).reshape(b, d), s)
+        assert np.array_equal(bits(out).reshape(-1, d), ref)
+
+
+# ------------------------------------------------------------------ RoPE / RMSNorm
+def eager_rope(x, freqs):
+    """Diffusers apply_rotary_emb_qwen(use_real=False) semantics."""
+    xr = torch.view_as_complex(x.float().reshape(*x.shape[:-1], -1, 2))
+    return torch.view_as_real(xr * freqs.unsqueeze(1)).flatten(3).type_as(x)
+
+
+def eager_rms(x, w, eps):
+    """Diffusers RMSNorm forward with a bf16 weight."""
+    var = x.to(torch.float32).pow(2).mean(-1, keepdim=True)
+    return (x * torch.rsqrt(var + eps)).to(w.dtype) * w
+
+
+@pytest.mark.parametrize("b,s,h", [(1, 49, 32), (2, 257, 32), (1, 4096, 24)])
+def test_rope_equals_eager(b, s, h):
+    from qwen_image_accel_b200.kernels.elementwise import rope_qk
+    g = torch.Generator(device=DEV).manual_seed(91)
+    q = torch.randn(b, s, h, 128, device=DEV, dtype=torch.bfloat16, generator=g)
+    k = torch.randn(b, s, h, 128, device=DEV, dtype=torch.bfloat16, generator=g)
+    phase = torch.randn(s, 64, device=DEV, generator=g)
+    freqs = torch.polar(torch.ones_like(phase), phase)
+    oq, ok = rope_qk(q, k, freqs)
+    assert torch.equal(oq, eager_rope(q, freqs)) and torch.equal(ok, eager_rope(k, freqs))
+    if s <= 257:
+        rq, rk = oracle.rope_qk(bits(q), bits(k), torch.view_as_real(freqs).cpu().numpy())
+        assert close_bf16(bits(oq), rq).all() and close_bf16(bits(ok), rk).all()
+
+
+@pytest.mark.parametrize("rows", [1, 49 * 32, 4096 * 24])
+def test_rms_norm_vs_eager(rows):
+    from qwen_image_accel_b200.kernels.bf16 import rms_norm
+    g = torch.Generator(device=DEV).manual_seed(3)
+    x = torch.randn(rows, 128, device=DEV, dtype=torch.bfloat16, generator=g) * 3
+    w = torch.randn(128, device=DEV, dtype=torch.bfloat16, generator=g)
+    out = rms_norm(x, w, 1e-6)
+    ref = eager_rms(x, w, 1e-6)
+    assert close_bf16(bits(out), bits(ref)).all()
+    assert (out == ref).float().mean().item() > 0.999
+    if rows <= 49 * 32:
+        assert close_bf16(bits(out), oracle.rms_norm(bits(x), bits(w))).all()
+
+
+@pytest.mark.parametrize("b,s,p,h", [(1, 49, 0, 32), (2, 257, 7, 32), (1, 1024, 99, 32), (1, 4096, 113, 32),
+                                     (2, 49, 1024, 32), (2, 300, 13, 24)])
+@pytest.mark.parametrize("scale", [1e-3, 1.0, 20.0])
+def test_prepare_attention_inputs_vs_eager(b, s, p, h, scale):
+    from qwen_image_accel_b200.kernels.attention import prepare_attention_inputs
+    g = torch.Generator(device=DEV).manual_seed(721)
+
+    class Norm:
+        eps = 1e-6
+        bias = None
+
+        def __init__(self):
+            self.weight = torch.randn(128, device=DEV, dtype=torch.bfloat16, generator=g)
+
+    nq, nk = Norm(), Norm()
+    q = torch.randn(b, s, h, 128, device=DEV, dtype=torch.bfloat16, generator=g) * scale
+    k = torch.randn(b, s, h, 128, device=DEV, dtype=torch.bfloat16, generator=g) * scale
+    v = torch.randn(b, s, h, 128, device=DEV, dtype=torch.bfloat16, generator=g)
+    ck = torch.randn(b, p, h, 128, device=DEV, dtype=torch.bfloat16, generator=g)
+    cv = torch.randn(b, p, h, 128, device=DEV, dtype=torch.bfloat16, generator=g)
+    phase = torch.randn(s, 64, device=DEV, generator=g)
+    f = torch.polar(torch.ones_like(phase), phase)
+    oq, ok, ov = prepare_attention_inputs(q, k, v, nq, nk, f, ck, cv)
+    rq = eager_rope(eager_rms(q, nq.weight, 1e-6), f)
+    rk = eager_rope(eager_rms(k, nk.weight, 1e-6), f)
+    assert close_bf16(bits(oq), bits(rq)).all() and (oq == rq).float().mean().item() > 0.999
+    assert close_bf16(bits(ok), bits(torch.cat([ck, rk], 1))).all()
+    assert torch.equal(ov, torch.cat([cv, v], 1)) and torch.equal(ok[:, :p], ck)
+    if b * s * h <= 2 * 300 * 24:
+        eq, ek, ev = oracle.qknorm_rope_pack(bits(q), bits(k), bits(v), bits(ck) if p else None,
+                                             bits(cv) if p else None, bits(nq.weight), bits(nk.weight),
+                                             torch.view_as_real(f).cpu().numpy())
+        assert close_bf16(bits(oq), eq).all() and close_bf16(bits(ok), ek).all() and np.array_equal(bits(ov), ev)
+
+
+def test_prepare_attention_inputs_fallback_contract():
+    from qwen_image_accel_b200.kernels.attention import prepare_attention_inputs
+
+    class Norm:
+        eps = 1e-6
+        bias = None
+        weight = torch.ones(128, device=DEV, dtype=torch.bfloat16)
+
+    q = torch.randn(1, 8, 4, 128, device=DEV, dtype=torch.bfloat16)
+    ck = torch.randn(1, 2, 4, 128, device=DEV, dtype=torch.bfloat16)
+    f = torch.polar(torch.ones(8, 64, device=DEV), torch.zeros(8, 64, device=DEV))
+    assert prepare_attention_inputs(q, q, q, Norm, Norm, None, ck, ck) is None
+    assert prepare_attention_inputs(q.float(), q.float(), q.float(), Norm, Norm, f, ck, ck) is None
+    assert prepare_attention_inputs(q.transpose(1, 2), q.transpose(1, 2), q.transpose(1, 2), Norm, Norm, f, ck,
+                                    ck) is None
+
+
+def test_joint_segment_vs_oracle():
+    from qwen_image_accel_b200.kernels.attention import joint_qk_norm_rope
+    g = torch.Generator(device=DEV).manual_seed(11)
+    b, h, ltxt, limg = 2, 3, 16, 40
+    qkv_t = torch.randn(b, ltxt, 3 * h * 128, device=DEV, dtype=torch.bfloat16, generator=g)
+    qkv_i = torch.randn(b, limg, 3 * h * 128, device=DEV, dtype=torch.bfloat16, generator=g) * 2
+    wt = [torch.randn(128, device=DEV, dtype=torch.bfloat16, generator=g) for _ in range(2)]
+    wi = [torch.randn(128, device=DEV, dtype=torch.bfloat16, generator=g) for _ in range(2)]
+    ft = torch.randn(ltxt, 64, 2, device=DEV, generator=g)
+    fi = torch.randn(limg, 64, 2, device=DEV, generator=g)
+    S = ltxt + limg
+    oq, ok, ov = (torch.empty(b, S, h, 128, device=DEV, dtype=torch.bfloat16) for _ in range(3))
+    joint_qk_norm_rope(qkv_t, wt[0], wt[1], ft, oq, ok, ov, 0)
+    joint_qk_norm_rope(qkv_i, wi[0], wi[1], fi, oq, ok, ov, ltxt)
+    eq, ek, ev = (np.zeros((b, S, h, 128), np.uint16) for _ in range(3))
+    oracle.qknorm_rope_segment(bits(qkv_t), bits(wt[0]), bits(wt[1]), ft.cpu().numpy(), eq, ek, ev, b, ltxt, 0, h)
+    oracle.qknorm_rope_segment(bits(qkv_i), bits(wi[0]), bits(wi[1]), fi.cpu().numpy(), eq, ek, ev, b, limg, ltxt, h)
+    assert close_bf16(bits(oq), eq).all() and close_bf16(bits(ok), ek).all() and np.array_equal(bits(ov), ev)
+    assert (bits(oq) == eq).mean() > 0.999
+
+
+# ------------------------------------------------------------------ FFN activations
+@pytest.mark.parametrize("rows,width", [(128, 12288), (1024, 12288), (2400, 12288)])
+def test_swiglu_and_quant(rows, width):
+    from qwen_image_accel_b200.kernels.bf16 import swiglu
+    from qwen_image_accel_b200.kernels.epilogue import swiglu_quantize
+    from qwen_image_accel_b200.kernels.mxfp8 import quantize
+    g = torch.Generator(device=DEV).manual_seed(0)
+    gt = torch.randn(rows, width, device=DEV, dtype=torch.bfloat16, generator=g) * 3
+    v = torch.randn(rows, width, device=DEV, dtype=torch.bfloat16, generator=g)
+    out = swiglu(gt, v)
+    assert torch.equal(out, F.silu(gt) * v)
+    fused = swiglu_quantize(gt, v)
+    sep = quantize(out)
+    assert np.array_equal(u8(fused.values), u8(sep.values)) and np.array_equal(u8(fused.scales), u8(sep.scales))
+    if rows <= 128:
+        ref = oracle.swiglu(bits(gt), bits(v))
+        assert close_bf16(bits(out), ref).all()
+
+
+def test_gelu_tanh_equals_torch():
+    from qwen_image_accel_b200.kernels.bf16 import gelu_tanh
+    g = torch.Generator(device=DEV).manual_seed(4)
+    x = torch.randn(4096, 12288, device=DEV, dtype=torch.bfloat16, generator=g) * 4
+    out = gelu_tanh(x)
+    assert torch.equal(out, F.gelu(x, approximate="tanh"))
+    small = x[:64]
+    assert close_bf16(bits(out[:64]), oracle.gelu_tanh(bits(small))).all()
+
+
+# ------------------------------------------------------------------ MXFP8 quantizer
+@pytest.mark.parametrize("m,k", [(128, 4096), (1024, 4096), (1536, 4096), (2400, 4096), (4096, 12288),
+                                 (16384, 4096), (77, 4096), (1, 4096), (4352, 3072), (16640, 3072)])
+def test_mxfp8_quantize_bit_exact(m, k):
+    from qwen_image_accel_b200.kernels.mxfp8 import quantize
+    g = torch.Generator(device=DEV).manual_seed(0)
+    x = torch.randn(m, k, device=DEV, dtype=torch.bfloat16, generator=g)
+    x[:, ::512] *= 40
+    if m > 200:
+        x[m // 3] *= 1e-3
+    a = quantize(x)
+    assert a.rows == m and a.values.shape == ((m + 127) // 128 * 128, k)
+    if m * k <= 2400 * 4096:
+        cq, cs = oracle.mx_quantize(bits(x))
+        assert np.array_equal(u8(a.values), cq) and np.array_equal(u8(a.scales), cs)
+    # size-independent: dequantize -> requantize is the identity (idempotence)
+    vals = a.values.float().view(-1, k // 32, 32)
+    sc = a.scales.view(torch.uint8)
+    padded = a.values.shape[0]
+    e = sc.view(padded // 128, k // 128, 32, 4, 4).permute(0, 3, 2, 1, 4).reshape(padded, k // 32)
+    deq = (vals * torch.exp2(e.float() - 127)[..., None]).view(padded, k)[:m].to(torch.bfloat16)
+    b = quantize(deq)
+    assert torch.equal(b.values.view(torch.uint8), a.values.view(torch.uint8))
+    assert torch.equal(b.scales.view(torch.uint8), a.scales.view(torch.uint8))
+
+
+def test_quantize_strided_rows():
+    from qwen_image_accel_b200.kernels.mxfp8 import quantize
+    x = torch.randn(300, 1024, device=DEV, dtype=torch.bfloat16)
+    sub = x[:, :512]
+    a = quantize(sub)
+    b = quantize(sub.contiguous())
+    assert torch.equal(a.values.view(torch.uint8), b.values.view(torch.uint8))
+    assert torch.equal(a.scales.view(torch.uint8), b.scales.view(torch.uint8))
