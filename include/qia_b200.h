@@ -161,6 +161,51 @@ int qia_gelu_tanh(const void* x, void* out, int64_t n, void* stream);
 int qia_mxfp8_quantize(const void* x, int64_t ld, void* q_values, void* q_scales,
                        int64_t rows, int64_t k, void* stream);
 
+/* ---------------------------------------------------------------------------
+ * Block-scaled MXFP8 GEMM (tcgen05, TMEM accumulators, TMA-fed)
+ *
+ * A: MXFP8 activation [ceil(m/128)*128, k] + scales; B: MXFP8 weight [n, k]
+ * (the nn.Linear weight layout) + scales; fp32 accumulation; bias: bf16 [n] or
+ * NULL. k and n multiples of 128. Rows past m are not written (bf16 outputs).
+ * Replaces: MXFP8Linear.matmul / torch._scaled_mm
+ * (src/qwen_image_accel/optimizations/mxfp8.py:229-233), with the epilogues
+ * of the dual-stream block's linears (WHL:diffusers/models/attention.py:1736,
+ * activations.py:81-90, transformer_qwenimage.py:767-774).
+ * ------------------------------------------------------------------------ */
+
+/* out[m, n] (row stride ldo) = bf16(A . B^T + bias). */
+int qia_mxfp8_gemm(const void* a_values, const void* a_scales, const void* b_values,
+                   const void* b_scales, const void* bias, void* out, int64_t m,
+                   int64_t n, int64_t k, int64_t ldo, void* stream);
+
+/* out = bf16(gelu_tanh(bf16(A . B^T + bias))). */
+int qia_mxfp8_gemm_gelu(const void* a_values, const void* a_scales,
+                        const void* b_values, const void* b_scales,
+                        const void* bias, void* out, int64_t m, int64_t n,
+                        int64_t k, int64_t ldo, void* stream);
+
+/* The FFN up-projection feeding the down-projection: the bf16 GELU result is
+ * quantized to MXFP8 in the epilogue (n becomes the next GEMM's K).
+ * q_values: [ceil(m/128)*128, n] e4m3 (padding rows zero), q_scales blocked. */
+int qia_mxfp8_gemm_gelu_quant(const void* a_values, const void* a_scales,
+                              const void* b_values, const void* b_scales,
+                              const void* bias, void* q_values, void* q_scales,
+                              int64_t m, int64_t n, int64_t k, void* stream);
+
+/* Gated residual epilogue: out = bf16(resid + bf16(gate[b] * bf16(A . B^T + bias)))
+ * with b = row / rows_per_batch; gate: [m / rows_per_batch, n]; resid and out
+ * share the row stride ldo and may be the same buffer (in-place update). */
+int qia_mxfp8_gemm_gate_residual(const void* a_values, const void* a_scales,
+                                 const void* b_values, const void* b_scales,
+                                 const void* bias, const void* gate,
+                                 const void* resid, void* out, int64_t m,
+                                 int64_t n, int64_t k, int64_t ldo,
+                                 int64_t rows_per_batch, void* stream);
+
+/* Reads and clears the device-side error word of the current device (set when
+ * a bounded wait inside a tensor-core kernel gave up). Synchronises the device. */
+int qia_device_error(int* code);
+
 #ifdef __cplusplus
 }
 #endif

@@ -228,20 +228,19 @@ void oracle_gated_residual(const uint16_t* h, const uint16_t* x, const uint16_t*
 }
 
 /* ---------------------------------------------------------------- QK norm + RoPE */
-/* reference kernels/bf16.py:46-55 (RMSNorm, two rounding points); the sum of
- * squares follows the GPU kernel's order: 16 sequential partial sums of 8
- * exact squares, then a 16-way xor tree (8, 4, 2, 1). */
+/* reference kernels/bf16.py:46-55 (RMSNorm, two rounding points). The sum of
+ * squares follows PyTorch's CUDA mean(-1) over 128 fp32 values (the eager
+ * Diffusers RMSNorm), checked against torch on the GPU: 32 vec4 partials
+ * ((a+b)+c)+d over contiguous groups, then a halving tree g[t] += g[t + w]
+ * for w = 16, 8, 4, 2, 1. Squares of bf16 values are exact in fp32. */
 static void rms_row(const float* in, const uint16_t* w, float eps, float* out) {
-  float part[16], nxt[16];
-  for (int t = 0; t < 16; ++t) {
-    float s = 0.0f;
-    for (int i = 0; i < 8; ++i) s = fmaf(in[t * 8 + i], in[t * 8 + i], s);
-    part[t] = s;
+  float part[32];
+  for (int t = 0; t < 32; ++t) {
+    const float* e = in + 4 * t;
+    part[t] = ((e[0] * e[0] + e[1] * e[1]) + e[2] * e[2]) + e[3] * e[3];
   }
-  for (int o = 8; o > 0; o >>= 1) {
-    for (int t = 0; t < 16; ++t) nxt[t] = part[t] + part[t ^ o];
-    memcpy(part, nxt, sizeof(part));
-  }
+  for (int width = 16; width >= 1; width >>= 1)
+    for (int t = 0; t < width; ++t) part[t] = part[t] + part[t + width];
   float r = rsqrt_ref(part[0] / 128.0f + eps);
   for (int c = 0; c < 128; ++c) out[c] = rbf(rbf(in[c] * r) * bf2f(w[c]));
 }

@@ -9,7 +9,7 @@
 //
 // Work split: one head row (128 bf16 = 256 B) per 16 threads, 8 contiguous
 // elements (one 16-byte load) per thread; the sum of squares is a per-thread
-// sequential sum followed by a 16-lane xor tree. RoPE pairs never cross a
+// sum in PyTorch's mean(-1) order (see rms_normalize). RoPE pairs never cross a
 // thread. Every access is a 16-byte vector access.
 #include "qia_common.cuh"
 
@@ -22,12 +22,20 @@ constexpr int kLanesPerRow = 16;
 __device__ __forceinline__ void rms_normalize(float (&f)[8], const float (&w)[8], float eps) {
   // Only the 16 lanes of this head row take part: the two half-warps may be
   // on different rows, loop trips or branches.
+  // Sum of squares in the order of PyTorch's CUDA mean(-1) over 128 fp32
+  // values (the eager Diffusers RMSNorm): 32 vec4 partials ((a+b)+c)+d over
+  // contiguous groups, then a halving tree g[t] += g[t + w] for w = 16, 8, 4,
+  // 2, 1. Lane j of the 16-lane row group holds groups 2j (p0) and 2j+1 (p1):
+  // w = 16..2 pair lanes j and j^8, j^4, j^2, j^1; w = 1 is p0 + p1.
   const unsigned mask = 0xffffu << (threadIdx.x & 16);
-  float ss = 0.0f;
+  float p0 = ((f[0] * f[0] + f[1] * f[1]) + f[2] * f[2]) + f[3] * f[3];
+  float p1 = ((f[4] * f[4] + f[5] * f[5]) + f[6] * f[6]) + f[7] * f[7];
 #pragma unroll
-  for (int i = 0; i < 8; ++i) ss = __fmaf_rn(f[i], f[i], ss);
-#pragma unroll
-  for (int o = 8; o > 0; o >>= 1) ss += __shfl_xor_sync(mask, ss, o);
+  for (int o = 8; o > 0; o >>= 1) {
+    p0 += __shfl_xor_sync(mask, p0, o);
+    p1 += __shfl_xor_sync(mask, p1, o);
+  }
+  const float ss = p0 + p1;
   const float r = rsqrtf(ss / float(kHeadDim) + eps);
 #pragma unroll
   for (int i = 0; i < 8; ++i) f[i] = round_bf16(__fmul_rn(round_bf16(__fmul_rn(f[i], r)), w[i]));

@@ -35,7 +35,35 @@ int sm_count() {
   return cached[dev];
 }
 
+__device__ int g_qia_device_error = 0;
+
+int* device_error_word() {
+  static int* cached[64] = {nullptr};
+  static std::mutex mu;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+  std::lock_guard<std::mutex> lock(mu);
+  if (!cached[dev]) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_qia_device_error) != cudaSuccess) return nullptr;
+    cached[dev] = static_cast<int*>(p);
+  }
+  return cached[dev];
+}
+
 }  // namespace qia
+
+extern "C" int qia_device_error(int* code) {
+  if (!code) return qia::set_error(QIA_ERR_INVALID, "qia_device_error: null output");
+  int v = 0;
+  cudaError_t e = cudaMemcpyFromSymbol(&v, qia::g_qia_device_error, sizeof(int));
+  if (e != cudaSuccess) return qia::set_error(QIA_ERR_CUDA, "qia_device_error: %s", cudaGetErrorString(e));
+  const int zero = 0;
+  e = cudaMemcpyToSymbol(qia::g_qia_device_error, &zero, sizeof(int));
+  if (e != cudaSuccess) return qia::set_error(QIA_ERR_CUDA, "qia_device_error: %s", cudaGetErrorString(e));
+  *code = v;
+  return QIA_OK;
+}
 
 extern "C" const char* qia_last_error_string(void) { return qia::g_last_error; }
 

@@ -22,13 +22,6 @@ namespace {
 
 __device__ __forceinline__ float silu_ref(float g) { return round_bf16(__fdiv_rn(g, 1.0f + expf(-g))); }
 
-__device__ __forceinline__ float gelu_tanh_ref(float x) {
-  const float k_beta = float(M_SQRT2 * M_2_SQRTPI * 0.5);
-  const float k_kappa = 0.044715f;
-  const float x_cube = __fmul_rn(__fmul_rn(x, x), x);
-  const float inner = __fmul_rn(k_beta, __fmaf_rn(k_kappa, x_cube, x));
-  return __fmul_rn(__fmul_rn(0.5f, x), 1.0f + tanhf(inner));
-}
 
 // Quantize 8 values (one quarter of an MX block) held by this lane; the 4 lanes
 // of the block are adjacent and aligned (lane % 4 == 0 starts a block).
@@ -103,7 +96,7 @@ __global__ void gelu_tanh_kernel(const uint4* __restrict__ x, uint4* __restrict_
     float f[8];
     unpack8(__ldg(x + i), f);
 #pragma unroll
-    for (int j = 0; j < 8; ++j) f[j] = gelu_tanh_ref(f[j]);
+    for (int j = 0; j < 8; ++j) f[j] = round_bf16(gelu_tanh_f32(f[j]));
     out[i] = pack8(f);
   }
 }

@@ -12,6 +12,7 @@
 #include <stdint.h>
 #include <stdarg.h>
 #include <stdio.h>
+#include <math.h>
 
 #include "../../include/qia_b200.h"
 
@@ -31,6 +32,11 @@ inline bool aligned(const void* p, uintptr_t a) {
 
 // Number of SMs of the current device (cached per device).
 int sm_count();
+
+// Device address of the library's device-side error word on the current
+// device (bounded waits that give up write QIA_ERR_TIMEOUT there); nullptr
+// if it cannot be resolved.
+int* device_error_word();
 
 // ---------------------------------------------------------------------------
 // Device helpers
@@ -111,6 +117,17 @@ __device__ __forceinline__ float mx_inverse_scale(int e) {
 // 512-byte tiles of 128 rows x 4 k-blocks, ordered (row % 32, row / 32 % 4, kb % 4).
 __host__ __device__ __forceinline__ int64_t mx_scale_offset(int64_t row, int64_t kb, int64_t kb_tiles) {
   return ((row >> 7) * kb_tiles + (kb >> 2)) * 512 + (row & 31) * 16 + ((row >> 5) & 3) * 4 + (kb & 3);
+}
+
+// PyTorch's CUDA GELU (approximate="tanh") in fp32 opmath:
+// 0.5*x*(1 + tanh(sqrt(2/pi) * (x + 0.044715*x^3))), with x^3 = (x*x)*x and the
+// inner sum contracted to one fma.
+__device__ __forceinline__ float gelu_tanh_f32(float x) {
+  const float k_beta = float(M_SQRT2 * M_2_SQRTPI * 0.5);
+  const float k_kappa = 0.044715f;
+  const float x_cube = __fmul_rn(__fmul_rn(x, x), x);
+  const float inner = __fmul_rn(k_beta, __fmaf_rn(k_kappa, x_cube, x));
+  return __fmul_rn(__fmul_rn(0.5f, x), 1.0f + tanhf(inner));
 }
 
 __device__ __forceinline__ float warp_max_xor(float v, int width_mask) {

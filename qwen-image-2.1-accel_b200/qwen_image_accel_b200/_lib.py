@@ -31,6 +31,11 @@ SIGNATURES: dict[str, list] = {
     "qia_swiglu_quant": [_P, _P, _P, _P, _I, _I, _P],
     "qia_gelu_tanh": [_P, _P, _I, _P],
     "qia_mxfp8_quantize": [_P, _I, _P, _P, _I, _I, _P],
+    "qia_mxfp8_gemm": [_P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _P],
+    "qia_mxfp8_gemm_gelu": [_P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _P],
+    "qia_mxfp8_gemm_gelu_quant": [_P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _P],
+    "qia_mxfp8_gemm_gate_residual": [_P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _P],
+    "qia_device_error": [_P],
 }
 
 _lock = threading.Lock()
@@ -77,6 +82,13 @@ def call(name: str, *args) -> None:
     if rc != 0:
         msg = lib.qia_last_error_string().decode(errors="replace")
         raise QiaError(name, rc, msg)
+
+
+def device_error() -> int:
+    """Read and clear the device-side error word (synchronises the device)."""
+    v = ctypes.c_int(0)
+    call("qia_device_error", ctypes.byref(v))
+    return v.value
 
 
 def ptr(t: torch.Tensor | None):

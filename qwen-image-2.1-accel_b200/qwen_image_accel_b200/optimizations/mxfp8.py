@@ -1,0 +1,151 @@
+"""Block-scaled MXFP8 linears on the tcgen05 GEMM.
+
+Mirrors src/qwen_image_accel/optimizations/mxfp8.py: MXFP8Linear (weight
+stored as E4M3 + swizzled E8M0, `.matmul(activation)` on an already-quantized
+activation, `.forward(x)`), LAYER_GROUPS, selected_layers and
+quantize_transformer. Extensions for the dual-stream (v1) block: linears with
+a bias, and the fused epilogues of qia_mxfp8_gemm_* (GELU-tanh, GELU-tanh +
+MXFP8 requantization, gate + residual).
+"""
+from __future__ import annotations
+
+import os
+
+import torch
+from torch import nn
+
+from .. import _lib
+from ..kernels.mxfp8 import Quantized, empty_quantized, quantize
+
+
+def _supported(k, n):
+    return k % 128 == 0 and n % 128 == 0
+
+
+class MXFP8Linear(nn.Module):
+    """Linear whose weight is stored as MXFP8 and multiplied as MXFP8."""
+
+    def __init__(self, linear: nn.Linear):
+        super().__init__()
+        self.in_features, self.out_features = linear.in_features, linear.out_features
+        if not _supported(self.in_features, self.out_features):
+            raise ValueError("MXFP8Linear needs in/out features that are multiples of 128")
+        weight = linear.weight.detach().to(torch.bfloat16).contiguous()
+        q = quantize(weight)
+        self.register_buffer("weight_fp8", q.values.t())     # (K, N) column-major, as in the reference
+        self.register_buffer("weight_scale", q.scales)
+        b = linear.bias
+        self.register_buffer("bias", None if b is None else b.detach().to(torch.bfloat16).contiguous())
+
+    # the [N, K] row-major view the kernels consume
+    def _w(self):
+        return self.weight_fp8.t()
+
+    def _args(self, activation: Quantized):
+        if activation.values.shape[1] != self.in_features:
+            raise ValueError(f"activation K={activation.values.shape[1]} != in_features={self.in_features}")
+        w = self._w()
+        return (_lib.ptr(activation.values), _lib.ptr(activation.scales), _lib.ptr(w), _lib.ptr(self.weight_scale),
+                _lib.ptr(self.bias))
+
+    def matmul(self, activation: Quantized, dtype=torch.bfloat16, out: torch.Tensor | None = None) -> torch.Tensor:
+        """bf16 (rows, N) = activation @ W^T (+ bias); several weights can share one activation."""
+        if dtype != torch.bfloat16:
+            raise NotImplementedError("MXFP8Linear.matmul produces bf16")
+        m, n = activation.rows, self.out_features
+        if out is None:
+            out = torch.empty((m, n), device=activation.values.device, dtype=torch.bfloat16)
+        _lib.call("qia_mxfp8_gemm", *self._args(activation), _lib.ptr(out), m, n, self.in_features, out.stride(0),
+                  _lib.stream(out.device))
+        return out
+
+    def matmul_gelu(self, activation: Quantized) -> torch.Tensor:
+        """bf16 gelu_tanh(activation @ W^T + bias)."""
+        m, n = activation.rows, self.out_features
+        out = torch.empty((m, n), device=activation.values.device, dtype=torch.bfloat16)
+        _lib.call("qia_mxfp8_gemm_gelu", *self._args(activation), _lib.ptr(out), m, n, self.in_features, n,
+                  _lib.stream(out.device))
+        return out
+
+    def matmul_gelu_quantize(self, activation: Quantized) -> Quantized:
+        """gelu_tanh(activation @ W^T + bias) quantized to MXFP8 in the GEMM epilogue."""
+        m, n = activation.rows, self.out_features
+        q = empty_quantized(m, n, activation.values.device)
+        _lib.call("qia_mxfp8_gemm_gelu_quant", *self._args(activation), _lib.ptr(q.values), _lib.ptr(q.scales), m, n,
+                  self.in_features, _lib.stream(q.values.device))
+        return q
+
+    def matmul_gate_residual(self, activation: Quantized, gate: torch.Tensor, residual: torch.Tensor,
+                             out: torch.Tensor | None = None) -> torch.Tensor:
+        """residual + gate * (activation @ W^T + bias), each step rounded to bf16.
+
+        residual/out: (B, S, N) or (B*S, N) bf16; gate: (B, 1, N) or (B, N).
+        out may be residual itself (in-place update)."""
+        m, n = activation.rows, self.out_features
+        res2 = residual.reshape(-1, n)
+        if res2.shape[0] != m or not res2.is_contiguous():
+            raise ValueError("residual must be contiguous with the activation's rows")
+        rows_per_batch = m // gate.reshape(-1, n).shape[0]
+        if out is None:
+            out = torch.empty_like(residual)
+        _lib.call("qia_mxfp8_gemm_gate_residual", *self._args(activation), _lib.ptr(gate), _lib.ptr(res2),
+                  _lib.ptr(out), m, n, self.in_features, n, rows_per_batch, _lib.stream(out.device))
+        return out
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        flat = x.reshape(-1, x.shape[-1])
+        activation = quantize(flat if flat.stride(-1) == 1 else flat.contiguous())
+        return self.matmul(activation, x.dtype).reshape(*x.shape[:-1], self.out_features)
+
+
+# Which of a block's linears each selection converts. `attention` covers the
+# projections around attention, `mlp` the feed-forward projections; names of
+# both the single-stream 2.1 block and the dual-stream v1 block are listed
+# (absent names are skipped).
+LAYER_GROUPS = {
+    "attention": ("attn.to_q", "attn.to_k", "attn.to_v", "attn.to_out.0",
+                  "attn.add_q_proj", "attn.add_k_proj", "attn.add_v_proj", "attn.to_add_out"),
+    "mlp": ("img_mlp.gate_layer", "img_mlp.proj", "img_mlp.out",
+            "img_mlp.net.0.proj", "img_mlp.net.2", "txt_mlp.net.0.proj", "txt_mlp.net.2"),
+}
+LAYER_GROUPS["all"] = LAYER_GROUPS["attention"] + LAYER_GROUPS["mlp"]
+
+
+def selected_layers(selection=None):
+    """Resolve QW21_MXFP8_LAYERS: a group name or an explicit comma-separated list."""
+    raw = (selection if selection is not None else os.environ.get("QW21_MXFP8_LAYERS", "all")).strip()
+    if raw in LAYER_GROUPS:
+        return set(LAYER_GROUPS[raw])
+    names = {n.strip() for n in raw.split(",") if n.strip()}
+    unknown = names - set(LAYER_GROUPS["all"])
+    if unknown:
+        raise ValueError(f"Unknown MXFP8 layer names {sorted(unknown)}; "
+                         f"choose from {sorted(LAYER_GROUPS['all'])} or {sorted(LAYER_GROUPS)}")
+    return names
+
+
+def quantize_transformer(transformer, skip_blocks=None, layers=None):
+    """Replace selected block linears with MXFP8Linear; everything else stays BF16.
+
+    Blocks listed in skip_blocks (default QW21_MXFP8_SKIP_BLOCKS or "0,31")
+    keep every linear in BF16. Returns the converted module names."""
+    raw = skip_blocks if skip_blocks is not None else os.environ.get("QW21_MXFP8_SKIP_BLOCKS", "0,31")
+    skip = {int(i) for i in str(raw).split(",") if i.strip()}
+    wanted = selected_layers(layers)
+    converted = []
+    with torch.no_grad():
+        for index, block in enumerate(transformer.transformer_blocks):
+            if index in skip:
+                continue
+            for name in sorted(wanted):
+                try:
+                    child = block.get_submodule(name)
+                except AttributeError:
+                    continue
+                if not isinstance(child, nn.Linear) or not _supported(child.in_features, child.out_features):
+                    continue
+                parent_name, _, leaf = name.rpartition(".")
+                parent = block.get_submodule(parent_name) if parent_name else block
+                setattr(parent, leaf, MXFP8Linear(child))
+                converted.append(f"transformer_blocks.{index}.{name}")
+    return converted

@@ -28,13 +28,18 @@ def u8(t: torch.Tensor) -> np.ndarray:
     return t.detach().contiguous().cpu().view(torch.uint8).numpy()
 
 
-def close_bf16(a_bits, b_bits, atol=1e-6):
+def close_bf16(a_bits, b_bits, atol=1e-6, ulps=1):
+    """Within `ulps` bf16 ulps or `atol` absolutely. Chains with two bf16
+    rounding points (RMSNorm: normalise -> bf16 -> * weight -> bf16) use
+    ulps=2 against the oracle: a one-ulp difference at the first rounding
+    (CUDA rsqrtf vs the oracle's correctly rounded rsqrt) can become two after
+    the weight multiply."""
     a = a_bits.astype(np.int32)
     b = b_bits.astype(np.int32)
     a = np.where(a & 0x8000, -(a & 0x7FFF), a)
     b = np.where(b & 0x8000, -(b & 0x7FFF), b)
     fa, fb = oracle.bf16_bits_to_f32(a_bits), oracle.bf16_bits_to_f32(b_bits)
-    return (np.abs(a - b) <= 1) | (np.abs(fa - fb) <= atol)
+    return (np.abs(a - b) <= ulps) | (np.abs(fa - fb) <= atol)
 
 
 @pytest.fixture(autouse=True)
@@ -160,7 +165,8 @@ def test_rms_norm_vs_eager(rows):
     assert close_bf16(bits(out), bits(ref)).all()
     assert (out == ref).float().mean().item() > 0.999
     if rows <= 49 * 32:
-        assert close_bf16(bits(out), oracle.rms_norm(bits(x), bits(w))).all()
+        ref = oracle.rms_norm(bits(x), bits(w))
+        assert close_bf16(bits(out), ref, ulps=2).all() and (bits(out) == ref).mean() > 0.999
 
 
 @pytest.mark.parametrize("b,s,p,h", [(1, 49, 0, 32), (2, 257, 7, 32), (1, 1024, 99, 32), (1, 4096, 113, 32),
@@ -188,14 +194,15 @@ def test_prepare_attention_inputs_vs_eager(b, s, p, h, scale):
     oq, ok, ov = prepare_attention_inputs(q, k, v, nq, nk, f, ck, cv)
     rq = eager_rope(eager_rms(q, nq.weight, 1e-6), f)
     rk = eager_rope(eager_rms(k, nk.weight, 1e-6), f)
-    assert close_bf16(bits(oq), bits(rq)).all() and (oq == rq).float().mean().item() > 0.999
-    assert close_bf16(bits(ok), bits(torch.cat([ck, rk], 1))).all()
+    assert close_bf16(bits(oq), bits(rq), ulps=2).all() and (oq == rq).float().mean().item() > 0.999
+    assert close_bf16(bits(ok), bits(torch.cat([ck, rk], 1)), ulps=2).all()
     assert torch.equal(ov, torch.cat([cv, v], 1)) and torch.equal(ok[:, :p], ck)
     if b * s * h <= 2 * 300 * 24:
         eq, ek, ev = oracle.qknorm_rope_pack(bits(q), bits(k), bits(v), bits(ck) if p else None,
                                              bits(cv) if p else None, bits(nq.weight), bits(nk.weight),
                                              torch.view_as_real(f).cpu().numpy())
-        assert close_bf16(bits(oq), eq).all() and close_bf16(bits(ok), ek).all() and np.array_equal(bits(ov), ev)
+        assert close_bf16(bits(oq), eq, ulps=2).all() and close_bf16(bits(ok), ek, ulps=2).all()
+        assert np.array_equal(bits(ov), ev)
 
 
 def test_prepare_attention_inputs_fallback_contract():
@@ -232,8 +239,8 @@ def test_joint_segment_vs_oracle():
     eq, ek, ev = (np.zeros((b, S, h, 128), np.uint16) for _ in range(3))
     oracle.qknorm_rope_segment(bits(qkv_t), bits(wt[0]), bits(wt[1]), ft.cpu().numpy(), eq, ek, ev, b, ltxt, 0, h)
     oracle.qknorm_rope_segment(bits(qkv_i), bits(wi[0]), bits(wi[1]), fi.cpu().numpy(), eq, ek, ev, b, limg, ltxt, h)
-    assert close_bf16(bits(oq), eq).all() and close_bf16(bits(ok), ek).all() and np.array_equal(bits(ov), ev)
-    assert (bits(oq) == eq).mean() > 0.999
+    assert close_bf16(bits(oq), eq, ulps=2).all() and close_bf16(bits(ok), ek, ulps=2).all()
+    assert np.array_equal(bits(ov), ev) and (bits(oq) == eq).mean() > 0.999
 
 
 # ------------------------------------------------------------------ FFN activations
@@ -280,15 +287,20 @@ def test_mxfp8_quantize_bit_exact(m, k):
     if m * k <= 2400 * 4096:
         cq, cs = oracle.mx_quantize(bits(x))
         assert np.array_equal(u8(a.values), cq) and np.array_equal(u8(a.scales), cs)
-    # size-independent: dequantize -> requantize is the identity (idempotence)
-    vals = a.values.float().view(-1, k // 32, 32)
-    sc = a.scales.view(torch.uint8)
-    padded = a.values.shape[0]
-    e = sc.view(padded // 128, k // 128, 32, 4, 4).permute(0, 3, 2, 1, 4).reshape(padded, k // 32)
-    deq = (vals * torch.exp2(e.float() - 127)[..., None]).view(padded, k)[:m].to(torch.bfloat16)
+    # size-independent: requantizing the dequantized values reproduces them
+    # exactly (value idempotence). Codes may change: a block max with mantissa
+    # in (1.75, 1.8125) rounds down to 224 and requantizes one binade lower.
+    deq = dequant_q(a, m, k).to(torch.bfloat16)
     b = quantize(deq)
-    assert torch.equal(b.values.view(torch.uint8), a.values.view(torch.uint8))
-    assert torch.equal(b.scales.view(torch.uint8), a.scales.view(torch.uint8))
+    assert torch.equal(dequant_q(b, m, k), dequant_q(a, m, k))
+
+
+def dequant_q(a, m, k):
+    vals = a.values.float().view(-1, k // 32, 32)
+    padded = a.values.shape[0]
+    e = a.scales.view(torch.uint8).view(padded // 128, k // 128, 32, 4, 4).permute(0, 3, 2, 1, 4).reshape(padded,
+                                                                                                           k // 32)
+    return (vals * torch.exp2(e.float() - 127)[..., None]).view(padded, k)[:m]
 
 
 def test_quantize_strided_rows():
