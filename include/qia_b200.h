@@ -202,6 +202,46 @@ int qia_mxfp8_gemm_gate_residual(const void* a_values, const void* a_scales,
                                  int64_t n, int64_t k, int64_t ldo,
                                  int64_t rows_per_batch, void* stream);
 
+/* ---------------------------------------------------------------------------
+ * Sage-style quantized attention (tcgen05: INT8 Q.K^T, FP8 P.V)
+ *
+ * q, k, v, out: bf16 [batch, seq, heads, 128] with element strides
+ * (batch, seq, head) given per tensor in `strides` (q, k, v, out: 12 values;
+ * the head_dim stride is 1). The caller provides a device workspace of
+ * qia_sage_workspace_bytes() bytes (256-byte aligned) for the quantized
+ * operands and their scales. sm_scale <= 0 selects 1/sqrt(head_dim).
+ * Replaces: sage_decode / sageattn_qk_int8_pv_fp8_cuda(tensor_layout="NHD",
+ * qk_quant_gran="per_warp", pv_accum_dtype="fp32+fp32")
+ * (src/qwen_image_accel/optimizations/sage_attention.py:19-25;
+ * SAGE:sageattention/core.py:636-828).
+ * ------------------------------------------------------------------------ */
+int64_t qia_sage_workspace_bytes(int64_t batch, int64_t heads, int64_t seq_q,
+                                 int64_t seq_kv);
+
+int qia_sage_attention(const void* q, const void* k, const void* v, void* out,
+                       int64_t batch, int64_t seq_q, int64_t seq_kv,
+                       int64_t heads, int64_t head_dim, const int64_t* strides,
+                       float sm_scale, void* workspace, int64_t workspace_bytes,
+                       void* stream);
+
+/* The quantization half alone: Q INT8 per 32-token block, K mean-smoothed
+ * INT8 per 64-token block, V FP8 per channel, written into the workspace
+ * (strides: q, k, v -- 9 values).
+ * Replaces: per_warp_int8 + per_channel_fp8 (SAGE:sageattention/quant.py). */
+int qia_sage_quantize(const void* q, const void* k, const void* v,
+                      int64_t batch, int64_t seq_q, int64_t seq_kv,
+                      int64_t heads, int64_t head_dim, const int64_t* strides,
+                      void* workspace, int64_t workspace_bytes, void* stream);
+
+/* The attention half alone, on a workspace filled by qia_sage_quantize
+ * (out_strides: 3 values).
+ * Replaces: qk_int8_sv_f8_accum_f32_fuse_v_scale_attn_inst_buf
+ * (SAGE:csrc/qattn/sm89_qk_int8_sv_f8_accum_f32_fuse_v_scale_attn_inst_buf.cu). */
+int qia_sage_attn_quantized(const void* workspace, void* out, int64_t batch,
+                            int64_t seq_q, int64_t seq_kv, int64_t heads,
+                            int64_t head_dim, const int64_t* out_strides,
+                            float sm_scale, void* stream);
+
 /* Reads and clears the device-side error word of the current device (set when
  * a bounded wait inside a tensor-core kernel gave up). Synchronises the device. */
 int qia_device_error(int* code);

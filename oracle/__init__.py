@@ -323,12 +323,22 @@ def sage_quant_q(q: np.ndarray, blk: int = 32):
     return codes.reshape(b, nblk * blk, h, d)[:, :s], scale
 
 
-def sage_quant_k(k: np.ndarray, blk: int = 64):
-    """K smoothing (minus the bf16-rounded mean over the whole sequence,
-    SAGE:sageattention/core.py:773) then per-(64-token block, head) INT8
-    (SAGE:csrc/fused/fused.cu:594-683)."""
+def sage_k_mean(k: np.ndarray) -> np.ndarray:
+    """Per-(batch, head, channel) mean of K over the sequence, rounded to bf16
+    (SAGE:sageattention/core.py:773, k.mean(dim=seq) on a bf16 tensor): a
+    sequential fp32 sum times fp32(1/S)."""
     b, s, h, d = k.shape
-    km = bf16_bits_to_f32(f32_to_bf16_bits(k.astype(np.float64).mean(axis=1).astype(np.float32)))  # [b, h, d]
+    acc = np.zeros((b, h, d), np.float32)
+    for i in range(s):
+        acc += k[:, i].astype(np.float32)
+    mean = (acc * np.float32(1.0 / s)).astype(np.float32)
+    return bf16_bits_to_f32(f32_to_bf16_bits(mean))
+
+
+def sage_quant_k(k: np.ndarray, blk: int = 64):
+    """K smoothing (minus the bf16-rounded sequence mean) then
+    per-(64-token block, head) INT8 (SAGE:csrc/fused/fused.cu:594-683)."""
+    km = sage_k_mean(k)                                  # [b, h, d]
     ks = (k - km[:, None]).astype(np.float32)
     codes, scale = sage_quant_q(ks, blk)
     return codes, scale, km
@@ -337,9 +347,10 @@ def sage_quant_k(k: np.ndarray, blk: int = 64):
 def sage_quant_v(v: np.ndarray, scale_max: float = 448.0):
     """Per-(batch, head, channel) FP8: scale = amax/448 over the sequence,
     codes = E4M3(x * 448/amax) (SAGE:csrc/fused/fused.cu:316-427, no smoothing)."""
-    amax = np.abs(v).max(axis=1)                                  # [b, h, d]
+    amax = np.abs(v).max(axis=1).astype(np.float32)              # [b, h, d]
     scale = (amax / np.float32(scale_max)).astype(np.float32)
-    recp = (np.float32(scale_max) / amax).astype(np.float32)
+    with np.errstate(divide="ignore"):
+        recp = np.where(amax > 0, np.float32(scale_max) / amax, np.float32(0)).astype(np.float32)
     codes = _encode_e4m3((v * recp[:, None]).astype(np.float32))
     return codes, scale
 

@@ -1,0 +1,661 @@
+// Sage-style quantized attention on tcgen05: INT8 Q.K^T, FP8 P.V, online
+// softmax in base 2, for the unmasked joint text+image attention.
+//
+// Semantics follow the reference's decode attention, sageattn_qk_int8_pv_fp8_cuda
+// with qk_quant_gran="per_warp", pv_accum_dtype="fp32+fp32", smooth_k=True
+// (reference src/qwen_image_accel/optimizations/sage_attention.py:19-25;
+// SAGE:sageattention/core.py:725-828):
+//  * K smoothing: k - mean_seq(k) (the mean rounded to bf16, core.py:773);
+//  * Q INT8 per (32-token block, head), K INT8 per (64-token block, head):
+//    scale = amax/127 (amax floored at 1e-7), codes = rint_sat(x * 127/amax)
+//    (SAGE:csrc/fused/fused.cu:140-184);
+//  * V FP8 E4M3 per (batch, head, channel): scale = amax/448
+//    (SAGE:csrc/fused/fused.cu:316-427);
+//  * S = int32 Q.K^T, s = S * (sm_scale*log2e) * (q_scale*k_scale); running
+//    max m offset by log2(448) so P = 2^(s - m) lies in [0, 448]
+//    (SAGE:csrc/qattn/attn_utils.cuh:353-440); P rounded to E4M3 for the
+//    P.V product, the row sum taken over the unrounded P;
+//  * "fp32+fp32": the P.V products accumulate in a full-fp32 TMEM accumulator
+//    rescaled by 2^(m_old - m_new) whenever a row's running max grows (the
+//    rescale happens in TMEM, only in warps where some row's max changed);
+//  * out = O / rowsum * v_scale, bf16 (SAGE:csrc/qattn/qk_int_sv_f8_cuda_sm89.cuh:566-600).
+//
+// Device layouts written by the quantization kernels here (head-major, rows
+// padded to a multiple of 128 with zeros): q8/k8 int8 [B*H, S_pad, 128],
+// v8 e4m3 [B*H, S_pad, 128], q_scale f32 [B*H, S_pad/32], k_scale f32
+// [B*H, S_pad/64], v_scale f32 [B*H, 128], k_mean bf16 [B*H, 128].
+#include <cudaTypedefs.h>
+
+#include <climits>
+#include <mutex>
+
+#include "sm100.cuh"
+
+namespace qia {
+namespace {
+
+constexpr int kD = 128;
+constexpr int kTile = 128;
+constexpr int kKvStages = 3;
+constexpr float kFp8Offset = 8.807f;  // log2(448): P = 2^(s - m) <= 448
+
+// ------------------------------------------------------------------ quantizers
+// Per (b, h): k_mean[d] = bf16(sum_s k[b, s, h, d] * (1/S)), sequential fp32 sum.
+__global__ void sage_k_mean_kernel(const __nv_bfloat16* __restrict__ k, int64_t stride_b, int64_t stride_s,
+                                   int64_t stride_h, int S, int H, __nv_bfloat16* __restrict__ k_mean) {
+  const int bh = blockIdx.x, b = bh / H, h = bh % H, d = threadIdx.x;
+  const __nv_bfloat16* p = k + b * stride_b + h * stride_h + d;
+  float acc = 0.0f;
+#pragma unroll 8
+  for (int s = 0; s < S; ++s) acc += __bfloat162float(p[int64_t(s) * stride_s]);
+  k_mean[int64_t(bh) * kD + d] = __float2bfloat16_rn(acc * (1.0f / float(S)));
+}
+
+// One warp per 32-row block (Q), or two warps per 64-row block (K, with the
+// mean subtracted). Each thread owns one token row of 128 values.
+template <int BLK, bool SUB_MEAN>
+__global__ void __launch_bounds__(128) sage_quant_int8_kernel(const __nv_bfloat16* __restrict__ x, int64_t stride_b,
+                                                              int64_t stride_s, int64_t stride_h, int S, int S_pad,
+                                                              int H, const __nv_bfloat16* __restrict__ mean,
+                                                              int8_t* __restrict__ out, float* __restrict__ scale) {
+  __shared__ float s_amax[4];
+  const int bh = blockIdx.x, b = bh / H, h = bh % H;
+  const int row = blockIdx.y * 128 + threadIdx.x;  // token index within the padded sequence
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  float v[kD];
+  if (row < S) {
+    const uint4* src = reinterpret_cast<const uint4*>(x + b * stride_b + int64_t(row) * stride_s + h * stride_h);
+#pragma unroll
+    for (int i = 0; i < 16; ++i) unpack8(__ldg(src + i), &v[i * 8]);
+    if (SUB_MEAN) {
+      const uint4* mp = reinterpret_cast<const uint4*>(mean + int64_t(bh) * kD);
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        float m8[8];
+        unpack8(__ldg(mp + i), m8);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[i * 8 + j] -= m8[j];
+      }
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < kD; ++i) v[i] = 0.0f;
+  }
+  float amax = 1e-7f;
+#pragma unroll
+  for (int i = 0; i < kD; ++i) amax = fmaxf(amax, fabsf(v[i]));
+  amax = warp_max_xor(amax, 16);
+  if (BLK == 64) {
+    if (lane == 0) s_amax[warp] = amax;
+    __syncthreads();
+    amax = fmaxf(s_amax[warp & ~1], s_amax[warp | 1]);
+  }
+  const float inv = __fdiv_rn(127.0f, amax);
+  const int blk = row / BLK;
+  if (lane == 0 && (BLK == 32 || (warp & 1) == 0)) scale[int64_t(bh) * (S_pad / BLK) + blk] = __fdiv_rn(amax, 127.0f);
+  int8_t* dst = out + (int64_t(bh) * S_pad + row) * kD;
+#pragma unroll
+  for (int i = 0; i < kD / 16; ++i) {
+    uint32_t w[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      uint32_t packed = 0;
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        int c;
+        asm("cvt.rni.sat.s8.f32 %0, %1;" : "=r"(c) : "f"(v[i * 16 + q * 4 + e] * inv));
+        packed |= (uint32_t(c) & 0xffu) << (8 * e);
+      }
+      w[q] = packed;
+    }
+    reinterpret_cast<uint4*>(dst)[i] = make_uint4(w[0], w[1], w[2], w[3]);
+  }
+}
+
+// Per (b, h): channel amax over the sequence, then E4M3 codes of v * 448/amax.
+// Thread d owns channel d.
+__global__ void __launch_bounds__(128) sage_quant_v_kernel(const __nv_bfloat16* __restrict__ v, int64_t stride_b,
+                                                           int64_t stride_s, int64_t stride_h, int S, int S_pad,
+                                                           int H, uint8_t* __restrict__ out,
+                                                           float* __restrict__ scale) {
+  const int bh = blockIdx.x, b = bh / H, h = bh % H, d = threadIdx.x;
+  const __nv_bfloat16* p = v + b * stride_b + h * stride_h + d;
+  float amax = 0.0f;
+#pragma unroll 8
+  for (int s = 0; s < S; ++s) amax = fmaxf(amax, fabsf(__bfloat162float(p[int64_t(s) * stride_s])));
+  scale[int64_t(bh) * kD + d] = amax / 448.0f;
+  // an all-zero channel quantizes to zero codes (no 0 * inf)
+  const float recp = amax > 0.0f ? 448.0f / amax : 0.0f;
+  uint8_t* dst = out + int64_t(bh) * S_pad * kD + d;
+#pragma unroll 4
+  for (int s = 0; s < S_pad; ++s) {
+    const float x = s < S ? __bfloat162float(p[int64_t(s) * stride_s]) : 0.0f;
+    dst[int64_t(s) * kD] = uint8_t(cvt_e4m3x2(x * recp, 0.0f) & 0xffu);
+  }
+}
+
+// ------------------------------------------------------------------ attention
+// Instruction descriptors (tcgen05 kind::i8 and kind::f8f6f4, M = N = 128).
+constexpr uint32_t kIdescQK = (2u << 4) | (1u << 7) | (1u << 10) | (uint32_t(kTile >> 3) << 17) |
+                              (uint32_t(128 >> 4) << 24);  // s32 accum, s8 x s8, K-major both
+constexpr uint32_t kIdescPV = (1u << 4) | (0u << 7) | (0u << 10) | (1u << 16) | (uint32_t(kD >> 3) << 17) |
+                              (uint32_t(128 >> 4) << 24);  // f32 accum, e4m3 x e4m3, B (V) MN-major
+
+__device__ __forceinline__ void tc_mma_i8(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(d),
+      "l"(a), "l"(b), "r"(idesc), "r"(acc)
+      : "memory");
+}
+
+__device__ __forceinline__ void tc_mma_f8(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}" ::"r"(d),
+      "l"(a), "l"(b), "r"(idesc), "r"(acc)
+      : "memory");
+}
+
+// MN-major, 128-byte swizzle descriptor (V as the B operand of P.V): 128 B of
+// N per row, 8-row (K) groups 1024 B apart.
+__device__ __forceinline__ uint64_t smem_desc_mn_sw128(uint32_t saddr) {
+  uint64_t d = 0;
+  d |= uint64_t((saddr & 0x3FFFFu) >> 4);
+  d |= uint64_t(1) << 16;
+  d |= uint64_t(1024 >> 4) << 32;
+  d |= uint64_t(1) << 46;
+  d |= uint64_t(2) << 61;
+  return d;
+}
+
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// int32 (|x| < 2^22) -> fp32 exactly, on the FMA/ALU pipes.
+__device__ __forceinline__ float i2f_small(uint32_t x) {
+  return __int_as_float(int(x) + 0x4B400000) - 12582912.0f;
+}
+
+struct AttnParams {
+  const float* q_scale;
+  const float* k_scale;
+  const float* v_scale;
+  __nv_bfloat16* out;       // NHD [B, Sq, H, 128]
+  int64_t out_stride_b, out_stride_s, out_stride_h;
+  int B, H, Sq, Skv, Sq_pad, Skv_pad;
+  float sm_scale_log2;      // sm_scale * log2(e)
+};
+
+constexpr int kSmemQ = 0;
+constexpr int kSmemK = kSmemQ + 16384;
+constexpr int kSmemV = kSmemK + kKvStages * 16384;
+constexpr int kSmemP = kSmemV + kKvStages * 16384;
+constexpr int kSmemBar = kSmemP + 2 * 16384;
+constexpr int kAttnSmem = kSmemBar + 1024 + 1024;
+
+__global__ void __launch_bounds__(192, 1)
+sage_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                 const __grid_constant__ CUtensorMap tm_v, AttnParams p, int* err) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kSmemBar);
+  uint64_t* q_full = bars;
+  uint64_t* k_full = bars + 1;
+  uint64_t* k_empty = k_full + kKvStages;
+  uint64_t* v_full = k_empty + kKvStages;
+  uint64_t* v_empty = v_full + kKvStages;
+  uint64_t* s_full = v_empty + kKvStages;
+  uint64_t* s_free = s_full + 2;
+  uint64_t* p_full = s_free + 2;
+  uint64_t* p_free = p_full + 2;
+  uint64_t* o_done = p_free + 2;   // one phase per P.V tile
+  uint64_t* drain = o_done + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int q_tile = blockIdx.x, bh = blockIdx.y;
+  const int nkv = p.Skv_pad / kTile;
+  const int q_row0 = bh * p.Sq_pad + q_tile * kTile;
+  const int kv_row0 = bh * p.Skv_pad;
+
+  if (threadIdx.x == 0) {
+    mbar_init(smem_u32(q_full), 1);
+    for (int s = 0; s < kKvStages; ++s) {
+      mbar_init(smem_u32(&k_full[s]), 1);
+      mbar_init(smem_u32(&k_empty[s]), 1);
+      mbar_init(smem_u32(&v_full[s]), 1);
+      mbar_init(smem_u32(&v_empty[s]), 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(smem_u32(&s_full[i]), 1);
+      mbar_init(smem_u32(&s_free[i]), 4);
+      mbar_init(smem_u32(&p_full[i]), 4);
+      mbar_init(smem_u32(&p_free[i]), 1);
+    }
+    mbar_init(smem_u32(o_done), 1);
+    mbar_init(smem_u32(drain), 1);
+    fence_barrier_init();
+    prefetch_tmap(&tm_q);
+    prefetch_tmap(&tm_k);
+    prefetch_tmap(&tm_v);
+  }
+  if (warp == 1) tmem_alloc(smem_u32(tmem_slot), 512);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  // TMEM columns: S0 [0,128), S1 [128,256), O [256,384)
+
+  if (warp == 0) {
+    if (lane == 0) {
+      bool ok = true;
+      int issued = 0;
+      mbar_arrive_expect_tx(smem_u32(q_full), 16384);
+      tma_load_2d(smem_u32(smem + kSmemQ), &tm_q, smem_u32(q_full), 0, q_row0);
+      for (int j = 0; j < nkv && ok; ++j) {
+        const int st = j % kKvStages;
+        const uint32_t ph = (j / kKvStages) & 1;
+        if (!mbar_wait(smem_u32(&k_empty[st]), ph ^ 1, err)) { ok = false; break; }
+        mbar_arrive_expect_tx(smem_u32(&k_full[st]), 16384);
+        tma_load_2d(smem_u32(smem + kSmemK + st * 16384), &tm_k, smem_u32(&k_full[st]), 0, kv_row0 + j * kTile);
+        if (!mbar_wait(smem_u32(&v_empty[st]), ph ^ 1, err)) { ok = false; break; }
+        mbar_arrive_expect_tx(smem_u32(&v_full[st]), 16384);
+        tma_load_2d(smem_u32(smem + kSmemV + st * 16384), &tm_v, smem_u32(&v_full[st]), 0, kv_row0 + j * kTile);
+        issued = j + 1;
+      }
+      if (!ok) {
+        // let queued copies land before the shared memory is released
+        mbar_wait(smem_u32(q_full), 0, nullptr, 100000000ull);
+        for (int j = (issued > kKvStages ? issued - kKvStages : 0); j < issued; ++j) {
+          mbar_wait(smem_u32(&k_full[j % kKvStages]), (j / kKvStages) & 1, nullptr, 100000000ull);
+          mbar_wait(smem_u32(&v_full[j % kKvStages]), (j / kKvStages) & 1, nullptr, 100000000ull);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      bool ok = mbar_wait(smem_u32(q_full), 0, err);
+      tc_fence_after();
+      const uint64_t qdesc = smem_desc_k_sw128(smem_u32(smem + kSmemQ));
+      for (int j = 0; j <= nkv && ok; ++j) {
+        if (j < nkv) {
+          const int sb = j & 1, st = j % kKvStages;
+          if (!mbar_wait(smem_u32(&k_full[st]), (j / kKvStages) & 1, err)) { ok = false; break; }
+          if (!mbar_wait(smem_u32(&s_free[sb]), ((j >> 1) & 1) ^ 1, err)) { ok = false; break; }
+          tc_fence_after();
+          const uint64_t kdesc = smem_desc_k_sw128(smem_u32(smem + kSmemK + st * 16384));
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk)
+            tc_mma_i8(tmem + uint32_t(sb * 128), qdesc + uint64_t(2 * kk), kdesc + uint64_t(2 * kk), kIdescQK, kk > 0);
+          tc_commit(smem_u32(&k_empty[st]));
+          tc_commit(smem_u32(&s_full[sb]));
+        }
+        if (j >= 1) {
+          const int i = j - 1, pb = i & 1, st = i % kKvStages;
+          const uint32_t pph = (i >> 1) & 1;
+          if (!mbar_wait(smem_u32(&p_full[pb]), pph, err)) { ok = false; break; }
+          if (!mbar_wait(smem_u32(&v_full[st]), (i / kKvStages) & 1, err)) { ok = false; break; }
+          tc_fence_after();
+          const uint64_t pdesc = smem_desc_k_sw128(smem_u32(smem + kSmemP + pb * 16384));
+          const uint64_t vdesc = smem_desc_mn_sw128(smem_u32(smem + kSmemV + st * 16384));
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk)
+            tc_mma_f8(tmem + 256u, pdesc + uint64_t(2 * kk), vdesc + uint64_t(256 * kk), kIdescPV, (i | kk) != 0);
+          tc_commit(smem_u32(&v_empty[st]));
+          tc_commit(smem_u32(&p_free[pb]));
+          tc_commit(smem_u32(o_done));
+        }
+      }
+      tc_commit(smem_u32(drain));
+      mbar_wait(smem_u32(drain), 0, ok ? err : nullptr, 100000000ull);
+    }
+  } else {
+    // ---------------------------------------------------------- softmax
+    // One thread per query row (TMEM lane). O lives in TMEM columns [256, 384).
+    const int sub = warp & 3;
+    const int r = sub * 32 + lane;            // row within the query tile
+    const int q_tok = q_tile * kTile + r;     // token index
+    const uint32_t t_lane = uint32_t(sub * 32) << 16;
+    const float qs = p.q_scale[int64_t(bh) * (p.Sq_pad / 32) + q_tok / 32];
+    const int kb_per_head = p.Skv_pad / 64;
+    float m_old = -5000000.0f, dsum = 0.0f;
+    bool ok = true;
+    uint8_t* p_smem = smem + kSmemP;
+    for (int j = 0; j < nkv; ++j) {
+      const int sb = j & 1;
+      const uint32_t sph = (j >> 1) & 1;
+      if (!__all_sync(0xffffffffu, mbar_wait(smem_u32(&s_full[sb]), sph, err))) { ok = false; break; }
+      tc_fence_after();
+      const float sc0 = p.sm_scale_log2 * (qs * p.k_scale[int64_t(bh) * kb_per_head + 2 * j]);
+      const float sc1 = p.sm_scale_log2 * (qs * p.k_scale[int64_t(bh) * kb_per_head + 2 * j + 1]);
+      const int valid = p.Skv - j * kTile;   // keys of this tile that exist (may exceed 128)
+      // pass 1: row max of the raw integer scores per 64-key half
+      int mx0 = INT_MIN, mx1 = INT_MIN;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint32_t sv[32];
+        tc_ld_32x32b_x32(tmem + t_lane + uint32_t(sb * 128 + c * 32), sv);
+        tc_wait_ld();
+#pragma unroll
+        for (int t = 0; t < 32; ++t) {
+          const int v = (c * 32 + t) < valid ? int(sv[t]) : INT_MIN;
+          if (c < 2) mx0 = max(mx0, v); else mx1 = max(mx1, v);
+        }
+      }
+      float m_new = m_old;
+      if (mx0 != INT_MIN) m_new = fmaxf(m_new, fmaf(float(mx0), sc0, -kFp8Offset));
+      if (mx1 != INT_MIN) m_new = fmaxf(m_new, fmaf(float(mx1), sc1, -kFp8Offset));
+      const float alpha = ex2_approx(m_old - m_new);
+      // rescale O in TMEM where some row of this warp raised its max; s_full(j)
+      // implies P.V tile j-2 finished, and tile j cannot start before this
+      // warp's p_full(j), so o_done is at phase j-1 or j here
+      if (__any_sync(0xffffffffu, j > 0 && alpha != 1.0f)) {
+        if (!__all_sync(0xffffffffu, mbar_wait(smem_u32(o_done), (j - 1) & 1, err))) { ok = false; break; }
+        tc_fence_after();
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+          uint32_t ov[32];
+          tc_ld_32x32b_x32(tmem + t_lane + uint32_t(256 + c * 32), ov);
+          tc_wait_ld();
+#pragma unroll
+          for (int t = 0; t < 32; ++t) ov[t] = __float_as_uint(__uint_as_float(ov[t]) * alpha);
+          tc_st_32x32b_x32(tmem + t_lane + uint32_t(256 + c * 32), ov);
+        }
+        tc_wait_st();
+      }
+      dsum *= alpha;
+      // pass 2: P = 2^(s - m) -> E4M3 into the swizzled K-major P tile
+      if (!__all_sync(0xffffffffu, mbar_wait(smem_u32(&p_free[sb]), sph ^ 1, err))) { ok = false; break; }
+      uint8_t* prow = p_smem + sb * 16384 + r * 128;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint32_t sv[32];
+        tc_ld_32x32b_x32(tmem + t_lane + uint32_t(sb * 128 + c * 32), sv);
+        tc_wait_ld();
+        const float sc = c < 2 ? sc0 : sc1;
+        uint32_t w[8];
+#pragma unroll
+        for (int t = 0; t < 32; t += 4) {
+          float pv[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int key = c * 32 + t + e;
+            pv[e] = key < valid ? ex2_approx(fmaf(i2f_small(sv[t + e]), sc, -m_new)) : 0.0f;
+            dsum += pv[e];
+          }
+          w[t / 4] = cvt_e4m3x4(pv[0], pv[1], pv[2], pv[3]);
+        }
+        // 32 keys = two 16-byte units (2c, 2c+1) of the 128-byte row, swizzled
+        const int u0 = (2 * c) ^ (r & 7), u1 = (2 * c + 1) ^ (r & 7);
+        *reinterpret_cast<uint4*>(prow + u0 * 16) = make_uint4(w[0], w[1], w[2], w[3]);
+        *reinterpret_cast<uint4*>(prow + u1 * 16) = make_uint4(w[4], w[5], w[6], w[7]);
+      }
+      tc_fence_before();
+      fence_proxy_async_shared();
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(smem_u32(&s_free[sb]));
+        mbar_arrive(smem_u32(&p_full[sb]));
+      }
+      m_old = m_new;
+    }
+    // s_full(j) only guarantees P.V tiles <= j-2 finished, so o_done may still
+    // be two phases behind: wait for phase nkv-2, then nkv-1 (a parity wait is
+    // unambiguous only one phase ahead).
+    if (ok && nkv >= 2)
+      ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(o_done), (nkv - 2) & 1, err));
+    if (ok && __all_sync(0xffffffffu, mbar_wait(smem_u32(o_done), (nkv - 1) & 1, err))) {
+      tc_fence_after();
+      const float rinv = 1.0f / dsum;
+      const float* vs = p.v_scale + int64_t(bh) * kD;
+      const int b = bh / p.H, h = bh % p.H;
+      uint4* dst = reinterpret_cast<uint4*>(p.out + b * p.out_stride_b + int64_t(q_tok) * p.out_stride_s +
+                                            h * p.out_stride_h);
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        uint32_t ov[32];
+        tc_ld_32x32b_x32(tmem + t_lane + uint32_t(256 + c * 32), ov);
+        tc_wait_ld();
+        if (q_tok < p.Sq) {
+#pragma unroll
+          for (int c8 = 0; c8 < 4; ++c8) {
+            float f[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e)
+              f[e] = __uint_as_float(ov[c8 * 8 + e]) * rinv * __ldg(vs + c * 32 + c8 * 8 + e);
+            dst[c * 4 + c8] = pack8(f);
+          }
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// ------------------------------------------------------------------ host
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  });
+  return fn;
+}
+
+int make_rows_tmap(CUtensorMap* map, const void* base, int64_t rows) {
+  auto fn = encode_fn();
+  if (!fn) return set_error(QIA_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  cuuint64_t dims[2] = {cuuint64_t(kD), cuuint64_t(rows)};
+  cuuint64_t strides[1] = {cuuint64_t(kD)};
+  cuuint32_t box[2] = {128u, 128u};
+  cuuint32_t estr[2] = {1u, 1u};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return set_error(QIA_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", int(r));
+  return QIA_OK;
+}
+
+int64_t pad128(int64_t s) { return (s + 127) / 128 * 128; }
+
+struct Workspace {
+  int8_t* q8;
+  int8_t* k8;
+  uint8_t* v8;
+  float* q_scale;
+  float* k_scale;
+  float* v_scale;
+  __nv_bfloat16* k_mean;
+};
+
+int64_t workspace_layout(int64_t B, int64_t H, int64_t Sq, int64_t Skv, uint8_t* base, Workspace* ws) {
+  const int64_t bh = B * H, sqp = pad128(Sq), skp = pad128(Skv);
+  int64_t off = 0;
+  auto take = [&](int64_t bytes) {
+    const int64_t at = off;
+    off += (bytes + 255) / 256 * 256;
+    return base ? base + at : nullptr;
+  };
+  uint8_t* q8 = take(bh * sqp * kD);
+  uint8_t* k8 = take(bh * skp * kD);
+  uint8_t* v8 = take(bh * skp * kD);
+  uint8_t* qs = take(bh * (sqp / 32) * 4);
+  uint8_t* ks = take(bh * (skp / 64) * 4);
+  uint8_t* vs = take(bh * kD * 4);
+  uint8_t* km = take(bh * kD * 2);
+  if (ws) {
+    ws->q8 = (int8_t*)q8;
+    ws->k8 = (int8_t*)k8;
+    ws->v8 = v8;
+    ws->q_scale = (float*)qs;
+    ws->k_scale = (float*)ks;
+    ws->v_scale = (float*)vs;
+    ws->k_mean = (__nv_bfloat16*)km;
+  }
+  return off;
+}
+
+struct Strides {
+  int64_t b, s, h;
+};
+
+int check_nhd(const void* t, const Strides& st, const char* who) {
+  if (!t) return set_error(QIA_ERR_INVALID, "%s: null tensor", who);
+  if (!aligned(t, 16) || st.b % 8 || st.s % 8 || st.h % 8)
+    return set_error(QIA_ERR_ALIGNMENT, "%s: tensors and strides must be 16-byte aligned", who);
+  return QIA_OK;
+}
+
+int quant_qkv(const void* q, Strides qs, const void* k, Strides ks, const void* v, Strides vs, int64_t B, int64_t H,
+              int64_t Sq, int64_t Skv, const Workspace& ws, cudaStream_t st) {
+  const int64_t sqp = pad128(Sq), skp = pad128(Skv);
+  const unsigned bh = unsigned(B * H);
+  sage_quant_int8_kernel<32, false><<<dim3(bh, unsigned(sqp / 128)), 128, 0, st>>>(
+      (const __nv_bfloat16*)q, qs.b, qs.s, qs.h, int(Sq), int(sqp), int(H), nullptr, ws.q8, ws.q_scale);
+  int rc = check_launch("sage_quant_int8_kernel<q>");
+  if (rc) return rc;
+  sage_k_mean_kernel<<<bh, kD, 0, st>>>((const __nv_bfloat16*)k, ks.b, ks.s, ks.h, int(Skv), int(H), ws.k_mean);
+  rc = check_launch("sage_k_mean_kernel");
+  if (rc) return rc;
+  sage_quant_int8_kernel<64, true><<<dim3(bh, unsigned(skp / 128)), 128, 0, st>>>(
+      (const __nv_bfloat16*)k, ks.b, ks.s, ks.h, int(Skv), int(skp), int(H), ws.k_mean, ws.k8, ws.k_scale);
+  rc = check_launch("sage_quant_int8_kernel<k>");
+  if (rc) return rc;
+  sage_quant_v_kernel<<<bh, kD, 0, st>>>((const __nv_bfloat16*)v, vs.b, vs.s, vs.h, int(Skv), int(skp), int(H),
+                                         ws.v8, ws.v_scale);
+  return check_launch("sage_quant_v_kernel");
+}
+
+int launch_attn(const Workspace& ws, void* out, Strides os, int64_t B, int64_t H, int64_t Sq, int64_t Skv,
+                float sm_scale, cudaStream_t st) {
+  static bool attr_done[64] = {false};
+  static std::mutex mu;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    if (dev >= 0 && dev < 64 && !attr_done[dev]) {
+      cudaError_t e = cudaFuncSetAttribute(sage_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kAttnSmem);
+      if (e != cudaSuccess) return set_error(QIA_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+      attr_done[dev] = true;
+    }
+  }
+  const int64_t sqp = pad128(Sq), skp = pad128(Skv);
+  CUtensorMap tq, tk, tv;
+  int rc = make_rows_tmap(&tq, ws.q8, B * H * sqp);
+  if (rc) return rc;
+  rc = make_rows_tmap(&tk, ws.k8, B * H * skp);
+  if (rc) return rc;
+  rc = make_rows_tmap(&tv, ws.v8, B * H * skp);
+  if (rc) return rc;
+  AttnParams p;
+  p.q_scale = ws.q_scale;
+  p.k_scale = ws.k_scale;
+  p.v_scale = ws.v_scale;
+  p.out = (__nv_bfloat16*)out;
+  p.out_stride_b = os.b;
+  p.out_stride_s = os.s;
+  p.out_stride_h = os.h;
+  p.B = int(B);
+  p.H = int(H);
+  p.Sq = int(Sq);
+  p.Skv = int(Skv);
+  p.Sq_pad = int(sqp);
+  p.Skv_pad = int(skp);
+  p.sm_scale_log2 = sm_scale * 1.44269504088896340736f;
+  sage_attn_kernel<<<dim3(unsigned(sqp / 128), unsigned(B * H)), 192, kAttnSmem, st>>>(tq, tk, tv, p,
+                                                                                        device_error_word());
+  return check_launch("sage_attn_kernel");
+}
+
+int check_sizes(int64_t B, int64_t H, int64_t Sq, int64_t Skv, int64_t D, const char* who) {
+  if (B <= 0 || H <= 0 || Sq <= 0 || Skv <= 0) return set_error(QIA_ERR_INVALID, "%s: bad sizes", who);
+  if (D != kD) return set_error(QIA_ERR_UNSUPPORTED, "%s: head_dim must be 128", who);
+  if (B * H > 65535 || pad128(Sq) * B * H > (1LL << 31) || pad128(Skv) * B * H > (1LL << 31))
+    return set_error(QIA_ERR_UNSUPPORTED, "%s: too large", who);
+  return QIA_OK;
+}
+
+}  // namespace
+}  // namespace qia
+
+using namespace qia;
+
+extern "C" int64_t qia_sage_workspace_bytes(int64_t batch, int64_t heads, int64_t seq_q, int64_t seq_kv) {
+  if (batch <= 0 || heads <= 0 || seq_q <= 0 || seq_kv <= 0) return -1;
+  return workspace_layout(batch, heads, seq_q, seq_kv, nullptr, nullptr);
+}
+
+extern "C" int qia_sage_attention(const void* q, const void* k, const void* v, void* out, int64_t batch,
+                                  int64_t seq_q, int64_t seq_kv, int64_t heads, int64_t head_dim,
+                                  const int64_t* strides, float sm_scale, void* workspace, int64_t workspace_bytes,
+                                  void* stream) {
+  int rc = check_sizes(batch, heads, seq_q, seq_kv, head_dim, "qia_sage_attention");
+  if (rc) return rc;
+  if (!strides) return set_error(QIA_ERR_INVALID, "qia_sage_attention: null strides");
+  const Strides sq{strides[0], strides[1], strides[2]}, sk{strides[3], strides[4], strides[5]},
+      sv{strides[6], strides[7], strides[8]}, so{strides[9], strides[10], strides[11]};
+  if ((rc = check_nhd(q, sq, "qia_sage_attention q")) || (rc = check_nhd(k, sk, "qia_sage_attention k")) ||
+      (rc = check_nhd(v, sv, "qia_sage_attention v")) || (rc = check_nhd(out, so, "qia_sage_attention out")))
+    return rc;
+  const int64_t need = workspace_layout(batch, heads, seq_q, seq_kv, nullptr, nullptr);
+  if (!workspace || workspace_bytes < need)
+    return set_error(QIA_ERR_INVALID, "qia_sage_attention: workspace of %lld bytes needed", (long long)need);
+  if (!aligned(workspace, 256)) return set_error(QIA_ERR_ALIGNMENT, "qia_sage_attention: workspace alignment 256");
+  Workspace ws;
+  workspace_layout(batch, heads, seq_q, seq_kv, (uint8_t*)workspace, &ws);
+  const float scale = sm_scale > 0.0f ? sm_scale : 1.0f / sqrtf(float(head_dim));
+  cudaStream_t st = as_stream(stream);
+  rc = quant_qkv(q, sq, k, sk, v, sv, batch, heads, seq_q, seq_kv, ws, st);
+  if (rc) return rc;
+  return launch_attn(ws, out, so, batch, heads, seq_q, seq_kv, scale, st);
+}
+
+extern "C" int qia_sage_quantize(const void* q, const void* k, const void* v, int64_t batch, int64_t seq_q,
+                                 int64_t seq_kv, int64_t heads, int64_t head_dim, const int64_t* strides,
+                                 void* workspace, int64_t workspace_bytes, void* stream) {
+  int rc = check_sizes(batch, heads, seq_q, seq_kv, head_dim, "qia_sage_quantize");
+  if (rc) return rc;
+  if (!strides) return set_error(QIA_ERR_INVALID, "qia_sage_quantize: null strides");
+  const Strides sq{strides[0], strides[1], strides[2]}, sk{strides[3], strides[4], strides[5]},
+      sv{strides[6], strides[7], strides[8]};
+  if ((rc = check_nhd(q, sq, "qia_sage_quantize q")) || (rc = check_nhd(k, sk, "qia_sage_quantize k")) ||
+      (rc = check_nhd(v, sv, "qia_sage_quantize v")))
+    return rc;
+  const int64_t need = workspace_layout(batch, heads, seq_q, seq_kv, nullptr, nullptr);
+  if (!workspace || workspace_bytes < need || !aligned(workspace, 256))
+    return set_error(QIA_ERR_INVALID, "qia_sage_quantize: workspace of %lld bytes (256-aligned) needed",
+                     (long long)need);
+  Workspace ws;
+  workspace_layout(batch, heads, seq_q, seq_kv, (uint8_t*)workspace, &ws);
+  return quant_qkv(q, sq, k, sk, v, sv, batch, heads, seq_q, seq_kv, ws, as_stream(stream));
+}
+
+extern "C" int qia_sage_attn_quantized(const void* workspace, void* out, int64_t batch, int64_t seq_q,
+                                       int64_t seq_kv, int64_t heads, int64_t head_dim, const int64_t* out_strides,
+                                       float sm_scale, void* stream) {
+  int rc = check_sizes(batch, heads, seq_q, seq_kv, head_dim, "qia_sage_attn_quantized");
+  if (rc) return rc;
+  if (!workspace || !aligned(workspace, 256) || !out_strides)
+    return set_error(QIA_ERR_INVALID, "qia_sage_attn_quantized: workspace/out_strides");
+  const Strides so{out_strides[0], out_strides[1], out_strides[2]};
+  if ((rc = check_nhd(out, so, "qia_sage_attn_quantized out"))) return rc;
+  Workspace ws;
+  workspace_layout(batch, heads, seq_q, seq_kv, (uint8_t*)const_cast<void*>(workspace), &ws);
+  const float scale = sm_scale > 0.0f ? sm_scale : 1.0f / sqrtf(float(head_dim));
+  return launch_attn(ws, out, so, batch, heads, seq_q, seq_kv, scale, as_stream(stream));
+}

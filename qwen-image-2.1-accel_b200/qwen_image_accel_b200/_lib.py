@@ -36,6 +36,14 @@ SIGNATURES: dict[str, list] = {
     "qia_mxfp8_gemm_gelu_quant": [_P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _P],
     "qia_mxfp8_gemm_gate_residual": [_P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _P],
     "qia_device_error": [_P],
+    "qia_sage_attention": [_P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _F, _P, _I, _P],
+    "qia_sage_quantize": [_P, _P, _P, _I, _I, _I, _I, _I, _P, _P, _I, _P],
+    "qia_sage_attn_quantized": [_P, _P, _I, _I, _I, _I, _I, _P, _F, _P],
+}
+
+# entry points that do not return a status code: name -> (restype, argtypes)
+RAW_SIGNATURES: dict[str, tuple] = {
+    "qia_sage_workspace_bytes": (ctypes.c_int64, [_I, _I, _I, _I]),
 }
 
 _lock = threading.Lock()
@@ -67,12 +75,16 @@ def load() -> ctypes.CDLL:
                 fn = getattr(lib, name)
                 fn.argtypes = args
                 fn.restype = ctypes.c_int
+            for name, (res, args) in RAW_SIGNATURES.items():
+                fn = getattr(lib, name)
+                fn.argtypes = args
+                fn.restype = res
             _lib = lib
     return _lib
 
 
 def declared_symbols() -> list[str]:
-    return ["qia_last_error_string", "qia_abi_version", *SIGNATURES]
+    return ["qia_last_error_string", "qia_abi_version", *SIGNATURES, *RAW_SIGNATURES]
 
 
 def call(name: str, *args) -> None:

@@ -1,0 +1,112 @@
+"""Sage-style INT8/FP8 joint attention on tcgen05 (decode path of the sage profiles).
+
+Mirrors src/qwen_image_accel/optimizations/sage_attention.py: the
+`qw21::sage_decode(q, k, v)` custom op (NHD bf16 in, NHD bf16 out) and the
+QW21_SAGE_ACCUM / QW21_SAGE_QK_GRAN settings, now served by the sm_100a
+kernels in libqia_b200.so instead of the SageAttention2 extension. The only
+accumulation implemented is the reference default "fp32+fp32" and the only
+granularity "per_warp"; other values raise.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+import torch
+
+from .. import _lib
+
+ACCUM = os.environ.get("QW21_SAGE_ACCUM", "fp32+fp32").strip()
+QK_GRAN = os.environ.get("QW21_SAGE_QK_GRAN", "per_warp").strip()
+
+
+def _check_settings():
+    if ACCUM != "fp32+fp32" or QK_GRAN != "per_warp":
+        raise NotImplementedError("only QW21_SAGE_ACCUM=fp32+fp32 and QW21_SAGE_QK_GRAN=per_warp are implemented")
+
+
+def workspace_bytes(batch: int, heads: int, seq_q: int, seq_kv: int) -> int:
+    n = _lib.load().qia_sage_workspace_bytes(batch, heads, seq_q, seq_kv)
+    if n < 0:
+        raise ValueError("bad attention sizes")
+    return int(n)
+
+
+def _pad128(s):
+    return (s + 127) // 128 * 128
+
+
+def workspace_views(ws: torch.Tensor, batch: int, heads: int, seq_q: int, seq_kv: int) -> dict:
+    """Typed views of the workspace regions (same layout as the C side)."""
+    bh, sqp, skp = batch * heads, _pad128(seq_q), _pad128(seq_kv)
+    regions = [("q8", bh * sqp * 128, torch.int8, (bh, sqp, 128)),
+               ("k8", bh * skp * 128, torch.int8, (bh, skp, 128)),
+               ("v8", bh * skp * 128, torch.float8_e4m3fn, (bh, skp, 128)),
+               ("q_scale", bh * (sqp // 32) * 4, torch.float32, (bh, sqp // 32)),
+               ("k_scale", bh * (skp // 64) * 4, torch.float32, (bh, skp // 64)),
+               ("v_scale", bh * 128 * 4, torch.float32, (bh, 128)),
+               ("k_mean", bh * 128 * 2, torch.bfloat16, (bh, 128))]
+    out, off = {}, 0
+    for name, nbytes, dtype, shape in regions:
+        out[name] = ws[off:off + nbytes].view(dtype).view(shape)
+        off += (nbytes + 255) // 256 * 256
+    return out
+
+
+def _strides(*ts):
+    vals = []
+    for t in ts:
+        if t.stride(-1) != 1:
+            raise NotImplementedError("head_dim must be contiguous")
+        vals += [t.stride(0), t.stride(1), t.stride(2)]
+    return (ctypes.c_int64 * len(vals))(*vals)
+
+
+def _validate(q, k, v):
+    _lib.require_cuda(q, k, v)
+    if q.ndim != 4 or k.ndim != 4 or v.shape != k.shape or q.shape[0] != k.shape[0] or q.shape[2:] != k.shape[2:]:
+        raise NotImplementedError("expects NHD q (B, Sq, H, 128) and k/v (B, Skv, H, 128)")
+    if q.shape[-1] != 128 or any(t.dtype != torch.bfloat16 for t in (q, k, v)):
+        raise NotImplementedError("expects bf16 tensors with head_dim 128")
+
+
+def sage_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, sm_scale: float | None = None,
+                   out: torch.Tensor | None = None, workspace: torch.Tensor | None = None) -> torch.Tensor:
+    """Sage-style attention: INT8 Q.K^T (K smoothed), FP8 P.V, NHD bf16 in and out."""
+    _check_settings()
+    _validate(q, k, v)
+    b, sq, h, d = q.shape
+    skv = k.shape[1]
+    if out is None:
+        out = torch.empty_like(q)
+    need = workspace_bytes(b, h, sq, skv)
+    if workspace is None or workspace.numel() < need:
+        workspace = torch.empty(need, device=q.device, dtype=torch.uint8)
+    _lib.call("qia_sage_attention", _lib.ptr(q), _lib.ptr(k), _lib.ptr(v), _lib.ptr(out), b, sq, skv, h, d,
+              _strides(q, k, v, out), float(sm_scale or 0.0), _lib.ptr(workspace), workspace.numel(),
+              _lib.stream(q.device))
+    return out
+
+
+def sage_quantize(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor) -> dict:
+    """Run only the quantization half; returns the workspace views."""
+    _validate(q, k, v)
+    b, sq, h, d = q.shape
+    skv = k.shape[1]
+    need = workspace_bytes(b, h, sq, skv)
+    ws = torch.empty(need, device=q.device, dtype=torch.uint8)
+    _lib.call("qia_sage_quantize", _lib.ptr(q), _lib.ptr(k), _lib.ptr(v), b, sq, skv, h, d, _strides(q, k, v),
+              _lib.ptr(ws), need, _lib.stream(q.device))
+    views = workspace_views(ws, b, h, sq, skv)
+    views["_workspace"] = ws
+    return views
+
+
+@torch.library.custom_op("qw21::sage_decode", mutates_args=())
+def sage_decode(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor) -> torch.Tensor:
+    return sage_attention(q, k, v)
+
+
+@sage_decode.register_fake
+def _(q, k, v):
+    return torch.empty_like(q)

@@ -12,7 +12,7 @@ HEADER = ROOT / "include" / "qia_b200.h"
 
 def declared():
     text = HEADER.read_text()
-    return sorted(set(re.findall(r"^(?:int|const char\*)\s+(qia_\w+)\(", text, flags=re.M)))
+    return sorted(set(re.findall(r"^(?:int64_t|int|const char\*)\s+(qia_\w+)\(", text, flags=re.M)))
 
 
 @pytest.fixture(scope="module")

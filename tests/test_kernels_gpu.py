@@ -194,8 +194,15 @@ def test_prepare_attention_inputs_vs_eager(b, s, p, h, scale):
     oq, ok, ov = prepare_attention_inputs(q, k, v, nq, nk, f, ck, cv)
     rq = eager_rope(eager_rms(q, nq.weight, 1e-6), f)
     rk = eager_rope(eager_rms(k, nk.weight, 1e-6), f)
-    assert close_bf16(bits(oq), bits(rq), ulps=2).all() and (oq == rq).float().mean().item() > 0.999
-    assert close_bf16(bits(ok), bits(torch.cat([ck, rk], 1)), ulps=2).all()
+    # torch's mean(-1) picks its reduction layout by tensor size; the kernel
+    # follows the large-batch order exactly, so small tensors may differ by one
+    # bf16 ulp after the norm, which RoPE's cancellation turns into a small
+    # absolute error: bound it by the row scale, and require near-total equality.
+    def row_close(a, b):
+        tol = 2 ** -7 * b.float().abs().amax(-1, keepdim=True)
+        return ((a.float() - b.float()).abs() <= tol).all().item()
+    assert row_close(oq, rq) and (oq == rq).float().mean().item() > 0.999
+    assert row_close(ok[:, p:], rk) and (ok[:, p:] == rk).float().mean().item() > 0.999
     assert torch.equal(ov, torch.cat([cv, v], 1)) and torch.equal(ok[:, :p], ck)
     if b * s * h <= 2 * 300 * 24:
         eq, ek, ev = oracle.qknorm_rope_pack(bits(q), bits(k), bits(v), bits(ck) if p else None,

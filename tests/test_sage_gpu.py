@@ -1,0 +1,115 @@
+"""GPU parity of the Sage-style INT8/FP8 attention (tcgen05).
+
+* quantization half: INT8 Q/K codes + scales, the bf16 K mean and the FP8 V
+  codes + scales are bit-exact against the CPU oracle (oracle.sage_quant_*);
+* attention: cosine >= 0.999 (BASELINE north_star gate) against the oracle's
+  Sage restatement, against exact fp32 attention, and at the full BASELINE
+  config-3 size against torch SDPA on the same inputs.
+"""
+import numpy as np
+import pytest
+import torch
+import torch.nn.functional as F
+
+import oracle
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+@pytest.fixture(autouse=True)
+def _cuda():
+    if not torch.cuda.is_available():
+        pytest.skip("needs a CUDA device")
+
+
+def cosine(a, b):
+    a, b = a.double().flatten(), b.double().flatten()
+    return (a @ b / (a.norm() * b.norm())).item()
+
+
+def make_qkv(b, sq, skv, h, seed, scale=1.0):
+    g = torch.Generator(device=DEV).manual_seed(seed)
+    q = torch.randn(b, sq, h, 128, device=DEV, dtype=torch.bfloat16, generator=g) * scale
+    k = torch.randn(b, skv, h, 128, device=DEV, dtype=torch.bfloat16, generator=g) * scale
+    v = torch.randn(b, skv, h, 128, device=DEV, dtype=torch.bfloat16, generator=g)
+    return q, k, v
+
+
+@pytest.mark.parametrize("b,sq,skv,h", [(1, 256, 256, 2), (2, 300, 300, 3), (1, 200, 777, 2)])
+def test_quantization_bit_exact(b, sq, skv, h):
+    from qwen_image_accel_b200.optimizations.sage_attention import sage_quantize
+    q, k, v = make_qkv(b, sq, skv, h, 1)
+    k = k + 0.5  # a non-zero mean exercises the smoothing
+    ws = sage_quantize(q, k, v)
+    qf, kf, vf = (t.float().cpu().numpy() for t in (q, k, v))
+    q8, qs = oracle.sage_quant_q(qf, 32)
+    k8, ks, km = oracle.sage_quant_k(kf, 64)
+    v8, vs = oracle.sage_quant_v(vf)
+    bh = b * h
+    # device layouts are head-major and padded; compare the live rows
+    got_q8 = ws["q8"].view(b, h, -1, 128)[:, :, :sq].permute(0, 2, 1, 3).cpu().numpy()
+    got_k8 = ws["k8"].view(b, h, -1, 128)[:, :, :skv].permute(0, 2, 1, 3).cpu().numpy()
+    got_v8 = ws["v8"].view(torch.uint8).view(b, h, -1, 128)[:, :, :skv].permute(0, 2, 1, 3).cpu().numpy()
+    assert np.array_equal(ws["k_mean"].float().view(b, h, 128).cpu().numpy(), km)
+    assert np.array_equal(got_q8, q8) and np.array_equal(got_k8, k8)
+    assert np.array_equal(ws["q_scale"].view(b, h, -1)[:, :, : qs.shape[-1]].cpu().numpy(), qs)
+    assert np.array_equal(ws["k_scale"].view(b, h, -1)[:, :, : ks.shape[-1]].cpu().numpy(), ks)
+    assert np.array_equal(got_v8, v8)
+    assert np.array_equal(ws["v_scale"].view(b, h, 128).cpu().numpy(), vs)
+    # padding rows are zero
+    assert int(ws["q8"].view(bh, -1, 128)[:, sq:].abs().sum()) == 0
+    assert int(ws["k8"].view(bh, -1, 128)[:, skv:].abs().sum()) == 0
+
+
+@pytest.mark.parametrize("b,sq,skv,h", [(1, 128, 128, 1), (1, 256, 256, 2), (2, 300, 300, 3), (1, 200, 777, 2),
+                                        (1, 1000, 1000, 1)])
+def test_attention_vs_oracle_and_exact(b, sq, skv, h):
+    from qwen_image_accel_b200 import _lib
+    from qwen_image_accel_b200.optimizations.sage_attention import sage_attention
+    q, k, v = make_qkv(b, sq, skv, h, 2)
+    out = sage_attention(q, k, v)
+    torch.cuda.synchronize()
+    assert _lib.device_error() == 0
+    qf, kf, vf = (t.float().cpu().numpy() for t in (q, k, v))
+    ref_sage = torch.from_numpy(oracle.sage_attention(qf, kf, vf))
+    ref_exact = torch.from_numpy(oracle.attention_fp32(qf, kf, vf))
+    got = out.float().cpu()
+    assert torch.isfinite(got).all()
+    assert cosine(got, ref_sage) >= 0.999
+    assert cosine(got, ref_exact) >= 0.999
+
+
+def test_attention_full_config3_vs_sdpa():
+    """B=2 (CFG), 24 heads, 256 text + 4096 image tokens."""
+    from qwen_image_accel_b200.optimizations.sage_attention import sage_attention
+    q, k, v = make_qkv(2, 4352, 4352, 24, 3)
+    out = sage_attention(q, k, v)
+    ref = F.scaled_dot_product_attention(q.transpose(1, 2).float(), k.transpose(1, 2).float(),
+                                         v.transpose(1, 2).float()).transpose(1, 2)
+    c = cosine(out.float(), ref)
+    print(f"config-3 cosine vs fp32 SDPA: {c:.6f}")
+    assert c >= 0.999
+
+
+def test_attention_per_head_cosine_and_strided_inputs():
+    """Cosine per (batch, head) and inputs read through a joint q|k|v buffer."""
+    from qwen_image_accel_b200.optimizations.sage_attention import sage_attention
+    b, s, h = 2, 520, 4
+    g = torch.Generator(device=DEV).manual_seed(4)
+    qkv = torch.randn(b, s, 3, h, 128, device=DEV, dtype=torch.bfloat16, generator=g)
+    q, k, v = qkv[:, :, 0], qkv[:, :, 1], qkv[:, :, 2]
+    out = sage_attention(q, k, v)
+    ref = F.scaled_dot_product_attention(q.transpose(1, 2).float(), k.transpose(1, 2).float(),
+                                         v.transpose(1, 2).float()).transpose(1, 2)
+    for bi in range(b):
+        for hi in range(h):
+            assert cosine(out[bi, :, hi].float(), ref[bi, :, hi]) >= 0.999
+
+
+def test_sage_decode_custom_op():
+    from qwen_image_accel_b200.optimizations import sage_attention as sa
+    q, k, v = make_qkv(1, 256, 256, 2, 5)
+    a = torch.ops.qw21.sage_decode(q, k, v)
+    b = sa.sage_attention(q, k, v)
+    assert torch.equal(a, b)
