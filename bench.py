@@ -1,0 +1,341 @@
+"""Benchmark: ms per MMDiT denoise step (1024^2) on B200.
+
+One step = the 60-block dual-stream MMDiT forward on the CFG batch of 2
+(4096 image + 256 text tokens per sample) through the `mxfp8_sage` profile,
+plus the CFG combine and the flow-matching Euler update. Random-init weights
+(~N(0, 0.02)) and seeded synthetic latents / text embeddings of the BASELINE
+shapes stand in for the checkpoint and the prompts (no network).
+
+Timing: W untimed warm-up steps, then K steps replayed from one CUDA graph of
+the step, bracketed by barrier + synchronize, timed with CUDA events on the
+launching stream; max over ranks. The working set (27 GB of weights streamed
+per step) is far larger than L2, so no flush is needed between steps.
+
+N > 1: replicas of the 1024^2 step (one per GPU, no collective on the data
+path), weak scaling; `value` = whole-job ms per step = max elapsed / (K * N).
+
+`--impl reference` times the reference's eager CPU path (oracle/mmdit_cpu.py,
+a restatement of the Diffusers block) on this host's cores: one full-size
+block per step sample, scaled by 60 blocks.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+for _p in (ROOT, ROOT / "qwen-image-2.1-accel_b200"):
+    if str(_p) not in sys.path:
+        sys.path.insert(0, str(_p))
+
+import torch  # noqa: E402
+
+METRIC = "ms per MMDiT denoise step at 1024^2 (60 blocks, CFG batch 2)"
+BLOCKS, HEADS, TXT_LEN, TXT_DIM = 60, 24, 256, 3584
+GRID = (1, 64, 64)                   # 1024^2 latent 16ch x 128 x 128, 2x2 patches
+IMG_LEN = GRID[0] * GRID[1] * GRID[2]
+
+
+def log(*a):
+    print(*a, file=sys.stderr, flush=True)
+
+
+def load_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), float(d["bf16_tflops"]), "measured"
+    return 6650.0, 1590.0, "fallback"
+
+
+# ----------------------------------------------------------------------------- clocks
+class ClockSampler:
+    def __init__(self, gpu_index: int):
+        self.proc = None
+        self.path = Path(f"/tmp/qia_clocks_{os.getpid()}.csv")
+        q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={gpu_index}", f"--query-gpu={q}",
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                         stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+
+    def stop(self):
+        out = {"sm_mhz": None, "sm_max_mhz": None, "reasons": []}
+        if self.proc is None:
+            return out
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        rows = []
+        for line in self.path.read_text().splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) >= 9:
+                rows.append(f)
+        if not rows:
+            return out
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        out["sm_mhz"] = statistics.median(sm) if sm else None
+        out["sm_max_mhz"] = float(rows[0][2]) if rows[0][2].replace(".", "").isdigit() else None
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = set()
+        for r in rows:
+            for i, n in enumerate(names):
+                if r[5 + i].lower().startswith("active"):
+                    reasons.add(n)
+        out["reasons"] = sorted(reasons)
+        out["samples"] = len(rows)
+        return out
+
+
+# ----------------------------------------------------------------------------- reference arm
+def cpu_block_sample(repeats: int = 1):
+    """Time one full-size v1 block (B=2 CFG, 4096+256 tokens) of the eager CPU
+    restatement on this host; returns (ms per block, threads)."""
+    from oracle import mmdit_cpu
+    from qwen_image_accel_b200.mmdit import MMDiTConfig, init_parameter, parameter_shapes, rope_tables
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    cfg = MMDiTConfig(num_layers=1)
+    shapes = parameter_shapes(cfg)
+    p = {n: init_parameter(n, s, seed=42) for n, s in shapes.items() if n.startswith("transformer_blocks.0.")}
+    g = torch.Generator().manual_seed(42)
+    D = cfg.dim
+    x = torch.randn(2, IMG_LEN, D, generator=g).to(torch.bfloat16)
+    c = torch.randn(2, TXT_LEN, D, generator=g).to(torch.bfloat16)
+    temb = torch.randn(2, D, generator=g).to(torch.bfloat16)
+    img_f, txt_f = rope_tables(*GRID, TXT_LEN)
+    times = []
+    with torch.no_grad():
+        for _ in range(repeats):
+            t0 = time.perf_counter()
+            mmdit_cpu.block_forward(p, "transformer_blocks.0.", x, c, temb, img_f, txt_f, HEADS)
+            times.append((time.perf_counter() - t0) * 1e3)
+    return min(times), threads
+
+
+def reference_arm(args, rank):
+    if rank != 0:
+        return
+    log("reference arm: eager CPU restatement of the v1 block, one block per step sample")
+    vals = []
+    for i in range(args.warmup + args.steps):
+        ms_block, threads = cpu_block_sample(1)
+        if i >= args.warmup:
+            vals.append(ms_block * BLOCKS)
+    v = statistics.mean(vals)
+    line = {"impl": "reference", "metric": METRIC, "value": round(v, 1), "unit": "ms/step", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(v, 1), "higher_is_better": False,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": "config4: 60-block dual-stream MMDiT, 1024^2 (4096 img + 256 txt tokens), "
+                                   "CFG batch 2", "global_batch": 2, "seq_len": IMG_LEN + TXT_LEN},
+            "cpu_baseline": {"value": round(v, 1), "unit": "ms/step", "cores": threads, "kind": "port",
+                             "sample": "one full-size block (B=2, 4352 tokens) of the eager bf16 CPU "
+                                       "restatement per step, x60 blocks"},
+            "e2e": {"value": round(v, 1), "unit": "ms/step", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# ----------------------------------------------------------------------------- our arm
+def build_model(device):
+    from qwen_image_accel_b200.mmdit import MMDiT, MMDiTConfig, random_parameters
+    cfg = MMDiTConfig(num_layers=BLOCKS)
+    t0 = time.time()
+    model = MMDiT(cfg, random_parameters(cfg, 42, device), device=device, profile="mxfp8_sage")
+    torch.cuda.synchronize()
+    log(f"model built in {time.time() - t0:.1f} s, {torch.cuda.memory_allocated() / 2**30:.1f} GiB allocated")
+    return model, cfg
+
+
+def gemm_roofline(model, device, peak_tflops_fp8, launches=20):
+    """Live timing of the dominant kernel class -- the FFN up-projection GEMM
+    (M = 8192 image rows, 3072 -> 12288, bias + GELU + MXFP8 requant epilogue),
+    exactly as launched in the step -- with CUDA events on its stream."""
+    from qwen_image_accel_b200.kernels.mxfp8 import quantize
+    blk = model.blocks[0]
+    g = torch.Generator(device=device).manual_seed(1)
+    x = torch.randn(2 * IMG_LEN, model.cfg.dim, device=device, dtype=torch.bfloat16, generator=g)
+    a = quantize(x)
+    for _ in range(3):
+        blk.img_up.mx.matmul_gelu_quantize(a)
+    st = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    e0.record(st)
+    for _ in range(launches):
+        blk.img_up.mx.matmul_gelu_quantize(a)
+    e1.record(st)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / launches
+    m, n, k = 2 * IMG_LEN, model.cfg.ffn_dim, model.cfg.dim
+    tflops = 2.0 * m * n * k / (ms * 1e-3) / 1e12
+    # library comparison on the same operands: cuBLASLt MXFP8 via torch._scaled_mm
+    lib_tflops = None
+    try:
+        w, ws = blk.img_up.mx.weight_fp8, blk.img_up.mx.weight_scale
+        for _ in range(3):
+            torch._scaled_mm(a.values, w, scale_a=a.scales, scale_b=ws, out_dtype=torch.bfloat16)
+        torch.cuda.synchronize()
+        e0.record(st)
+        for _ in range(launches):
+            torch._scaled_mm(a.values, w, scale_a=a.scales, scale_b=ws, out_dtype=torch.bfloat16)
+        e1.record(st)
+        torch.cuda.synchronize()
+        lib_tflops = 2.0 * m * n * k / (e0.elapsed_time(e1) / launches * 1e-3) / 1e12
+    except Exception as exc:  # noqa: BLE001
+        log(f"torch._scaled_mm comparison unavailable: {exc!r}")
+    return {"bound": "tensor", "kernel": "mxfp8_gemm_kernel (FFN up, M=8192 N=12288 K=3072, GELU+requant)",
+            "achieved": round(tflops, 1), "peak": round(peak_tflops_fp8, 1), "unit": "TFLOP/s",
+            "frac": round(tflops / peak_tflops_fp8, 3), "traffic": None, "ms_per_launch": round(ms, 4),
+            "cublaslt_mxfp8_tflops_same_operands": None if lib_tflops is None else round(lib_tflops, 1)}
+
+
+def our_arm(args, rank, world, local_rank):
+    from qwen_image_accel_b200 import _lib
+    device = torch.device("cuda", local_rank)
+    torch.cuda.set_device(device)
+    hbm, bf16_tf, peak_kind = load_peaks()
+    fp8_peak = 2.0 * bf16_tf   # FP8 tensor rate = 2x the bf16 rate; denominator = 2x measured cuBLAS bf16
+    model, cfg = build_model(device)
+    g = torch.Generator(device=device).manual_seed(42)
+    latents = torch.randn(1, IMG_LEN, 64, device=device, dtype=torch.bfloat16, generator=g)
+    pe = torch.randn(1, TXT_LEN, TXT_DIM, device=device, dtype=torch.bfloat16, generator=g)
+    ne = torch.randn(1, TXT_LEN, TXT_DIM, device=device, dtype=torch.bfloat16, generator=g)
+    sig, sig_next = 1.0, 0.975
+
+    static_in = latents.clone()
+    static_pe, static_ne = pe.clone(), ne.clone()
+
+    def step():
+        return model.denoise_step(static_in, static_pe, static_ne, sig, sig_next, GRID)
+
+    # warm-up (eager), then capture the step once
+    _lib.launch_count = 0
+    for _ in range(max(args.warmup, 3)):
+        out = step()
+        static_in.copy_(out)
+    torch.cuda.synchronize()
+    launches_per_step = _lib.launch_count // max(args.warmup, 3)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        static_out = step()
+    for _ in range(2):
+        graph.replay()
+    torch.cuda.synchronize()
+    if world > 1:
+        torch.distributed.barrier()
+
+    # ---------------------------------------------------------------- device-timed K steps
+    sampler = ClockSampler(torch.cuda.current_device()) if rank == 0 else None
+    st = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    e0.record(st)
+    for _ in range(args.steps):
+        graph.replay()
+        static_in.copy_(static_out)
+    e1.record(st)
+    torch.cuda.synchronize()
+    if world > 1:
+        torch.distributed.barrier()
+    elapsed = e0.elapsed_time(e1)
+    clocks = sampler.stop() if sampler else None
+    if world > 1:
+        t = torch.tensor([elapsed], device=device)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        elapsed = t.item()
+    ms_step = elapsed / args.steps
+
+    # ---------------------------------------------------------------- end to end through the API
+    host_lat = torch.empty_like(latents, device="cpu").pin_memory()
+    host_lat.copy_(latents.cpu())
+    host_pe = pe.cpu().pin_memory()
+    host_ne = ne.cpu().pin_memory()
+    host_out = torch.empty_like(host_lat).pin_memory()
+    torch.cuda.synchronize()
+    e0.record(st)
+    for _ in range(args.steps):
+        static_in.copy_(host_lat, non_blocking=True)
+        static_pe.copy_(host_pe, non_blocking=True)
+        static_ne.copy_(host_ne, non_blocking=True)
+        graph.replay()
+        host_out.copy_(static_out, non_blocking=True)
+    e1.record(st)
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1) / args.steps
+    if world > 1:
+        t = torch.tensor([e2e_ms], device=device)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        e2e_ms = t.item()
+    h2d = host_lat.numel() * 2 + host_pe.numel() * 2 + host_ne.numel() * 2
+    d2h = host_out.numel() * 2
+
+    roof = gemm_roofline(model, device, fp8_peak) if rank == 0 else None
+    if roof:
+        roof["peak_kind"] = f"2x {peak_kind} cuBLAS bf16 burst ({bf16_tf} TFLOP/s)"
+    assert _lib.device_error() == 0, "a device-side wait timed out"
+
+    del graph
+    cpu = None
+    if rank == 0 and not args.no_cpu_baseline:
+        ms_block, threads = cpu_block_sample(1)
+        cpu = {"value": round(ms_block * BLOCKS, 1), "unit": "ms/step", "cores": threads, "kind": "port",
+               "sample": "one full-size block (B=2, 4352 tokens) of the eager bf16 CPU restatement, x60 blocks"}
+
+    if rank == 0:
+        line = {"metric": METRIC, "value": round(ms_step / world, 3), "unit": "ms/step", "n_gpus": world,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 3),
+                "higher_is_better": False, "scaling": "weak", "vs_baseline": None, "dtype": "mxfp8+int8/fp8 attn",
+                "data": "synthetic (random-init weights ~N(0,0.02), seeded latents/text)",
+                "config": {"workload": "config4: 60-block dual-stream MMDiT denoise step, 1024^2 "
+                                       "(4096 img + 256 txt tokens), CFG batch 2, profile mxfp8_sage",
+                           "global_batch": 2 * world, "seq_len": IMG_LEN + TXT_LEN,
+                           "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
+                           "cuda_graph": True, "l2": "working set (27 GB weights/step) >> L2; no flush"},
+                "e2e": {"value": round(e2e_ms / world, 3), "unit": "ms/step", "h2d_bytes_per_step": h2d,
+                        "d2h_bytes_per_step": d2h},
+                "gpu_launches": launches_per_step * args.steps,
+                "roofline": roof, "cpu_baseline": cpu, "clocks": clocks}
+        print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        reference_arm(args, rank)
+        return
+    if world > 1:
+        from datetime import timedelta
+        torch.cuda.set_device(local_rank)
+        torch.distributed.init_process_group("nccl", timeout=timedelta(seconds=300))
+    try:
+        our_arm(args, rank, world, local_rank)
+    finally:
+        if world > 1:
+            torch.distributed.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -224,6 +224,20 @@ int qia_sage_attention(const void* q, const void* k, const void* v, void* out,
                        float sm_scale, void* workspace, int64_t workspace_bytes,
                        void* stream);
 
+/* The joint [text, image] sequence written back as two streams: query tokens
+ * [0, split) go to out_a ([batch, split, heads, 128]) and [split, seq_q) to
+ * out_b ([batch, seq_q - split, heads, 128]); strides: q, k, v, out_a, out_b
+ * (15 values). Replaces the joint attention + split of
+ * QwenDoubleStreamAttnProcessor2_0
+ * (WHL:diffusers/models/transformers/transformer_qwenimage.py:577-601). */
+int qia_sage_attention_split(const void* q, const void* k, const void* v,
+                             void* out_a, void* out_b, int64_t split,
+                             int64_t batch, int64_t seq_q, int64_t seq_kv,
+                             int64_t heads, int64_t head_dim,
+                             const int64_t* strides, float sm_scale,
+                             void* workspace, int64_t workspace_bytes,
+                             void* stream);
+
 /* The quantization half alone: Q INT8 per 32-token block, K mean-smoothed
  * INT8 per 64-token block, V FP8 per channel, written into the workspace
  * (strides: q, k, v -- 9 values).

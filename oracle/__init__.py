@@ -325,13 +325,17 @@ def sage_quant_q(q: np.ndarray, blk: int = 32):
 
 def sage_k_mean(k: np.ndarray) -> np.ndarray:
     """Per-(batch, head, channel) mean of K over the sequence, rounded to bf16
-    (SAGE:sageattention/core.py:773, k.mean(dim=seq) on a bf16 tensor): a
-    sequential fp32 sum times fp32(1/S)."""
+    (SAGE:sageattention/core.py:773, k.mean(dim=seq) on a bf16 tensor), in the
+    kernel's order: fp32 sums over 128-row tiles (rows in order), tile sums
+    added in order, times fp32(1/S)."""
     b, s, h, d = k.shape
-    acc = np.zeros((b, h, d), np.float32)
-    for i in range(s):
-        acc += k[:, i].astype(np.float32)
-    mean = (acc * np.float32(1.0 / s)).astype(np.float32)
+    total = np.zeros((b, h, d), np.float32)
+    for t0 in range(0, s, 128):
+        part = np.zeros((b, h, d), np.float32)
+        for i in range(t0, min(s, t0 + 128)):
+            part += k[:, i].astype(np.float32)
+        total += part
+    mean = (total * np.float32(1.0 / s)).astype(np.float32)
     return bf16_bits_to_f32(f32_to_bf16_bits(mean))
 
 

@@ -17,8 +17,11 @@
 //               and issues four tcgen05.mma.kind::mxf8f6f4.block_scale (K=32
 //               each, scale id = k step) into a TMEM accumulator; commits free
 //               the smem stage and, per tile, publish the accumulator.
-//   warps 2-5   epilogue: tcgen05.ld 32 columns at a time (one TMEM lane per
-//               output row), apply the epilogue in registers, store to HBM.
+//   warps 2-9   epilogue: two warps per TMEM sub-partition (warp % 4), each
+//               owning half of the tile's columns; tcgen05.ld 32 columns at a
+//               time (one TMEM lane per output row), apply the epilogue in
+//               registers, store to HBM. Eight warps keep the accurate-tanh
+//               GELU epilogue shorter than the next tile's main loop.
 // TMEM columns: NACC accumulators of BN columns (double-buffered when they
 // fit, so the epilogue of tile i overlaps the MMAs of tile i+1), then the A
 // scale slot (4 columns) and the B scale slot (4 per 128 rows of the tile).
@@ -44,6 +47,9 @@ struct EpiParams {
   uint8_t* q_values;           // [Mpad, N] e4m3 (kEpiGeluQuant)
   uint8_t* q_scales;           // blocked E8M0 (kEpiGeluQuant)
 };
+
+constexpr int kEpiWarps = 8;
+constexpr int kGemmThreads = 64 + 32 * kEpiWarps;
 
 template <int BN>
 struct Cfg {
@@ -72,7 +78,7 @@ __host__ __device__ constexpr uint32_t mxf8_idesc() {
 }
 
 template <int BN, int EPI>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(kGemmThreads, 1)
 mxfp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                   const uint8_t* __restrict__ sfa, const uint8_t* __restrict__ sfb, EpiParams ep, int M, int N,
                   int K, int* err) {
@@ -99,7 +105,7 @@ mxfp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_const
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(smem_u32(&acc_full[a]), 1);
-      mbar_init(smem_u32(&acc_empty[a]), 4);
+      mbar_init(smem_u32(&acc_empty[a]), kEpiWarps);
     }
     mbar_init(smem_u32(drain), 1);
     fence_barrier_init();
@@ -193,7 +199,9 @@ mxfp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_const
   } else {
     // ------------------------------------------------------------ epilogue
     const int sub = warp & 3;  // TMEM sub-partition this warp may access
+    const int half = (warp - 2) / 4;  // which half of the tile's columns
     const int row_in_tile = sub * 32 + lane;
+    constexpr int kChunks = BN / 64;  // 32-column chunks per warp
     int it = 0;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++it) {
       const int a = (C::NACC == 2) ? (it & 1) : 0;
@@ -207,11 +215,12 @@ mxfp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_const
       const bool live = row < M;
       const uint32_t t_row = tmem_base + (uint32_t(sub * 32) << 16) + uint32_t(a * BN);
 #pragma unroll 1
-      for (int j = 0; j < BN / 32; ++j) {
+      for (int jj = 0; jj < kChunks; ++jj) {
+        const int j = half * kChunks + jj;
         uint32_t r[32];
         tc_ld_32x32b_x32(t_row + uint32_t(j * 32), r);
         tc_wait_ld();
-        if (j == BN / 32 - 1) {
+        if (jj == kChunks - 1) {
           // all columns of this accumulator are in registers: hand it back
           tc_fence_before();
           __syncwarp();
@@ -349,7 +358,7 @@ int launch_gemm(const void* a, const void* sa, const void* b, const void* sb, co
   const int64_t tiles = (m_pad / 128) * (N / BN);
   int64_t grid = sm_count();
   if (grid > tiles) grid = tiles;
-  mxfp8_gemm_kernel<BN, EPI><<<unsigned(grid), 192, C::SMEM, st>>>(
+  mxfp8_gemm_kernel<BN, EPI><<<unsigned(grid), kGemmThreads, C::SMEM, st>>>(
       ta, tb, (const uint8_t*)sa, (const uint8_t*)sb, ep, int(M), int(N), int(K), device_error_word());
   return check_launch("mxfp8_gemm_kernel");
 }

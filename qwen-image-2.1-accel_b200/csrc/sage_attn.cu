@@ -40,15 +40,44 @@ constexpr int kKvStages = 3;
 constexpr float kFp8Offset = 8.807f;  // log2(448): P = 2^(s - m) <= 448
 
 // ------------------------------------------------------------------ quantizers
-// Per (b, h): k_mean[d] = bf16(sum_s k[b, s, h, d] * (1/S)), sequential fp32 sum.
-__global__ void sage_k_mean_kernel(const __nv_bfloat16* __restrict__ k, int64_t stride_b, int64_t stride_s,
-                                   int64_t stride_h, int S, int H, __nv_bfloat16* __restrict__ k_mean) {
-  const int bh = blockIdx.x, b = bh / H, h = bh % H, d = threadIdx.x;
-  const __nv_bfloat16* p = k + b * stride_b + h * stride_h + d;
-  float acc = 0.0f;
+// Per (b, h, 128-row tile): partial column sums of K (sequential over the
+// tile's rows) and partial column maxima of |V|. Thread d owns channel d.
+__global__ void __launch_bounds__(128) sage_kv_partials_kernel(
+    const __nv_bfloat16* __restrict__ k, int64_t k_sb, int64_t k_ss, int64_t k_sh,
+    const __nv_bfloat16* __restrict__ v, int64_t v_sb, int64_t v_ss, int64_t v_sh, int S, int H,
+    float* __restrict__ k_part, float* __restrict__ v_part) {
+  const int bh = blockIdx.x, b = bh / H, h = bh % H, tile = blockIdx.y, d = threadIdx.x;
+  const int r0 = tile * 128, r1 = min(S, r0 + 128);
+  const __nv_bfloat16* kp = k + b * k_sb + h * k_sh + d;
+  const __nv_bfloat16* vp = v + b * v_sb + h * v_sh + d;
+  float sum = 0.0f, amax = 0.0f;
 #pragma unroll 8
-  for (int s = 0; s < S; ++s) acc += __bfloat162float(p[int64_t(s) * stride_s]);
-  k_mean[int64_t(bh) * kD + d] = __float2bfloat16_rn(acc * (1.0f / float(S)));
+  for (int r = r0; r < r1; ++r) {
+    sum += __bfloat162float(kp[int64_t(r) * k_ss]);
+    amax = fmaxf(amax, fabsf(__bfloat162float(vp[int64_t(r) * v_ss])));
+  }
+  const int64_t o = (int64_t(bh) * gridDim.y + tile) * kD + d;
+  k_part[o] = sum;
+  v_part[o] = amax;
+}
+
+// Per (b, h): k_mean = bf16(sum of the tile partials in order * (1/S));
+// V scale = amax/448 and its reciprocal 448/amax (0 for an all-zero channel).
+__global__ void __launch_bounds__(128) sage_kv_finalize_kernel(const float* __restrict__ k_part,
+                                                               const float* __restrict__ v_part, int tiles, int S,
+                                                               __nv_bfloat16* __restrict__ k_mean,
+                                                               float* __restrict__ v_scale,
+                                                               float* __restrict__ v_recp) {
+  const int bh = blockIdx.x, d = threadIdx.x;
+  float sum = 0.0f, amax = 0.0f;
+  for (int t = 0; t < tiles; ++t) {
+    const int64_t o = (int64_t(bh) * tiles + t) * kD + d;
+    sum += k_part[o];
+    amax = fmaxf(amax, v_part[o]);
+  }
+  k_mean[int64_t(bh) * kD + d] = __float2bfloat16_rn(sum * (1.0f / float(S)));
+  v_scale[int64_t(bh) * kD + d] = amax / 448.0f;
+  v_recp[int64_t(bh) * kD + d] = amax > 0.0f ? 448.0f / amax : 0.0f;
 }
 
 // One warp per 32-row block (Q), or two warps per 64-row block (K, with the
@@ -112,23 +141,18 @@ __global__ void __launch_bounds__(128) sage_quant_int8_kernel(const __nv_bfloat1
   }
 }
 
-// Per (b, h): channel amax over the sequence, then E4M3 codes of v * 448/amax.
-// Thread d owns channel d.
+// Per (b, h, 128-row tile): E4M3 codes of v * 448/amax (zeros past S).
+// Thread d owns channel d; each row is one coalesced 128-byte store.
 __global__ void __launch_bounds__(128) sage_quant_v_kernel(const __nv_bfloat16* __restrict__ v, int64_t stride_b,
                                                            int64_t stride_s, int64_t stride_h, int S, int S_pad,
-                                                           int H, uint8_t* __restrict__ out,
-                                                           float* __restrict__ scale) {
-  const int bh = blockIdx.x, b = bh / H, h = bh % H, d = threadIdx.x;
+                                                           int H, const float* __restrict__ v_recp,
+                                                           uint8_t* __restrict__ out) {
+  const int bh = blockIdx.x, b = bh / H, h = bh % H, tile = blockIdx.y, d = threadIdx.x;
   const __nv_bfloat16* p = v + b * stride_b + h * stride_h + d;
-  float amax = 0.0f;
-#pragma unroll 8
-  for (int s = 0; s < S; ++s) amax = fmaxf(amax, fabsf(__bfloat162float(p[int64_t(s) * stride_s])));
-  scale[int64_t(bh) * kD + d] = amax / 448.0f;
-  // an all-zero channel quantizes to zero codes (no 0 * inf)
-  const float recp = amax > 0.0f ? 448.0f / amax : 0.0f;
+  const float recp = v_recp[int64_t(bh) * kD + d];
   uint8_t* dst = out + int64_t(bh) * S_pad * kD + d;
-#pragma unroll 4
-  for (int s = 0; s < S_pad; ++s) {
+#pragma unroll 8
+  for (int s = tile * 128; s < tile * 128 + 128; ++s) {
     const float x = s < S ? __bfloat162float(p[int64_t(s) * stride_s]) : 0.0f;
     dst[int64_t(s) * kD] = uint8_t(cvt_e4m3x2(x * recp, 0.0f) & 0xffu);
   }
@@ -184,8 +208,11 @@ struct AttnParams {
   const float* q_scale;
   const float* k_scale;
   const float* v_scale;
-  __nv_bfloat16* out;       // NHD [B, Sq, H, 128]
+  __nv_bfloat16* out;       // NHD [B, split, H, 128]: query tokens [0, split)
   int64_t out_stride_b, out_stride_s, out_stride_h;
+  __nv_bfloat16* out2;      // NHD [B, Sq - split, H, 128]: query tokens [split, Sq)
+  int64_t out2_stride_b, out2_stride_s, out2_stride_h;
+  int split;
   int B, H, Sq, Skv, Sq_pad, Skv_pad;
   float sm_scale_log2;      // sm_scale * log2(e)
 };
@@ -413,8 +440,12 @@ sage_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
       const float rinv = 1.0f / dsum;
       const float* vs = p.v_scale + int64_t(bh) * kD;
       const int b = bh / p.H, h = bh % p.H;
-      uint4* dst = reinterpret_cast<uint4*>(p.out + b * p.out_stride_b + int64_t(q_tok) * p.out_stride_s +
-                                            h * p.out_stride_h);
+      // the joint [text, image] sequence can be written back as two streams
+      uint4* dst = q_tok < p.split
+                       ? reinterpret_cast<uint4*>(p.out + b * p.out_stride_b + int64_t(q_tok) * p.out_stride_s +
+                                                  h * p.out_stride_h)
+                       : reinterpret_cast<uint4*>(p.out2 + b * p.out2_stride_b +
+                                                  int64_t(q_tok - p.split) * p.out2_stride_s + h * p.out2_stride_h);
 #pragma unroll 1
       for (int c = 0; c < 4; ++c) {
         uint32_t ov[32];
@@ -480,6 +511,9 @@ struct Workspace {
   float* k_scale;
   float* v_scale;
   __nv_bfloat16* k_mean;
+  float* v_recp;
+  float* k_part;   // [B*H, S_kv_pad/128, 128] partial K sums
+  float* v_part;   // [B*H, S_kv_pad/128, 128] partial |V| maxima
 };
 
 int64_t workspace_layout(int64_t B, int64_t H, int64_t Sq, int64_t Skv, uint8_t* base, Workspace* ws) {
@@ -497,6 +531,9 @@ int64_t workspace_layout(int64_t B, int64_t H, int64_t Sq, int64_t Skv, uint8_t*
   uint8_t* ks = take(bh * (skp / 64) * 4);
   uint8_t* vs = take(bh * kD * 4);
   uint8_t* km = take(bh * kD * 2);
+  uint8_t* vr = take(bh * kD * 4);
+  uint8_t* kpart = take(bh * (skp / 128) * kD * 4);
+  uint8_t* vpart = take(bh * (skp / 128) * kD * 4);
   if (ws) {
     ws->q8 = (int8_t*)q8;
     ws->k8 = (int8_t*)k8;
@@ -505,6 +542,9 @@ int64_t workspace_layout(int64_t B, int64_t H, int64_t Sq, int64_t Skv, uint8_t*
     ws->k_scale = (float*)ks;
     ws->v_scale = (float*)vs;
     ws->k_mean = (__nv_bfloat16*)km;
+    ws->v_recp = (float*)vr;
+    ws->k_part = (float*)kpart;
+    ws->v_part = (float*)vpart;
   }
   return off;
 }
@@ -528,20 +568,27 @@ int quant_qkv(const void* q, Strides qs, const void* k, Strides ks, const void* 
       (const __nv_bfloat16*)q, qs.b, qs.s, qs.h, int(Sq), int(sqp), int(H), nullptr, ws.q8, ws.q_scale);
   int rc = check_launch("sage_quant_int8_kernel<q>");
   if (rc) return rc;
-  sage_k_mean_kernel<<<bh, kD, 0, st>>>((const __nv_bfloat16*)k, ks.b, ks.s, ks.h, int(Skv), int(H), ws.k_mean);
-  rc = check_launch("sage_k_mean_kernel");
+  const unsigned kv_tiles = unsigned(skp / 128);
+  sage_kv_partials_kernel<<<dim3(bh, kv_tiles), kD, 0, st>>>((const __nv_bfloat16*)k, ks.b, ks.s, ks.h,
+                                                              (const __nv_bfloat16*)v, vs.b, vs.s, vs.h, int(Skv),
+                                                              int(H), ws.k_part, ws.v_part);
+  rc = check_launch("sage_kv_partials_kernel");
+  if (rc) return rc;
+  sage_kv_finalize_kernel<<<bh, kD, 0, st>>>(ws.k_part, ws.v_part, int(kv_tiles), int(Skv), ws.k_mean, ws.v_scale,
+                                             ws.v_recp);
+  rc = check_launch("sage_kv_finalize_kernel");
   if (rc) return rc;
   sage_quant_int8_kernel<64, true><<<dim3(bh, unsigned(skp / 128)), 128, 0, st>>>(
       (const __nv_bfloat16*)k, ks.b, ks.s, ks.h, int(Skv), int(skp), int(H), ws.k_mean, ws.k8, ws.k_scale);
   rc = check_launch("sage_quant_int8_kernel<k>");
   if (rc) return rc;
-  sage_quant_v_kernel<<<bh, kD, 0, st>>>((const __nv_bfloat16*)v, vs.b, vs.s, vs.h, int(Skv), int(skp), int(H),
-                                         ws.v8, ws.v_scale);
+  sage_quant_v_kernel<<<dim3(bh, kv_tiles), kD, 0, st>>>((const __nv_bfloat16*)v, vs.b, vs.s, vs.h, int(Skv),
+                                                         int(skp), int(H), ws.v_recp, ws.v8);
   return check_launch("sage_quant_v_kernel");
 }
 
-int launch_attn(const Workspace& ws, void* out, Strides os, int64_t B, int64_t H, int64_t Sq, int64_t Skv,
-                float sm_scale, cudaStream_t st) {
+int launch_attn(const Workspace& ws, void* out, Strides os, void* out2, Strides os2, int64_t split, int64_t B,
+                int64_t H, int64_t Sq, int64_t Skv, float sm_scale, cudaStream_t st) {
   static bool attr_done[64] = {false};
   static std::mutex mu;
   int dev = 0;
@@ -570,6 +617,11 @@ int launch_attn(const Workspace& ws, void* out, Strides os, int64_t B, int64_t H
   p.out_stride_b = os.b;
   p.out_stride_s = os.s;
   p.out_stride_h = os.h;
+  p.out2 = (__nv_bfloat16*)out2;
+  p.out2_stride_b = os2.b;
+  p.out2_stride_s = os2.s;
+  p.out2_stride_h = os2.h;
+  p.split = out2 ? int(split) : int(Sq);
   p.B = int(B);
   p.H = int(H);
   p.Sq = int(Sq);
@@ -622,7 +674,36 @@ extern "C" int qia_sage_attention(const void* q, const void* k, const void* v, v
   cudaStream_t st = as_stream(stream);
   rc = quant_qkv(q, sq, k, sk, v, sv, batch, heads, seq_q, seq_kv, ws, st);
   if (rc) return rc;
-  return launch_attn(ws, out, so, batch, heads, seq_q, seq_kv, scale, st);
+  return launch_attn(ws, out, so, nullptr, so, 0, batch, heads, seq_q, seq_kv, scale, st);
+}
+
+extern "C" int qia_sage_attention_split(const void* q, const void* k, const void* v, void* out_a, void* out_b,
+                                        int64_t split, int64_t batch, int64_t seq_q, int64_t seq_kv, int64_t heads,
+                                        int64_t head_dim, const int64_t* strides, float sm_scale, void* workspace,
+                                        int64_t workspace_bytes, void* stream) {
+  int rc = check_sizes(batch, heads, seq_q, seq_kv, head_dim, "qia_sage_attention_split");
+  if (rc) return rc;
+  if (!strides) return set_error(QIA_ERR_INVALID, "qia_sage_attention_split: null strides");
+  if (split <= 0 || split >= seq_q) return set_error(QIA_ERR_INVALID, "qia_sage_attention_split: 0 < split < seq_q");
+  const Strides sq{strides[0], strides[1], strides[2]}, sk{strides[3], strides[4], strides[5]},
+      sv{strides[6], strides[7], strides[8]}, sa{strides[9], strides[10], strides[11]},
+      sb{strides[12], strides[13], strides[14]};
+  if ((rc = check_nhd(q, sq, "qia_sage_attention_split q")) || (rc = check_nhd(k, sk, "qia_sage_attention_split k")) ||
+      (rc = check_nhd(v, sv, "qia_sage_attention_split v")) ||
+      (rc = check_nhd(out_a, sa, "qia_sage_attention_split out_a")) ||
+      (rc = check_nhd(out_b, sb, "qia_sage_attention_split out_b")))
+    return rc;
+  const int64_t need = workspace_layout(batch, heads, seq_q, seq_kv, nullptr, nullptr);
+  if (!workspace || workspace_bytes < need || !aligned(workspace, 256))
+    return set_error(QIA_ERR_INVALID, "qia_sage_attention_split: workspace of %lld bytes (256-aligned) needed",
+                     (long long)need);
+  Workspace ws;
+  workspace_layout(batch, heads, seq_q, seq_kv, (uint8_t*)workspace, &ws);
+  const float scale = sm_scale > 0.0f ? sm_scale : 1.0f / sqrtf(float(head_dim));
+  cudaStream_t st = as_stream(stream);
+  rc = quant_qkv(q, sq, k, sk, v, sv, batch, heads, seq_q, seq_kv, ws, st);
+  if (rc) return rc;
+  return launch_attn(ws, out_a, sa, out_b, sb, split, batch, heads, seq_q, seq_kv, scale, st);
 }
 
 extern "C" int qia_sage_quantize(const void* q, const void* k, const void* v, int64_t batch, int64_t seq_q,
@@ -657,5 +738,5 @@ extern "C" int qia_sage_attn_quantized(const void* workspace, void* out, int64_t
   Workspace ws;
   workspace_layout(batch, heads, seq_q, seq_kv, (uint8_t*)const_cast<void*>(workspace), &ws);
   const float scale = sm_scale > 0.0f ? sm_scale : 1.0f / sqrtf(float(head_dim));
-  return launch_attn(ws, out, so, batch, heads, seq_q, seq_kv, scale, as_stream(stream));
+  return launch_attn(ws, out, so, nullptr, so, 0, batch, heads, seq_q, seq_kv, scale, as_stream(stream));
 }

@@ -37,6 +37,7 @@ SIGNATURES: dict[str, list] = {
     "qia_mxfp8_gemm_gate_residual": [_P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _P],
     "qia_device_error": [_P],
     "qia_sage_attention": [_P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _F, _P, _I, _P],
+    "qia_sage_attention_split": [_P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _P, _F, _P, _I, _P],
     "qia_sage_quantize": [_P, _P, _P, _I, _I, _I, _I, _I, _P, _P, _I, _P],
     "qia_sage_attn_quantized": [_P, _P, _I, _I, _I, _I, _I, _P, _F, _P],
 }
@@ -87,9 +88,17 @@ def declared_symbols() -> list[str]:
     return ["qia_last_error_string", "qia_abi_version", *SIGNATURES, *RAW_SIGNATURES]
 
 
+# kernels each entry point queues (for launch accounting); default 1
+KERNELS_PER_CALL = {"qia_sage_attention": 6, "qia_sage_attention_split": 6, "qia_sage_quantize": 5,
+                    "qia_device_error": 0}
+launch_count = 0
+
+
 def call(name: str, *args) -> None:
     """Invoke a qia_* entry point and raise QiaError on a non-zero status."""
+    global launch_count
     lib = load()
+    launch_count += KERNELS_PER_CALL.get(name, 1)
     rc = getattr(lib, name)(*args)
     if rc != 0:
         msg = lib.qia_last_error_string().decode(errors="replace")

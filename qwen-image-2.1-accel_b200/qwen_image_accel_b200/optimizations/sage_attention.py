@@ -45,7 +45,10 @@ def workspace_views(ws: torch.Tensor, batch: int, heads: int, seq_q: int, seq_kv
                ("q_scale", bh * (sqp // 32) * 4, torch.float32, (bh, sqp // 32)),
                ("k_scale", bh * (skp // 64) * 4, torch.float32, (bh, skp // 64)),
                ("v_scale", bh * 128 * 4, torch.float32, (bh, 128)),
-               ("k_mean", bh * 128 * 2, torch.bfloat16, (bh, 128))]
+               ("k_mean", bh * 128 * 2, torch.bfloat16, (bh, 128)),
+               ("v_recp", bh * 128 * 4, torch.float32, (bh, 128)),
+               ("k_part", bh * (skp // 128) * 128 * 4, torch.float32, (bh, skp // 128, 128)),
+               ("v_part", bh * (skp // 128) * 128 * 4, torch.float32, (bh, skp // 128, 128))]
     out, off = {}, 0
     for name, nbytes, dtype, shape in regions:
         out[name] = ws[off:off + nbytes].view(dtype).view(shape)
@@ -86,6 +89,23 @@ def sage_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, sm_scale: 
               _strides(q, k, v, out), float(sm_scale or 0.0), _lib.ptr(workspace), workspace.numel(),
               _lib.stream(q.device))
     return out
+
+
+def sage_attention_split(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, split: int, out_a: torch.Tensor,
+                         out_b: torch.Tensor, sm_scale: float | None = None,
+                         workspace: torch.Tensor | None = None) -> None:
+    """Joint attention whose query tokens [0, split) land in out_a and
+    [split, Sq) in out_b (both NHD bf16), e.g. the text and image streams."""
+    _check_settings()
+    _validate(q, k, v)
+    b, sq, h, d = q.shape
+    skv = k.shape[1]
+    need = workspace_bytes(b, h, sq, skv)
+    if workspace is None or workspace.numel() < need:
+        workspace = torch.empty(need, device=q.device, dtype=torch.uint8)
+    _lib.call("qia_sage_attention_split", _lib.ptr(q), _lib.ptr(k), _lib.ptr(v), _lib.ptr(out_a), _lib.ptr(out_b),
+              split, b, sq, skv, h, d, _strides(q, k, v, out_a, out_b), float(sm_scale or 0.0), _lib.ptr(workspace),
+              workspace.numel(), _lib.stream(q.device))
 
 
 def sage_quantize(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor) -> dict:

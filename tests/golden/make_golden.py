@@ -17,6 +17,11 @@ modified). Sources of truth, per fixture:
   from the pinned wheel (the oracle of tests/gpu/check_attention_ops.py:264-267),
   with freqs from QwenEmbedRope for a (1, 4, 4) grid and 16 text tokens.
 * activations.npz -- eager F.silu(g) * v and F.gelu(x, approximate="tanh").
+* mmdit_tiny.npz -- the Diffusers QwenImageTransformer2DModel (v1 dual-stream
+  MMDiT, WHL:diffusers/models/transformers/transformer_qwenimage.py) at a tiny
+  size (2 blocks, 4x128 heads, text dim 512) in bf16 on the CPU, weights from
+  the package's seeded recipe (mmdit.init_parameter, torch CPU generator),
+  seeded inputs; plus its RoPE tables and timestep embedding input.
 
 Usage: python tests/golden/make_golden.py [--reference /path/to/checkout]
 """
@@ -141,6 +146,40 @@ def make_eager(reference: Path):
     np.savez_compressed(OUT / "activations.npz", **act)
 
 
+def make_mmdit(reference: Path):
+    import torch
+    _import_diffusers(reference)
+    from diffusers.models.transformers.transformer_qwenimage import QwenImageTransformer2DModel
+    sys.path.insert(0, str(OUT.parents[1] / "qwen-image-2.1-accel_b200"))
+    from qwen_image_accel_b200.mmdit import MMDiTConfig, init_parameter, parameter_shapes, rope_tables
+
+    cfg = MMDiTConfig(num_layers=2, num_attention_heads=4, joint_attention_dim=512)
+    model = QwenImageTransformer2DModel(patch_size=2, in_channels=64, out_channels=16, num_layers=2,
+                                        attention_head_dim=128, num_attention_heads=4, joint_attention_dim=512,
+                                        axes_dims_rope=(16, 56, 56)).to(torch.bfloat16)
+    shapes = parameter_shapes(cfg)
+    sd = model.state_dict()
+    assert set(sd) == set(shapes), sorted(set(sd) ^ set(shapes))
+    model.load_state_dict({n: init_parameter(n, shapes[n], seed=7) for n in sd})
+    model.eval()
+    g = torch.Generator().manual_seed(42)
+    f, h, w, lt = 1, 12, 16, 40
+    x = torch.randn(2, f * h * w, 64, generator=g).to(torch.bfloat16)
+    enc = torch.randn(2, lt, 512, generator=g).to(torch.bfloat16)
+    t = torch.tensor([0.7, 0.7]).to(torch.bfloat16)
+    with torch.no_grad():
+        out = model(hidden_states=x, encoder_hidden_states=enc, timestep=t, img_shapes=[(f, h, w)] * 2,
+                    return_dict=False)[0]
+        img_f, txt_f = model.pos_embed([(f, h, w)], max_txt_seq_len=lt, device=torch.device("cpu"))
+    mine_img, mine_txt = rope_tables(f, h, w, lt)
+    assert torch.equal(mine_img, img_f) and torch.equal(mine_txt, txt_f)
+    np.savez_compressed(OUT / "mmdit_tiny.npz", x=_bits(x), enc=_bits(enc), out=_bits(out),
+                        img_freqs=torch.view_as_real(img_f).numpy().copy(),
+                        txt_freqs=torch.view_as_real(txt_f).numpy().copy(),
+                        shape=np.array([f, h, w, lt]), timestep=np.float32(0.7),
+                        keys=np.array(sorted(sd)))
+
+
 if __name__ == "__main__":
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default="/root/reference")
@@ -148,4 +187,5 @@ if __name__ == "__main__":
     ref = Path(args.reference)
     make_mxfp8(ref)   # first: the interpreter flag must precede the first triton import
     make_eager(ref)
+    make_mmdit(ref)
     print("wrote", sorted(p.name for p in OUT.glob("*.npz")))
