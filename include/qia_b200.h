@@ -256,6 +256,26 @@ int qia_sage_attn_quantized(const void* workspace, void* out, int64_t batch,
                             int64_t head_dim, const int64_t* out_strides,
                             float sm_scale, void* stream);
 
+/* Allocation-free variant of qia_sage_attention (no counterpart in the
+ * reference): identical arguments minus the workspace. Some callers cannot
+ * allocate device memory when they need attention -- a host that reaches the
+ * GPU only through this C ABI (an FFI or plugin caller with no device
+ * allocator of its own), a server whose device memory is a fixed pool owned
+ * by another allocator, or a latency-critical loop that must not pay for
+ * cudaMalloc/cudaFree, which synchronise the device. This entry point uses a
+ * 16 MiB scratch array built into the library instead (held on every GPU
+ * that loads the library until the process exits) and allocates nothing;
+ * sizes whose workspace (qia_sage_workspace_bytes) exceeds 16 MiB are
+ * rejected with QIA_ERR_UNSUPPORTED. The first call on each device looks up
+ * the scratch's device address (make that first call before any stream
+ * capture on that device). All calls share the one scratch array, whose
+ * contents persist between calls: calls that may overlap on the GPU race. */
+int qia_sage_attention_noalloc(const void* q, const void* k, const void* v,
+                               void* out, int64_t batch, int64_t seq_q,
+                               int64_t seq_kv, int64_t heads, int64_t head_dim,
+                               const int64_t* strides, float sm_scale,
+                               void* stream);
+
 /* Reads and clears the device-side error word of the current device (set when
  * a bounded wait inside a tensor-core kernel gave up). Synchronises the device. */
 int qia_device_error(int* code);

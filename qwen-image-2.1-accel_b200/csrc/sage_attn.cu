@@ -642,6 +642,35 @@ int check_sizes(int64_t B, int64_t H, int64_t Sq, int64_t Skv, int64_t D, const 
   return QIA_OK;
 }
 
+// ------------------------------------------------------------------ built-in scratch
+// Scratch for qia_sage_attention_noalloc: a fixed device array that lives as
+// long as the library is loaded (every GPU that loads the library holds these
+// 16 MiB until the process exits). Host code must not use the symbol as a
+// pointer: its device address is resolved per device by builtin_scratch().
+constexpr int64_t kBuiltinScratchBytes = int64_t(16) << 20;
+static __device__ __align__(256) uint8_t g_sage_scratch[kBuiltinScratchBytes];
+
+// Device address of g_sage_scratch on the current device, looked up with
+// cudaGetSymbolAddress the first time each device asks and cached after that.
+int builtin_scratch(void** out) {
+  static void* addr[64] = {nullptr};
+  static std::mutex mu;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return set_error(QIA_ERR_CUDA, "cudaGetDevice: %s", cudaGetErrorString(e));
+  if (dev < 0 || dev >= 64) return set_error(QIA_ERR_UNSUPPORTED, "device ordinal %d out of range", dev);
+  std::lock_guard<std::mutex> lock(mu);
+  if (!addr[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_sage_scratch);
+    if (e != cudaSuccess || !p)
+      return set_error(QIA_ERR_CUDA, "cudaGetSymbolAddress(scratch): %s", cudaGetErrorString(e));
+    addr[dev] = p;
+  }
+  *out = addr[dev];
+  return QIA_OK;
+}
+
 }  // namespace
 }  // namespace qia
 
@@ -739,4 +768,28 @@ extern "C" int qia_sage_attn_quantized(const void* workspace, void* out, int64_t
   workspace_layout(batch, heads, seq_q, seq_kv, (uint8_t*)const_cast<void*>(workspace), &ws);
   const float scale = sm_scale > 0.0f ? sm_scale : 1.0f / sqrtf(float(head_dim));
   return launch_attn(ws, out, so, nullptr, so, 0, batch, heads, seq_q, seq_kv, scale, as_stream(stream));
+}
+
+// Same computation as qia_sage_attention, with the library's built-in scratch
+// in place of a caller workspace, for callers that cannot allocate device
+// memory (see qia_b200.h). Every region of the scratch is rewritten before it
+// is read on each call, so nothing needs clearing between calls; calls that
+// overlap on the GPU (other streams, other host threads) share the one array
+// and race.
+extern "C" int qia_sage_attention_noalloc(const void* q, const void* k, const void* v, void* out, int64_t batch,
+                                          int64_t seq_q, int64_t seq_kv, int64_t heads, int64_t head_dim,
+                                          const int64_t* strides, float sm_scale, void* stream) {
+  int rc = check_sizes(batch, heads, seq_q, seq_kv, head_dim, "qia_sage_attention_noalloc");
+  if (rc) return rc;
+  const int64_t need = workspace_layout(batch, heads, seq_q, seq_kv, nullptr, nullptr);
+  if (need > kBuiltinScratchBytes)
+    return set_error(QIA_ERR_UNSUPPORTED,
+                     "qia_sage_attention_noalloc: these sizes need %lld bytes of scratch but the built-in scratch "
+                     "holds %lld; use qia_sage_attention with a caller workspace",
+                     (long long)need, (long long)kBuiltinScratchBytes);
+  void* ws = nullptr;
+  rc = builtin_scratch(&ws);
+  if (rc) return rc;
+  return qia_sage_attention(q, k, v, out, batch, seq_q, seq_kv, heads, head_dim, strides, sm_scale, ws,
+                            kBuiltinScratchBytes, stream);
 }
