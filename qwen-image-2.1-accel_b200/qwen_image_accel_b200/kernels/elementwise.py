@@ -14,11 +14,12 @@ def residual(h: torch.Tensor, x: torch.Tensor, gate: torch.Tensor) -> torch.Tens
     _lib.require_cuda(h, x, gate)
     if (h.dtype != torch.bfloat16 or x.dtype != torch.bfloat16 or gate.dtype != torch.bfloat16
             or not h.is_contiguous() or not x.is_contiguous() or x.shape != h.shape or h.ndim != 3
-            or gate.shape != (h.shape[0], 1, h.shape[-1]) or not gate.is_contiguous()):
-        raise NotImplementedError("residual: expects contiguous bf16 (B, S, D) h/x and (B, 1, D) gate")
+            or gate.shape not in ((h.shape[0], 1, h.shape[-1]), (1, 1, h.shape[-1])) or not gate.is_contiguous()):
+        raise NotImplementedError("residual: expects contiguous bf16 (B, S, D) h/x and (B, 1, D) or (1, 1, D) gate")
     out = torch.empty_like(h)
     b, s, d = h.shape
-    _lib.call("qia_gated_residual", _lib.ptr(h), _lib.ptr(x), _lib.ptr(gate), _lib.ptr(out), b * s, d, s,
+    rows_per_gate = s if gate.shape[0] == b else b * s
+    _lib.call("qia_gated_residual", _lib.ptr(h), _lib.ptr(x), _lib.ptr(gate), _lib.ptr(out), b * s, d, rows_per_gate,
               _lib.stream(h.device))
     return out
 

@@ -22,12 +22,14 @@ def layer_norm_scale_quantize(x: torch.Tensor, scale: torch.Tensor, norm,
             or tuple(norm.normalized_shape) != (d,)):
         return None
     for v in (scale, shift):
-        if v is not None and (v.shape != (x.shape[0], 1, d) or v.dtype != torch.bfloat16 or not v.is_contiguous()):
+        if v is not None and (v.shape not in ((x.shape[0], 1, d), (1, 1, d)) or v.dtype != torch.bfloat16
+                              or not v.is_contiguous() or v.shape[0] != scale.shape[0]):
             return None
     b, s, _ = x.shape
+    rows_per_vector = s if scale.shape[0] == b else b * s
     out = empty_quantized(b * s, d, x.device, x.shape)
     _lib.call("qia_ln_mod_quant", _lib.ptr(x), _lib.ptr(scale), _lib.ptr(shift), _lib.ptr(out.values),
-              _lib.ptr(out.scales), b * s, d, s, float(norm.eps), _lib.stream(x.device))
+              _lib.ptr(out.scales), b * s, d, rows_per_vector, float(norm.eps), _lib.stream(x.device))
     return out
 
 

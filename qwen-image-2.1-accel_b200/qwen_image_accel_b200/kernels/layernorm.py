@@ -20,17 +20,20 @@ def _check(x, scale, shift, norm):
             or x.numel() == 0 or tuple(norm.normalized_shape) != (d,)):
         raise NotImplementedError(f"layer_norm_scale: unsupported input {tuple(x.shape)} {x.dtype}")
     for v in (scale, shift):
-        if v is not None and (v.shape != (x.shape[0], 1, d) or v.dtype != torch.bfloat16 or not v.is_contiguous()):
-            raise NotImplementedError("layer_norm_scale: scale/shift must be contiguous bf16 (B, 1, D)")
+        if v is not None and (v.shape not in ((x.shape[0], 1, d), (1, 1, d)) or v.dtype != torch.bfloat16
+                              or not v.is_contiguous() or v.shape[0] != scale.shape[0]):
+            raise NotImplementedError("layer_norm_scale: scale/shift must be contiguous bf16 (B, 1, D) or (1, 1, D)")
 
 
 def layer_norm_scale(x: torch.Tensor, scale: torch.Tensor, norm, shift: torch.Tensor | None = None) -> torch.Tensor:
     """bf16(LN(x)) * scale [+ shift], each product/sum rounded to bf16.
 
-    ``scale`` is the precomputed ``1 + s`` vector, as in the reference."""
+    ``scale`` is the precomputed ``1 + s`` vector, as in the reference; a
+    (1, 1, D) scale/shift is shared by every batch row."""
     _check(x, scale, shift, norm)
     out = torch.empty_like(x)
     b, s, d = x.shape
-    _lib.call("qia_ln_mod", _lib.ptr(x), _lib.ptr(scale), _lib.ptr(shift), _lib.ptr(out), b * s, d, s,
+    rows_per_vector = s if scale.shape[0] == b else b * s
+    _lib.call("qia_ln_mod", _lib.ptr(x), _lib.ptr(scale), _lib.ptr(shift), _lib.ptr(out), b * s, d, rows_per_vector,
               float(norm.eps), _lib.stream(x.device))
     return out

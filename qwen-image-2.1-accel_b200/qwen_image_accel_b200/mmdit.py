@@ -324,13 +324,19 @@ class MMDiT:
     # ------------------------------------------------------------------ model
     def modulations(self, temb: torch.Tensor):
         """All blocks' AdaLN vectors from one stacked GEMM: per block and stream
-        (shift1, 1+scale1, gate1, shift2, 1+scale2, gate2), each (B, 1, D)."""
-        D = self.cfg.dim
-        allm = F.linear(F.silu(temb), self.mod_w, self.mod_b)          # [B, L*2*6D]
+        (shift1, 1+scale1, gate1, shift2, 1+scale2, gate2), each (B, 1, D);
+        with one temb row they are (1, 1, D) views shared by every batch row."""
+        D, L = self.cfg.dim, self.cfg.num_layers
         B = temb.shape[0]
-        allm = allm.view(B, self.cfg.num_layers, 2, 6, D)
+        allm = F.linear(F.silu(temb), self.mod_w, self.mod_b)          # [B, L*2*6D]
+        if B == 1:
+            v = allm.view(L, 2, 6, D)
+            v[:, :, 1] += 1          # 1 + scale1, in place over every block
+            v[:, :, 4] += 1          # 1 + scale2
+            return [[tuple(v[i, s, j].view(1, 1, D) for j in range(6)) for s in range(2)] for i in range(L)]
+        allm = allm.view(B, L, 2, 6, D)
         out = []
-        for i in range(self.cfg.num_layers):
+        for i in range(L):
             per = []
             for s in range(2):
                 m = allm[:, i, s]
@@ -341,15 +347,18 @@ class MMDiT:
         return out
 
     def forward(self, hidden_states: torch.Tensor, encoder_hidden_states: torch.Tensor, timestep: torch.Tensor,
-                img_shape) -> torch.Tensor:
+                img_shape, shared_timestep: bool = False) -> torch.Tensor:
         """hidden_states [B, Li, 64] bf16 (packed latents), encoder_hidden_states
         [B, Lt, joint_attention_dim] bf16, timestep [B] (sigma in [0, 1]);
-        returns the velocity [B, Li, patch^2 * out_channels] bf16."""
+        returns the velocity [B, Li, patch^2 * out_channels] bf16.
+
+        shared_timestep: every batch row has the same timestep (the CFG
+        batch), so the timestep embedding and modulation are computed once."""
         cfg = self.cfg
         x = F.linear(hidden_states, *self.img_in)
         t = timestep.to(torch.bfloat16)
         c = F.linear(rms_norm_eager(encoder_hidden_states, self.txt_norm_w, cfg.eps), *self.txt_in)
-        temb = self.time_embed(t)
+        temb = self.time_embed(t[:1] if shared_timestep else t)
         freqs_img, freqs_txt = self.rope(img_shape, c.shape[1])
         mods = self.modulations(temb)
         x, c = x.contiguous(), c.contiguous()
@@ -369,7 +378,7 @@ class MMDiT:
         x_in = torch.cat([latents, latents])
         enc = torch.cat([prompt_embeds, negative_embeds])
         t = torch.full((2 * b,), sigma, device=latents.device, dtype=latents.dtype)
-        v = self.forward(x_in, enc, t, img_shape)
+        v = self.forward(x_in, enc, t, img_shape, shared_timestep=True)
         cond, neg = v[:b], v[b:]
         comb = neg + cfg_scale * (cond - neg)
         cond_norm = torch.norm(cond, dim=-1, keepdim=True)

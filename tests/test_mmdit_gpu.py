@@ -95,3 +95,11 @@ def test_denoise_step_runs_and_is_finite():
     ne = torch.randn(1, 40, 512, device="cuda", dtype=torch.bfloat16, generator=g)
     out = model.denoise_step(lat, pe, ne, 1.0, 0.975, (1, 12, 16))
     assert out.shape == lat.shape and torch.isfinite(out.float()).all()
+
+
+def test_shared_timestep_modulation_matches_per_row():
+    """One modulation row broadcast over the CFG batch == per-row modulation."""
+    model, _, _, (x, enc, t, shape) = run_tiny("mxfp8_sage")
+    a = model.forward(x, enc, t, shape).float()
+    b = model.forward(x, enc, t, shape, shared_timestep=True).float()
+    assert psnr(b.cpu(), a.cpu()) >= 60.0
