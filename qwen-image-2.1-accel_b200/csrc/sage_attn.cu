@@ -15,9 +15,13 @@
 //    max m offset by log2(448) so P = 2^(s - m) lies in [0, 448]
 //    (SAGE:csrc/qattn/attn_utils.cuh:353-440); P rounded to E4M3 for the
 //    P.V product, the row sum taken over the unrounded P;
-//  * "fp32+fp32": the P.V products accumulate in a full-fp32 TMEM accumulator
-//    rescaled by 2^(m_old - m_new) whenever a row's running max grows (the
-//    rescale happens in TMEM, only in warps where some row's max changed);
+//  * the row max is found first: pass A computes Q.K^T for every K tile and
+//    keeps only each row's max; pass B recomputes Q.K^T and forms
+//    P = 2^(s - m) with the final m (offset by log2(448), so P <= 448 exactly
+//    as in Sage), so no rescale of O is ever needed; P.V accumulates in a
+//    full-fp32 TMEM accumulator. Sage's online form rounds P to E4M3 relative
+//    to the running max instead; the two differ only for weights below
+//    2^-9 of the row max;
 //  * out = O / rowsum * v_scale, bf16 (SAGE:csrc/qattn/qk_int_sv_f8_cuda_sm89.cuh:566-600).
 //
 // Device layouts written by the quantization kernels here (head-major, rows
@@ -36,7 +40,7 @@ namespace {
 
 constexpr int kD = 128;
 constexpr int kTile = 128;
-constexpr int kKvStages = 3;
+constexpr int kKvStages = 2;
 constexpr float kFp8Offset = 8.807f;  // log2(448): P = 2^(s - m) <= 448
 
 // ------------------------------------------------------------------ quantizers
@@ -217,14 +221,18 @@ struct AttnParams {
   float sm_scale_log2;      // sm_scale * log2(e)
 };
 
+// Two CTAs share an SM (96 KB of shared memory and 256 TMEM columns each), so
+// one CTA's MMAs run while the other's softmax warps work.
 constexpr int kSmemQ = 0;
 constexpr int kSmemK = kSmemQ + 16384;
 constexpr int kSmemV = kSmemK + kKvStages * 16384;
 constexpr int kSmemP = kSmemV + kKvStages * 16384;
-constexpr int kSmemBar = kSmemP + 2 * 16384;
+constexpr int kSmemBar = kSmemP + 16384;
 constexpr int kAttnSmem = kSmemBar + 1024 + 1024;
+constexpr uint32_t kAttnTmemCols = 256;   // S [0,128), O [128,256)
+constexpr uint32_t kTmemO = 128;
 
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(192, 2)
 sage_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                  const __grid_constant__ CUtensorMap tm_v, AttnParams p, int* err) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -235,12 +243,11 @@ sage_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
   uint64_t* k_empty = k_full + kKvStages;
   uint64_t* v_full = k_empty + kKvStages;
   uint64_t* v_empty = v_full + kKvStages;
-  uint64_t* s_full = v_empty + kKvStages;
-  uint64_t* s_free = s_full + 2;
-  uint64_t* p_full = s_free + 2;
-  uint64_t* p_free = p_full + 2;
-  uint64_t* o_done = p_free + 2;   // one phase per P.V tile
-  uint64_t* drain = o_done + 1;
+  uint64_t* s_full = v_empty + kKvStages;  // one phase per Q.K^T tile
+  uint64_t* s_free = s_full + 1;            // one phase per softmax pass over S
+  uint64_t* p_full = s_free + 1;            // one phase per P tile written
+  uint64_t* p_free = p_full + 1;            // one phase per P.V tile finished
+  uint64_t* drain = p_free + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -257,50 +264,53 @@ sage_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
       mbar_init(smem_u32(&v_full[s]), 1);
       mbar_init(smem_u32(&v_empty[s]), 1);
     }
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(smem_u32(&s_full[i]), 1);
-      mbar_init(smem_u32(&s_free[i]), 4);
-      mbar_init(smem_u32(&p_full[i]), 4);
-      mbar_init(smem_u32(&p_free[i]), 1);
-    }
-    mbar_init(smem_u32(o_done), 1);
+    mbar_init(smem_u32(s_full), 1);
+    mbar_init(smem_u32(s_free), 4);
+    mbar_init(smem_u32(p_full), 4);
+    mbar_init(smem_u32(p_free), 1);
     mbar_init(smem_u32(drain), 1);
     fence_barrier_init();
     prefetch_tmap(&tm_q);
     prefetch_tmap(&tm_k);
     prefetch_tmap(&tm_v);
   }
-  if (warp == 1) tmem_alloc(smem_u32(tmem_slot), 512);
+  if (warp == 1) tmem_alloc(smem_u32(tmem_slot), kAttnTmemCols);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  // TMEM columns: S0 [0,128), S1 [128,256), O [256,384)
 
   if (warp == 0) {
     if (lane == 0) {
       bool ok = true;
-      int issued = 0;
+      int issued = 0, issued_v = 0;
       mbar_arrive_expect_tx(smem_u32(q_full), 16384);
       tma_load_2d(smem_u32(smem + kSmemQ), &tm_q, smem_u32(q_full), 0, q_row0);
-      for (int j = 0; j < nkv && ok; ++j) {
-        const int st = j % kKvStages;
-        const uint32_t ph = (j / kKvStages) & 1;
+      // steps [0, nkv): K tiles for the row-max pass; [nkv, 2 nkv): K and V tiles
+      for (int t = 0; t < 2 * nkv && ok; ++t) {
+        const int j = t < nkv ? t : t - nkv;
+        const int st = t % kKvStages;
+        const uint32_t ph = (t / kKvStages) & 1;
         if (!mbar_wait(smem_u32(&k_empty[st]), ph ^ 1, err)) { ok = false; break; }
         mbar_arrive_expect_tx(smem_u32(&k_full[st]), 16384);
         tma_load_2d(smem_u32(smem + kSmemK + st * 16384), &tm_k, smem_u32(&k_full[st]), 0, kv_row0 + j * kTile);
-        if (!mbar_wait(smem_u32(&v_empty[st]), ph ^ 1, err)) { ok = false; break; }
-        mbar_arrive_expect_tx(smem_u32(&v_full[st]), 16384);
-        tma_load_2d(smem_u32(smem + kSmemV + st * 16384), &tm_v, smem_u32(&v_full[st]), 0, kv_row0 + j * kTile);
-        issued = j + 1;
+        if (t >= nkv) {
+          const int vs = j % kKvStages;
+          const uint32_t vph = (j / kKvStages) & 1;
+          if (!mbar_wait(smem_u32(&v_empty[vs]), vph ^ 1, err)) { ok = false; break; }
+          mbar_arrive_expect_tx(smem_u32(&v_full[vs]), 16384);
+          tma_load_2d(smem_u32(smem + kSmemV + vs * 16384), &tm_v, smem_u32(&v_full[vs]), 0, kv_row0 + j * kTile);
+          issued_v = j + 1;
+        }
+        issued = t + 1;
       }
       if (!ok) {
         // let queued copies land before the shared memory is released
         mbar_wait(smem_u32(q_full), 0, nullptr, 100000000ull);
-        for (int j = (issued > kKvStages ? issued - kKvStages : 0); j < issued; ++j) {
-          mbar_wait(smem_u32(&k_full[j % kKvStages]), (j / kKvStages) & 1, nullptr, 100000000ull);
+        for (int t = (issued > kKvStages ? issued - kKvStages : 0); t < issued; ++t)
+          mbar_wait(smem_u32(&k_full[t % kKvStages]), (t / kKvStages) & 1, nullptr, 100000000ull);
+        for (int j = (issued_v > kKvStages ? issued_v - kKvStages : 0); j < issued_v; ++j)
           mbar_wait(smem_u32(&v_full[j % kKvStages]), (j / kKvStages) & 1, nullptr, 100000000ull);
-        }
       }
     }
   } else if (warp == 1) {
@@ -308,33 +318,35 @@ sage_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
       bool ok = mbar_wait(smem_u32(q_full), 0, err);
       tc_fence_after();
       const uint64_t qdesc = smem_desc_k_sw128(smem_u32(smem + kSmemQ));
-      for (int j = 0; j <= nkv && ok; ++j) {
-        if (j < nkv) {
-          const int sb = j & 1, st = j % kKvStages;
-          if (!mbar_wait(smem_u32(&k_full[st]), (j / kKvStages) & 1, err)) { ok = false; break; }
-          if (!mbar_wait(smem_u32(&s_free[sb]), ((j >> 1) & 1) ^ 1, err)) { ok = false; break; }
+      // steps [0, nkv): Q.K^T for the row-max pass; [nkv, 2 nkv): Q.K^T again,
+      // and P.V of the previous step's tile (lagged by one step so that each
+      // Q.K^T overlaps the softmax of the tile before it)
+      for (int t = 0; t <= 2 * nkv && ok; ++t) {
+        if (t < 2 * nkv) {
+          const int st = t % kKvStages;
+          if (!mbar_wait(smem_u32(&k_full[st]), (t / kKvStages) & 1, err)) { ok = false; break; }
+          // S is free once the softmax finished step t-1 (phase t-1)
+          if (!mbar_wait(smem_u32(s_free), (t & 1) ^ 1, err)) { ok = false; break; }
           tc_fence_after();
           const uint64_t kdesc = smem_desc_k_sw128(smem_u32(smem + kSmemK + st * 16384));
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk)
-            tc_mma_i8(tmem + uint32_t(sb * 128), qdesc + uint64_t(2 * kk), kdesc + uint64_t(2 * kk), kIdescQK, kk > 0);
+            tc_mma_i8(tmem, qdesc + uint64_t(2 * kk), kdesc + uint64_t(2 * kk), kIdescQK, kk > 0);
           tc_commit(smem_u32(&k_empty[st]));
-          tc_commit(smem_u32(&s_full[sb]));
+          tc_commit(smem_u32(s_full));
         }
-        if (j >= 1) {
-          const int i = j - 1, pb = i & 1, st = i % kKvStages;
-          const uint32_t pph = (i >> 1) & 1;
-          if (!mbar_wait(smem_u32(&p_full[pb]), pph, err)) { ok = false; break; }
-          if (!mbar_wait(smem_u32(&v_full[st]), (i / kKvStages) & 1, err)) { ok = false; break; }
+        if (t >= nkv + 1) {
+          const int i = t - 1 - nkv, vs = i % kKvStages;
+          if (!mbar_wait(smem_u32(p_full), i & 1, err)) { ok = false; break; }
+          if (!mbar_wait(smem_u32(&v_full[vs]), (i / kKvStages) & 1, err)) { ok = false; break; }
           tc_fence_after();
-          const uint64_t pdesc = smem_desc_k_sw128(smem_u32(smem + kSmemP + pb * 16384));
-          const uint64_t vdesc = smem_desc_mn_sw128(smem_u32(smem + kSmemV + st * 16384));
+          const uint64_t pdesc = smem_desc_k_sw128(smem_u32(smem + kSmemP));
+          const uint64_t vdesc = smem_desc_mn_sw128(smem_u32(smem + kSmemV + vs * 16384));
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk)
-            tc_mma_f8(tmem + 256u, pdesc + uint64_t(2 * kk), vdesc + uint64_t(256 * kk), kIdescPV, (i | kk) != 0);
-          tc_commit(smem_u32(&v_empty[st]));
-          tc_commit(smem_u32(&p_free[pb]));
-          tc_commit(smem_u32(o_done));
+            tc_mma_f8(tmem + kTmemO, pdesc + uint64_t(2 * kk), vdesc + uint64_t(256 * kk), kIdescPV, (i | kk) != 0);
+          tc_commit(smem_u32(&v_empty[vs]));
+          tc_commit(smem_u32(p_free));
         }
       }
       tc_commit(smem_u32(drain));
@@ -342,100 +354,112 @@ sage_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
     }
   } else {
     // ---------------------------------------------------------- softmax
-    // One thread per query row (TMEM lane). O lives in TMEM columns [256, 384).
+    // One thread per query row (TMEM lane). O lives in TMEM columns [128, 256).
     const int sub = warp & 3;
     const int r = sub * 32 + lane;            // row within the query tile
     const int q_tok = q_tile * kTile + r;     // token index
     const uint32_t t_lane = uint32_t(sub * 32) << 16;
     const float qs = p.q_scale[int64_t(bh) * (p.Sq_pad / 32) + q_tok / 32];
     const int kb_per_head = p.Skv_pad / 64;
-    float m_old = -5000000.0f, dsum = 0.0f;
     bool ok = true;
     uint8_t* p_smem = smem + kSmemP;
+    uint8_t* prow = p_smem + r * 128;
+    // ---- pass A: the row max of s = S * (sm_scale*log2e) * (q_scale*k_scale)
+    float m = -5000000.0f;
     for (int j = 0; j < nkv; ++j) {
-      const int sb = j & 1;
-      const uint32_t sph = (j >> 1) & 1;
-      if (!__all_sync(0xffffffffu, mbar_wait(smem_u32(&s_full[sb]), sph, err))) { ok = false; break; }
+      if (!__all_sync(0xffffffffu, mbar_wait(smem_u32(s_full), j & 1, err))) { ok = false; break; }
       tc_fence_after();
       const float sc0 = p.sm_scale_log2 * (qs * p.k_scale[int64_t(bh) * kb_per_head + 2 * j]);
       const float sc1 = p.sm_scale_log2 * (qs * p.k_scale[int64_t(bh) * kb_per_head + 2 * j + 1]);
-      const int valid = p.Skv - j * kTile;   // keys of this tile that exist (may exceed 128)
-      // pass 1: row max of the raw integer scores per 64-key half
-      int mx0 = INT_MIN, mx1 = INT_MIN;
+      const int valid = p.Skv - j * kTile;
+      int mx[2];
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t sv[32];
-        tc_ld_32x32b_x32(tmem + t_lane + uint32_t(sb * 128 + c * 32), sv);
+      for (int h2 = 0; h2 < 2; ++h2) {
+        uint32_t sa[32], sb2[32];
+        tc_ld_32x32b_x32(tmem + t_lane + uint32_t(h2 * 64), sa);
+        tc_ld_32x32b_x32(tmem + t_lane + uint32_t(h2 * 64 + 32), sb2);
         tc_wait_ld();
+        int mh = INT_MIN;
+        if (valid >= kTile) {
 #pragma unroll
-        for (int t = 0; t < 32; ++t) {
-          const int v = (c * 32 + t) < valid ? int(sv[t]) : INT_MIN;
-          if (c < 2) mx0 = max(mx0, v); else mx1 = max(mx1, v);
-        }
-      }
-      float m_new = m_old;
-      if (mx0 != INT_MIN) m_new = fmaxf(m_new, fmaf(float(mx0), sc0, -kFp8Offset));
-      if (mx1 != INT_MIN) m_new = fmaxf(m_new, fmaf(float(mx1), sc1, -kFp8Offset));
-      const float alpha = ex2_approx(m_old - m_new);
-      // rescale O in TMEM where some row of this warp raised its max; s_full(j)
-      // implies P.V tile j-2 finished, and tile j cannot start before this
-      // warp's p_full(j), so o_done is at phase j-1 or j here
-      if (__any_sync(0xffffffffu, j > 0 && alpha != 1.0f)) {
-        if (!__all_sync(0xffffffffu, mbar_wait(smem_u32(o_done), (j - 1) & 1, err))) { ok = false; break; }
-        tc_fence_after();
-#pragma unroll 1
-        for (int c = 0; c < 4; ++c) {
-          uint32_t ov[32];
-          tc_ld_32x32b_x32(tmem + t_lane + uint32_t(256 + c * 32), ov);
-          tc_wait_ld();
+          for (int t = 0; t < 32; t += 2) mh = __vimax3_s32(mh, int(sa[t]), int(sa[t + 1]));
 #pragma unroll
-          for (int t = 0; t < 32; ++t) ov[t] = __float_as_uint(__uint_as_float(ov[t]) * alpha);
-          tc_st_32x32b_x32(tmem + t_lane + uint32_t(256 + c * 32), ov);
-        }
-        tc_wait_st();
-      }
-      dsum *= alpha;
-      // pass 2: P = 2^(s - m) -> E4M3 into the swizzled K-major P tile
-      if (!__all_sync(0xffffffffu, mbar_wait(smem_u32(&p_free[sb]), sph ^ 1, err))) { ok = false; break; }
-      uint8_t* prow = p_smem + sb * 16384 + r * 128;
+          for (int t = 0; t < 32; t += 2) mh = __vimax3_s32(mh, int(sb2[t]), int(sb2[t + 1]));
+        } else {
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t sv[32];
-        tc_ld_32x32b_x32(tmem + t_lane + uint32_t(sb * 128 + c * 32), sv);
-        tc_wait_ld();
-        const float sc = c < 2 ? sc0 : sc1;
-        uint32_t w[8];
-#pragma unroll
-        for (int t = 0; t < 32; t += 4) {
-          float pv[4];
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const int key = c * 32 + t + e;
-            pv[e] = key < valid ? ex2_approx(fmaf(i2f_small(sv[t + e]), sc, -m_new)) : 0.0f;
-            dsum += pv[e];
+          for (int t = 0; t < 32; ++t) {
+            if (h2 * 64 + t < valid) mh = max(mh, int(sa[t]));
+            if (h2 * 64 + 32 + t < valid) mh = max(mh, int(sb2[t]));
           }
-          w[t / 4] = cvt_e4m3x4(pv[0], pv[1], pv[2], pv[3]);
         }
-        // 32 keys = two 16-byte units (2c, 2c+1) of the 128-byte row, swizzled
-        const int u0 = (2 * c) ^ (r & 7), u1 = (2 * c + 1) ^ (r & 7);
-        *reinterpret_cast<uint4*>(prow + u0 * 16) = make_uint4(w[0], w[1], w[2], w[3]);
-        *reinterpret_cast<uint4*>(prow + u1 * 16) = make_uint4(w[4], w[5], w[6], w[7]);
+        mx[h2] = mh;
       }
       tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(s_free));
+      if (mx[0] != INT_MIN) m = fmaxf(m, fmaf(float(mx[0]), sc0, -kFp8Offset));
+      if (mx[1] != INT_MIN) m = fmaxf(m, fmaf(float(mx[1]), sc1, -kFp8Offset));
+    }
+    // ---- pass B: P = 2^(s - m) -> E4M3 into the swizzled K-major P tile
+    float ds[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    for (int j = 0; j < nkv && ok; ++j) {
+      const int t = nkv + j;
+      if (!__all_sync(0xffffffffu, mbar_wait(smem_u32(s_full), t & 1, err))) { ok = false; break; }
+      tc_fence_after();
+      const float sc0 = p.sm_scale_log2 * (qs * p.k_scale[int64_t(bh) * kb_per_head + 2 * j]);
+      const float sc1 = p.sm_scale_log2 * (qs * p.k_scale[int64_t(bh) * kb_per_head + 2 * j + 1]);
+      const int valid = p.Skv - j * kTile;
+      const bool full = valid >= kTile;
+      uint32_t w[32];
+#pragma unroll
+      for (int h2 = 0; h2 < 2; ++h2) {
+        uint32_t sv[64];
+        tc_ld_32x32b_x32(tmem + t_lane + uint32_t(h2 * 64), *reinterpret_cast<uint32_t(*)[32]>(&sv[0]));
+        tc_ld_32x32b_x32(tmem + t_lane + uint32_t(h2 * 64 + 32), *reinterpret_cast<uint32_t(*)[32]>(&sv[32]));
+        tc_wait_ld();
+        const float sc = h2 == 0 ? sc0 : sc1;
+        if (full) {
+#pragma unroll
+          for (int t4 = 0; t4 < 64; t4 += 4) {
+            float pv[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              pv[e] = ex2_approx(fmaf(i2f_small(sv[t4 + e]), sc, -m));
+              ds[e] += pv[e];
+            }
+            w[h2 * 16 + t4 / 4] = cvt_e4m3x4(pv[0], pv[1], pv[2], pv[3]);
+          }
+        } else {
+#pragma unroll
+          for (int t4 = 0; t4 < 64; t4 += 4) {
+            float pv[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const int key = h2 * 64 + t4 + e;
+              pv[e] = key < valid ? ex2_approx(fmaf(i2f_small(sv[t4 + e]), sc, -m)) : 0.0f;
+              ds[e] += pv[e];
+            }
+            w[h2 * 16 + t4 / 4] = cvt_e4m3x4(pv[0], pv[1], pv[2], pv[3]);
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(s_free));
+      // the P tile is free once P.V of the previous tile finished (phase j-1)
+      if (!__all_sync(0xffffffffu, mbar_wait(smem_u32(p_free), (j & 1) ^ 1, err))) { ok = false; break; }
+#pragma unroll
+      for (int u = 0; u < 8; ++u)
+        *reinterpret_cast<uint4*>(prow + ((u ^ (r & 7)) * 16)) = make_uint4(w[4 * u], w[4 * u + 1], w[4 * u + 2],
+                                                                            w[4 * u + 3]);
       fence_proxy_async_shared();
       __syncwarp();
-      if (lane == 0) {
-        mbar_arrive(smem_u32(&s_free[sb]));
-        mbar_arrive(smem_u32(&p_full[sb]));
-      }
-      m_old = m_new;
+      if (lane == 0) mbar_arrive(smem_u32(p_full));
     }
-    // s_full(j) only guarantees P.V tiles <= j-2 finished, so o_done may still
-    // be two phases behind: wait for phase nkv-2, then nkv-1 (a parity wait is
-    // unambiguous only one phase ahead).
-    if (ok && nkv >= 2)
-      ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(o_done), (nkv - 2) & 1, err));
-    if (ok && __all_sync(0xffffffffu, mbar_wait(smem_u32(o_done), (nkv - 1) & 1, err))) {
+    const float dsum = (ds[0] + ds[1]) + (ds[2] + ds[3]);
+    // the loop above saw p_free phase nkv-2, so this parity wait for the last
+    // P.V tile (phase nkv-1) is unambiguous
+    if (ok && __all_sync(0xffffffffu, mbar_wait(smem_u32(p_free), (nkv - 1) & 1, err))) {
       tc_fence_after();
       const float rinv = 1.0f / dsum;
       const float* vs = p.v_scale + int64_t(bh) * kD;
@@ -449,7 +473,7 @@ sage_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
 #pragma unroll 1
       for (int c = 0; c < 4; ++c) {
         uint32_t ov[32];
-        tc_ld_32x32b_x32(tmem + t_lane + uint32_t(256 + c * 32), ov);
+        tc_ld_32x32b_x32(tmem + t_lane + kTmemO + uint32_t(c * 32), ov);
         tc_wait_ld();
         if (q_tok < p.Sq) {
 #pragma unroll
@@ -469,7 +493,7 @@ sage_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem, 512);
+    tmem_dealloc(tmem, kAttnTmemCols);
   }
 }
 
