@@ -232,6 +232,13 @@ constexpr int kAttnSmem = kSmemBar + 1024 + 1024;
 constexpr uint32_t kAttnTmemCols = 256;   // S [0,128), O [128,256)
 constexpr uint32_t kTmemO = 128;
 
+// Q.K^T step t of 2*nkv: steps [0, nkv) are the row-max pass and alternate
+// between S buffers 0 and 1 (TMEM columns [0,128) and [128,256); buffer 1 is
+// the O accumulator later, idle during that pass); steps [nkv, 2 nkv) use
+// buffer 0. s_use is the use count of that buffer (its barrier phase).
+__device__ __forceinline__ int s_buffer(int t, int nkv) { return t < nkv ? (t & 1) : 0; }
+__device__ __forceinline__ int s_use(int t, int nkv) { return t < nkv ? (t >> 1) : (nkv + 1) / 2 + (t - nkv); }
+
 __global__ void __launch_bounds__(192, 2)
 sage_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                  const __grid_constant__ CUtensorMap tm_v, AttnParams p, int* err) {
@@ -243,9 +250,9 @@ sage_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
   uint64_t* k_empty = k_full + kKvStages;
   uint64_t* v_full = k_empty + kKvStages;
   uint64_t* v_empty = v_full + kKvStages;
-  uint64_t* s_full = v_empty + kKvStages;  // one phase per Q.K^T tile
-  uint64_t* s_free = s_full + 1;            // one phase per softmax pass over S
-  uint64_t* p_full = s_free + 1;            // one phase per P tile written
+  uint64_t* s_full = v_empty + kKvStages;  // [2]: one phase per Q.K^T into S buffer b
+  uint64_t* s_free = s_full + 2;            // [2]: one phase per softmax read of S buffer b
+  uint64_t* p_full = s_free + 2;            // one phase per P tile written
   uint64_t* p_free = p_full + 1;            // one phase per P.V tile finished
   uint64_t* drain = p_free + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
@@ -264,8 +271,10 @@ sage_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
       mbar_init(smem_u32(&v_full[s]), 1);
       mbar_init(smem_u32(&v_empty[s]), 1);
     }
-    mbar_init(smem_u32(s_full), 1);
-    mbar_init(smem_u32(s_free), 4);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(smem_u32(&s_full[b]), 1);
+      mbar_init(smem_u32(&s_free[b]), 4);
+    }
     mbar_init(smem_u32(p_full), 4);
     mbar_init(smem_u32(p_free), 1);
     mbar_init(smem_u32(drain), 1);
@@ -324,16 +333,18 @@ sage_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
       for (int t = 0; t <= 2 * nkv && ok; ++t) {
         if (t < 2 * nkv) {
           const int st = t % kKvStages;
+          const int sb = s_buffer(t, nkv), su = s_use(t, nkv);
           if (!mbar_wait(smem_u32(&k_full[st]), (t / kKvStages) & 1, err)) { ok = false; break; }
-          // S is free once the softmax finished step t-1 (phase t-1)
-          if (!mbar_wait(smem_u32(s_free), (t & 1) ^ 1, err)) { ok = false; break; }
+          // S buffer sb is free once the softmax read its previous use (phase su-1)
+          if (!mbar_wait(smem_u32(&s_free[sb]), (su & 1) ^ 1, err)) { ok = false; break; }
           tc_fence_after();
           const uint64_t kdesc = smem_desc_k_sw128(smem_u32(smem + kSmemK + st * 16384));
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk)
-            tc_mma_i8(tmem, qdesc + uint64_t(2 * kk), kdesc + uint64_t(2 * kk), kIdescQK, kk > 0);
+            tc_mma_i8(tmem + uint32_t(sb * 128), qdesc + uint64_t(2 * kk), kdesc + uint64_t(2 * kk), kIdescQK,
+                      kk > 0);
           tc_commit(smem_u32(&k_empty[st]));
-          tc_commit(smem_u32(s_full));
+          tc_commit(smem_u32(&s_full[sb]));
         }
         if (t >= nkv + 1) {
           const int i = t - 1 - nkv, vs = i % kKvStages;
@@ -365,38 +376,54 @@ sage_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
     uint8_t* p_smem = smem + kSmemP;
     uint8_t* prow = p_smem + r * 128;
     // ---- pass A: the row max of s = S * (sm_scale*log2e) * (q_scale*k_scale)
+    // (the two K-block scales of a tile are fetched one tile ahead)
+    const float* ks_head = p.k_scale + int64_t(bh) * kb_per_head;
+    const float qsl = p.sm_scale_log2 * qs;
+    float2 ks_next = make_float2(__ldg(ks_head), __ldg(ks_head + 1));
     float m = -5000000.0f;
     for (int j = 0; j < nkv; ++j) {
-      if (!__all_sync(0xffffffffu, mbar_wait(smem_u32(s_full), j & 1, err))) { ok = false; break; }
+      const float sc0 = qsl * ks_next.x, sc1 = qsl * ks_next.y;
+      const int jn = j + 1 < nkv ? j + 1 : 0;
+      ks_next = make_float2(__ldg(ks_head + 2 * jn), __ldg(ks_head + 2 * jn + 1));
+      if (!__all_sync(0xffffffffu, mbar_wait(smem_u32(&s_full[j & 1]), (j >> 1) & 1, err))) { ok = false; break; }
       tc_fence_after();
-      const float sc0 = p.sm_scale_log2 * (qs * p.k_scale[int64_t(bh) * kb_per_head + 2 * j]);
-      const float sc1 = p.sm_scale_log2 * (qs * p.k_scale[int64_t(bh) * kb_per_head + 2 * j + 1]);
       const int valid = p.Skv - j * kTile;
-      int mx[2];
+      uint32_t sv[128];
 #pragma unroll
-      for (int h2 = 0; h2 < 2; ++h2) {
-        uint32_t sa[32], sb2[32];
-        tc_ld_32x32b_x32(tmem + t_lane + uint32_t(h2 * 64), sa);
-        tc_ld_32x32b_x32(tmem + t_lane + uint32_t(h2 * 64 + 32), sb2);
-        tc_wait_ld();
-        int mh = INT_MIN;
-        if (valid >= kTile) {
-#pragma unroll
-          for (int t = 0; t < 32; t += 2) mh = __vimax3_s32(mh, int(sa[t]), int(sa[t + 1]));
-#pragma unroll
-          for (int t = 0; t < 32; t += 2) mh = __vimax3_s32(mh, int(sb2[t]), int(sb2[t + 1]));
-        } else {
-#pragma unroll
-          for (int t = 0; t < 32; ++t) {
-            if (h2 * 64 + t < valid) mh = max(mh, int(sa[t]));
-            if (h2 * 64 + 32 + t < valid) mh = max(mh, int(sb2[t]));
-          }
-        }
-        mx[h2] = mh;
-      }
+      for (int c = 0; c < 4; ++c)
+        tc_ld_32x32b_x32(tmem + t_lane + uint32_t((j & 1) * 128 + c * 32), *reinterpret_cast<uint32_t(*)[32]>(&sv[c * 32]));
+      tc_wait_ld();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(smem_u32(s_free));
+      if (lane == 0) mbar_arrive(smem_u32(&s_free[j & 1]));
+      int mx[2];
+      if (valid >= kTile) {
+#pragma unroll
+        for (int h2 = 0; h2 < 2; ++h2) {
+          // four independent chains, then a 4-way merge
+          const uint32_t* x = sv + h2 * 64;
+          int c0 = int(x[0]), c1 = int(x[1]), c2 = int(x[2]), c3 = int(x[3]);
+#pragma unroll
+          for (int t = 4; t < 60; t += 8) {   // x[4..59]
+            c0 = __vimax3_s32(c0, int(x[t]), int(x[t + 1]));
+            c1 = __vimax3_s32(c1, int(x[t + 2]), int(x[t + 3]));
+            c2 = __vimax3_s32(c2, int(x[t + 4]), int(x[t + 5]));
+            c3 = __vimax3_s32(c3, int(x[t + 6]), int(x[t + 7]));
+          }
+          c0 = __vimax3_s32(c0, int(x[60]), int(x[61]));
+          c1 = __vimax3_s32(c1, int(x[62]), int(x[63]));
+          mx[h2] = max(__vimax3_s32(c0, c1, c2), c3);
+        }
+      } else {
+#pragma unroll
+        for (int h2 = 0; h2 < 2; ++h2) {
+          int mh = INT_MIN;
+#pragma unroll
+          for (int t = 0; t < 64; ++t)
+            if (h2 * 64 + t < valid) mh = max(mh, int(sv[h2 * 64 + t]));
+          mx[h2] = mh;
+        }
+      }
       if (mx[0] != INT_MIN) m = fmaxf(m, fmaf(float(mx[0]), sc0, -kFp8Offset));
       if (mx[1] != INT_MIN) m = fmaxf(m, fmaf(float(mx[1]), sc1, -kFp8Offset));
     }
@@ -404,27 +431,38 @@ sage_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
     float ds[4] = {0.0f, 0.0f, 0.0f, 0.0f};
     for (int j = 0; j < nkv && ok; ++j) {
       const int t = nkv + j;
-      if (!__all_sync(0xffffffffu, mbar_wait(smem_u32(s_full), t & 1, err))) { ok = false; break; }
+      const float sc0 = qsl * ks_next.x, sc1 = qsl * ks_next.y;
+      const int jn = j + 1 < nkv ? j + 1 : 0;
+      ks_next = make_float2(__ldg(ks_head + 2 * jn), __ldg(ks_head + 2 * jn + 1));
+      const int su = s_use(t, nkv);
+      if (!__all_sync(0xffffffffu, mbar_wait(smem_u32(&s_full[0]), su & 1, err))) { ok = false; break; }
       tc_fence_after();
-      const float sc0 = p.sm_scale_log2 * (qs * p.k_scale[int64_t(bh) * kb_per_head + 2 * j]);
-      const float sc1 = p.sm_scale_log2 * (qs * p.k_scale[int64_t(bh) * kb_per_head + 2 * j + 1]);
       const int valid = p.Skv - j * kTile;
       const bool full = valid >= kTile;
+      // the whole S tile goes to registers first so that the next Q.K^T
+      // overlaps all of this tile's exponentials
+      uint32_t sv[128];
+#pragma unroll
+      for (int c = 0; c < 4; ++c)
+        tc_ld_32x32b_x32(tmem + t_lane + uint32_t(c * 32), *reinterpret_cast<uint32_t(*)[32]>(&sv[c * 32]));
+      tc_wait_ld();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(&s_free[0]));
       uint32_t w[32];
 #pragma unroll
       for (int h2 = 0; h2 < 2; ++h2) {
-        uint32_t sv[64];
-        tc_ld_32x32b_x32(tmem + t_lane + uint32_t(h2 * 64), *reinterpret_cast<uint32_t(*)[32]>(&sv[0]));
-        tc_ld_32x32b_x32(tmem + t_lane + uint32_t(h2 * 64 + 32), *reinterpret_cast<uint32_t(*)[32]>(&sv[32]));
-        tc_wait_ld();
         const float sc = h2 == 0 ? sc0 : sc1;
+        // s*sc - m = X*sc - (2^23+2^22)*sc - m with X = float(2^23+2^22+s)
+        // exactly (|s| < 2^22): one FMA per score after an integer add
+        const float bias = fmaf(12582912.0f, sc, m);
         if (full) {
 #pragma unroll
           for (int t4 = 0; t4 < 64; t4 += 4) {
             float pv[4];
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
-              pv[e] = ex2_approx(fmaf(i2f_small(sv[t4 + e]), sc, -m));
+              pv[e] = ex2_approx(fmaf(__int_as_float(int(sv[h2 * 64 + t4 + e]) + 0x4B400000), sc, -bias));
               ds[e] += pv[e];
             }
             w[h2 * 16 + t4 / 4] = cvt_e4m3x4(pv[0], pv[1], pv[2], pv[3]);
@@ -436,16 +474,13 @@ sage_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
               const int key = h2 * 64 + t4 + e;
-              pv[e] = key < valid ? ex2_approx(fmaf(i2f_small(sv[t4 + e]), sc, -m)) : 0.0f;
+              pv[e] = key < valid ? ex2_approx(fmaf(i2f_small(sv[key]), sc, -m)) : 0.0f;
               ds[e] += pv[e];
             }
             w[h2 * 16 + t4 / 4] = cvt_e4m3x4(pv[0], pv[1], pv[2], pv[3]);
           }
         }
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(smem_u32(s_free));
       // the P tile is free once P.V of the previous tile finished (phase j-1)
       if (!__all_sync(0xffffffffu, mbar_wait(smem_u32(p_free), (j & 1) ^ 1, err))) { ok = false; break; }
 #pragma unroll
