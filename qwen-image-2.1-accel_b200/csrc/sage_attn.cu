@@ -177,14 +177,6 @@ __device__ __forceinline__ void tc_mma_i8(uint32_t d, uint64_t a, uint64_t b, ui
       : "memory");
 }
 
-__device__ __forceinline__ void tc_mma_f8(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}" ::"r"(d),
-      "l"(a), "l"(b), "r"(idesc), "r"(acc)
-      : "memory");
-}
-
 // MN-major, 128-byte swizzle descriptor (V as the B operand of P.V): 128 B of
 // N per row, 8-row (K) groups 1024 B apart.
 __device__ __forceinline__ uint64_t smem_desc_mn_sw128(uint32_t saddr) {
@@ -221,23 +213,44 @@ struct AttnParams {
   float sm_scale_log2;      // sm_scale * log2(e)
 };
 
-// Two CTAs share an SM (96 KB of shared memory and 256 TMEM columns each), so
+// Two CTAs share an SM (82 KB of shared memory and 256 TMEM columns each), so
 // one CTA's MMAs run while the other's softmax warps work.
+//
+// TMEM columns of a CTA:
+//   row-max pass: S buffers [0,128) and [128,256), alternating per K tile;
+//   P pass:       S halves of 64 keys at [0,64) and [64,128), alternating; P of
+//                 a half (E4M3, 4 per column) overwrites the first 16 columns
+//                 of its own S half and is the TMEM A operand of P.V; the O
+//                 accumulator is [128,256).
+// MMAs issued by one thread execute in issue order, so the Q.K^T that reuses
+// an S half is issued right after the P.V that reads the P stored there.
 constexpr int kSmemQ = 0;
 constexpr int kSmemK = kSmemQ + 16384;
 constexpr int kSmemV = kSmemK + kKvStages * 16384;
-constexpr int kSmemP = kSmemV + kKvStages * 16384;
-constexpr int kSmemBar = kSmemP + 16384;
+constexpr int kSmemBar = kSmemV + kKvStages * 16384;
 constexpr int kAttnSmem = kSmemBar + 1024 + 1024;
-constexpr uint32_t kAttnTmemCols = 256;   // S [0,128), O [128,256)
+constexpr uint32_t kAttnTmemCols = 256;
 constexpr uint32_t kTmemO = 128;
+constexpr int kHalf = 64;   // keys per S half in the P pass (= one K scale block)
+constexpr uint32_t kIdescQK64 = (kIdescQK & ~(0x3Fu << 17)) | (uint32_t(kHalf >> 3) << 17);
 
-// Q.K^T step t of 2*nkv: steps [0, nkv) are the row-max pass and alternate
-// between S buffers 0 and 1 (TMEM columns [0,128) and [128,256); buffer 1 is
-// the O accumulator later, idle during that pass); steps [nkv, 2 nkv) use
-// buffer 0. s_use is the use count of that buffer (its barrier phase).
-__device__ __forceinline__ int s_buffer(int t, int nkv) { return t < nkv ? (t & 1) : 0; }
-__device__ __forceinline__ int s_use(int t, int nkv) { return t < nkv ? (t >> 1) : (nkv + 1) / 2 + (t - nkv); }
+__device__ __forceinline__ void tc_mma_f8_tmem_a(uint32_t d, uint32_t a_tmem, uint64_t b, uint32_t idesc,
+                                                 uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d),
+      "r"(a_tmem), "l"(b), "r"(idesc), "r"(acc)
+      : "memory");
+}
+
+__device__ __forceinline__ void tc_st_32x32b_x16(uint32_t taddr, const uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+      "%15, %16};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+      "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+      : "memory");
+}
 
 __global__ void __launch_bounds__(192, 2)
 sage_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
@@ -250,16 +263,18 @@ sage_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
   uint64_t* k_empty = k_full + kKvStages;
   uint64_t* v_full = k_empty + kKvStages;
   uint64_t* v_empty = v_full + kKvStages;
-  uint64_t* s_full = v_empty + kKvStages;  // [2]: one phase per Q.K^T into S buffer b
-  uint64_t* s_free = s_full + 2;            // [2]: one phase per softmax read of S buffer b
-  uint64_t* p_full = s_free + 2;            // one phase per P tile written
-  uint64_t* p_free = p_full + 1;            // one phase per P.V tile finished
-  uint64_t* drain = p_free + 1;
+  uint64_t* sa_full = v_empty + kKvStages;  // [2] row-max pass: S buffer b written (one phase per use)
+  uint64_t* sa_free = sa_full + 2;          // [2] row-max pass: S buffer b read by the softmax warps
+  uint64_t* sb_full = sa_free + 2;          // [2] P pass: S half h written
+  uint64_t* pb_full = sb_full + 2;          // [2] P pass: P of half h stored (S half h consumed)
+  uint64_t* o_full = pb_full + 2;           // all P.V done
+  uint64_t* drain = o_full + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int q_tile = blockIdx.x, bh = blockIdx.y;
   const int nkv = p.Skv_pad / kTile;
+  const int nh = 2 * nkv;                   // 64-key halves in the P pass
   const int q_row0 = bh * p.Sq_pad + q_tile * kTile;
   const int kv_row0 = bh * p.Skv_pad;
 
@@ -272,11 +287,12 @@ sage_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
       mbar_init(smem_u32(&v_empty[s]), 1);
     }
     for (int b = 0; b < 2; ++b) {
-      mbar_init(smem_u32(&s_full[b]), 1);
-      mbar_init(smem_u32(&s_free[b]), 4);
+      mbar_init(smem_u32(&sa_full[b]), 1);
+      mbar_init(smem_u32(&sa_free[b]), 4);
+      mbar_init(smem_u32(&sb_full[b]), 1);
+      mbar_init(smem_u32(&pb_full[b]), 4);
     }
-    mbar_init(smem_u32(p_full), 4);
-    mbar_init(smem_u32(p_free), 1);
+    mbar_init(smem_u32(o_full), 1);
     mbar_init(smem_u32(drain), 1);
     fence_barrier_init();
     prefetch_tmap(&tm_q);
@@ -327,45 +343,70 @@ sage_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
       bool ok = mbar_wait(smem_u32(q_full), 0, err);
       tc_fence_after();
       const uint64_t qdesc = smem_desc_k_sw128(smem_u32(smem + kSmemQ));
-      // steps [0, nkv): Q.K^T for the row-max pass; [nkv, 2 nkv): Q.K^T again,
-      // and P.V of the previous step's tile (lagged by one step so that each
-      // Q.K^T overlaps the softmax of the tile before it)
-      for (int t = 0; t <= 2 * nkv && ok; ++t) {
-        if (t < 2 * nkv) {
-          const int st = t % kKvStages;
-          const int sb = s_buffer(t, nkv), su = s_use(t, nkv);
-          if (!mbar_wait(smem_u32(&k_full[st]), (t / kKvStages) & 1, err)) { ok = false; break; }
-          // S buffer sb is free once the softmax read its previous use (phase su-1)
-          if (!mbar_wait(smem_u32(&s_free[sb]), (su & 1) ^ 1, err)) { ok = false; break; }
-          tc_fence_after();
-          const uint64_t kdesc = smem_desc_k_sw128(smem_u32(smem + kSmemK + st * 16384));
+      // ---- row-max pass: Q.K^T of K tile j into S buffer j&1
+      for (int j = 0; j < nkv && ok; ++j) {
+        const int st = j % kKvStages, b = j & 1, u = j >> 1;
+        if (!mbar_wait(smem_u32(&k_full[st]), (j / kKvStages) & 1, err)) { ok = false; break; }
+        // buffer b is free once the softmax read its previous use (phase u-1)
+        if (!mbar_wait(smem_u32(&sa_free[b]), (u & 1) ^ 1, err)) { ok = false; break; }
+        tc_fence_after();
+        const uint64_t kdesc = smem_desc_k_sw128(smem_u32(smem + kSmemK + st * 16384));
 #pragma unroll
-          for (int kk = 0; kk < 4; ++kk)
-            tc_mma_i8(tmem + uint32_t(sb * 128), qdesc + uint64_t(2 * kk), kdesc + uint64_t(2 * kk), kIdescQK,
-                      kk > 0);
-          tc_commit(smem_u32(&k_empty[st]));
-          tc_commit(smem_u32(&s_full[sb]));
-        }
-        if (t >= nkv + 1) {
-          const int i = t - 1 - nkv, vs = i % kKvStages;
-          if (!mbar_wait(smem_u32(p_full), i & 1, err)) { ok = false; break; }
-          if (!mbar_wait(smem_u32(&v_full[vs]), (i / kKvStages) & 1, err)) { ok = false; break; }
-          tc_fence_after();
-          const uint64_t pdesc = smem_desc_k_sw128(smem_u32(smem + kSmemP));
-          const uint64_t vdesc = smem_desc_mn_sw128(smem_u32(smem + kSmemV + vs * 16384));
-#pragma unroll
-          for (int kk = 0; kk < 4; ++kk)
-            tc_mma_f8(tmem + kTmemO, pdesc + uint64_t(2 * kk), vdesc + uint64_t(256 * kk), kIdescPV, (i | kk) != 0);
-          tc_commit(smem_u32(&v_empty[vs]));
-          tc_commit(smem_u32(p_free));
-        }
+        for (int kk = 0; kk < 4; ++kk)
+          tc_mma_i8(tmem + uint32_t(b * 128), qdesc + uint64_t(2 * kk), kdesc + uint64_t(2 * kk), kIdescQK, kk > 0);
+        tc_commit(smem_u32(&k_empty[st]));
+        tc_commit(smem_u32(&sa_full[b]));
       }
+      // ---- P pass. The S halves overwrite S buffer 0 of the row-max pass:
+      // wait for the softmax's read of its last use there (use ua-1). Buffer 1
+      // (O) is free once P of half 0 arrives, which follows the whole pass.
+      const int ua = (nkv + 1) / 2;
+      if (ok && !mbar_wait(smem_u32(&sa_free[0]), (ua & 1) ^ 1, err)) ok = false;
+      tc_fence_after();
+      // Q.K^T of half i (keys [64 i, 64 i + 64)) into S half i&1
+      auto qk_half = [&](int i) -> bool {
+        const int h = i & 1, t = nkv + (i >> 1), st = t % kKvStages;
+        if (h == 0) {
+          if (!mbar_wait(smem_u32(&k_full[st]), (t / kKvStages) & 1, err)) return false;
+          tc_fence_after();
+        }
+        // rows [64 h, 64 h + 64) of the K tile start 8 KB in (8-row groups of 1 KB)
+        const uint64_t kdesc = smem_desc_k_sw128(smem_u32(smem + kSmemK + st * 16384 + h * 8192));
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk)
+          tc_mma_i8(tmem + uint32_t(h * kHalf), qdesc + uint64_t(2 * kk), kdesc + uint64_t(2 * kk), kIdescQK64,
+                    kk > 0);
+        tc_commit(smem_u32(&sb_full[h]));
+        if (h == 1) tc_commit(smem_u32(&k_empty[st]));
+        return true;
+      };
+      // O += P(half i) . V(keys of half i); A (P) from TMEM
+      auto pv_half = [&](int i) -> bool {
+        const int h = i & 1, jv = i >> 1, vs = jv % kKvStages;
+        if (!mbar_wait(smem_u32(&pb_full[h]), (i >> 1) & 1, err)) return false;
+        if (h == 0 && !mbar_wait(smem_u32(&v_full[vs]), (jv / kKvStages) & 1, err)) return false;
+        tc_fence_after();
+        const uint64_t vdesc = smem_desc_mn_sw128(smem_u32(smem + kSmemV + vs * 16384));
+#pragma unroll
+        for (int kk = 0; kk < 2; ++kk)
+          tc_mma_f8_tmem_a(tmem + kTmemO, tmem + uint32_t(h * kHalf + 8 * kk), vdesc + uint64_t(256 * (2 * h + kk)),
+                           kIdescPV, (i | kk) != 0);
+        if (h == 1) tc_commit(smem_u32(&v_empty[vs]));
+        return true;
+      };
+      if (ok) ok = qk_half(0);
+      if (ok) ok = qk_half(1);
+      for (int i = 0; i < nh && ok; ++i) {
+        ok = pv_half(i);
+        if (ok && i + 2 < nh) ok = qk_half(i + 2);
+      }
+      if (ok) tc_commit(smem_u32(o_full));
       tc_commit(smem_u32(drain));
       mbar_wait(smem_u32(drain), 0, ok ? err : nullptr, 100000000ull);
     }
   } else {
     // ---------------------------------------------------------- softmax
-    // One thread per query row (TMEM lane). O lives in TMEM columns [128, 256).
+    // One thread per query row (TMEM lane).
     const int sub = warp & 3;
     const int r = sub * 32 + lane;            // row within the query tile
     const int q_tok = q_tile * kTile + r;     // token index
@@ -373,9 +414,7 @@ sage_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
     const float qs = p.q_scale[int64_t(bh) * (p.Sq_pad / 32) + q_tok / 32];
     const int kb_per_head = p.Skv_pad / 64;
     bool ok = true;
-    uint8_t* p_smem = smem + kSmemP;
-    uint8_t* prow = p_smem + r * 128;
-    // ---- pass A: the row max of s = S * (sm_scale*log2e) * (q_scale*k_scale)
+    // ---- row-max pass: the row max of s = S * (sm_scale*log2e) * (q_scale*k_scale)
     // (the two K-block scales of a tile are fetched one tile ahead)
     const float* ks_head = p.k_scale + int64_t(bh) * kb_per_head;
     const float qsl = p.sm_scale_log2 * qs;
@@ -385,17 +424,18 @@ sage_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
       const float sc0 = qsl * ks_next.x, sc1 = qsl * ks_next.y;
       const int jn = j + 1 < nkv ? j + 1 : 0;
       ks_next = make_float2(__ldg(ks_head + 2 * jn), __ldg(ks_head + 2 * jn + 1));
-      if (!__all_sync(0xffffffffu, mbar_wait(smem_u32(&s_full[j & 1]), (j >> 1) & 1, err))) { ok = false; break; }
+      if (!__all_sync(0xffffffffu, mbar_wait(smem_u32(&sa_full[j & 1]), (j >> 1) & 1, err))) { ok = false; break; }
       tc_fence_after();
       const int valid = p.Skv - j * kTile;
       uint32_t sv[128];
 #pragma unroll
       for (int c = 0; c < 4; ++c)
-        tc_ld_32x32b_x32(tmem + t_lane + uint32_t((j & 1) * 128 + c * 32), *reinterpret_cast<uint32_t(*)[32]>(&sv[c * 32]));
+        tc_ld_32x32b_x32(tmem + t_lane + uint32_t((j & 1) * 128 + c * 32),
+                         *reinterpret_cast<uint32_t(*)[32]>(&sv[c * 32]));
       tc_wait_ld();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(smem_u32(&s_free[j & 1]));
+      if (lane == 0) mbar_arrive(smem_u32(&sa_free[j & 1]));
       int mx[2];
       if (valid >= kTile) {
 #pragma unroll
@@ -427,74 +467,55 @@ sage_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
       if (mx[0] != INT_MIN) m = fmaxf(m, fmaf(float(mx[0]), sc0, -kFp8Offset));
       if (mx[1] != INT_MIN) m = fmaxf(m, fmaf(float(mx[1]), sc1, -kFp8Offset));
     }
-    // ---- pass B: P = 2^(s - m) -> E4M3 into the swizzled K-major P tile
+    // ---- P pass: P = 2^(s - m) per 64-key half -> E4M3 into TMEM
     float ds[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-    for (int j = 0; j < nkv && ok; ++j) {
-      const int t = nkv + j;
-      const float sc0 = qsl * ks_next.x, sc1 = qsl * ks_next.y;
-      const int jn = j + 1 < nkv ? j + 1 : 0;
-      ks_next = make_float2(__ldg(ks_head + 2 * jn), __ldg(ks_head + 2 * jn + 1));
-      const int su = s_use(t, nkv);
-      if (!__all_sync(0xffffffffu, mbar_wait(smem_u32(&s_full[0]), su & 1, err))) { ok = false; break; }
+    float ks_cur = __ldg(ks_head);
+    for (int i = 0; i < nh && ok; ++i) {
+      const int h = i & 1;
+      const float sc = qsl * ks_cur;          // one K scale block per half
+      ks_cur = __ldg(ks_head + (i + 1 < nh ? i + 1 : 0));
+      if (!__all_sync(0xffffffffu, mbar_wait(smem_u32(&sb_full[h]), (i >> 1) & 1, err))) { ok = false; break; }
       tc_fence_after();
-      const int valid = p.Skv - j * kTile;
-      const bool full = valid >= kTile;
-      // the whole S tile goes to registers first so that the next Q.K^T
-      // overlaps all of this tile's exponentials
-      uint32_t sv[128];
-#pragma unroll
-      for (int c = 0; c < 4; ++c)
-        tc_ld_32x32b_x32(tmem + t_lane + uint32_t(c * 32), *reinterpret_cast<uint32_t(*)[32]>(&sv[c * 32]));
+      const int valid = p.Skv - i * kHalf;
+      uint32_t sv[64];
+      tc_ld_32x32b_x32(tmem + t_lane + uint32_t(h * kHalf), *reinterpret_cast<uint32_t(*)[32]>(&sv[0]));
+      tc_ld_32x32b_x32(tmem + t_lane + uint32_t(h * kHalf + 32), *reinterpret_cast<uint32_t(*)[32]>(&sv[32]));
       tc_wait_ld();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(smem_u32(&s_free[0]));
-      uint32_t w[32];
-#pragma unroll
-      for (int h2 = 0; h2 < 2; ++h2) {
-        const float sc = h2 == 0 ? sc0 : sc1;
+      uint32_t w[16];
+      if (valid >= kHalf) {
         // s*sc - m = X*sc - (2^23+2^22)*sc - m with X = float(2^23+2^22+s)
         // exactly (|s| < 2^22): one FMA per score after an integer add
         const float bias = fmaf(12582912.0f, sc, m);
-        if (full) {
 #pragma unroll
-          for (int t4 = 0; t4 < 64; t4 += 4) {
-            float pv[4];
+        for (int t4 = 0; t4 < 64; t4 += 4) {
+          float pv[4];
 #pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              pv[e] = ex2_approx(fmaf(__int_as_float(int(sv[h2 * 64 + t4 + e]) + 0x4B400000), sc, -bias));
-              ds[e] += pv[e];
-            }
-            w[h2 * 16 + t4 / 4] = cvt_e4m3x4(pv[0], pv[1], pv[2], pv[3]);
+          for (int e = 0; e < 4; ++e) {
+            pv[e] = ex2_approx(fmaf(__int_as_float(int(sv[t4 + e]) + 0x4B400000), sc, -bias));
+            ds[e] += pv[e];
           }
-        } else {
+          w[t4 / 4] = cvt_e4m3x4(pv[0], pv[1], pv[2], pv[3]);
+        }
+      } else {
 #pragma unroll
-          for (int t4 = 0; t4 < 64; t4 += 4) {
-            float pv[4];
+        for (int t4 = 0; t4 < 64; t4 += 4) {
+          float pv[4];
 #pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              const int key = h2 * 64 + t4 + e;
-              pv[e] = key < valid ? ex2_approx(fmaf(i2f_small(sv[key]), sc, -m)) : 0.0f;
-              ds[e] += pv[e];
-            }
-            w[h2 * 16 + t4 / 4] = cvt_e4m3x4(pv[0], pv[1], pv[2], pv[3]);
+          for (int e = 0; e < 4; ++e) {
+            pv[e] = t4 + e < valid ? ex2_approx(fmaf(i2f_small(sv[t4 + e]), sc, -m)) : 0.0f;
+            ds[e] += pv[e];
           }
+          w[t4 / 4] = cvt_e4m3x4(pv[0], pv[1], pv[2], pv[3]);
         }
       }
-      // the P tile is free once P.V of the previous tile finished (phase j-1)
-      if (!__all_sync(0xffffffffu, mbar_wait(smem_u32(p_free), (j & 1) ^ 1, err))) { ok = false; break; }
-#pragma unroll
-      for (int u = 0; u < 8; ++u)
-        *reinterpret_cast<uint4*>(prow + ((u ^ (r & 7)) * 16)) = make_uint4(w[4 * u], w[4 * u + 1], w[4 * u + 2],
-                                                                            w[4 * u + 3]);
-      fence_proxy_async_shared();
+      tc_st_32x32b_x16(tmem + t_lane + uint32_t(h * kHalf), w);
+      tc_wait_st();
+      tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(smem_u32(p_full));
+      if (lane == 0) mbar_arrive(smem_u32(&pb_full[h]));
     }
     const float dsum = (ds[0] + ds[1]) + (ds[2] + ds[3]);
-    // the loop above saw p_free phase nkv-2, so this parity wait for the last
-    // P.V tile (phase nkv-1) is unambiguous
-    if (ok && __all_sync(0xffffffffu, mbar_wait(smem_u32(p_free), (nkv - 1) & 1, err))) {
+    if (ok && __all_sync(0xffffffffu, mbar_wait(smem_u32(o_full), 0, err))) {
       tc_fence_after();
       const float rinv = 1.0f / dsum;
       const float* vs = p.v_scale + int64_t(bh) * kD;
