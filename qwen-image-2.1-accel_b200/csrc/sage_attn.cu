@@ -40,7 +40,8 @@ namespace {
 
 constexpr int kD = 128;
 constexpr int kTile = 128;
-constexpr int kKvStages = 2;
+constexpr int kKStages = 3;   // K tiles in flight (the row-max pass streams K only)
+constexpr int kVStages = 2;
 constexpr float kFp8Offset = 8.807f;  // log2(448): P = 2^(s - m) <= 448
 
 // ------------------------------------------------------------------ quantizers
@@ -213,7 +214,7 @@ struct AttnParams {
   float sm_scale_log2;      // sm_scale * log2(e)
 };
 
-// Two CTAs share an SM (82 KB of shared memory and 256 TMEM columns each), so
+// Two CTAs share an SM (98 KB of shared memory and 256 TMEM columns each), so
 // one CTA's MMAs run while the other's softmax warps work.
 //
 // TMEM columns of a CTA:
@@ -226,8 +227,8 @@ struct AttnParams {
 // an S half is issued right after the P.V that reads the P stored there.
 constexpr int kSmemQ = 0;
 constexpr int kSmemK = kSmemQ + 16384;
-constexpr int kSmemV = kSmemK + kKvStages * 16384;
-constexpr int kSmemBar = kSmemV + kKvStages * 16384;
+constexpr int kSmemV = kSmemK + kKStages * 16384;
+constexpr int kSmemBar = kSmemV + kVStages * 16384;
 constexpr int kAttnSmem = kSmemBar + 1024 + 1024;
 constexpr uint32_t kAttnTmemCols = 256;
 constexpr uint32_t kTmemO = 128;
@@ -260,10 +261,10 @@ sage_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kSmemBar);
   uint64_t* q_full = bars;
   uint64_t* k_full = bars + 1;
-  uint64_t* k_empty = k_full + kKvStages;
-  uint64_t* v_full = k_empty + kKvStages;
-  uint64_t* v_empty = v_full + kKvStages;
-  uint64_t* sa_full = v_empty + kKvStages;  // [2] row-max pass: S buffer b written (one phase per use)
+  uint64_t* k_empty = k_full + kKStages;
+  uint64_t* v_full = k_empty + kKStages;
+  uint64_t* v_empty = v_full + kVStages;
+  uint64_t* sa_full = v_empty + kVStages;  // [2] row-max pass: S buffer b written (one phase per use)
   uint64_t* sa_free = sa_full + 2;          // [2] row-max pass: S buffer b read by the softmax warps
   uint64_t* sb_full = sa_free + 2;          // [2] P pass: S half h written
   uint64_t* pb_full = sb_full + 2;          // [2] P pass: P of half h stored (S half h consumed)
@@ -280,9 +281,11 @@ sage_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
 
   if (threadIdx.x == 0) {
     mbar_init(smem_u32(q_full), 1);
-    for (int s = 0; s < kKvStages; ++s) {
+    for (int s = 0; s < kKStages; ++s) {
       mbar_init(smem_u32(&k_full[s]), 1);
       mbar_init(smem_u32(&k_empty[s]), 1);
+    }
+    for (int s = 0; s < kVStages; ++s) {
       mbar_init(smem_u32(&v_full[s]), 1);
       mbar_init(smem_u32(&v_empty[s]), 1);
     }
@@ -314,14 +317,14 @@ sage_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
       // steps [0, nkv): K tiles for the row-max pass; [nkv, 2 nkv): K and V tiles
       for (int t = 0; t < 2 * nkv && ok; ++t) {
         const int j = t < nkv ? t : t - nkv;
-        const int st = t % kKvStages;
-        const uint32_t ph = (t / kKvStages) & 1;
+        const int st = t % kKStages;
+        const uint32_t ph = (t / kKStages) & 1;
         if (!mbar_wait(smem_u32(&k_empty[st]), ph ^ 1, err)) { ok = false; break; }
         mbar_arrive_expect_tx(smem_u32(&k_full[st]), 16384);
         tma_load_2d(smem_u32(smem + kSmemK + st * 16384), &tm_k, smem_u32(&k_full[st]), 0, kv_row0 + j * kTile);
         if (t >= nkv) {
-          const int vs = j % kKvStages;
-          const uint32_t vph = (j / kKvStages) & 1;
+          const int vs = j % kVStages;
+          const uint32_t vph = (j / kVStages) & 1;
           if (!mbar_wait(smem_u32(&v_empty[vs]), vph ^ 1, err)) { ok = false; break; }
           mbar_arrive_expect_tx(smem_u32(&v_full[vs]), 16384);
           tma_load_2d(smem_u32(smem + kSmemV + vs * 16384), &tm_v, smem_u32(&v_full[vs]), 0, kv_row0 + j * kTile);
@@ -332,10 +335,10 @@ sage_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
       if (!ok) {
         // let queued copies land before the shared memory is released
         mbar_wait(smem_u32(q_full), 0, nullptr, 100000000ull);
-        for (int t = (issued > kKvStages ? issued - kKvStages : 0); t < issued; ++t)
-          mbar_wait(smem_u32(&k_full[t % kKvStages]), (t / kKvStages) & 1, nullptr, 100000000ull);
-        for (int j = (issued_v > kKvStages ? issued_v - kKvStages : 0); j < issued_v; ++j)
-          mbar_wait(smem_u32(&v_full[j % kKvStages]), (j / kKvStages) & 1, nullptr, 100000000ull);
+        for (int t = (issued > kKStages ? issued - kKStages : 0); t < issued; ++t)
+          mbar_wait(smem_u32(&k_full[t % kKStages]), (t / kKStages) & 1, nullptr, 100000000ull);
+        for (int j = (issued_v > kVStages ? issued_v - kVStages : 0); j < issued_v; ++j)
+          mbar_wait(smem_u32(&v_full[j % kVStages]), (j / kVStages) & 1, nullptr, 100000000ull);
       }
     }
   } else if (warp == 1) {
@@ -345,8 +348,8 @@ sage_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
       const uint64_t qdesc = smem_desc_k_sw128(smem_u32(smem + kSmemQ));
       // ---- row-max pass: Q.K^T of K tile j into S buffer j&1
       for (int j = 0; j < nkv && ok; ++j) {
-        const int st = j % kKvStages, b = j & 1, u = j >> 1;
-        if (!mbar_wait(smem_u32(&k_full[st]), (j / kKvStages) & 1, err)) { ok = false; break; }
+        const int st = j % kKStages, b = j & 1, u = j >> 1;
+        if (!mbar_wait(smem_u32(&k_full[st]), (j / kKStages) & 1, err)) { ok = false; break; }
         // buffer b is free once the softmax read its previous use (phase u-1)
         if (!mbar_wait(smem_u32(&sa_free[b]), (u & 1) ^ 1, err)) { ok = false; break; }
         tc_fence_after();
@@ -365,9 +368,9 @@ sage_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
       tc_fence_after();
       // Q.K^T of half i (keys [64 i, 64 i + 64)) into S half i&1
       auto qk_half = [&](int i) -> bool {
-        const int h = i & 1, t = nkv + (i >> 1), st = t % kKvStages;
+        const int h = i & 1, t = nkv + (i >> 1), st = t % kKStages;
         if (h == 0) {
-          if (!mbar_wait(smem_u32(&k_full[st]), (t / kKvStages) & 1, err)) return false;
+          if (!mbar_wait(smem_u32(&k_full[st]), (t / kKStages) & 1, err)) return false;
           tc_fence_after();
         }
         // rows [64 h, 64 h + 64) of the K tile start 8 KB in (8-row groups of 1 KB)
@@ -382,9 +385,9 @@ sage_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
       };
       // O += P(half i) . V(keys of half i); A (P) from TMEM
       auto pv_half = [&](int i) -> bool {
-        const int h = i & 1, jv = i >> 1, vs = jv % kKvStages;
+        const int h = i & 1, jv = i >> 1, vs = jv % kVStages;
         if (!mbar_wait(smem_u32(&pb_full[h]), (i >> 1) & 1, err)) return false;
-        if (h == 0 && !mbar_wait(smem_u32(&v_full[vs]), (jv / kKvStages) & 1, err)) return false;
+        if (h == 0 && !mbar_wait(smem_u32(&v_full[vs]), (jv / kVStages) & 1, err)) return false;
         tc_fence_after();
         const uint64_t vdesc = smem_desc_mn_sw128(smem_u32(smem + kSmemV + vs * 16384));
 #pragma unroll
