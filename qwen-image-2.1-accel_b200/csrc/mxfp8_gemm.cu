@@ -8,7 +8,7 @@
 // the dual-stream block needs (bias, GELU-tanh + MXFP8 requantization, gate +
 // residual).
 //
-// Structure (one CTA per SM, persistent over output tiles, 6 warps):
+// Structure (one CTA per SM, persistent over output tiles, 10 warps):
 //   warp 0      TMA producer: A tile 128x128 B, B tile BNx128 B (128-byte
 //               swizzle) plus the 512-byte scale chunks (bulk copies) into a
 //               STAGES-deep ring guarded by full/empty mbarriers.
@@ -20,12 +20,20 @@
 //   warps 2-9   epilogue: two warps per TMEM sub-partition (warp % 4), each
 //               owning half of the tile's columns; tcgen05.ld 32 columns at a
 //               time (one TMEM lane per output row), apply the epilogue in
-//               registers, store to HBM. Eight warps keep the accurate-tanh
-//               GELU epilogue shorter than the next tile's main loop.
+//               registers, store to HBM. The GELU epilogues use the
+//               two-MUFU sigmoid form of GELU-tanh (gelu_tanh_fast) and run on
+//               BN=192 tiles, whose double-buffered accumulators let the
+//               epilogue of one tile overlap the main loop of the next.
+// A second kernel (mxfp8_gemm_pair_kernel, below) runs the same roles on a
+// cluster of two CTAs sharing each MMA (cta_group::2); QIA_GEMM_PAIR=1 selects it.
+//
 // TMEM columns: NACC accumulators of BN columns (double-buffered when they
-// fit, so the epilogue of tile i overlaps the MMAs of tile i+1), then the A
-// scale slot (4 columns) and the B scale slot (4 per 128 rows of the tile).
-// No TMA multicast and no clusters are used.
+// fit, so the epilogue of tile i overlaps the MMAs of tile i+1; with the one
+// accumulator of BN=256 the epilogue warps take all their columns into
+// registers and release it before the epilogue math), then
+// SF_SLOTS scale slots used round-robin per K block, each the A scales (4
+// columns) and the B scales (4 per 128 rows of the tile).
+// No TMA multicast is used anywhere.
 #include <cudaTypedefs.h>
 
 #include <mutex>
@@ -61,12 +69,15 @@ struct Cfg {
   static constexpr int STAGE_BYTES = (A_BYTES + B_BYTES + SF_BYTES + 1023) / 1024 * 1024;
   static constexpr int STAGES = BN == 128 ? 6 : (BN == 192 ? 5 : 4);
   static constexpr int NACC = BN <= 192 ? 2 : 1;
-  static constexpr int SFA_COL = NACC * BN;
-  static constexpr int SFB_COL = SFA_COL + 4;
+  // scale-factor slots in TMEM, used round-robin per K block so that the copy
+  // for block kb+1 never overwrites scales the MMAs of block kb still read
+  static constexpr int SF_SLOTS = 4;
+  static constexpr int SF_COLS = 4 + 4 * SFB_CHUNKS;
+  static constexpr int SFA_COL = NACC * BN;   // slot s: A at SFA_COL + s*SF_COLS, B 4 columns later
   static constexpr int TMEM_COLS = 512;
   static constexpr int BAR_BYTES = 1024;
   static constexpr int SMEM = STAGES * STAGE_BYTES + BAR_BYTES + 1024;
-  static_assert(SFB_COL + 4 * SFB_CHUNKS <= TMEM_COLS, "TMEM budget");
+  static_assert(SFA_COL + SF_SLOTS * SF_COLS <= TMEM_COLS, "TMEM budget");
   static_assert(SMEM <= 232448, "shared memory budget");
 };
 
@@ -75,6 +86,72 @@ struct Cfg {
 template <int BN>
 __host__ __device__ constexpr uint32_t mxf8_idesc() {
   return (uint32_t(BN >> 3) << 17) | (1u << 23) | (uint32_t(128 >> 4) << 24);
+}
+
+// Epilogue of one 32-column chunk of an accumulator row (v: fp32 sums).
+template <int EPI>
+__device__ __forceinline__ void epilogue_chunk(float (&v)[32], const EpiParams& ep, int64_t row, int col, bool live,
+                                               int N) {
+  if (ep.bias) {
+    const uint4* bp = reinterpret_cast<const uint4*>(ep.bias + col);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      float bf[8];
+      unpack8(__ldg(bp + q), bf);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) v[q * 8 + i] += bf[i];
+    }
+  }
+  if (EPI == kEpiBf16 || EPI == kEpiGeluBf16) {
+    if (live) {
+      if (EPI == kEpiGeluBf16) {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] = gelu_tanh_fast(round_bf16(v[i]));
+      }
+      uint4* op = reinterpret_cast<uint4*>(ep.out + row * ep.ldo + col);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) op[q] = pack8(&v[q * 8]);
+    }
+  } else if (EPI == kEpiGateResidual) {
+    if (live) {
+      const int64_t b = row / ep.rows_per_batch;
+      const uint4* gp = reinterpret_cast<const uint4*>(ep.gate + b * N + col);
+      const uint4* hp = reinterpret_cast<const uint4*>(ep.resid + row * ep.ldo + col);
+      uint4* op = reinterpret_cast<uint4*>(ep.out + row * ep.ldo + col);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        float g[8], h[8], o[8];
+        unpack8(__ldg(gp + q), g);
+        unpack8(hp[q], h);
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+          o[i] = __fadd_rn(h[i], round_bf16(__fmul_rn(g[i], round_bf16(v[q * 8 + i]))));
+        op[q] = pack8(o);
+      }
+    }
+  } else {  // kEpiGeluQuant: the 32 columns are exactly one MX block of the next GEMM's K
+    float amax = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      v[i] = live ? round_bf16(gelu_tanh_fast(round_bf16(v[i]))) : 0.0f;
+      amax = fmaxf(amax, fabsf(v[i]));
+    }
+    const int e = mx_exponent(amax);
+    const float inv = mx_inverse_scale(e);
+    uint4 c0, c1;
+    c0.x = cvt_e4m3x4(v[0] * inv, v[1] * inv, v[2] * inv, v[3] * inv);
+    c0.y = cvt_e4m3x4(v[4] * inv, v[5] * inv, v[6] * inv, v[7] * inv);
+    c0.z = cvt_e4m3x4(v[8] * inv, v[9] * inv, v[10] * inv, v[11] * inv);
+    c0.w = cvt_e4m3x4(v[12] * inv, v[13] * inv, v[14] * inv, v[15] * inv);
+    c1.x = cvt_e4m3x4(v[16] * inv, v[17] * inv, v[18] * inv, v[19] * inv);
+    c1.y = cvt_e4m3x4(v[20] * inv, v[21] * inv, v[22] * inv, v[23] * inv);
+    c1.z = cvt_e4m3x4(v[24] * inv, v[25] * inv, v[26] * inv, v[27] * inv);
+    c1.w = cvt_e4m3x4(v[28] * inv, v[29] * inv, v[30] * inv, v[31] * inv);
+    uint4* qp = reinterpret_cast<uint4*>(ep.q_values + row * int64_t(N) + col);
+    qp[0] = c0;
+    qp[1] = c1;
+    ep.q_scales[mx_scale_offset(row, col >> 5, N >> 7)] = uint8_t(e);
+  }
 }
 
 template <int BN, int EPI>
@@ -157,7 +234,7 @@ mxfp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_const
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
-      int s = 0;
+      int s = 0, sf_slot = 0;
       uint32_t phase = 0;
       bool ok = true;
       int it = 0;
@@ -168,17 +245,19 @@ mxfp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_const
         tc_fence_after();
         const int n0 = (tile % n_tiles) * BN;
         const uint32_t d_tmem = tmem_base + uint32_t(a * BN);
-        const uint32_t sfa_tmem = tmem_base + C::SFA_COL;
-        const uint32_t sfb_tmem = tmem_base + C::SFB_COL + uint32_t((n0 & 127) >> 5);
         for (int kb = 0; kb < k_blocks; ++kb) {
           if (!mbar_wait(smem_u32(&full[s]), phase, err)) { ok = false; break; }
           tc_fence_after();
           const uint32_t st = smem_u32(smem + s * C::STAGE_BYTES);
-          tc_cp_32x128b_warpx4(tmem_base + C::SFA_COL, smem_desc_sf(st + C::A_BYTES + C::B_BYTES));
+          const uint32_t sfa_tmem = tmem_base + uint32_t(C::SFA_COL + sf_slot * C::SF_COLS);
+          const uint32_t sfb_base = sfa_tmem + 4;
+          // BN=192 tiles at odd multiples of 64 start 2 columns into the chunk
+          const uint32_t sfb_tmem = sfb_base + uint32_t((n0 & 127) >> 5);
+          if (++sf_slot == C::SF_SLOTS) sf_slot = 0;
+          tc_cp_32x128b_warpx4(sfa_tmem, smem_desc_sf(st + C::A_BYTES + C::B_BYTES));
 #pragma unroll
           for (int c = 0; c < C::SFB_CHUNKS; ++c)
-            tc_cp_32x128b_warpx4(tmem_base + C::SFB_COL + 4 * c,
-                                 smem_desc_sf(st + C::A_BYTES + C::B_BYTES + 512 + 512 * c));
+            tc_cp_32x128b_warpx4(sfb_base + 4 * c, smem_desc_sf(st + C::A_BYTES + C::B_BYTES + 512 + 512 * c));
           const uint64_t adesc = smem_desc_k_sw128(st);
           const uint64_t bdesc = smem_desc_k_sw128(st + C::A_BYTES);
 #pragma unroll
@@ -214,81 +293,41 @@ mxfp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_const
       const int64_t row = m0 + row_in_tile;
       const bool live = row < M;
       const uint32_t t_row = tmem_base + (uint32_t(sub * 32) << 16) + uint32_t(a * BN);
-#pragma unroll 1
-      for (int jj = 0; jj < kChunks; ++jj) {
-        const int j = half * kChunks + jj;
-        uint32_t r[32];
-        tc_ld_32x32b_x32(t_row + uint32_t(j * 32), r);
+      if constexpr (C::NACC == 1) {
+        // one accumulator: the next tile's MMAs wait for it, so take all of
+        // this warp's columns into registers and hand it back before the math
+        uint32_t r[kChunks][32];
+#pragma unroll
+        for (int jj = 0; jj < kChunks; ++jj) tc_ld_32x32b_x32(t_row + uint32_t((half * kChunks + jj) * 32), r[jj]);
         tc_wait_ld();
-        if (jj == kChunks - 1) {
-          // all columns of this accumulator are in registers: hand it back
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(smem_u32(&acc_empty[a]));
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(smem_u32(&acc_empty[a]));
+#pragma unroll
+        for (int jj = 0; jj < kChunks; ++jj) {
+          float v[32];
+#pragma unroll
+          for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[jj][i]);
+          epilogue_chunk<EPI>(v, ep, row, n0 + (half * kChunks + jj) * 32, live, N);
         }
-        const int col = n0 + j * 32;
-        float v[32];
-#pragma unroll
-        for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
-        if (ep.bias) {
-          const uint4* bp = reinterpret_cast<const uint4*>(ep.bias + col);
-#pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            float bf[8];
-            unpack8(__ldg(bp + q), bf);
-#pragma unroll
-            for (int i = 0; i < 8; ++i) v[q * 8 + i] += bf[i];
+      } else {
+#pragma unroll 1
+        for (int jj = 0; jj < kChunks; ++jj) {
+          const int j = half * kChunks + jj;
+          uint32_t r[32];
+          tc_ld_32x32b_x32(t_row + uint32_t(j * 32), r);
+          tc_wait_ld();
+          if (jj == kChunks - 1) {
+            // all columns of this accumulator are in registers: hand it back
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(smem_u32(&acc_empty[a]));
           }
-        }
-        if (EPI == kEpiBf16 || EPI == kEpiGeluBf16) {
-          if (live) {
-            if (EPI == kEpiGeluBf16) {
+          const int col = n0 + j * 32;
+          float v[32];
 #pragma unroll
-              for (int i = 0; i < 32; ++i) v[i] = gelu_tanh_f32(round_bf16(v[i]));
-            }
-            uint4* op = reinterpret_cast<uint4*>(ep.out + row * ep.ldo + col);
-#pragma unroll
-            for (int q = 0; q < 4; ++q) op[q] = pack8(&v[q * 8]);
-          }
-        } else if (EPI == kEpiGateResidual) {
-          if (live) {
-            const int64_t b = row / ep.rows_per_batch;
-            const uint4* gp = reinterpret_cast<const uint4*>(ep.gate + b * N + col);
-            const uint4* hp = reinterpret_cast<const uint4*>(ep.resid + row * ep.ldo + col);
-            uint4* op = reinterpret_cast<uint4*>(ep.out + row * ep.ldo + col);
-#pragma unroll
-            for (int q = 0; q < 4; ++q) {
-              float g[8], h[8], o[8];
-              unpack8(__ldg(gp + q), g);
-              unpack8(hp[q], h);
-#pragma unroll
-              for (int i = 0; i < 8; ++i)
-                o[i] = __fadd_rn(h[i], round_bf16(__fmul_rn(g[i], round_bf16(v[q * 8 + i]))));
-              op[q] = pack8(o);
-            }
-          }
-        } else {  // kEpiGeluQuant: the 32 columns are exactly one MX block of the next GEMM's K
-          float amax = 0.0f;
-#pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            v[i] = live ? round_bf16(gelu_tanh_f32(round_bf16(v[i]))) : 0.0f;
-            amax = fmaxf(amax, fabsf(v[i]));
-          }
-          const int e = mx_exponent(amax);
-          const float inv = mx_inverse_scale(e);
-          uint4 c0, c1;
-          c0.x = cvt_e4m3x4(v[0] * inv, v[1] * inv, v[2] * inv, v[3] * inv);
-          c0.y = cvt_e4m3x4(v[4] * inv, v[5] * inv, v[6] * inv, v[7] * inv);
-          c0.z = cvt_e4m3x4(v[8] * inv, v[9] * inv, v[10] * inv, v[11] * inv);
-          c0.w = cvt_e4m3x4(v[12] * inv, v[13] * inv, v[14] * inv, v[15] * inv);
-          c1.x = cvt_e4m3x4(v[16] * inv, v[17] * inv, v[18] * inv, v[19] * inv);
-          c1.y = cvt_e4m3x4(v[20] * inv, v[21] * inv, v[22] * inv, v[23] * inv);
-          c1.z = cvt_e4m3x4(v[24] * inv, v[25] * inv, v[26] * inv, v[27] * inv);
-          c1.w = cvt_e4m3x4(v[28] * inv, v[29] * inv, v[30] * inv, v[31] * inv);
-          uint4* qp = reinterpret_cast<uint4*>(ep.q_values + row * int64_t(N) + col);
-          qp[0] = c0;
-          qp[1] = c1;
-          ep.q_scales[mx_scale_offset(row, col >> 5, N >> 7)] = uint8_t(e);
+          for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+          epilogue_chunk<EPI>(v, ep, row, col, live, N);
         }
       }
     }
@@ -299,6 +338,255 @@ mxfp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_const
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_base, C::TMEM_COLS);
+  }
+}
+
+// ------------------------------------------------------------------ CTA-pair kernel
+// The same GEMM with one tcgen05 MMA shared by a cluster of two CTAs on two
+// SMs (cta_group::2): an output tile is 256 x BN; each CTA loads its own 128
+// rows of A and half (BN/2 rows) of B into its shared memory, so per SM the
+// tensor cores read half the B bytes of the single-CTA kernel and shared
+// memory bandwidth stops being the bound. Each CTA also loads its 128 rows of
+// A scales and all BN columns of B scales. Rank 0 issues the scale copies and
+// MMAs for both; every CTA's TMA loads count on rank 0's `full` barrier, rank
+// 0's commits arrive on both CTAs' `empty` / `acc_full` barriers, and both
+// CTAs' epilogue warps release the accumulator on rank 0's `acc_empty`.
+// Every load is a plain (non-multicast) TMA into the loading CTA's own memory.
+template <int BN>
+struct PairCfg {
+  static constexpr int BM = 128, BK = 128;   // rows of A per CTA
+  static constexpr int A_BYTES = BM * BK;
+  static constexpr int B_BYTES = BN / 2 * BK;  // this CTA's half of the B tile
+  static constexpr int SFB_CHUNKS = (BN + 127) / 128;  // BN=192 tiles at odd multiples of 64 span two
+  static constexpr int SF_BYTES = 512 + 512 * SFB_CHUNKS;
+  static constexpr int STAGE_BYTES = (A_BYTES + B_BYTES + SF_BYTES + 1023) / 1024 * 1024;
+  static constexpr int BAR_BYTES = 1024;
+  static constexpr int STAGES = (232448 - BAR_BYTES - 1024) / STAGE_BYTES > 8 ? 8
+                                                                            : (232448 - BAR_BYTES - 1024) / STAGE_BYTES;
+  static constexpr int TX_BYTES = 2 * (A_BYTES + B_BYTES + SF_BYTES);  // both CTAs, counted on rank 0
+  static constexpr int NACC = BN <= 192 ? 2 : 1;
+  static constexpr int SF_SLOTS = 4;
+  static constexpr int SF_COLS = 4 + 4 * SFB_CHUNKS;
+  static constexpr int SFA_COL = NACC * BN;
+  static constexpr int TMEM_COLS = 512;
+  static constexpr int SMEM = STAGES * STAGE_BYTES + BAR_BYTES + 1024;
+  static_assert(SFA_COL + SF_SLOTS * SF_COLS <= TMEM_COLS, "TMEM budget");
+  static_assert(SMEM <= 232448, "shared memory budget");
+  static_assert(STAGES >= 4, "pipeline depth");
+};
+
+template <int BN>
+__host__ __device__ constexpr uint32_t mxf8_idesc_pair() {
+  return (uint32_t(BN >> 3) << 17) | (1u << 23) | (uint32_t(256 >> 4) << 24);
+}
+
+template <int BN, int EPI>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+mxfp8_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
+                       const __grid_constant__ CUtensorMap tmap_sfa, const __grid_constant__ CUtensorMap tmap_sfb,
+                       EpiParams ep, int M, int N, int K, int* err) {
+  using C = PairCfg<BN>;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* bar_area = smem + C::STAGES * C::STAGE_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(bar_area);   // used on rank 0 only
+  uint64_t* empty = full + C::STAGES;
+  uint64_t* acc_full = empty + C::STAGES;
+  uint64_t* acc_empty = acc_full + 2;                        // used on rank 0 only
+  uint64_t* drain = acc_empty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const int pair = blockIdx.x >> 1, num_pairs = gridDim.x >> 1;
+  const int m_blocks = (M + 127) / 128, m_pairs = (m_blocks + 1) / 2;
+  const int n_tiles = N / BN, k_blocks = K / 128;
+  const int num_tiles = m_pairs * n_tiles;
+  const int kb_tiles = K / 128;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::STAGES; ++s) {
+      mbar_init(smem_u32(&full[s]), 1);
+      mbar_init(smem_u32(&empty[s]), 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(smem_u32(&acc_full[a]), 1);
+      mbar_init(smem_u32(&acc_empty[a]), 2 * kEpiWarps);
+    }
+    mbar_init(smem_u32(drain), 1);
+    fence_barrier_init();
+    prefetch_tmap(&tmap_a);
+    prefetch_tmap(&tmap_b);
+    prefetch_tmap(&tmap_sfa);
+    prefetch_tmap(&tmap_sfb);
+  }
+  if (warp == 1) tmem_alloc_pair(smem_u32(tmem_slot), C::TMEM_COLS);
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // both CTAs' barriers initialised before any cross-CTA arrive
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer (both CTAs)
+    if (lane == 0) {
+      int s = 0;
+      uint32_t phase = 0;
+      int issued = 0;
+      bool ok = true;
+      for (int tile = pair; tile < num_tiles && ok; tile += num_pairs) {
+        const int m_pair = tile / n_tiles, n_blk = tile % n_tiles;
+        const int m_blk = m_pair * 2 + int(rank);
+        const int m0 = m_blk * 128, n0 = n_blk * BN;
+        const int nb0 = n0 + int(rank) * (BN / 2);
+        const int c0 = n0 >> 7;
+        for (int kb = 0; kb < k_blocks; ++kb) {
+          if (!mbar_wait(smem_u32(&empty[s]), phase ^ 1, err)) { ok = false; break; }
+          uint8_t* st = smem + s * C::STAGE_BYTES;
+          if (rank == 0) mbar_arrive_expect_tx(smem_u32(&full[s]), C::TX_BYTES);
+          const uint32_t fb = map_to_rank(smem_u32(&full[s]), 0);
+          tma_load_2d_pair(smem_u32(st), &tmap_a, fb, kb * 128, m0);
+          tma_load_2d_pair(smem_u32(st + C::A_BYTES), &tmap_b, fb, kb * 128, nb0);
+          // scale chunks: 512 B = rows {2i, 2i+1} of the [*, 256] byte views
+          tma_load_2d_pair(smem_u32(st + C::A_BYTES + C::B_BYTES), &tmap_sfa, fb, 0, (m_blk * kb_tiles + kb) * 2);
+#pragma unroll
+          for (int c = 0; c < C::SFB_CHUNKS; ++c)
+            tma_load_2d_pair(smem_u32(st + C::A_BYTES + C::B_BYTES + 512 + 512 * c), &tmap_sfb, fb, 0,
+                             ((c0 + c) * kb_tiles + kb) * 2);
+          ++issued;
+          if (++s == C::STAGES) { s = 0; phase ^= 1; }
+        }
+      }
+      if (!ok && rank == 0) {
+        // Let the copies already queued land before shared memory goes away
+        // (rank 0's full barriers count both CTAs' bytes).
+        for (int i = 0; i < C::STAGES && i < issued; ++i) {
+          if (--s < 0) { s = C::STAGES - 1; phase ^= 1; }
+          mbar_wait(smem_u32(&full[s]), phase, nullptr, 100000000ull);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer (rank 0)
+    if (lane == 0) {
+      bool ok = true;
+      if (rank == 0) {
+        int s = 0, sf_slot = 0;
+        uint32_t phase = 0;
+        int it = 0;
+        for (int tile = pair; tile < num_tiles && ok; tile += num_pairs, ++it) {
+          const int a = (C::NACC == 2) ? (it & 1) : 0;
+          const uint32_t acc_phase = (C::NACC == 2) ? ((it >> 1) & 1) : (it & 1);
+          if (!mbar_wait(smem_u32(&acc_empty[a]), acc_phase ^ 1, err)) { ok = false; break; }
+          tc_fence_after();
+          const int n0 = (tile % n_tiles) * BN;
+          const uint32_t d_tmem = tmem_base + uint32_t(a * BN);
+          for (int kb = 0; kb < k_blocks; ++kb) {
+            if (!mbar_wait(smem_u32(&full[s]), phase, err)) { ok = false; break; }
+            tc_fence_after();
+            const uint32_t st = smem_u32(smem + s * C::STAGE_BYTES);
+            const uint32_t sfa_tmem = tmem_base + uint32_t(C::SFA_COL + sf_slot * C::SF_COLS);
+            const uint32_t sfb_base = sfa_tmem + 4;
+            const uint32_t sfb_tmem = sfb_base + uint32_t((n0 & 127) >> 5);
+            if (++sf_slot == C::SF_SLOTS) sf_slot = 0;
+            tc_cp_32x128b_warpx4_pair(sfa_tmem, smem_desc_sf(st + C::A_BYTES + C::B_BYTES));
+#pragma unroll
+            for (int c = 0; c < C::SFB_CHUNKS; ++c)
+              tc_cp_32x128b_warpx4_pair(sfb_base + 4 * c, smem_desc_sf(st + C::A_BYTES + C::B_BYTES + 512 + 512 * c));
+            const uint64_t adesc = smem_desc_k_sw128(st);
+            const uint64_t bdesc = smem_desc_k_sw128(st + C::A_BYTES);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              const uint32_t idesc = mxf8_idesc_pair<BN>() | (uint32_t(j) << 4) | (uint32_t(j) << 29);
+              tc_mma_mxf8_pair(d_tmem, adesc + uint64_t(2 * j), bdesc + uint64_t(2 * j), idesc, sfa_tmem, sfb_tmem,
+                               (kb | j) != 0);
+            }
+            tc_commit_pair(smem_u32(&empty[s]), 0x3);
+            if (++s == C::STAGES) { s = 0; phase ^= 1; }
+          }
+          if (ok) tc_commit_pair(smem_u32(&acc_full[a]), 0x3);
+        }
+        // drain: every MMA has finished reading both CTAs' shared memory and
+        // writing both CTAs' TMEM (arrives on both CTAs' drain barriers)
+        tc_commit_pair(smem_u32(drain), 0x3);
+      }
+      mbar_wait(smem_u32(drain), 0, ok ? err : nullptr, 100000000ull);
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue (both CTAs)
+    const int sub = warp & 3;
+    const int half = (warp - 2) / 4;
+    const int row_in_tile = sub * 32 + lane;
+    constexpr int kChunks = BN / 64;
+    const uint32_t release_bar_local = smem_u32(&acc_empty[0]);
+    int it = 0;
+    for (int tile = pair; tile < num_tiles; tile += num_pairs, ++it) {
+      const int a = (C::NACC == 2) ? (it & 1) : 0;
+      const uint32_t acc_phase = (C::NACC == 2) ? ((it >> 1) & 1) : (it & 1);
+      const bool got = __all_sync(0xffffffffu, mbar_wait(smem_u32(&acc_full[a]), acc_phase, err));
+      if (!got) break;
+      tc_fence_after();
+      const int m_blk = (tile / n_tiles) * 2 + int(rank);
+      const int n0 = (tile % n_tiles) * BN;
+      const int64_t row = int64_t(m_blk) * 128 + row_in_tile;
+      const bool live = row < M;
+      const bool in_pad = m_blk < m_blocks;   // rows of the padded [m_blocks*128, N] outputs
+      const uint32_t t_row = tmem_base + (uint32_t(sub * 32) << 16) + uint32_t(a * BN);
+      const uint32_t bar = release_bar_local + uint32_t(a * 8);
+      if constexpr (C::NACC == 1) {
+        // one accumulator: release it before the math (see the single-CTA kernel)
+        uint32_t r[kChunks][32];
+#pragma unroll
+        for (int jj = 0; jj < kChunks; ++jj) tc_ld_32x32b_x32(t_row + uint32_t((half * kChunks + jj) * 32), r[jj]);
+        tc_wait_ld();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) {
+          if (rank == 0) mbar_arrive(bar);
+          else mbar_arrive_cluster(map_to_rank(bar, 0));
+        }
+        if (in_pad) {
+#pragma unroll
+          for (int jj = 0; jj < kChunks; ++jj) {
+            float v[32];
+#pragma unroll
+            for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[jj][i]);
+            epilogue_chunk<EPI>(v, ep, row, n0 + (half * kChunks + jj) * 32, live, N);
+          }
+        }
+      } else {
+#pragma unroll 1
+        for (int jj = 0; jj < kChunks; ++jj) {
+          const int j = half * kChunks + jj;
+          uint32_t r[32];
+          tc_ld_32x32b_x32(t_row + uint32_t(j * 32), r);
+          tc_wait_ld();
+          if (jj == kChunks - 1) {
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) {
+              if (rank == 0) mbar_arrive(bar);
+              else mbar_arrive_cluster(map_to_rank(bar, 0));
+            }
+          }
+          if (in_pad) {
+            const int col = n0 + j * 32;
+            float v[32];
+#pragma unroll
+            for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+            epilogue_chunk<EPI>(v, ep, row, col, live, N);
+          }
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // both CTAs finished with TMEM and with each other's barriers
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, C::TMEM_COLS);
   }
 }
 
@@ -363,11 +651,105 @@ int launch_gemm(const void* a, const void* sa, const void* b, const void* sb, co
   return check_launch("mxfp8_gemm_kernel");
 }
 
-int pick_bn(int64_t M, int64_t N) {
+// 2-D uint8 view [rows, 256] of a scale-factor array (512-byte chunks = two
+// rows), box {256, 2}, no swizzle: one TMA copy per chunk.
+int make_sf_tmap(CUtensorMap* map, const void* base, int64_t bytes) {
+  auto fn = encode_fn();
+  if (!fn) return set_error(QIA_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  cuuint64_t dims[2] = {256u, cuuint64_t(bytes / 256)};
+  cuuint64_t strides[1] = {256u};
+  cuuint32_t box[2] = {256u, 2u};
+  cuuint32_t estr[2] = {1u, 1u};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return set_error(QIA_ERR_CUDA, "cuTensorMapEncodeTiled (scales) failed (%d)", int(r));
+  return QIA_OK;
+}
+
+// Clusters of two that can be resident at once (1 CTA per SM), per device and
+// tile width; the persistent grid never exceeds it so that no pair waits for
+// another to finish.
+template <int BN, int EPI>
+int pair_clusters() {
+  using C = PairCfg<BN>;
+  static int cached[64] = {0};
+  static std::mutex mu;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  std::lock_guard<std::mutex> lock(mu);
+  if (dev < 0 || dev >= 64) return 0;
+  if (cached[dev] == 0) {
+    cudaError_t e = cudaFuncSetAttribute(mxfp8_gemm_pair_kernel<BN, EPI>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+    if (e != cudaSuccess) { set_error(QIA_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e)); return 0; }
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.gridDim = dim3(2 * unsigned(sm_count() / 2));
+    cfg.blockDim = dim3(kGemmThreads);
+    cfg.dynamicSmemBytes = C::SMEM;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    e = cudaOccupancyMaxActiveClusters(&n, mxfp8_gemm_pair_kernel<BN, EPI>, &cfg);
+    if (e != cudaSuccess || n <= 0) {
+      set_error(QIA_ERR_CUDA, "cudaOccupancyMaxActiveClusters: %s", cudaGetErrorString(e));
+      return 0;
+    }
+    cached[dev] = n;
+  }
+  return cached[dev];
+}
+
+template <int BN, int EPI>
+int launch_gemm_pair(const void* a, const void* sa, const void* b, const void* sb, const EpiParams& ep, int64_t M,
+                     int64_t N, int64_t K, cudaStream_t st) {
+  using C = PairCfg<BN>;
+  const int clusters_max = pair_clusters<BN, EPI>();
+  if (clusters_max <= 0) return QIA_ERR_CUDA;
+  const int64_t m_blocks = (M + 127) / 128, m_pad = m_blocks * 128, kb_tiles = K / 128;
+  CUtensorMap ta, tb, tsa, tsb;
+  int rc = make_tmap(&ta, a, m_pad, K, 128);
+  if (rc) return rc;
+  rc = make_tmap(&tb, b, N, K, BN / 2);
+  if (rc) return rc;
+  rc = make_sf_tmap(&tsa, sa, m_blocks * kb_tiles * 512);
+  if (rc) return rc;
+  rc = make_sf_tmap(&tsb, sb, (N / 128) * kb_tiles * 512);
+  if (rc) return rc;
+  const int64_t tiles = ((m_blocks + 1) / 2) * (N / BN);
+  int64_t clusters = clusters_max;
+  if (clusters > tiles) clusters = tiles;
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.gridDim = dim3(unsigned(2 * clusters));
+  cfg.blockDim = dim3(kGemmThreads);
+  cfg.dynamicSmemBytes = C::SMEM;
+  cfg.stream = st;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, mxfp8_gemm_pair_kernel<BN, EPI>, ta, tb, tsa, tsb, ep, int(M), int(N),
+                                     int(K), device_error_word());
+  if (e != cudaSuccess) return set_error(QIA_ERR_CUDA, "mxfp8_gemm_pair_kernel launch: %s", cudaGetErrorString(e));
+  return check_launch("mxfp8_gemm_pair_kernel");
+}
+
+int pick_bn(int64_t M, int64_t N, bool heavy_epilogue) {
   // QIA_GEMM_BN (128, 192 or 256) pins the tile width, for tuning and tests.
   const char* env = getenv("QIA_GEMM_BN");
   const int forced = env ? atoi(env) : 0;
   if ((forced == 128 || forced == 192 || forced == 256) && N % forced == 0) return forced;
+  // GELU epilogues take longer than a K=3072 main loop of a BN=256 tile: keep
+  // them on the double-buffered accumulators of BN=192
+  if (heavy_epilogue && N % 192 == 0) return 192;
   // Prefer the tile width with the best last-wave occupancy over the SMs.
   const int64_t m_tiles = (M + 127) / 128;
   const int sms = sm_count();
@@ -377,8 +759,37 @@ int pick_bn(int64_t M, int64_t N) {
     if (N % bn) continue;
     const int64_t tiles = m_tiles * (N / bn);
     const int64_t waves = (tiles + sms - 1) / sms;
-    // double-buffered accumulators hide the epilogue; single-buffered do not
-    const double eff = double(tiles) / double(waves * sms) * (bn == 256 ? 0.92 : 1.0) * (bn == 128 ? 0.95 : 1.0);
+    // measured per-tile efficiency on B200: BN=256 (one accumulator, released
+    // before the epilogue math) > 192 > 128
+    const double eff = double(tiles) / double(waves * sms) * (bn == 192 ? 0.92 : 1.0) * (bn == 128 ? 0.8 : 1.0);
+    if (eff > best_eff + 1e-9) { best_eff = eff; best = bn; }
+  }
+  return best;
+}
+
+// The CTA-pair kernel is opt-in: QIA_GEMM_PAIR=1 selects it (measured on
+// B200 it reads less L2 per output but issues its MMAs no faster than the
+// single-CTA kernel with BN=256, which stays the default).
+bool use_pair(int64_t M) {
+  const char* env = getenv("QIA_GEMM_PAIR");
+  return env && env[0] == '1' && M > 0;
+}
+
+int pick_bn_pair(int64_t M, int64_t N) {
+  const char* env = getenv("QIA_GEMM_BN");
+  const int forced = env ? atoi(env) : 0;
+  if ((forced == 128 || forced == 192 || forced == 256) && N % forced == 0) return forced;
+  const int64_t m_pairs = ((M + 127) / 128 + 1) / 2;
+  const int pairs = sm_count() / 2;
+  int best = 0;
+  double best_eff = -1.0;
+  for (int bn : {192, 256, 128}) {
+    if (N % bn) continue;
+    const int64_t tiles = m_pairs * (N / bn);
+    const int64_t waves = (tiles + pairs - 1) / pairs;
+    // BN=256 has one accumulator (epilogue not overlapped); BN=128 reads the
+    // most shared memory per MMA
+    const double eff = double(tiles) / double(waves * pairs) * (bn == 256 ? 0.93 : 1.0) * (bn == 128 ? 0.9 : 1.0);
     if (eff > best_eff + 1e-9) { best_eff = eff; best = bn; }
   }
   return best;
@@ -394,8 +805,16 @@ int dispatch(const void* a, const void* sa, const void* b, const void* sb, const
   if (M > (1LL << 30) || K > (1LL << 20) || N > (1LL << 20)) return set_error(QIA_ERR_UNSUPPORTED, "%s: too large", who);
   if (!aligned(a, 16) || !aligned(b, 16) || !aligned(sa, 16) || !aligned(sb, 16))
     return set_error(QIA_ERR_ALIGNMENT, "%s: operands must be 16-byte aligned", who);
-  const int bn = pick_bn(M, N);
   cudaStream_t st = as_stream(stream);
+  if (use_pair(M)) {
+    switch (pick_bn_pair(M, N)) {
+      case 128: return launch_gemm_pair<128, EPI>(a, sa, b, sb, ep, M, N, K, st);
+      case 192: return launch_gemm_pair<192, EPI>(a, sa, b, sb, ep, M, N, K, st);
+      case 256: return launch_gemm_pair<256, EPI>(a, sa, b, sb, ep, M, N, K, st);
+      default: return set_error(QIA_ERR_UNSUPPORTED, "%s: N=%lld has no supported tile width", who, (long long)N);
+    }
+  }
+  const int bn = pick_bn(M, N, EPI == kEpiGeluQuant || EPI == kEpiGeluBf16);
   switch (bn) {
     case 128: return launch_gemm<128, EPI>(a, sa, b, sb, ep, M, N, K, st);
     case 192: return launch_gemm<192, EPI>(a, sa, b, sb, ep, M, N, K, st);

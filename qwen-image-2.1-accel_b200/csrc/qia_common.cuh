@@ -130,6 +130,22 @@ __device__ __forceinline__ float gelu_tanh_f32(float x) {
   return __fmul_rn(__fmul_rn(0.5f, x), 1.0f + tanhf(inner));
 }
 
+// The same GELU (tanh form) as x * sigmoid(2u), since 0.5 (1 + tanh u) =
+// 1 / (1 + e^(-2u)): two MUFU operations (ex2, rcp; relative errors ~2^-22)
+// instead of the accurate tanhf, and no cancellation for negative x. Within a
+// few fp32 ulps of gelu_tanh_f32, so after bf16 rounding the two agree except
+// at rounding boundaries. Used where the GELU sits in a GEMM epilogue.
+__device__ __forceinline__ float gelu_tanh_fast(float x) {
+  // -2 * sqrt(2/pi) * log2(e)
+  const float k_arg = float(-2.0 * M_SQRT2 * M_2_SQRTPI * 0.5 * 1.4426950408889634);
+  const float k_kappa = 0.044715f;
+  const float p = fmaf(k_kappa * (x * x), x, x);   // x + 0.044715 x^3
+  float e, r;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e) : "f"(p * k_arg));
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(1.0f + e));
+  return x * r;
+}
+
 __device__ __forceinline__ float warp_max_xor(float v, int width_mask) {
   for (int o = width_mask; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
   return v;
