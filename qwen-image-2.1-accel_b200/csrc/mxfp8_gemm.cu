@@ -54,6 +54,7 @@ struct EpiParams {
   int64_t rows_per_batch;
   uint8_t* q_values;           // [Mpad, N] e4m3 (kEpiGeluQuant)
   uint8_t* q_scales;           // blocked E8M0 (kEpiGeluQuant)
+  int wide;                    // out/resid/q_values rows allow 32-byte accesses
 };
 
 constexpr int kEpiWarps = 8;
@@ -72,8 +73,9 @@ struct Cfg {
   // scale-factor slots in TMEM, used round-robin per K block so that the copy
   // for block kb+1 never overwrites scales the MMAs of block kb still read
   static constexpr int SF_SLOTS = 4;
-  static constexpr int SF_COLS = 4 + 4 * SFB_CHUNKS;
-  static constexpr int SFA_COL = NACC * BN;   // slot s: A at SFA_COL + s*SF_COLS, B 4 columns later
+  static constexpr int SF_COLS = 16;       // A scales at +0, B scales at +8 (8-column aligned)
+  static constexpr int SFB_OFF = 8;
+  static constexpr int SFA_COL = NACC * BN;   // slot s: A at SFA_COL + s*SF_COLS, B SFB_OFF columns later
   static constexpr int TMEM_COLS = 512;
   static constexpr int BAR_BYTES = 1024;
   static constexpr int SMEM = STAGES * STAGE_BYTES + BAR_BYTES + 1024;
@@ -102,15 +104,26 @@ __device__ __forceinline__ void epilogue_chunk(float (&v)[32], const EpiParams& 
       for (int i = 0; i < 8; ++i) v[q * 8 + i] += bf[i];
     }
   }
+  // Each thread owns one row: a 32-column chunk is 64 contiguous bytes of bf16,
+  // written (and, for the residual, read) as two full 32-byte sectors when the
+  // row start allows it, else as four 16-byte pieces.
   if (EPI == kEpiBf16 || EPI == kEpiGeluBf16) {
     if (live) {
       if (EPI == kEpiGeluBf16) {
 #pragma unroll
         for (int i = 0; i < 32; ++i) v[i] = gelu_tanh_fast(round_bf16(v[i]));
       }
-      uint4* op = reinterpret_cast<uint4*>(ep.out + row * ep.ldo + col);
+      uint4 pk[4];
 #pragma unroll
-      for (int q = 0; q < 4; ++q) op[q] = pack8(&v[q * 8]);
+      for (int q = 0; q < 4; ++q) pk[q] = pack8(&v[q * 8]);
+      uint4* op = reinterpret_cast<uint4*>(ep.out + row * ep.ldo + col);
+      if (ep.wide) {
+        st_global_v8(op, pk[0], pk[1]);
+        st_global_v8(op + 2, pk[2], pk[3]);
+      } else {
+#pragma unroll
+        for (int q = 0; q < 4; ++q) op[q] = pk[q];
+      }
     }
   } else if (EPI == kEpiGateResidual) {
     if (live) {
@@ -118,15 +131,30 @@ __device__ __forceinline__ void epilogue_chunk(float (&v)[32], const EpiParams& 
       const uint4* gp = reinterpret_cast<const uint4*>(ep.gate + b * N + col);
       const uint4* hp = reinterpret_cast<const uint4*>(ep.resid + row * ep.ldo + col);
       uint4* op = reinterpret_cast<uint4*>(ep.out + row * ep.ldo + col);
+      uint4 hv[4], ov[4];
+      if (ep.wide) {
+        ld_global_v8(hp, hv[0], hv[1]);
+        ld_global_v8(hp + 2, hv[2], hv[3]);
+      } else {
+#pragma unroll
+        for (int q = 0; q < 4; ++q) hv[q] = hp[q];
+      }
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
         float g[8], h[8], o[8];
         unpack8(__ldg(gp + q), g);
-        unpack8(hp[q], h);
+        unpack8(hv[q], h);
 #pragma unroll
         for (int i = 0; i < 8; ++i)
           o[i] = __fadd_rn(h[i], round_bf16(__fmul_rn(g[i], round_bf16(v[q * 8 + i]))));
-        op[q] = pack8(o);
+        ov[q] = pack8(o);
+      }
+      if (ep.wide) {
+        st_global_v8(op, ov[0], ov[1]);
+        st_global_v8(op + 2, ov[2], ov[3]);
+      } else {
+#pragma unroll
+        for (int q = 0; q < 4; ++q) op[q] = ov[q];
       }
     }
   } else {  // kEpiGeluQuant: the 32 columns are exactly one MX block of the next GEMM's K
@@ -148,8 +176,12 @@ __device__ __forceinline__ void epilogue_chunk(float (&v)[32], const EpiParams& 
     c1.z = cvt_e4m3x4(v[24] * inv, v[25] * inv, v[26] * inv, v[27] * inv);
     c1.w = cvt_e4m3x4(v[28] * inv, v[29] * inv, v[30] * inv, v[31] * inv);
     uint4* qp = reinterpret_cast<uint4*>(ep.q_values + row * int64_t(N) + col);
-    qp[0] = c0;
-    qp[1] = c1;
+    if (ep.wide) {
+      st_global_v8(qp, c0, c1);
+    } else {
+      qp[0] = c0;
+      qp[1] = c1;
+    }
     ep.q_scales[mx_scale_offset(row, col >> 5, N >> 7)] = uint8_t(e);
   }
 }
@@ -246,11 +278,12 @@ mxfp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_const
         const int n0 = (tile % n_tiles) * BN;
         const uint32_t d_tmem = tmem_base + uint32_t(a * BN);
         for (int kb = 0; kb < k_blocks; ++kb) {
+          // TMA completion on `full` orders the stage's bytes for the MMAs
+          // (async proxy on both sides): no tcgen05 fence per K block
           if (!mbar_wait(smem_u32(&full[s]), phase, err)) { ok = false; break; }
-          tc_fence_after();
           const uint32_t st = smem_u32(smem + s * C::STAGE_BYTES);
           const uint32_t sfa_tmem = tmem_base + uint32_t(C::SFA_COL + sf_slot * C::SF_COLS);
-          const uint32_t sfb_base = sfa_tmem + 4;
+          const uint32_t sfb_base = sfa_tmem + C::SFB_OFF;
           // BN=192 tiles at odd multiples of 64 start 2 columns into the chunk
           const uint32_t sfb_tmem = sfb_base + uint32_t((n0 & 127) >> 5);
           if (++sf_slot == C::SF_SLOTS) sf_slot = 0;
@@ -366,7 +399,8 @@ struct PairCfg {
   static constexpr int TX_BYTES = 2 * (A_BYTES + B_BYTES + SF_BYTES);  // both CTAs, counted on rank 0
   static constexpr int NACC = BN <= 192 ? 2 : 1;
   static constexpr int SF_SLOTS = 4;
-  static constexpr int SF_COLS = 4 + 4 * SFB_CHUNKS;
+  static constexpr int SF_COLS = 16;       // A scales at +0, B scales at +8 (8-column aligned)
+  static constexpr int SFB_OFF = 8;
   static constexpr int SFA_COL = NACC * BN;
   static constexpr int TMEM_COLS = 512;
   static constexpr int SMEM = STAGES * STAGE_BYTES + BAR_BYTES + 1024;
@@ -483,10 +517,9 @@ mxfp8_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_
           const uint32_t d_tmem = tmem_base + uint32_t(a * BN);
           for (int kb = 0; kb < k_blocks; ++kb) {
             if (!mbar_wait(smem_u32(&full[s]), phase, err)) { ok = false; break; }
-            tc_fence_after();
             const uint32_t st = smem_u32(smem + s * C::STAGE_BYTES);
             const uint32_t sfa_tmem = tmem_base + uint32_t(C::SFA_COL + sf_slot * C::SF_COLS);
-            const uint32_t sfb_base = sfa_tmem + 4;
+            const uint32_t sfb_base = sfa_tmem + C::SFB_OFF;
             const uint32_t sfb_tmem = sfb_base + uint32_t((n0 & 127) >> 5);
             if (++sf_slot == C::SF_SLOTS) sf_slot = 0;
             tc_cp_32x128b_warpx4_pair(sfa_tmem, smem_desc_sf(st + C::A_BYTES + C::B_BYTES));
@@ -805,20 +838,23 @@ int dispatch(const void* a, const void* sa, const void* b, const void* sb, const
   if (M > (1LL << 30) || K > (1LL << 20) || N > (1LL << 20)) return set_error(QIA_ERR_UNSUPPORTED, "%s: too large", who);
   if (!aligned(a, 16) || !aligned(b, 16) || !aligned(sa, 16) || !aligned(sb, 16))
     return set_error(QIA_ERR_ALIGNMENT, "%s: operands must be 16-byte aligned", who);
+  EpiParams epw = ep;
+  epw.wide = (!ep.out || (aligned(ep.out, 32) && ep.ldo % 16 == 0)) && (!ep.resid || aligned(ep.resid, 32)) &&
+             (!ep.q_values || aligned(ep.q_values, 32));
   cudaStream_t st = as_stream(stream);
   if (use_pair(M)) {
     switch (pick_bn_pair(M, N)) {
-      case 128: return launch_gemm_pair<128, EPI>(a, sa, b, sb, ep, M, N, K, st);
-      case 192: return launch_gemm_pair<192, EPI>(a, sa, b, sb, ep, M, N, K, st);
-      case 256: return launch_gemm_pair<256, EPI>(a, sa, b, sb, ep, M, N, K, st);
+      case 128: return launch_gemm_pair<128, EPI>(a, sa, b, sb, epw, M, N, K, st);
+      case 192: return launch_gemm_pair<192, EPI>(a, sa, b, sb, epw, M, N, K, st);
+      case 256: return launch_gemm_pair<256, EPI>(a, sa, b, sb, epw, M, N, K, st);
       default: return set_error(QIA_ERR_UNSUPPORTED, "%s: N=%lld has no supported tile width", who, (long long)N);
     }
   }
   const int bn = pick_bn(M, N, EPI == kEpiGeluQuant || EPI == kEpiGeluBf16);
   switch (bn) {
-    case 128: return launch_gemm<128, EPI>(a, sa, b, sb, ep, M, N, K, st);
-    case 192: return launch_gemm<192, EPI>(a, sa, b, sb, ep, M, N, K, st);
-    case 256: return launch_gemm<256, EPI>(a, sa, b, sb, ep, M, N, K, st);
+    case 128: return launch_gemm<128, EPI>(a, sa, b, sb, epw, M, N, K, st);
+    case 192: return launch_gemm<192, EPI>(a, sa, b, sb, epw, M, N, K, st);
+    case 256: return launch_gemm<256, EPI>(a, sa, b, sb, epw, M, N, K, st);
     default: return set_error(QIA_ERR_UNSUPPORTED, "%s: N=%lld has no supported tile width", who, (long long)N);
   }
 }

@@ -198,3 +198,23 @@ def test_pair_and_single_kernels_agree(monkeypatch, m, n, k):
     diff = (y0.float() - y1.float()).abs()
     assert (diff <= y0.float().abs() * 2 ** -7 + 1e-6).all()
     print(f"pair vs single: {(diff == 0).float().mean().item():.4f} of outputs bit-identical")
+
+
+@pytest.mark.parametrize("pad", [0, 8, 16])
+def test_gemm_output_row_stride(pad):
+    """Output rows whose start is only 16-byte aligned (pad=8: ldo = N+8) take
+    the 16-byte store path; 32-byte aligned rows (pad 0, 16) the 32-byte one.
+    Both must write exactly the [M, N] window."""
+    from qwen_image_accel_b200.kernels.mxfp8 import quantize
+    from qwen_image_accel_b200.optimizations.mxfp8 import MXFP8Linear
+    m, n, k = 300, 1536, 384
+    lin = make_linear(n, k, 16)
+    mx = MXFP8Linear(lin)
+    a = quantize(make_x(m, k, 17))
+    ref = mx.matmul(a)
+    buf = torch.full((m, n + pad + 8), -7.0, device=DEV, dtype=torch.bfloat16)
+    out = buf[:, pad:pad + n]
+    mx.matmul(a, out=out)
+    torch.cuda.synchronize()
+    assert torch.equal(out, ref)
+    assert bool((buf[:, :pad] == -7.0).all()) and bool((buf[:, pad + n:] == -7.0).all())
