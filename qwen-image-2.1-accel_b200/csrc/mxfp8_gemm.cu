@@ -794,7 +794,7 @@ int pick_bn(int64_t M, int64_t N, bool heavy_epilogue) {
     const int64_t waves = (tiles + sms - 1) / sms;
     // measured per-tile efficiency on B200: BN=256 (one accumulator, released
     // before the epilogue math) > 192 > 128
-    const double eff = double(tiles) / double(waves * sms) * (bn == 192 ? 0.92 : 1.0) * (bn == 128 ? 0.8 : 1.0);
+    const double eff = double(tiles) / double(waves * sms) * (bn == 192 ? 0.8 : 1.0) * (bn == 128 ? 0.7 : 1.0);
     if (eff > best_eff + 1e-9) { best_eff = eff; best = bn; }
   }
   return best;

@@ -200,21 +200,28 @@ def test_pair_and_single_kernels_agree(monkeypatch, m, n, k):
     print(f"pair vs single: {(diff == 0).float().mean().item():.4f} of outputs bit-identical")
 
 
+@pytest.mark.parametrize("bn", ["192", "256"])
 @pytest.mark.parametrize("pad", [0, 8, 16])
-def test_gemm_output_row_stride(pad):
-    """Output rows whose start is only 16-byte aligned (pad=8: ldo = N+8) take
-    the 16-byte store path; 32-byte aligned rows (pad 0, 16) the 32-byte one.
-    Both must write exactly the [M, N] window."""
+def test_gemm_output_row_stride(monkeypatch, bn, pad):
+    """Outputs with a row stride ldo = N + pad + 8 and a start offset of `pad`
+    elements: rows whose start is 32-byte aligned take 32-byte stores, the
+    others 16-byte stores. Every path must write exactly the [M, N] window,
+    including the partial last row block (M = 300), at both tile widths."""
     from qwen_image_accel_b200.kernels.mxfp8 import quantize
     from qwen_image_accel_b200.optimizations.mxfp8 import MXFP8Linear
+    monkeypatch.setenv("QIA_GEMM_BN", bn)
     m, n, k = 300, 1536, 384
     lin = make_linear(n, k, 16)
     mx = MXFP8Linear(lin)
     a = quantize(make_x(m, k, 17))
+    monkeypatch.setenv("QIA_GEMM_BN", "128")
     ref = mx.matmul(a)
+    monkeypatch.setenv("QIA_GEMM_BN", bn)
     buf = torch.full((m, n + pad + 8), -7.0, device=DEV, dtype=torch.bfloat16)
     out = buf[:, pad:pad + n]
     mx.matmul(a, out=out)
     torch.cuda.synchronize()
     assert torch.equal(out, ref)
     assert bool((buf[:, :pad] == -7.0).all()) and bool((buf[:, pad + n:] == -7.0).all())
+    from qwen_image_accel_b200 import _lib
+    assert _lib.device_error() == 0
