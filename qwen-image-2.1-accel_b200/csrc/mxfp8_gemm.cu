@@ -265,7 +265,18 @@ mxfp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_const
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
+    // Kept to a few instructions per K block (this warp shares its SM
+    // sub-partition with busy epilogue warps): the stage's descriptors advance
+    // by a constant (STAGE_BYTES/16 in the start-address field), the scale
+    // slot and barrier addresses by fixed strides.
     if (lane == 0) {
+      constexpr uint32_t kStageDesc = C::STAGE_BYTES >> 4;
+      const uint32_t smem0 = smem_u32(smem);
+      const uint64_t adesc0 = smem_desc_k_sw128(smem0);
+      const uint64_t bdesc0 = smem_desc_k_sw128(smem0 + C::A_BYTES);
+      const uint64_t sfdesc0 = smem_desc_sf(smem0 + C::A_BYTES + C::B_BYTES);
+      const uint32_t full0 = smem_u32(&full[0]), empty0 = smem_u32(&empty[0]);
+      const uint32_t sf0 = tmem_base + uint32_t(C::SFA_COL);
       int s = 0, sf_slot = 0;
       uint32_t phase = 0;
       bool ok = true;
@@ -277,29 +288,27 @@ mxfp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_const
         tc_fence_after();
         const int n0 = (tile % n_tiles) * BN;
         const uint32_t d_tmem = tmem_base + uint32_t(a * BN);
+        // BN=192 tiles at odd multiples of 64 start 2 columns into the chunk
+        const uint32_t sfb_shift = uint32_t(C::SFB_OFF + ((n0 & 127) >> 5));
         for (int kb = 0; kb < k_blocks; ++kb) {
           // TMA completion on `full` orders the stage's bytes for the MMAs
           // (async proxy on both sides): no tcgen05 fence per K block
-          if (!mbar_wait(smem_u32(&full[s]), phase, err)) { ok = false; break; }
-          const uint32_t st = smem_u32(smem + s * C::STAGE_BYTES);
-          const uint32_t sfa_tmem = tmem_base + uint32_t(C::SFA_COL + sf_slot * C::SF_COLS);
-          const uint32_t sfb_base = sfa_tmem + C::SFB_OFF;
-          // BN=192 tiles at odd multiples of 64 start 2 columns into the chunk
-          const uint32_t sfb_tmem = sfb_base + uint32_t((n0 & 127) >> 5);
+          if (!mbar_wait(full0 + 8u * uint32_t(s), phase, err)) { ok = false; break; }
+          const uint64_t off = uint64_t(uint32_t(s) * kStageDesc);
+          const uint32_t sfa_tmem = sf0 + uint32_t(sf_slot * C::SF_COLS);
           if (++sf_slot == C::SF_SLOTS) sf_slot = 0;
-          tc_cp_32x128b_warpx4(sfa_tmem, smem_desc_sf(st + C::A_BYTES + C::B_BYTES));
+          tc_cp_32x128b_warpx4(sfa_tmem, sfdesc0 + off);
 #pragma unroll
           for (int c = 0; c < C::SFB_CHUNKS; ++c)
-            tc_cp_32x128b_warpx4(sfb_base + 4 * c, smem_desc_sf(st + C::A_BYTES + C::B_BYTES + 512 + 512 * c));
-          const uint64_t adesc = smem_desc_k_sw128(st);
-          const uint64_t bdesc = smem_desc_k_sw128(st + C::A_BYTES);
+            tc_cp_32x128b_warpx4(sfa_tmem + uint32_t(C::SFB_OFF + 4 * c), sfdesc0 + off + uint64_t(32 + 32 * c));
+          const uint64_t adesc = adesc0 + off, bdesc = bdesc0 + off;
+          const uint32_t sfb_tmem = sfa_tmem + sfb_shift;
+          tc_mma_mxf8(d_tmem, adesc, bdesc, mxf8_idesc<BN>(), sfa_tmem, sfb_tmem, kb != 0);
 #pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            const uint32_t idesc = mxf8_idesc<BN>() | (uint32_t(j) << 4) | (uint32_t(j) << 29);
-            tc_mma_mxf8(d_tmem, adesc + uint64_t(2 * j), bdesc + uint64_t(2 * j), idesc, sfa_tmem, sfb_tmem,
-                        (kb | j) != 0);
-          }
-          tc_commit(smem_u32(&empty[s]));
+          for (int j = 1; j < 4; ++j)
+            tc_mma_mxf8(d_tmem, adesc + uint64_t(2 * j), bdesc + uint64_t(2 * j),
+                        mxf8_idesc<BN>() | (uint32_t(j) << 4) | (uint32_t(j) << 29), sfa_tmem, sfb_tmem, 1u);
+          tc_commit(empty0 + 8u * uint32_t(s));
           if (++s == C::STAGES) { s = 0; phase ^= 1; }
         }
         if (ok) tc_commit(smem_u32(&acc_full[a]));
