@@ -159,6 +159,56 @@ __device__ __forceinline__ void ld_global_v8(const void* p, uint4& a, uint4& b) 
                : "l"(p));
 }
 
+// ---- packed fp32 pairs (sm_100 f32x2 FMA-pipe instructions): each lane of a
+// pair is rounded exactly as the scalar instruction would round it.
+__device__ __forceinline__ uint64_t f2_pack(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ void f2_unpack(uint64_t r, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(r));
+}
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ uint64_t f2_mul(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+  return r;
+}
+// Both lanes rounded to bf16 (nearest even) and widened back to fp32.
+__device__ __forceinline__ void round_bf16_x2(float& lo, float& hi) {
+  uint32_t b;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(b) : "f"(hi), "f"(lo));
+  lo = __uint_as_float(b << 16);
+  hi = __uint_as_float(b & 0xffff0000u);
+}
+
+// gelu_tanh_fast on a pair: the same operations in the same order (so the
+// same results), with the FMA-pipe steps issued as f32x2 instructions.
+__device__ __forceinline__ void gelu_tanh_fast_x2(float& x0, float& x1) {
+  const float k_arg = float(-2.0 * M_SQRT2 * M_2_SQRTPI * 0.5 * 1.4426950408889634);
+  const float k_kappa = 0.044715f;
+  const uint64_t x = f2_pack(x0, x1);
+  const uint64_t p = f2_fma(f2_mul(f2_pack(k_kappa, k_kappa), f2_mul(x, x)), x, x);
+  float a0, a1, e0, e1, d0, d1, r0, r1;
+  f2_unpack(f2_mul(p, f2_pack(k_arg, k_arg)), a0, a1);
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e0) : "f"(a0));
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e1) : "f"(a1));
+  f2_unpack(f2_add(f2_pack(1.0f, 1.0f), f2_pack(e0, e1)), d0, d1);
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r0) : "f"(d0));
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r1) : "f"(d1));
+  f2_unpack(f2_mul(x, f2_pack(r0, r1)), x0, x1);
+}
+
 __device__ __forceinline__ float warp_max_xor(float v, int width_mask) {
   for (int o = width_mask; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
   return v;
