@@ -472,6 +472,7 @@ sage_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
     }
     // ---- P pass: P = 2^(s - m) per 64-key half -> E4M3 into TMEM
     float ds[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    uint64_t ds01 = f2_pack(0.0f, 0.0f), ds23 = f2_pack(0.0f, 0.0f);   // ds[0..3] as lane pairs
     float ks_cur = __ldg(ks_head);
     for (int i = 0; i < nh && ok; ++i) {
       const int h = i & 1;
@@ -489,14 +490,18 @@ sage_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
         // s*sc - m = X*sc - (2^23+2^22)*sc - m with X = float(2^23+2^22+s)
         // exactly (|s| < 2^22): one FMA per score after an integer add
         const float bias = fmaf(12582912.0f, sc, m);
+        const uint64_t sc2 = f2_pack(sc, sc), nb2 = f2_pack(-bias, -bias);
 #pragma unroll
         for (int t4 = 0; t4 < 64; t4 += 4) {
-          float pv[4];
+          float a[4], pv[4];
+          f2_unpack(f2_fma(f2_pack(__int_as_float(int(sv[t4]) + 0x4B400000), __int_as_float(int(sv[t4 + 1]) + 0x4B400000)),
+                           sc2, nb2), a[0], a[1]);
+          f2_unpack(f2_fma(f2_pack(__int_as_float(int(sv[t4 + 2]) + 0x4B400000), __int_as_float(int(sv[t4 + 3]) + 0x4B400000)),
+                           sc2, nb2), a[2], a[3]);
 #pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            pv[e] = ex2_approx(fmaf(__int_as_float(int(sv[t4 + e]) + 0x4B400000), sc, -bias));
-            ds[e] += pv[e];
-          }
+          for (int e = 0; e < 4; ++e) pv[e] = ex2_approx(a[e]);
+          ds01 = f2_add(ds01, f2_pack(pv[0], pv[1]));
+          ds23 = f2_add(ds23, f2_pack(pv[2], pv[3]));
           w[t4 / 4] = cvt_e4m3x4(pv[0], pv[1], pv[2], pv[3]);
         }
       } else {
@@ -516,6 +521,15 @@ sage_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(smem_u32(&pb_full[h]));
+    }
+    {
+      float d0, d1, d2, d3;
+      f2_unpack(ds01, d0, d1);
+      f2_unpack(ds23, d2, d3);
+      ds[0] += d0;
+      ds[1] += d1;
+      ds[2] += d2;
+      ds[3] += d3;
     }
     const float dsum = (ds[0] + ds[1]) + (ds[2] + ds[3]);
     if (ok && __all_sync(0xffffffffu, mbar_wait(smem_u32(o_full), 0, err))) {
