@@ -13,6 +13,8 @@ per step) is far larger than L2, so no flush is needed between steps.
 
 N > 1: replicas of the 1024^2 step (one per GPU, no collective on the data
 path), weak scaling; `value` = whole-job ms per step = max elapsed / (K * N).
+`--config c5`: the 2048^2 step, on N >= 2 GPUs split into CFG halves of
+Ulysses groups (NCCL all-to-all); strong scaling, `value` = ms per step.
 
 `--impl reference` times the reference's eager CPU path (oracle/mmdit_cpu.py,
 a restatement of the Diffusers block) on this host's cores: one full-size
@@ -312,6 +314,134 @@ def our_arm(args, rank, world, local_rank):
         print(json.dumps(line), flush=True)
 
 
+METRIC_C5 = "ms per MMDiT denoise step at 2048^2 (60 blocks, CFG batch 2)"
+GRID_C5 = (1, 128, 128)              # 2048^2 latent 16ch x 256 x 256, 2x2 patches
+FLOP_C5 = 860.5e12                   # per step (both CFG rows): linears + attention
+
+
+def c5_arm(args, rank, world, local_rank):
+    """the 2048^2 step (16384 image + 256 text tokens per CFG
+    row). One GPU runs the CFG batch of 2; N >= 2 GPUs split it into the two
+    CFG halves, each a Ulysses group of N/2 ranks over NCCL (all-to-all Q/K/V
+    and O per block, one velocity swap per step). Strong scaling: the same
+    step at every N."""
+    from qwen_image_accel_b200 import _lib
+    device = torch.device("cuda", local_rank)
+    torch.cuda.set_device(device)
+    model, cfg = build_model(device)
+    img_len = GRID_C5[0] * GRID_C5[1] * GRID_C5[2]
+    g = torch.Generator(device=device).manual_seed(42)
+    latents = torch.randn(1, img_len, 64, device=device, dtype=torch.bfloat16, generator=g)
+    pe = torch.randn(1, TXT_LEN, TXT_DIM, device=device, dtype=torch.bfloat16, generator=g)
+    ne = torch.randn(1, TXT_LEN, TXT_DIM, device=device, dtype=torch.bfloat16, generator=g)
+    sig, sig_next = 1.0, 0.975
+    plan = None
+    if world > 1:
+        from qwen_image_accel_b200.ulysses import make_plan
+        plan = make_plan(cfg_split=True)
+        lo, hi = plan.image_slice(img_len)
+        static_in = latents[:, lo:hi].clone()
+        step = lambda: model.denoise_step_sharded(static_in, pe, ne, sig, sig_next, GRID_C5, plan)  # noqa: E731
+    else:
+        static_in = latents.clone()
+        step = lambda: model.denoise_step(static_in, pe, ne, sig, sig_next, GRID_C5)  # noqa: E731
+    _lib.launch_count = 0
+    for _ in range(max(args.warmup, 3)):
+        static_in.copy_(step())
+    torch.cuda.synchronize()
+    launches_per_step = _lib.launch_count // max(args.warmup, 3)
+    graph = None
+    try:
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            static_out = step()
+        graph.replay()
+        torch.cuda.synchronize()
+    except Exception as exc:  # noqa: BLE001
+        log(f"CUDA graph capture of the sharded step failed ({exc!r}); timing eager steps")
+        graph = None
+        torch.cuda.synchronize()
+    if world > 1:
+        torch.distributed.barrier()
+    sampler = ClockSampler(torch.cuda.current_device()) if rank == 0 else None
+    st = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    if world > 1:
+        torch.distributed.barrier()
+    e0.record(st)
+    for _ in range(args.steps):
+        if graph is not None:
+            graph.replay()
+            static_in.copy_(static_out)
+        else:
+            static_in.copy_(step())
+    e1.record(st)
+    torch.cuda.synchronize()
+    if world > 1:
+        torch.distributed.barrier()
+    elapsed = e0.elapsed_time(e1)
+    clocks = sampler.stop() if sampler else None
+    if world > 1:
+        t = torch.tensor([elapsed], device=device)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        elapsed = t.item()
+    ms_step = elapsed / args.steps
+    # end to end: this rank's latent shard and its half's text in from pinned
+    # host memory, its updated shard back, every step
+    host_lat = static_in.cpu().pin_memory()
+    host_pe, host_ne = pe.cpu().pin_memory(), ne.cpu().pin_memory()
+    host_out = torch.empty_like(host_lat).pin_memory()
+    torch.cuda.synchronize()
+    if world > 1:
+        torch.distributed.barrier()
+    e0.record(st)
+    for _ in range(args.steps):
+        static_in.copy_(host_lat, non_blocking=True)
+        pe.copy_(host_pe, non_blocking=True)
+        ne.copy_(host_ne, non_blocking=True)
+        if graph is not None:
+            graph.replay()
+            host_out.copy_(static_out, non_blocking=True)
+        else:
+            host_out.copy_(step(), non_blocking=True)
+    e1.record(st)
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1) / args.steps
+    if world > 1:
+        t = torch.tensor([e2e_ms], device=device)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        e2e_ms = t.item()
+    assert _lib.device_error() == 0, "a device-side wait timed out"
+    used_graph = graph is not None
+    del graph   # a graph holding NCCL calls must go before the process group
+    if rank == 0:
+        hbm, bf16_tf, peak_kind = load_peaks()
+        per_gpu_tf = FLOP_C5 / (ms_step * 1e-3) / world / 1e12
+        line = {"metric": METRIC_C5, "value": round(ms_step, 3), "unit": "ms/step", "n_gpus": world,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 3),
+                "higher_is_better": False, "scaling": "strong", "vs_baseline": None,
+                "dtype": "mxfp8+int8/fp8 attn",
+                "data": "synthetic (random-init weights ~N(0,0.02), seeded latents/text)",
+                "config": {"workload": "config5: 60-block dual-stream MMDiT denoise step, 2048^2 "
+                                       "(16384 img + 256 txt tokens), CFG batch 2, profile mxfp8_sage",
+                           "global_batch": 2, "seq_len": img_len + TXT_LEN,
+                           "parallelism": (f"CFG split x Ulysses {plan.ulysses} (NCCL all-to-all)" if plan
+                                           else "single GPU"),
+                           "cuda_graph": used_graph,
+                           "l2": "working set >> L2; no flush"},
+                "e2e": {"value": round(e2e_ms, 3), "unit": "ms/step",
+                        "h2d_bytes_per_step": host_lat.numel() * 2 + host_pe.numel() * 2 + host_ne.numel() * 2,
+                        "d2h_bytes_per_step": host_out.numel() * 2},
+                "gpu_launches": launches_per_step * args.steps,
+                "roofline": {"bound": "tensor", "kernel": "whole step (860.5 TFLOP)", "achieved": round(per_gpu_tf, 1),
+                             "peak": round(2 * bf16_tf, 1), "unit": "TFLOP/s",
+                             "frac": round(per_gpu_tf / (2 * bf16_tf), 3), "traffic": None,
+                             "peak_kind": f"2x {peak_kind} cuBLAS bf16 burst, per GPU"},
+                "cpu_baseline": None, "clocks": clocks}
+        print(json.dumps(line), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -319,6 +449,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--config", default="c4", choices=["c4", "c5"],
+                    help="c4: 1024^2 step (replicas for N>1); c5: 2048^2 step, CFG split x Ulysses for N>1")
     args = ap.parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -331,7 +463,10 @@ def main():
         torch.cuda.set_device(local_rank)
         torch.distributed.init_process_group("nccl", timeout=timedelta(seconds=300))
     try:
-        our_arm(args, rank, world, local_rank)
+        if args.config == "c5":
+            c5_arm(args, rank, world, local_rank)
+        else:
+            our_arm(args, rank, world, local_rank)
     finally:
         if world > 1:
             torch.distributed.destroy_process_group()

@@ -321,6 +321,56 @@ class MMDiT:
             c = residual(c, F.linear(ht, blk.txt_down.w, blk.txt_down.b), g2_t)
         return x, c
 
+    # ------------------------------------------------------------------ sharded block
+    def block_forward_sharded(self, blk: DualStreamBlock, x: torch.Tensor, c: torch.Tensor, mod_img, mod_txt,
+                              freqs_img, freqs_txt, plan):
+        """block_forward for one rank of a Ulysses group (see ulysses.py): x is
+        this rank's image tokens [B, S_loc, D] (freqs_img sliced to them), c the
+        replicated text stream [B, Lt, D]. Joint attention runs on this rank's
+        H/U heads over every token; the results are the unsharded block's."""
+        from .ulysses import gather_heads, head_to_seq, seq_to_head
+        cfg = self.cfg
+        B, Sl, D = x.shape
+        Lt = c.shape[1]
+        H, hd = cfg.num_attention_heads, cfg.attention_head_dim
+        U = plan.ulysses
+        Hl, h0 = H // U, plan.u * (H // U)
+        sh1_i, s1_i, g1_i, sh2_i, s2_i, g2_i = mod_img
+        sh1_t, s1_t, g1_t, sh2_t, s2_t, g2_t = mod_txt
+        if not self.quantized:
+            raise NotImplementedError("the sharded step runs the MXFP8 profiles")
+        qkv_i = blk.img_qkv.mx.matmul(layer_norm_scale_quantize(x, s1_i, self.ln, shift=sh1_i))
+        qkv_t = blk.txt_qkv.mx.matmul(layer_norm_scale_quantize(c, s1_t, self.ln, shift=sh1_t))
+        # local Q/K/V: image tokens (all heads), text tokens (all heads)
+        qi, ki, vi = (torch.empty(B, Sl, H, hd, device=x.device, dtype=torch.bfloat16) for _ in range(3))
+        qt, kt, vt = (torch.empty(B, Lt, H, hd, device=x.device, dtype=torch.bfloat16) for _ in range(3))
+        joint_qk_norm_rope(qkv_i.view(B, Sl, 3 * D), blk.norm_q, blk.norm_k, freqs_img, qi, ki, vi, 0, cfg.eps)
+        joint_qk_norm_rope(qkv_t.view(B, Lt, 3 * D), blk.norm_added_q, blk.norm_added_k, freqs_txt, qt, kt, vt, 0,
+                           cfg.eps)
+        # joint [text, image] sequence of this rank's heads
+        S = Lt + U * Sl
+        a_t = torch.empty(B, Lt, H, hd, device=x.device, dtype=torch.bfloat16)
+        a_i = torch.empty(B, Sl, H, hd, device=x.device, dtype=torch.bfloat16)
+        for b in range(B):
+            qj, kj, vj = (torch.empty(1, S, Hl, hd, device=x.device, dtype=torch.bfloat16) for _ in range(3))
+            for dst, src_t, src_i in ((qj, qt, qi), (kj, kt, ki), (vj, vt, vi)):
+                dst[0, :Lt].copy_(src_t[b, :, h0:h0 + Hl])
+                seq_to_head(src_i[b], plan, out=dst[0, Lt:])
+            o_t = torch.empty(1, Lt, Hl, hd, device=x.device, dtype=torch.bfloat16)
+            o_i = torch.empty(1, U * Sl, Hl, hd, device=x.device, dtype=torch.bfloat16)
+            self._attention(qj, kj, vj, Lt, o_t, o_i)
+            del qj, kj, vj
+            a_i[b] = head_to_seq(o_i[0], plan)
+            a_t[b] = gather_heads(o_t[0], plan)
+        del qi, ki, vi, qt, kt, vt
+        blk.img_out.mx.matmul_gate_residual(quantize(a_i.view(B * Sl, D)), g1_i, x, out=x)
+        blk.txt_out.mx.matmul_gate_residual(quantize(a_t.view(B * Lt, D)), g1_t, c, out=c)
+        hi = blk.img_up.mx.matmul_gelu_quantize(layer_norm_scale_quantize(x, s2_i, self.ln, shift=sh2_i))
+        blk.img_down.mx.matmul_gate_residual(hi, g2_i, x, out=x)
+        ht = blk.txt_up.mx.matmul_gelu_quantize(layer_norm_scale_quantize(c, s2_t, self.ln, shift=sh2_t))
+        blk.txt_down.mx.matmul_gate_residual(ht, g2_t, c, out=c)
+        return x, c
+
     # ------------------------------------------------------------------ model
     def modulations(self, temb: torch.Tensor):
         """All blocks' AdaLN vectors from one stacked GEMM: per block and stream
@@ -385,6 +435,50 @@ class MMDiT:
         comb_norm = torch.norm(comb, dim=-1, keepdim=True)
         v = comb * (cond_norm / comb_norm)
         return (latents.to(torch.float32) + (sigma_next - sigma) * v).to(latents.dtype)
+
+
+    def forward_sharded(self, hidden_local: torch.Tensor, encoder_hidden_states: torch.Tensor,
+                        timestep: torch.Tensor, img_shape, plan) -> torch.Tensor:
+        """forward() for one rank of a Ulysses group: hidden_local holds this
+        rank's image tokens [B, S_loc, 64] (plan.image_slice of the packed
+        latents), the text and timestep are the full ones (all rows share the
+        timestep); returns the velocity of this rank's tokens [B, S_loc, 64]."""
+        cfg = self.cfg
+        x = F.linear(hidden_local, *self.img_in)
+        t = timestep.to(torch.bfloat16)
+        c = F.linear(rms_norm_eager(encoder_hidden_states, self.txt_norm_w, cfg.eps), *self.txt_in)
+        temb = self.time_embed(t[:1])
+        freqs_img, freqs_txt = self.rope(img_shape, c.shape[1])
+        lo, hi = plan.image_slice(freqs_img.shape[0])
+        freqs_loc = freqs_img[lo:hi].contiguous()
+        mods = self.modulations(temb)
+        x, c = x.contiguous(), c.contiguous()
+        for blk, (m_img, m_txt) in zip(self.blocks, mods):
+            x, c = self.block_forward_sharded(blk, x, c, m_img, m_txt, freqs_loc, freqs_txt, plan)
+        emb = F.linear(F.silu(temb), *self.norm_out)
+        scale, shift = emb.chunk(2, dim=1)
+        y = layer_norm_scale(x, (1 + scale)[:, None].contiguous(), self.ln, shift=shift[:, None].contiguous())
+        return F.linear(y, *self.proj_out)
+
+    def denoise_step_sharded(self, latents_local: torch.Tensor, prompt_embeds: torch.Tensor,
+                             negative_embeds: torch.Tensor, sigma: float, sigma_next: float, img_shape, plan,
+                             cfg_scale: float = 4.0) -> torch.Tensor:
+        """denoise_step() split over ranks: CFG half 0 runs the prompt, half 1 the
+        negative prompt, each on its Ulysses group; latents_local is this rank's
+        token shard [b, S_loc, 64] and the updated shard is returned."""
+        from .ulysses import exchange_cfg
+        if not plan.cfg_split:
+            raise ValueError("denoise_step_sharded needs a plan with a CFG split")
+        b = latents_local.shape[0]
+        enc = prompt_embeds if plan.half == 0 else negative_embeds
+        t = torch.full((b,), sigma, device=latents_local.device, dtype=latents_local.dtype)
+        v = self.forward_sharded(latents_local, enc, t, img_shape, plan)
+        cond, neg = exchange_cfg(v, plan)
+        comb = neg + cfg_scale * (cond - neg)
+        cond_norm = torch.norm(cond, dim=-1, keepdim=True)
+        comb_norm = torch.norm(comb, dim=-1, keepdim=True)
+        v = comb * (cond_norm / comb_norm)
+        return (latents_local.to(torch.float32) + (sigma_next - sigma) * v).to(latents_local.dtype)
 
 
 def parameter_shapes_block_names() -> list[str]:
