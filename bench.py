@@ -160,6 +160,12 @@ def build_model(device):
     return model, cfg
 
 
+# dram__bytes_read.sum + dram__bytes_write.sum of one launch of this GEMM shape
+# (M=8192, 3072 -> 12288, GELU+MXFP8 epilogue) from `ncu --set full` on a B200:
+# 65.55 MB + 83.21 MB; algorithmic bytes are 168.7 MB (operands, scales, output).
+FFN_UP_TRAFFIC_BYTES = 148_761_344
+
+
 def gemm_roofline(model, device, peak_tflops_fp8, launches=20):
     """Live timing of the dominant kernel class -- the FFN up-projection GEMM
     (M = 8192 image rows, 3072 -> 12288, bias + GELU + MXFP8 requant epilogue),
@@ -199,7 +205,9 @@ def gemm_roofline(model, device, peak_tflops_fp8, launches=20):
         log(f"torch._scaled_mm comparison unavailable: {exc!r}")
     return {"bound": "tensor", "kernel": "mxfp8_gemm_kernel (FFN up, M=8192 N=12288 K=3072, GELU+requant)",
             "achieved": round(tflops, 1), "peak": round(peak_tflops_fp8, 1), "unit": "TFLOP/s",
-            "frac": round(tflops / peak_tflops_fp8, 3), "traffic": None, "ms_per_launch": round(ms, 4),
+            "frac": round(tflops / peak_tflops_fp8, 3), "traffic": FFN_UP_TRAFFIC_BYTES,
+            "traffic_unit": "bytes per launch (dram read + write, one ncu capture of this shape: "
+                            "bench.py --profile-case ffn_up)", "ms_per_launch": round(ms, 4),
             "cublaslt_mxfp8_tflops_same_operands": None if lib_tflops is None else round(lib_tflops, 1)}
 
 
@@ -442,6 +450,46 @@ def c5_arm(args, rank, world, local_rank):
         print(json.dumps(line), flush=True)
 
 
+def profile_case(name: str):
+    """Small fixed cases for ncu captures (no timing, no JSON line):
+    ffn_up  - the FFN-up GEMM with the GELU+MXFP8 epilogue, M=8192 (one launch)
+    attn    - Sage attention B=1, H=24, S=4352 (three calls)
+    step8   - an 8-block 1024^2 step: two warm-up steps, then one inside an NVTX
+              range named `step` (for `ncu --nvtx --nvtx-include step/`)."""
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    g = torch.Generator(device=device).manual_seed(0)
+    if name == "ffn_up":
+        from qwen_image_accel_b200.kernels.mxfp8 import quantize
+        from qwen_image_accel_b200.optimizations.mxfp8 import MXFP8Linear
+        lin = torch.nn.Linear(3072, 12288, bias=True, device=device, dtype=torch.bfloat16)
+        a = quantize(torch.randn(8192, 3072, device=device, dtype=torch.bfloat16, generator=g))
+        MXFP8Linear(lin).matmul_gelu_quantize(a)
+    elif name == "attn":
+        from qwen_image_accel_b200.optimizations.sage_attention import sage_attention
+        q, k, v = (torch.randn(1, IMG_LEN + TXT_LEN, HEADS, 128, device=device, dtype=torch.bfloat16, generator=g)
+                   for _ in range(3))
+        for _ in range(3):
+            sage_attention(q, k, v)
+    elif name == "step8":
+        from qwen_image_accel_b200.mmdit import MMDiT, MMDiTConfig, random_parameters
+        cfg = MMDiTConfig(num_layers=8)
+        model = MMDiT(cfg, random_parameters(cfg, 42, device), device=device, profile="mxfp8_sage")
+        lat = torch.randn(1, IMG_LEN, 64, device=device, dtype=torch.bfloat16, generator=g)
+        pe = torch.randn(1, TXT_LEN, TXT_DIM, device=device, dtype=torch.bfloat16, generator=g)
+        ne = torch.randn(1, TXT_LEN, TXT_DIM, device=device, dtype=torch.bfloat16, generator=g)
+        for _ in range(2):
+            model.denoise_step(lat, pe, ne, 1.0, 0.975, GRID)
+        torch.cuda.synchronize()
+        torch.cuda.nvtx.range_push("step")
+        model.denoise_step(lat, pe, ne, 1.0, 0.975, GRID)
+        torch.cuda.nvtx.range_pop()
+    else:
+        raise SystemExit(f"unknown profile case {name!r}")
+    torch.cuda.synchronize()
+    log(f"profile case {name}: done")
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -451,7 +499,12 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--config", default="c4", choices=["c4", "c5"],
                     help="c4: 1024^2 step (replicas for N>1); c5: 2048^2 step, CFG split x Ulysses for N>1")
+    ap.add_argument("--profile-case", choices=["ffn_up", "attn", "step8"],
+                    help="run one small fixed case for an ncu capture and exit")
     args = ap.parse_args()
+    if args.profile_case:
+        profile_case(args.profile_case)
+        return
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
