@@ -238,6 +238,24 @@ int qia_sage_attention_split(const void* q, const void* k, const void* v,
                              void* workspace, int64_t workspace_bytes,
                              void* stream);
 
+/* qia_sage_attention_split with MXFP8 outputs: the two streams' attention
+ * outputs bf16(O) are quantized in the attention epilogue to E4M3 rows
+ * [batch * tokens, heads * 128] (a_*: query tokens [0, split), b_*: [split,
+ * seq_q); rows padded to 128 are not written) with E8M0 scales in the 128x4
+ * blocked layout -- byte-identical to qia_mxfp8_quantize of the bf16 outputs
+ * and the A operand of the output-projection GEMMs (strides: q, k, v -- 9
+ * values; values 32-byte, scales 4-byte aligned).
+ * Replaces: the attention output -> MXFP8 quantize step of MXFusedProcessor
+ * (src/qwen_image_accel/optimizations/quantized_decode.py:31-78). */
+int qia_sage_attention_split_mx(const void* q, const void* k, const void* v,
+                                void* a_values, void* a_scales,
+                                void* b_values, void* b_scales, int64_t split,
+                                int64_t batch, int64_t seq_q, int64_t seq_kv,
+                                int64_t heads, int64_t head_dim,
+                                const int64_t* strides, float sm_scale,
+                                void* workspace, int64_t workspace_bytes,
+                                void* stream);
+
 /* The quantization half alone: Q INT8 per 32-token block, K mean-smoothed
  * INT8 per 64-token block, V FP8 per channel, written into the workspace
  * (strides: q, k, v -- 9 values).

@@ -212,6 +212,12 @@ struct AttnParams {
   int split;
   int B, H, Sq, Skv, Sq_pad, Skv_pad;
   float sm_scale_log2;      // sm_scale * log2(e)
+  // MXFP8 output (instead of bf16): the two streams as E4M3 rows [tokens, H*128]
+  // with E8M0 scales in the 128x4 blocked layout -- the next GEMM's operand
+  uint8_t* qa_values;       // null: bf16 output through out / out2
+  uint8_t* qa_scales;
+  uint8_t* qb_values;
+  uint8_t* qb_scales;
 };
 
 // Two CTAs share an SM (98 KB of shared memory and 256 TMEM columns each), so
@@ -537,6 +543,41 @@ sage_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
       const float rinv = 1.0f / dsum;
       const float* vs = p.v_scale + int64_t(bh) * kD;
       const int b = bh / p.H, h = bh % p.H;
+      if (p.qa_values) {
+        // bf16(O * rinv * v_scale) quantized to MXFP8 in place of the bf16 store:
+        // this thread's 128 channels of head h are four 32-wide MX blocks of row
+        // `row` of its stream, K index 128 h .. 128 h + 127 of the next GEMM
+        const bool in_a = q_tok < p.split;
+        const int64_t len = in_a ? p.split : p.Sq - p.split;
+        const int64_t row = int64_t(b) * len + (in_a ? q_tok : q_tok - p.split);
+        uint8_t* qv = (in_a ? p.qa_values : p.qb_values) + row * int64_t(p.H * kD) + h * kD;
+        uint8_t* qsc = in_a ? p.qa_scales : p.qb_scales;
+        uint32_t e4 = 0;
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+          uint32_t ov[32];
+          tc_ld_32x32b_x32(tmem + t_lane + kTmemO + uint32_t(c * 32), ov);
+          tc_wait_ld();
+          float f[32];
+          float amax = 0.0f;
+#pragma unroll
+          for (int e = 0; e < 32; ++e) {
+            f[e] = round_bf16(__uint_as_float(ov[e]) * rinv * __ldg(vs + c * 32 + e));
+            amax = fmaxf(amax, fabsf(f[e]));
+          }
+          const int ex = mx_exponent(amax);
+          const float inv = mx_inverse_scale(ex);
+          uint32_t w[8];
+#pragma unroll
+          for (int q4 = 0; q4 < 8; ++q4)
+            w[q4] = cvt_e4m3x4(f[4 * q4] * inv, f[4 * q4 + 1] * inv, f[4 * q4 + 2] * inv, f[4 * q4 + 3] * inv);
+          if (q_tok < p.Sq)
+            st_global_v8(qv + c * 32, make_uint4(w[0], w[1], w[2], w[3]), make_uint4(w[4], w[5], w[6], w[7]));
+          e4 |= uint32_t(ex) << (8 * c);
+        }
+        // the four scale bytes (K blocks 4h .. 4h+3) are adjacent in the blocked layout
+        if (q_tok < p.Sq) *reinterpret_cast<uint32_t*>(qsc + mx_scale_offset(row, 4 * h, p.H)) = e4;
+      } else {
       // the joint [text, image] sequence can be written back as two streams
       uint4* dst = q_tok < p.split
                        ? reinterpret_cast<uint4*>(p.out + b * p.out_stride_b + int64_t(q_tok) * p.out_stride_s +
@@ -558,6 +599,7 @@ sage_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
             dst[c * 4 + c8] = pack8(f);
           }
         }
+      }
       }
     }
   }
@@ -684,8 +726,15 @@ int quant_qkv(const void* q, Strides qs, const void* k, Strides ks, const void* 
   return check_launch("sage_quant_v_kernel");
 }
 
+struct MxOut {
+  void* a_values = nullptr;
+  void* a_scales = nullptr;
+  void* b_values = nullptr;
+  void* b_scales = nullptr;
+};
+
 int launch_attn(const Workspace& ws, void* out, Strides os, void* out2, Strides os2, int64_t split, int64_t B,
-                int64_t H, int64_t Sq, int64_t Skv, float sm_scale, cudaStream_t st) {
+                int64_t H, int64_t Sq, int64_t Skv, float sm_scale, cudaStream_t st, const MxOut& mx = MxOut()) {
   static bool attr_done[64] = {false};
   static std::mutex mu;
   int dev = 0;
@@ -718,7 +767,7 @@ int launch_attn(const Workspace& ws, void* out, Strides os, void* out2, Strides 
   p.out2_stride_b = os2.b;
   p.out2_stride_s = os2.s;
   p.out2_stride_h = os2.h;
-  p.split = out2 ? int(split) : int(Sq);
+  p.split = (out2 || mx.a_values) ? int(split) : int(Sq);
   p.B = int(B);
   p.H = int(H);
   p.Sq = int(Sq);
@@ -726,6 +775,10 @@ int launch_attn(const Workspace& ws, void* out, Strides os, void* out2, Strides 
   p.Sq_pad = int(sqp);
   p.Skv_pad = int(skp);
   p.sm_scale_log2 = sm_scale * 1.44269504088896340736f;
+  p.qa_values = (uint8_t*)mx.a_values;
+  p.qa_scales = (uint8_t*)mx.a_scales;
+  p.qb_values = (uint8_t*)mx.b_values;
+  p.qb_scales = (uint8_t*)mx.b_scales;
   sage_attn_kernel<<<dim3(unsigned(sqp / 128), unsigned(B * H)), 192, kAttnSmem, st>>>(tq, tk, tv, p,
                                                                                         device_error_word());
   return check_launch("sage_attn_kernel");
@@ -830,6 +883,45 @@ extern "C" int qia_sage_attention_split(const void* q, const void* k, const void
   rc = quant_qkv(q, sq, k, sk, v, sv, batch, heads, seq_q, seq_kv, ws, st);
   if (rc) return rc;
   return launch_attn(ws, out_a, sa, out_b, sb, split, batch, heads, seq_q, seq_kv, scale, st);
+}
+
+extern "C" int qia_sage_attention_split_mx(const void* q, const void* k, const void* v, void* a_values,
+                                           void* a_scales, void* b_values, void* b_scales, int64_t split,
+                                           int64_t batch, int64_t seq_q, int64_t seq_kv, int64_t heads,
+                                           int64_t head_dim, const int64_t* strides, float sm_scale, void* workspace,
+                                           int64_t workspace_bytes, void* stream) {
+  int rc = check_sizes(batch, heads, seq_q, seq_kv, head_dim, "qia_sage_attention_split_mx");
+  if (rc) return rc;
+  if (!strides) return set_error(QIA_ERR_INVALID, "qia_sage_attention_split_mx: null strides");
+  if (split <= 0 || split >= seq_q)
+    return set_error(QIA_ERR_INVALID, "qia_sage_attention_split_mx: 0 < split < seq_q");
+  if (!a_values || !a_scales || !b_values || !b_scales)
+    return set_error(QIA_ERR_INVALID, "qia_sage_attention_split_mx: null output");
+  if (!aligned(a_values, 32) || !aligned(b_values, 32) || !aligned(a_scales, 4) || !aligned(b_scales, 4))
+    return set_error(QIA_ERR_ALIGNMENT, "qia_sage_attention_split_mx: values 32-byte, scales 4-byte aligned");
+  const Strides sq{strides[0], strides[1], strides[2]}, sk{strides[3], strides[4], strides[5]},
+      sv{strides[6], strides[7], strides[8]};
+  if ((rc = check_nhd(q, sq, "qia_sage_attention_split_mx q")) ||
+      (rc = check_nhd(k, sk, "qia_sage_attention_split_mx k")) ||
+      (rc = check_nhd(v, sv, "qia_sage_attention_split_mx v")))
+    return rc;
+  const int64_t need = workspace_layout(batch, heads, seq_q, seq_kv, nullptr, nullptr);
+  if (!workspace || workspace_bytes < need || !aligned(workspace, 256))
+    return set_error(QIA_ERR_INVALID, "qia_sage_attention_split_mx: workspace of %lld bytes (256-aligned) needed",
+                     (long long)need);
+  Workspace ws;
+  workspace_layout(batch, heads, seq_q, seq_kv, (uint8_t*)workspace, &ws);
+  const float scale = sm_scale > 0.0f ? sm_scale : 1.0f / sqrtf(float(head_dim));
+  cudaStream_t st = as_stream(stream);
+  rc = quant_qkv(q, sq, k, sk, v, sv, batch, heads, seq_q, seq_kv, ws, st);
+  if (rc) return rc;
+  MxOut mx;
+  mx.a_values = a_values;
+  mx.a_scales = a_scales;
+  mx.b_values = b_values;
+  mx.b_scales = b_scales;
+  const Strides none{0, 0, 0};
+  return launch_attn(ws, nullptr, none, nullptr, none, split, batch, heads, seq_q, seq_kv, scale, st, mx);
 }
 
 extern "C" int qia_sage_quantize(const void* q, const void* k, const void* v, int64_t batch, int64_t seq_q,

@@ -38,6 +38,7 @@ SIGNATURES: dict[str, list] = {
     "qia_device_error": [_P],
     "qia_sage_attention": [_P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _F, _P, _I, _P],
     "qia_sage_attention_split": [_P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _P, _F, _P, _I, _P],
+    "qia_sage_attention_split_mx": [_P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _P, _F, _P, _I, _P],
     "qia_sage_attention_noalloc": [_P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _F, _P],
     "qia_sage_quantize": [_P, _P, _P, _I, _I, _I, _I, _I, _P, _P, _I, _P],
     "qia_sage_attn_quantized": [_P, _P, _I, _I, _I, _I, _I, _P, _F, _P],
@@ -91,6 +92,7 @@ def declared_symbols() -> list[str]:
 
 # kernels each entry point queues (for launch accounting); default 1
 KERNELS_PER_CALL = {"qia_sage_attention": 6, "qia_sage_attention_split": 6, "qia_sage_quantize": 5,
+                    "qia_sage_attention_split_mx": 6,
                     "qia_sage_attention_noalloc": 6,
                     "qia_device_error": 0}
 launch_count = 0

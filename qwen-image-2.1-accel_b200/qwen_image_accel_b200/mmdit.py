@@ -11,8 +11,8 @@ Per block and stream the hot path is:
   LN + (1+scale), +shift -> MXFP8         qia_ln_mod_quant
   fused Q|K|V GEMM (+bias)                 qia_mxfp8_gemm
   QK-RMSNorm + RoPE + joint [txt, img]     qia_qknorm_rope_segment (x2 streams)
-  Sage INT8/FP8 joint attention            qia_sage_attention_split
-  out-proj GEMM + gate + residual          qia_mxfp8_quantize + qia_mxfp8_gemm_gate_residual
+  Sage INT8/FP8 joint attention -> MXFP8   qia_sage_attention_split_mx
+  out-proj GEMM + gate + residual          qia_mxfp8_gemm_gate_residual
   LN + (1+scale), +shift -> MXFP8          qia_ln_mod_quant
   FFN up GEMM + bias + GELU -> MXFP8       qia_mxfp8_gemm_gelu_quant
   FFN down GEMM + gate + residual          qia_mxfp8_gemm_gate_residual
@@ -41,7 +41,7 @@ from .kernels.epilogue import layer_norm_scale_quantize
 from .kernels.layernorm import layer_norm_scale
 from .kernels.mxfp8 import quantize
 from .optimizations.mxfp8 import MXFP8Linear
-from .optimizations.sage_attention import sage_attention_split, workspace_bytes
+from .optimizations.sage_attention import sage_attention_split, sage_attention_split_quantized, workspace_bytes
 from .kernels.bf16 import gelu_tanh
 from .profiles import get_profile
 
@@ -296,13 +296,23 @@ class MMDiT:
         joint_qk_norm_rope(qkv_t.view(B, Lt, 3 * D), blk.norm_added_q, blk.norm_added_k, freqs_txt, q, k, v, 0,
                            cfg.eps)
         joint_qk_norm_rope(qkv_i.view(B, Li, 3 * D), blk.norm_q, blk.norm_k, freqs_img, q, k, v, Lt, cfg.eps)
-        # ---- joint attention, written back per stream
-        a_t = torch.empty(B, Lt, H, hd, device=x.device, dtype=torch.bfloat16)
-        a_i = torch.empty(B, Li, H, hd, device=x.device, dtype=torch.bfloat16)
-        self._attention(q, k, v, Lt, a_t, a_i)
-        del q, k, v
+        # ---- joint attention, written back per stream (as MXFP8 straight from
+        # the attention epilogue when the output projections are MXFP8 GEMMs)
+        if self.quantized and self.sage:
+            qa_t, qa_i = sage_attention_split_quantized(q, k, v, Lt, workspace=self._attn_ws(q, k))
+            del q, k, v
+            blk.img_out.mx.matmul_gate_residual(qa_i, g1_i, x, out=x)
+            blk.txt_out.mx.matmul_gate_residual(qa_t, g1_t, c, out=c)
+            del qa_t, qa_i
+        else:
+            a_t = torch.empty(B, Lt, H, hd, device=x.device, dtype=torch.bfloat16)
+            a_i = torch.empty(B, Li, H, hd, device=x.device, dtype=torch.bfloat16)
+            self._attention(q, k, v, Lt, a_t, a_i)
+            del q, k, v
         # ---- output projections + gated residual (in place on the streams)
-        if self.quantized:
+        if self.quantized and self.sage:
+            pass
+        elif self.quantized:
             blk.img_out.mx.matmul_gate_residual(quantize(a_i.view(B * Li, D)), g1_i, x, out=x)
             blk.txt_out.mx.matmul_gate_residual(quantize(a_t.view(B * Lt, D)), g1_t, c, out=c)
         else:

@@ -108,6 +108,32 @@ def sage_attention_split(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, spli
               workspace.numel(), _lib.stream(q.device))
 
 
+def sage_attention_split_quantized(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, split: int,
+                                   sm_scale: float | None = None, workspace: torch.Tensor | None = None):
+    """sage_attention_split whose two outputs come back as MXFP8 activations
+    (Quantized, rows = batch * stream tokens, K = heads * 128) ready for the
+    output projections: byte-identical to quantize() of the bf16 outputs."""
+    from ..kernels.mxfp8 import empty_quantized
+    _check_settings()
+    _validate(q, k, v)
+    b, sq, h, d = q.shape
+    skv = k.shape[1]
+    need = workspace_bytes(b, h, sq, skv)
+    if workspace is None or workspace.numel() < need:
+        workspace = torch.empty(need, device=q.device, dtype=torch.uint8)
+    qa = empty_quantized(b * split, h * d, q.device)
+    qb = empty_quantized(b * (sq - split), h * d, q.device)
+    for t in (qa, qb):             # rows past the live ones (padding to 128) stay zero
+        if t.values.shape[0] > t.rows:
+            t.values[t.rows:].view(torch.uint8).zero_()
+            t.scales.view(torch.uint8).zero_()
+    _lib.call("qia_sage_attention_split_mx", _lib.ptr(q), _lib.ptr(k), _lib.ptr(v), _lib.ptr(qa.values),
+              _lib.ptr(qa.scales), _lib.ptr(qb.values), _lib.ptr(qb.scales), split, b, sq, skv, h, d,
+              _strides(q, k, v), float(sm_scale or 0.0), _lib.ptr(workspace), workspace.numel(),
+              _lib.stream(q.device))
+    return qa, qb
+
+
 def sage_quantize(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor) -> dict:
     """Run only the quantization half; returns the workspace views."""
     _validate(q, k, v)

@@ -113,3 +113,28 @@ def test_sage_decode_custom_op():
     a = torch.ops.qw21.sage_decode(q, k, v)
     b = sa.sage_attention(q, k, v)
     assert torch.equal(a, b)
+
+
+@pytest.mark.parametrize("b,lt,li,h", [(2, 256, 4096, 24), (1, 40, 192, 4), (2, 77, 300, 2)])
+def test_split_attention_mxfp8_outputs_match_quantize(b, lt, li, h):
+    """The MXFP8 epilogue of the split attention writes exactly quantize() of
+    the bf16 outputs of the bf16 split attention (codes and scales), including
+    rows padded to 128 (zero)."""
+    from qwen_image_accel_b200.kernels.mxfp8 import quantize
+    from qwen_image_accel_b200.optimizations.sage_attention import (sage_attention_split,
+                                                                    sage_attention_split_quantized)
+    g = torch.Generator(device="cuda").manual_seed(21)
+    s = lt + li
+    q, k, v = (torch.randn(b, s, h, 128, device="cuda", dtype=torch.bfloat16, generator=g) for _ in range(3))
+    out_t = torch.empty(b, lt, h, 128, device="cuda", dtype=torch.bfloat16)
+    out_i = torch.empty(b, li, h, 128, device="cuda", dtype=torch.bfloat16)
+    sage_attention_split(q, k, v, lt, out_t, out_i)
+    qa, qb = sage_attention_split_quantized(q, k, v, lt)
+    torch.cuda.synchronize()
+    from qwen_image_accel_b200 import _lib
+    assert _lib.device_error() == 0
+    for got, ref_bf16 in ((qa, out_t), (qb, out_i)):
+        ref = quantize(ref_bf16.reshape(-1, h * 128))
+        assert got.rows == ref.rows and got.values.shape == ref.values.shape
+        assert torch.equal(got.values.view(torch.uint8), ref.values.view(torch.uint8))
+        assert torch.equal(got.scales.view(torch.uint8), ref.scales.view(torch.uint8))
