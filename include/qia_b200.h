@@ -265,6 +265,45 @@ int qia_sage_quantize(const void* q, const void* k, const void* v,
                       int64_t heads, int64_t head_dim, const int64_t* strides,
                       void* workspace, int64_t workspace_bytes, void* stream);
 
+/* qia_sage_quantize for the dual-stream block's joint [stream 0, stream 1]
+ * sequence, reading Q/K/V straight from the two streams' fused q|k|v
+ * projection outputs (rows b*len_i + s, leading dimension ld_i elements; q at
+ * column 0, k at heads*128, v at 2*heads*128) and applying each stream's
+ * per-head RMSNorm (weight_q_i / weight_k_i, eps) and RoPE (freqs_i: float32
+ * [len_i, 64, 2]) on load, with the roundings of qia_qknorm_rope_segment: the
+ * workspace is byte-identical to qia_qknorm_rope_segment on both streams
+ * followed by qia_sage_quantize, without the bf16 Q/K/V in memory.
+ * Replaces: the norm + RoPE + cat of QwenDoubleStreamAttnProcessor2_0
+ * (WHL:diffusers/models/transformers/transformer_qwenimage.py:540-575) fused
+ * with the quantization half of the reference's decode attention
+ * (src/qwen_image_accel/optimizations/sage_attention.py:19-25). */
+int qia_sage_quantize_joint(const void* qkv0, int64_t ld0, const void* qkv1,
+                            int64_t ld1, const void* weight_q0,
+                            const void* weight_k0, const void* weight_q1,
+                            const void* weight_k1, const void* freqs0,
+                            const void* freqs1, int64_t batch, int64_t len0,
+                            int64_t len1, int64_t heads, int64_t head_dim,
+                            float eps, void* workspace,
+                            int64_t workspace_bytes, void* stream);
+
+/* qia_sage_quantize_joint followed by the attention with MXFP8 outputs per
+ * stream (as qia_sage_attention_split_mx with split = len0): stream 0's rows
+ * to a_values/a_scales, stream 1's to b_values/b_scales.
+ * Replaces: the joint attention of QwenDoubleStreamAttnProcessor2_0
+ * (WHL:diffusers/models/transformers/transformer_qwenimage.py:540-600) with
+ * the reference's Sage decode attention
+ * (src/qwen_image_accel/optimizations/quantized_decode.py:31-78). */
+int qia_sage_attention_joint_mx(const void* qkv0, int64_t ld0, const void* qkv1,
+                                int64_t ld1, const void* weight_q0,
+                                const void* weight_k0, const void* weight_q1,
+                                const void* weight_k1, const void* freqs0,
+                                const void* freqs1, void* a_values,
+                                void* a_scales, void* b_values, void* b_scales,
+                                int64_t batch, int64_t len0, int64_t len1,
+                                int64_t heads, int64_t head_dim, float eps,
+                                float sm_scale, void* workspace,
+                                int64_t workspace_bytes, void* stream);
+
 /* The attention half alone, on a workspace filled by qia_sage_quantize
  * (out_strides: 3 values).
  * Replaces: qk_int8_sv_f8_accum_f32_fuse_v_scale_attn_inst_buf

@@ -326,14 +326,18 @@ def sage_quant_q(q: np.ndarray, blk: int = 32):
 def sage_k_mean(k: np.ndarray) -> np.ndarray:
     """Per-(batch, head, channel) mean of K over the sequence, rounded to bf16
     (SAGE:sageattention/core.py:773, k.mean(dim=seq) on a bf16 tensor), in the
-    kernel's order: fp32 sums over 128-row tiles (rows in order), tile sums
-    added in order, times fp32(1/S)."""
+    kernel's order: per 64-row tile, sixteen fp32 row-group sums (rows g,
+    g+16, g+32, g+48 of the tile in order), added in group order; tile sums
+    added in order; times fp32(1/S)."""
     b, s, h, d = k.shape
     total = np.zeros((b, h, d), np.float32)
-    for t0 in range(0, s, 128):
+    for t0 in range(0, s, 64):
         part = np.zeros((b, h, d), np.float32)
-        for i in range(t0, min(s, t0 + 128)):
-            part += k[:, i].astype(np.float32)
+        for g in range(16):
+            grp = np.zeros((b, h, d), np.float32)
+            for i in range(t0 + g, min(s, t0 + 64), 16):
+                grp += k[:, i].astype(np.float32)
+            part += grp
         total += part
     mean = (total * np.float32(1.0 / s)).astype(np.float32)
     return bf16_bits_to_f32(f32_to_bf16_bits(mean))

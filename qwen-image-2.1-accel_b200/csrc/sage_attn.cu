@@ -27,12 +27,16 @@
 // Device layouts written by the quantization kernels here (head-major, rows
 // padded to a multiple of 128 with zeros): q8/k8 int8 [B*H, S_pad, 128],
 // v8 e4m3 [B*H, S_pad, 128], q_scale f32 [B*H, S_pad/32], k_scale f32
-// [B*H, S_pad/64], v_scale f32 [B*H, 128], k_mean bf16 [B*H, 128].
+// [B*H, S_pad/64], v_scale f32 [B*H, 128], k_mean bf16 [B*H, 128]; scratch:
+// v_recp f32 [B*H, 128], per-64-row-tile K sums and |V| maxima f32
+// [B*H, S_pad/64, 128] each, normalised K bf16 [B*H, S_pad, 128] (joint
+// entry points only).
 #include <cudaTypedefs.h>
 
 #include <climits>
 #include <mutex>
 
+#include "qk_norm_rope.cuh"
 #include "sm100.cuh"
 
 namespace qia {
@@ -45,121 +49,392 @@ constexpr int kVStages = 2;
 constexpr float kFp8Offset = 8.807f;  // log2(448): P = 2^(s - m) <= 448
 
 // ------------------------------------------------------------------ quantizers
-// Per (b, h, 128-row tile): partial column sums of K (sequential over the
-// tile's rows) and partial column maxima of |V|. Thread d owns channel d.
-__global__ void __launch_bounds__(128) sage_kv_partials_kernel(
-    const __nv_bfloat16* __restrict__ k, int64_t k_sb, int64_t k_ss, int64_t k_sh,
-    const __nv_bfloat16* __restrict__ v, int64_t v_sb, int64_t v_ss, int64_t v_sh, int S, int H,
-    float* __restrict__ k_part, float* __restrict__ v_part) {
-  const int bh = blockIdx.x, b = bh / H, h = bh % H, tile = blockIdx.y, d = threadIdx.x;
-  const int r0 = tile * 128, r1 = min(S, r0 + 128);
-  const __nv_bfloat16* kp = k + b * k_sb + h * k_sh + d;
-  const __nv_bfloat16* vp = v + b * v_sb + h * v_sh + d;
-  float sum = 0.0f, amax = 0.0f;
-#pragma unroll 8
-  for (int r = r0; r < r1; ++r) {
-    sum += __bfloat162float(kp[int64_t(r) * k_ss]);
-    amax = fmaxf(amax, fabsf(__bfloat162float(vp[int64_t(r) * v_ss])));
+// Three launches fill the workspace.
+//  1. sage_quant_q_stats_kernel, per (b, h, 64-row tile), 256 threads: Q codes
+//     and scales; per tile the column sums of K and column maxima of |V|; for
+//     a source that normalises Q/K on load, also the normalised K (bf16, in
+//     the workspace) for launch 3. Sixteen lanes per row (eight channels
+//     each), sixteen rows per pass, four passes (row p*16 + t/16 of the tile in
+//     pass p). Every thread first stages all the 16-byte pieces it will read
+//     (its Q/K/V row pieces and, with RoPE, its 32 bytes of each row's RoPE
+//     table) into shared memory with cp.async, so the tile's loads are all in
+//     flight at once, then reads back only its own pieces. A thread sums its
+//     four K rows in pass order from 0.0; the sixteen row-group sums are then
+//     added in group order (0.0 + g0 + ... + g15).
+//  2. sage_quant_finalize_kernel, per (b, h): the tile partials reduced in
+//     tile order: k_mean = bf16(sum * (1/S)); v_scale = amax/448 and
+//     v_recp = 448/amax (0 for an all-zero channel).
+//  3. sage_quant_kv_kernel, per (b, h, 64-row tile) and z (0: K, 1: V): K
+//     codes of k - k_mean in one 64-row block, or V E4M3 codes of
+//     v * 448/amax, staged the same way.
+// INT8 blocks: scale = amax/127 (amax floored at 1e-7), codes =
+// rint_sat(x * 127/amax); rows past S are zeros. The rows come from a source:
+// strided [B, S, H, 128] bf16 tensors (PlainQKV), or the fused q|k|v
+// projection outputs of the two streams of the joint [text, image] sequence
+// (JointQKV), whose Q and K are normalised (per-head RMSNorm) and rotated
+// (RoPE) on load with the roundings of the separate attention-input kernel.
+constexpr int kQTile = 64;
+
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem, bool valid) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(smem)), "l"(gmem),
+               "r"(valid ? 16 : 0)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
+// Q, K, V rows of [B, S, H, 128] bf16 tensors with element strides (b, s, h).
+struct PlainQKV {
+  static constexpr bool kNormRope = false;
+  const __nv_bfloat16* x[3];
+  int64_t sb[3], ss[3], sh[3];
+  float eps;
+  __device__ __forceinline__ const __nv_bfloat16* row(int c, int b, int h, int s) const {
+    return x[c] + b * sb[c] + int64_t(s) * ss[c] + h * sh[c];
   }
-  const int64_t o = (int64_t(bh) * gridDim.y + tile) * kD + d;
-  k_part[o] = sum;
-  v_part[o] = amax;
+  // The K rows the K-quantization launch reads (no normalised copy is kept).
+  __device__ __forceinline__ const __nv_bfloat16* krow(int b, int h, int s) const { return row(1, b, h, s); }
+  __device__ __forceinline__ __nv_bfloat16* knrow(int, int, int) const { return nullptr; }
+  __device__ __forceinline__ const float* freqs(int) const { return nullptr; }
+  __device__ __forceinline__ bool first(int) const { return true; }
+  __device__ __forceinline__ uint4 weight(int, int) const { return make_uint4(0u, 0u, 0u, 0u); }
+};
+
+// The joint sequence: tokens [0, len0) from stream 0's projection output (rows
+// b*len0 + s, leading dimension ld0; q at column 0, k at H*128, v at 2*H*128),
+// tokens [len0, len0 + len1) from stream 1's; each stream's norm weights
+// (wq*, wk*) and RoPE table (f*: [len, 64] (cos, sin) pairs). kn: the
+// normalised K, [B*H, S_pad, 128] bf16, written by launch 1.
+struct JointQKV {
+  static constexpr bool kNormRope = true;
+  const __nv_bfloat16* qkv0;
+  const __nv_bfloat16* qkv1;
+  int64_t ld0, ld1;
+  const __nv_bfloat16* wq0;
+  const __nv_bfloat16* wk0;
+  const __nv_bfloat16* wq1;
+  const __nv_bfloat16* wk1;
+  const float* f0;
+  const float* f1;
+  __nv_bfloat16* kn;
+  int len0, len1, H, S_pad;
+  float eps;
+  __device__ __forceinline__ const __nv_bfloat16* row(int c, int b, int h, int s) const {
+    const bool first = s < len0;
+    return (first ? qkv0 + (int64_t(b) * len0 + s) * ld0 : qkv1 + (int64_t(b) * len1 + (s - len0)) * ld1) +
+           (int64_t(c) * H + h) * kD;
+  }
+  __device__ __forceinline__ __nv_bfloat16* knrow(int b, int h, int s) const {
+    return kn + ((int64_t(b) * H + h) * S_pad + s) * kD;
+  }
+  __device__ __forceinline__ const __nv_bfloat16* krow(int b, int h, int s) const { return knrow(b, h, s); }
+  __device__ __forceinline__ const float* freqs(int s) const {
+    return s < len0 ? f0 + int64_t(s) * kD : f1 + int64_t(s - len0) * kD;
+  }
+  __device__ __forceinline__ bool first(int s) const { return s < len0; }
+  // This lane's eight weights of component c (0 = q, 1 = k) of stream i.
+  __device__ __forceinline__ uint4 weight(int c, int i) const {
+    const __nv_bfloat16* w = c == 0 ? (i == 0 ? wq0 : wq1) : (i == 0 ? wk0 : wk1);
+    return __ldg(reinterpret_cast<const uint4*>(w + (threadIdx.x & 15) * 8));
+  }
+};
+
+__device__ __forceinline__ uint32_t cvt_bf16x2(float lo, float hi) {
+  uint32_t r;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+// Product of two bf16 pairs, rounded once to bf16: the exact product of two
+// bf16 values fits an fp32 mantissa, so this equals bf16(fp32(a) * fp32(b))
+// (for products down to 2^-135 in magnitude; smaller ones are zero or the
+// smallest bf16 subnormal either way).
+__device__ __forceinline__ uint32_t mul_bf16x2(uint32_t a, uint32_t b) {
+  uint32_t r;
+  asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+__device__ __forceinline__ uint32_t max_bf16x2(uint32_t a, uint32_t b) {
+  uint32_t r;
+  asm("max.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+__device__ __forceinline__ uint32_t abs_bf16x2(uint32_t a) { return a & 0x7fff7fffu; }
+
+// max(floor, |x_i|) over the eight bf16 values of a row piece.
+__device__ __forceinline__ float piece_amax(const uint4& x, float floor) {
+  const uint32_t m = max_bf16x2(max_bf16x2(abs_bf16x2(x.x), abs_bf16x2(x.y)),
+                                max_bf16x2(abs_bf16x2(x.z), abs_bf16x2(x.w)));
+  return fmaxf(floor, fmaxf(bf16_lo(m), bf16_hi(m)));
 }
 
-// Per (b, h): k_mean = bf16(sum of the tile partials in order * (1/S));
-// V scale = amax/448 and its reciprocal 448/amax (0 for an all-zero channel).
-__global__ void __launch_bounds__(128) sage_kv_finalize_kernel(const float* __restrict__ k_part,
-                                                               const float* __restrict__ v_part, int tiles, int S,
-                                                               __nv_bfloat16* __restrict__ k_mean,
-                                                               float* __restrict__ v_scale,
-                                                               float* __restrict__ v_recp) {
+// RMSNorm (weight w, eps) + RoPE (cs = four (cos, sin) pairs) of a bf16 row
+// piece, returned as bf16: the attention-input kernel's values
+// (bf16(bf16(x * r) * w), then the complex product, then bf16), with the
+// weight product as one bf16x2 multiply per pair.
+__device__ __forceinline__ uint4 norm_rope_piece(const uint4& x, const uint4& w, const float (&cs)[8], float eps) {
+  float f[8];
+  unpack8(x, f);
+  const float r = qkrows::rms_inverse(f, eps);
+  const uint32_t wv[4] = {w.x, w.y, w.z, w.w};
+  uint32_t o[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const uint32_t y = mul_bf16x2(cvt_bf16x2(__fmul_rn(f[2 * i], r), __fmul_rn(f[2 * i + 1], r)), wv[i]);
+    const float re = bf16_lo(y), im = bf16_hi(y), c = cs[2 * i], s = cs[2 * i + 1];
+    o[i] = cvt_bf16x2(__fmaf_rn(re, c, -__fmul_rn(im, s)), __fmaf_rn(im, c, __fmul_rn(re, s)));
+  }
+  return make_uint4(o[0], o[1], o[2], o[3]);
+}
+
+__device__ __forceinline__ void load_cs(const uint4* sf0, const uint4* sf1, float (&cs)[8]) {
+  const uint4 a = *sf0, b = *sf1;
+  cs[0] = __uint_as_float(a.x); cs[1] = __uint_as_float(a.y); cs[2] = __uint_as_float(a.z);
+  cs[3] = __uint_as_float(a.w); cs[4] = __uint_as_float(b.x); cs[5] = __uint_as_float(b.y);
+  cs[6] = __uint_as_float(b.z); cs[7] = __uint_as_float(b.w);
+}
+
+// Maximum over the row's 16 lanes (xor shuffles stay inside the half-warp),
+// and over the whole warp (both rows of a pass).
+__device__ __forceinline__ float row_amax(float v) {
+#pragma unroll
+  for (int o = 8; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+__device__ __forceinline__ float pair_amax(float v) { return fmaxf(v, __shfl_xor_sync(0xffffffffu, v, 16)); }
+
+// INT8 codes rint_sat(x * inv) of a bf16 row piece (minus mf when SUB_MEAN),
+// four codes per 32-bit word.
+template <bool SUB_MEAN>
+__device__ __forceinline__ uint2 int8_piece(const uint4& x, const float (&mf)[8], float inv) {
+  float f[8];
+  unpack8(x, f);
+  int c[8];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
+    const float v = SUB_MEAN ? f[e] - mf[e] : f[e];
+    asm("cvt.rni.sat.s8.f32 %0, %1;" : "=r"(c[e]) : "f"(v * inv));
+  }
+  const uint32_t lo = __byte_perm(__byte_perm(c[0], c[1], 0x0040), __byte_perm(c[2], c[3], 0x0040), 0x5410);
+  const uint32_t hi = __byte_perm(__byte_perm(c[4], c[5], 0x0040), __byte_perm(c[6], c[7], 0x0040), 0x5410);
+  return make_uint2(lo, hi);
+}
+
+// Dynamic shared memory of the staged kernels (16-byte slots, one per thread).
+template <class Src>
+constexpr int q_stats_smem() {
+  return (3 + (Src::kNormRope ? 2 : 0)) * 4 * 256 * 16;
+}
+constexpr int kKvSmem = 4 * 256 * 16;
+
+// Grid (B*H, max(Sq_pad/64, ceil(Skv/64))), 256 threads.
+template <class Src>
+__global__ void __launch_bounds__(256, 2) sage_quant_q_stats_kernel(Src src, int Sq, int Sq_pad, int Skv, int H,
+                                                                    int kv_tiles, int part_stride,
+                                                                    int8_t* __restrict__ q8,
+                                                                    float* __restrict__ q_scale,
+                                                                    float* __restrict__ k_part,
+                                                                    float* __restrict__ v_part) {
+  extern __shared__ __align__(16) uint4 q_stage[];
+  __shared__ __align__(16) float s_k[16][kD];
+  __shared__ __align__(16) float s_v[16][kD];
+  __shared__ __align__(16) float s_wmax[2][8];
+  const int bh = blockIdx.x, b = bh / H, h = bh % H, tile = blockIdx.y, t = threadIdx.x;
+  const int cg = t & 15, rs = t >> 4, warp = t >> 5;
+  const bool do_q = tile * kQTile < Sq_pad, do_kv = tile < kv_tiles;
+  // slots: x[c][p][t] (c = q, k, v), then the rows' RoPE pieces f[half][p][t]
+  // (Q and K of a row share them; a source with RoPE has Sq == Skv)
+  auto sx = [&](int c, int p) { return q_stage + (c * 4 + p) * 256 + t; };
+  auto sf = [&](int half, int p) { return q_stage + 3 * 4 * 256 + (half * 4 + p) * 256 + t; };
+#pragma unroll
+  for (int p = 0; p < 4; ++p) {
+    const int row = tile * kQTile + p * 16 + rs;
+    const bool vq = row < Sq, vkv = row < Skv;
+    cp_async16(sx(0, p), (vq ? src.row(0, b, h, row) : src.row(0, 0, 0, 0)) + cg * 8, vq);
+    cp_async16(sx(1, p), (vkv ? src.row(1, b, h, row) : src.row(1, 0, 0, 0)) + cg * 8, vkv);
+    cp_async16(sx(2, p), (vkv ? src.row(2, b, h, row) : src.row(2, 0, 0, 0)) + cg * 8, vkv);
+    if (Src::kNormRope) {
+      const float* f = (vq ? src.freqs(row) : src.freqs(0)) + cg * 8;
+      cp_async16(sf(0, p), f, vq);
+      cp_async16(sf(1, p), f + 4, vq);
+    }
+  }
+  uint4 wq[2], wk[2];
+  if (Src::kNormRope) {
+    wq[0] = src.weight(0, 0);
+    wq[1] = src.weight(0, 1);
+    wk[0] = src.weight(1, 0);
+    wk[1] = src.weight(1, 1);
+  }
+  cp_async_wait_all();
+  uint4 qx[4];
+  float rmax[4];
+  float ks[8];
+  uint32_t vm2[4] = {0u, 0u, 0u, 0u};
+#pragma unroll
+  for (int e = 0; e < 8; ++e) ks[e] = 0.0f;
+#pragma unroll
+  for (int p = 0; p < 4; ++p) {
+    const int row = tile * kQTile + p * 16 + rs;
+    float cs[8];
+    const bool first = src.first(row);
+    if (Src::kNormRope) load_cs(sf(0, p), sf(1, p), cs);
+    float amax = 1e-7f;
+    qx[p] = make_uint4(0u, 0u, 0u, 0u);
+    if (row < Sq) {
+      qx[p] = *sx(0, p);
+      if (Src::kNormRope) qx[p] = norm_rope_piece(qx[p], first ? wq[0] : wq[1], cs, src.eps);
+      amax = piece_amax(qx[p], amax);
+    }
+    if (row < Skv) {
+      uint4 y = *sx(1, p);
+      if (Src::kNormRope) {
+        y = norm_rope_piece(y, first ? wk[0] : wk[1], cs, src.eps);
+        *reinterpret_cast<uint4*>(src.knrow(b, h, row) + cg * 8) = y;
+      }
+      float f[8];
+      unpack8(y, f);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) ks[e] += f[e];
+      const uint4 v = *sx(2, p);
+      vm2[0] = max_bf16x2(vm2[0], abs_bf16x2(v.x));
+      vm2[1] = max_bf16x2(vm2[1], abs_bf16x2(v.y));
+      vm2[2] = max_bf16x2(vm2[2], abs_bf16x2(v.z));
+      vm2[3] = max_bf16x2(vm2[3], abs_bf16x2(v.w));
+    }
+    rmax[p] = row_amax(amax);
+  }
+  // 32-row Q blocks: passes {0, 1} and {2, 3}; per warp, then across warps
+  const float w0 = pair_amax(fmaxf(rmax[0], rmax[1])), w1 = pair_amax(fmaxf(rmax[2], rmax[3]));
+  if ((t & 31) == 0) {
+    s_wmax[0][warp] = w0;
+    s_wmax[1][warp] = w1;
+  }
+  float4* sk = reinterpret_cast<float4*>(&s_k[rs][cg * 8]);
+  float4* sv = reinterpret_cast<float4*>(&s_v[rs][cg * 8]);
+  sk[0] = make_float4(ks[0], ks[1], ks[2], ks[3]);
+  sk[1] = make_float4(ks[4], ks[5], ks[6], ks[7]);
+  sv[0] = make_float4(bf16_lo(vm2[0]), bf16_hi(vm2[0]), bf16_lo(vm2[1]), bf16_hi(vm2[1]));
+  sv[1] = make_float4(bf16_lo(vm2[2]), bf16_hi(vm2[2]), bf16_lo(vm2[3]), bf16_hi(vm2[3]));
+  __syncthreads();
+  if (t < kD && do_kv) {
+    float sum = 0.0f, amax = 0.0f;
+#pragma unroll
+    for (int g = 0; g < 16; ++g) {
+      sum += s_k[g][t];
+      amax = fmaxf(amax, s_v[g][t]);
+    }
+    const int64_t o = (int64_t(bh) * part_stride + tile) * kD + t;
+    k_part[o] = sum;
+    v_part[o] = amax;
+  }
+  if (!do_q) return;
+  float bm[2];
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const float4 a = *reinterpret_cast<const float4*>(&s_wmax[i][0]);
+    const float4 c = *reinterpret_cast<const float4*>(&s_wmax[i][4]);
+    bm[i] = fmaxf(fmaxf(fmaxf(a.x, a.y), fmaxf(a.z, a.w)), fmaxf(fmaxf(c.x, c.y), fmaxf(c.z, c.w)));
+  }
+  if (t < 2) q_scale[int64_t(bh) * (Sq_pad / 32) + tile * 2 + t] = __fdiv_rn(t == 0 ? bm[0] : bm[1], 127.0f);
+  const float inv0 = __fdiv_rn(127.0f, bm[0]), inv1 = __fdiv_rn(127.0f, bm[1]);
+  const float none[8] = {};
+  int8_t* dst = q8 + (int64_t(bh) * Sq_pad + tile * kQTile) * kD + cg * 8;
+#pragma unroll
+  for (int p = 0; p < 4; ++p) {
+    const int r = p * 16 + rs;
+    const uint2 code = tile * kQTile + r < Sq ? int8_piece<false>(qx[p], none, p < 2 ? inv0 : inv1)
+                                              : make_uint2(0u, 0u);
+    *reinterpret_cast<uint2*>(dst + int64_t(r) * kD) = code;
+  }
+}
+
+// Grid (B*H), 128 threads: the tile partials reduced in tile order.
+__global__ void __launch_bounds__(128) sage_quant_finalize_kernel(const float* __restrict__ k_part,
+                                                                  const float* __restrict__ v_part, int tiles,
+                                                                  int part_stride, int S,
+                                                                  __nv_bfloat16* __restrict__ k_mean,
+                                                                  float* __restrict__ v_scale,
+                                                                  float* __restrict__ v_recp) {
   const int bh = blockIdx.x, d = threadIdx.x;
+  const int64_t base = int64_t(bh) * part_stride * kD + d;
   float sum = 0.0f, amax = 0.0f;
-  for (int t = 0; t < tiles; ++t) {
-    const int64_t o = (int64_t(bh) * tiles + t) * kD + d;
-    sum += k_part[o];
-    amax = fmaxf(amax, v_part[o]);
+#pragma unroll 8
+  for (int i = 0; i < tiles; ++i) {
+    sum += k_part[base + int64_t(i) * kD];
+    amax = fmaxf(amax, v_part[base + int64_t(i) * kD]);
   }
   k_mean[int64_t(bh) * kD + d] = __float2bfloat16_rn(sum * (1.0f / float(S)));
   v_scale[int64_t(bh) * kD + d] = amax / 448.0f;
   v_recp[int64_t(bh) * kD + d] = amax > 0.0f ? 448.0f / amax : 0.0f;
 }
 
-// One warp per 32-row block (Q), or two warps per 64-row block (K, with the
-// mean subtracted). Each thread owns one token row of 128 values.
-template <int BLK, bool SUB_MEAN>
-__global__ void __launch_bounds__(128) sage_quant_int8_kernel(const __nv_bfloat16* __restrict__ x, int64_t stride_b,
-                                                              int64_t stride_s, int64_t stride_h, int S, int S_pad,
-                                                              int H, const __nv_bfloat16* __restrict__ mean,
-                                                              int8_t* __restrict__ out, float* __restrict__ scale) {
-  __shared__ float s_amax[4];
-  const int bh = blockIdx.x, b = bh / H, h = bh % H;
-  const int row = blockIdx.y * 128 + threadIdx.x;  // token index within the padded sequence
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  float v[kD];
-  if (row < S) {
-    const uint4* src = reinterpret_cast<const uint4*>(x + b * stride_b + int64_t(row) * stride_s + h * stride_h);
+// Grid (B*H, S_pad/64, 2), 256 threads. z = 0: K codes of k - k_mean (one
+// 64-row block per tile); z = 1: V codes of v * 448/amax.
+template <class Src>
+__global__ void __launch_bounds__(256, 4) sage_quant_kv_kernel(Src src, int S, int S_pad, int H,
+                                                               const __nv_bfloat16* __restrict__ k_mean,
+                                                               const float* __restrict__ v_recp,
+                                                               int8_t* __restrict__ k8, float* __restrict__ k_scale,
+                                                               uint8_t* __restrict__ v8) {
+  extern __shared__ __align__(16) uint4 kv_stage[];
+  __shared__ __align__(16) float s_wmax[8];
+  const int bh = blockIdx.x, b = bh / H, h = bh % H, tile = blockIdx.y, t = threadIdx.x;
+  const int cg = t & 15, rs = t >> 4, warp = t >> 5;
+  const bool is_k = blockIdx.z == 0;
 #pragma unroll
-    for (int i = 0; i < 16; ++i) unpack8(__ldg(src + i), &v[i * 8]);
-    if (SUB_MEAN) {
-      const uint4* mp = reinterpret_cast<const uint4*>(mean + int64_t(bh) * kD);
-#pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        float m8[8];
-        unpack8(__ldg(mp + i), m8);
-#pragma unroll
-        for (int j = 0; j < 8; ++j) v[i * 8 + j] -= m8[j];
-      }
-    }
+  for (int p = 0; p < 4; ++p) {
+    const int row = tile * kQTile + p * 16 + rs;
+    const bool valid = row < S;
+    const __nv_bfloat16* g = is_k ? (valid ? src.krow(b, h, row) : src.krow(0, 0, 0))
+                                  : (valid ? src.row(2, b, h, row) : src.row(2, 0, 0, 0));
+    cp_async16(kv_stage + p * 256 + t, g + cg * 8, valid);
+  }
+  float cc[8];
+  if (is_k) {
+    unpack8(__ldg(reinterpret_cast<const uint4*>(k_mean + int64_t(bh) * kD + cg * 8)), cc);
   } else {
-#pragma unroll
-    for (int i = 0; i < kD; ++i) v[i] = 0.0f;
+    const float4 a = __ldg(reinterpret_cast<const float4*>(v_recp + int64_t(bh) * kD + cg * 8));
+    const float4 c = __ldg(reinterpret_cast<const float4*>(v_recp + int64_t(bh) * kD + cg * 8 + 4));
+    cc[0] = a.x; cc[1] = a.y; cc[2] = a.z; cc[3] = a.w; cc[4] = c.x; cc[5] = c.y; cc[6] = c.z; cc[7] = c.w;
   }
-  float amax = 1e-7f;
+  cp_async_wait_all();
+  if (is_k) {
+    uint4 kx[4];
+    float rmax = 1e-7f;
 #pragma unroll
-  for (int i = 0; i < kD; ++i) amax = fmaxf(amax, fabsf(v[i]));
-  amax = warp_max_xor(amax, 16);
-  if (BLK == 64) {
-    if (lane == 0) s_amax[warp] = amax;
-    __syncthreads();
-    amax = fmaxf(s_amax[warp & ~1], s_amax[warp | 1]);
-  }
-  const float inv = __fdiv_rn(127.0f, amax);
-  const int blk = row / BLK;
-  if (lane == 0 && (BLK == 32 || (warp & 1) == 0)) scale[int64_t(bh) * (S_pad / BLK) + blk] = __fdiv_rn(amax, 127.0f);
-  int8_t* dst = out + (int64_t(bh) * S_pad + row) * kD;
+    for (int p = 0; p < 4; ++p) {
+      kx[p] = kv_stage[p * 256 + t];
+      if (tile * kQTile + p * 16 + rs < S) {
+        float f[8];
+        unpack8(kx[p], f);
 #pragma unroll
-  for (int i = 0; i < kD / 16; ++i) {
-    uint32_t w[4];
-#pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      uint32_t packed = 0;
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        int c;
-        asm("cvt.rni.sat.s8.f32 %0, %1;" : "=r"(c) : "f"(v[i * 16 + q * 4 + e] * inv));
-        packed |= (uint32_t(c) & 0xffu) << (8 * e);
+        for (int e = 0; e < 8; ++e) rmax = fmaxf(rmax, fabsf(f[e] - cc[e]));
       }
-      w[q] = packed;
     }
-    reinterpret_cast<uint4*>(dst)[i] = make_uint4(w[0], w[1], w[2], w[3]);
+    rmax = pair_amax(row_amax(rmax));
+    if ((t & 31) == 0) s_wmax[warp] = rmax;
+    __syncthreads();
+    const float4 a = *reinterpret_cast<const float4*>(&s_wmax[0]);
+    const float4 c = *reinterpret_cast<const float4*>(&s_wmax[4]);
+    const float bm = fmaxf(fmaxf(fmaxf(a.x, a.y), fmaxf(a.z, a.w)), fmaxf(fmaxf(c.x, c.y), fmaxf(c.z, c.w)));
+    if (t == 0) k_scale[int64_t(bh) * (S_pad / 64) + tile] = __fdiv_rn(bm, 127.0f);
+    const float inv = __fdiv_rn(127.0f, bm);
+    int8_t* dst = k8 + (int64_t(bh) * S_pad + tile * kQTile) * kD + cg * 8;
+#pragma unroll
+    for (int p = 0; p < 4; ++p) {
+      const int r = p * 16 + rs;
+      const uint2 code = tile * kQTile + r < S ? int8_piece<true>(kx[p], cc, inv) : make_uint2(0u, 0u);
+      *reinterpret_cast<uint2*>(dst + int64_t(r) * kD) = code;
+    }
+    return;
   }
-}
-
-// Per (b, h, 128-row tile): E4M3 codes of v * 448/amax (zeros past S).
-// Thread d owns channel d; each row is one coalesced 128-byte store.
-__global__ void __launch_bounds__(128) sage_quant_v_kernel(const __nv_bfloat16* __restrict__ v, int64_t stride_b,
-                                                           int64_t stride_s, int64_t stride_h, int S, int S_pad,
-                                                           int H, const float* __restrict__ v_recp,
-                                                           uint8_t* __restrict__ out) {
-  const int bh = blockIdx.x, b = bh / H, h = bh % H, tile = blockIdx.y, d = threadIdx.x;
-  const __nv_bfloat16* p = v + b * stride_b + h * stride_h + d;
-  const float recp = v_recp[int64_t(bh) * kD + d];
-  uint8_t* dst = out + int64_t(bh) * S_pad * kD + d;
-#pragma unroll 8
-  for (int s = tile * 128; s < tile * 128 + 128; ++s) {
-    const float x = s < S ? __bfloat162float(p[int64_t(s) * stride_s]) : 0.0f;
-    dst[int64_t(s) * kD] = uint8_t(cvt_e4m3x2(x * recp, 0.0f) & 0xffu);
+  uint8_t* dst = v8 + (int64_t(bh) * S_pad + tile * kQTile) * kD + cg * 8;
+#pragma unroll
+  for (int p = 0; p < 4; ++p) {
+    float f[8];
+    unpack8(kv_stage[p * 256 + t], f);      // zero-filled past S
+    const uint32_t lo = cvt_e4m3x4(f[0] * cc[0], f[1] * cc[1], f[2] * cc[2], f[3] * cc[3]);
+    const uint32_t hi = cvt_e4m3x4(f[4] * cc[4], f[5] * cc[5], f[6] * cc[6], f[7] * cc[7]);
+    *reinterpret_cast<uint2*>(dst + int64_t(p * 16 + rs) * kD) = make_uint2(lo, hi);
   }
 }
 
@@ -651,8 +926,9 @@ struct Workspace {
   float* v_scale;
   __nv_bfloat16* k_mean;
   float* v_recp;
-  float* k_part;   // [B*H, S_kv_pad/128, 128] partial K sums
-  float* v_part;   // [B*H, S_kv_pad/128, 128] partial |V| maxima
+  float* k_part;   // [B*H, S_kv_pad/64, 128] per-64-row-tile K column sums
+  float* v_part;   // [B*H, S_kv_pad/64, 128] per-64-row-tile |V| column maxima
+  __nv_bfloat16* kn;  // [B*H, S_kv_pad, 128] normalised K (joint-sequence entry points)
 };
 
 int64_t workspace_layout(int64_t B, int64_t H, int64_t Sq, int64_t Skv, uint8_t* base, Workspace* ws) {
@@ -671,8 +947,9 @@ int64_t workspace_layout(int64_t B, int64_t H, int64_t Sq, int64_t Skv, uint8_t*
   uint8_t* vs = take(bh * kD * 4);
   uint8_t* km = take(bh * kD * 2);
   uint8_t* vr = take(bh * kD * 4);
-  uint8_t* kpart = take(bh * (skp / 128) * kD * 4);
-  uint8_t* vpart = take(bh * (skp / 128) * kD * 4);
+  uint8_t* kpart = take(bh * (skp / 64) * kD * 4);
+  uint8_t* vpart = take(bh * (skp / 64) * kD * 4);
+  uint8_t* kn = take(bh * skp * kD * 2);
   if (ws) {
     ws->q8 = (int8_t*)q8;
     ws->k8 = (int8_t*)k8;
@@ -684,6 +961,7 @@ int64_t workspace_layout(int64_t B, int64_t H, int64_t Sq, int64_t Skv, uint8_t*
     ws->v_recp = (float*)vr;
     ws->k_part = (float*)kpart;
     ws->v_part = (float*)vpart;
+    ws->kn = (__nv_bfloat16*)kn;
   }
   return off;
 }
@@ -699,31 +977,60 @@ int check_nhd(const void* t, const Strides& st, const char* who) {
   return QIA_OK;
 }
 
+// Opt the staged quantizer kernels of one source type into their dynamic
+// shared memory, once per device.
+template <class Src>
+int quant_smem_attrs() {
+  static bool done[64] = {false};
+  static std::mutex mu;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  std::lock_guard<std::mutex> lock(mu);
+  if (dev >= 0 && dev < 64 && done[dev]) return QIA_OK;
+  cudaError_t e = cudaFuncSetAttribute(sage_quant_q_stats_kernel<Src>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       q_stats_smem<Src>());
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(sage_quant_kv_kernel<Src>, cudaFuncAttributeMaxDynamicSharedMemorySize, kKvSmem);
+  if (e != cudaSuccess) return set_error(QIA_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+  if (dev >= 0 && dev < 64) done[dev] = true;
+  return QIA_OK;
+}
+
+template <class Src>
+int quant_rows(const Src& src, int64_t B, int64_t H, int64_t Sq, int64_t Skv, const Workspace& ws, cudaStream_t st) {
+  int rc = quant_smem_attrs<Src>();
+  if (rc) return rc;
+  const int64_t sqp = pad128(Sq), skp = pad128(Skv);
+  const unsigned bh = unsigned(B * H), q_tiles = unsigned(sqp / kQTile);
+  const unsigned kv_tiles = unsigned((Skv + kQTile - 1) / kQTile);
+  const int part_stride = int(skp / kQTile);
+  sage_quant_q_stats_kernel<Src><<<dim3(bh, q_tiles > kv_tiles ? q_tiles : kv_tiles), 256, q_stats_smem<Src>(), st>>>(
+      src, int(Sq), int(sqp), int(Skv), int(H), int(kv_tiles), part_stride, ws.q8, ws.q_scale, ws.k_part, ws.v_part);
+  rc = check_launch("sage_quant_q_stats_kernel");
+  if (rc) return rc;
+  sage_quant_finalize_kernel<<<bh, kD, 0, st>>>(ws.k_part, ws.v_part, int(kv_tiles), part_stride, int(Skv), ws.k_mean,
+                                                 ws.v_scale, ws.v_recp);
+  rc = check_launch("sage_quant_finalize_kernel");
+  if (rc) return rc;
+  sage_quant_kv_kernel<Src><<<dim3(bh, unsigned(skp / kQTile), 2), 256, kKvSmem, st>>>(
+      src, int(Skv), int(skp), int(H), ws.k_mean, ws.v_recp, ws.k8, ws.k_scale, ws.v8);
+  return check_launch("sage_quant_kv_kernel");
+}
+
 int quant_qkv(const void* q, Strides qs, const void* k, Strides ks, const void* v, Strides vs, int64_t B, int64_t H,
               int64_t Sq, int64_t Skv, const Workspace& ws, cudaStream_t st) {
-  const int64_t sqp = pad128(Sq), skp = pad128(Skv);
-  const unsigned bh = unsigned(B * H);
-  sage_quant_int8_kernel<32, false><<<dim3(bh, unsigned(sqp / 128)), 128, 0, st>>>(
-      (const __nv_bfloat16*)q, qs.b, qs.s, qs.h, int(Sq), int(sqp), int(H), nullptr, ws.q8, ws.q_scale);
-  int rc = check_launch("sage_quant_int8_kernel<q>");
-  if (rc) return rc;
-  const unsigned kv_tiles = unsigned(skp / 128);
-  sage_kv_partials_kernel<<<dim3(bh, kv_tiles), kD, 0, st>>>((const __nv_bfloat16*)k, ks.b, ks.s, ks.h,
-                                                              (const __nv_bfloat16*)v, vs.b, vs.s, vs.h, int(Skv),
-                                                              int(H), ws.k_part, ws.v_part);
-  rc = check_launch("sage_kv_partials_kernel");
-  if (rc) return rc;
-  sage_kv_finalize_kernel<<<bh, kD, 0, st>>>(ws.k_part, ws.v_part, int(kv_tiles), int(Skv), ws.k_mean, ws.v_scale,
-                                             ws.v_recp);
-  rc = check_launch("sage_kv_finalize_kernel");
-  if (rc) return rc;
-  sage_quant_int8_kernel<64, true><<<dim3(bh, unsigned(skp / 128)), 128, 0, st>>>(
-      (const __nv_bfloat16*)k, ks.b, ks.s, ks.h, int(Skv), int(skp), int(H), ws.k_mean, ws.k8, ws.k_scale);
-  rc = check_launch("sage_quant_int8_kernel<k>");
-  if (rc) return rc;
-  sage_quant_v_kernel<<<dim3(bh, kv_tiles), kD, 0, st>>>((const __nv_bfloat16*)v, vs.b, vs.s, vs.h, int(Skv),
-                                                         int(skp), int(H), ws.v_recp, ws.v8);
-  return check_launch("sage_quant_v_kernel");
+  PlainQKV src;
+  src.x[0] = (const __nv_bfloat16*)q;
+  src.x[1] = (const __nv_bfloat16*)k;
+  src.x[2] = (const __nv_bfloat16*)v;
+  const Strides all[3] = {qs, ks, vs};
+  for (int c = 0; c < 3; ++c) {
+    src.sb[c] = all[c].b;
+    src.ss[c] = all[c].s;
+    src.sh[c] = all[c].h;
+  }
+  src.eps = 0.0f;
+  return quant_rows(src, B, H, Sq, Skv, ws, st);
 }
 
 struct MxOut {
@@ -789,6 +1096,38 @@ int check_sizes(int64_t B, int64_t H, int64_t Sq, int64_t Skv, int64_t D, const 
   if (D != kD) return set_error(QIA_ERR_UNSUPPORTED, "%s: head_dim must be 128", who);
   if (B * H > 65535 || pad128(Sq) * B * H > (1LL << 31) || pad128(Skv) * B * H > (1LL << 31))
     return set_error(QIA_ERR_UNSUPPORTED, "%s: too large", who);
+  return QIA_OK;
+}
+
+// The Q/K/V source of the joint [stream 0, stream 1] sequence read straight
+// from the two streams' fused q|k|v projection outputs.
+int make_joint(const void* qkv0, int64_t ld0, const void* qkv1, int64_t ld1, const void* wq0, const void* wk0,
+               const void* wq1, const void* wk1, const void* freqs0, const void* freqs1, int64_t len0, int64_t len1,
+               int64_t heads, float eps, JointQKV* src, const char* who) {
+  if (!qkv0 || !qkv1 || !wq0 || !wk0 || !wq1 || !wk1 || !freqs0 || !freqs1)
+    return set_error(QIA_ERR_INVALID, "%s: null pointer", who);
+  if (len0 <= 0 || len1 <= 0) return set_error(QIA_ERR_INVALID, "%s: stream lengths must be positive", who);
+  if (ld0 < 3 * heads * kD || ld1 < 3 * heads * kD || ld0 % 8 || ld1 % 8)
+    return set_error(QIA_ERR_INVALID, "%s: leading dimensions must be >= 3*heads*128 and multiples of 8", who);
+  const void* ptrs[8] = {qkv0, qkv1, wq0, wk0, wq1, wk1, freqs0, freqs1};
+  for (const void* p : ptrs)
+    if (!aligned(p, 16)) return set_error(QIA_ERR_ALIGNMENT, "%s: 16-byte alignment", who);
+  src->qkv0 = (const __nv_bfloat16*)qkv0;
+  src->qkv1 = (const __nv_bfloat16*)qkv1;
+  src->ld0 = ld0;
+  src->ld1 = ld1;
+  src->wq0 = (const __nv_bfloat16*)wq0;
+  src->wk0 = (const __nv_bfloat16*)wk0;
+  src->wq1 = (const __nv_bfloat16*)wq1;
+  src->wk1 = (const __nv_bfloat16*)wk1;
+  src->f0 = (const float*)freqs0;
+  src->f1 = (const float*)freqs1;
+  src->len0 = int(len0);
+  src->len1 = int(len1);
+  src->H = int(heads);
+  src->eps = eps;
+  src->kn = nullptr;
+  src->S_pad = 0;
   return QIA_OK;
 }
 
@@ -942,6 +1281,68 @@ extern "C" int qia_sage_quantize(const void* q, const void* k, const void* v, in
   Workspace ws;
   workspace_layout(batch, heads, seq_q, seq_kv, (uint8_t*)workspace, &ws);
   return quant_qkv(q, sq, k, sk, v, sv, batch, heads, seq_q, seq_kv, ws, as_stream(stream));
+}
+
+extern "C" int qia_sage_quantize_joint(const void* qkv0, int64_t ld0, const void* qkv1, int64_t ld1,
+                                       const void* weight_q0, const void* weight_k0, const void* weight_q1,
+                                       const void* weight_k1, const void* freqs0, const void* freqs1, int64_t batch,
+                                       int64_t len0, int64_t len1, int64_t heads, int64_t head_dim, float eps,
+                                       void* workspace, int64_t workspace_bytes, void* stream) {
+  const int64_t S = len0 + len1;
+  int rc = check_sizes(batch, heads, S, S, head_dim, "qia_sage_quantize_joint");
+  if (rc) return rc;
+  JointQKV src;
+  rc = make_joint(qkv0, ld0, qkv1, ld1, weight_q0, weight_k0, weight_q1, weight_k1, freqs0, freqs1, len0, len1, heads,
+                  eps, &src, "qia_sage_quantize_joint");
+  if (rc) return rc;
+  const int64_t need = workspace_layout(batch, heads, S, S, nullptr, nullptr);
+  if (!workspace || workspace_bytes < need || !aligned(workspace, 256))
+    return set_error(QIA_ERR_INVALID, "qia_sage_quantize_joint: workspace of %lld bytes (256-aligned) needed",
+                     (long long)need);
+  Workspace ws;
+  workspace_layout(batch, heads, S, S, (uint8_t*)workspace, &ws);
+  src.kn = ws.kn;
+  src.S_pad = int(pad128(S));
+  return quant_rows(src, batch, heads, S, S, ws, as_stream(stream));
+}
+
+extern "C" int qia_sage_attention_joint_mx(const void* qkv0, int64_t ld0, const void* qkv1, int64_t ld1,
+                                           const void* weight_q0, const void* weight_k0, const void* weight_q1,
+                                           const void* weight_k1, const void* freqs0, const void* freqs1,
+                                           void* a_values, void* a_scales, void* b_values, void* b_scales,
+                                           int64_t batch, int64_t len0, int64_t len1, int64_t heads,
+                                           int64_t head_dim, float eps, float sm_scale, void* workspace,
+                                           int64_t workspace_bytes, void* stream) {
+  const int64_t S = len0 + len1;
+  int rc = check_sizes(batch, heads, S, S, head_dim, "qia_sage_attention_joint_mx");
+  if (rc) return rc;
+  if (!a_values || !a_scales || !b_values || !b_scales)
+    return set_error(QIA_ERR_INVALID, "qia_sage_attention_joint_mx: null output");
+  if (!aligned(a_values, 32) || !aligned(b_values, 32) || !aligned(a_scales, 4) || !aligned(b_scales, 4))
+    return set_error(QIA_ERR_ALIGNMENT, "qia_sage_attention_joint_mx: values 32-byte, scales 4-byte aligned");
+  JointQKV src;
+  rc = make_joint(qkv0, ld0, qkv1, ld1, weight_q0, weight_k0, weight_q1, weight_k1, freqs0, freqs1, len0, len1, heads,
+                  eps, &src, "qia_sage_attention_joint_mx");
+  if (rc) return rc;
+  const int64_t need = workspace_layout(batch, heads, S, S, nullptr, nullptr);
+  if (!workspace || workspace_bytes < need || !aligned(workspace, 256))
+    return set_error(QIA_ERR_INVALID, "qia_sage_attention_joint_mx: workspace of %lld bytes (256-aligned) needed",
+                     (long long)need);
+  Workspace ws;
+  workspace_layout(batch, heads, S, S, (uint8_t*)workspace, &ws);
+  const float scale = sm_scale > 0.0f ? sm_scale : 1.0f / sqrtf(float(head_dim));
+  cudaStream_t st = as_stream(stream);
+  src.kn = ws.kn;
+  src.S_pad = int(pad128(S));
+  rc = quant_rows(src, batch, heads, S, S, ws, st);
+  if (rc) return rc;
+  MxOut mx;
+  mx.a_values = a_values;
+  mx.a_scales = a_scales;
+  mx.b_values = b_values;
+  mx.b_scales = b_scales;
+  const Strides none{0, 0, 0};
+  return launch_attn(ws, nullptr, none, nullptr, none, len0, batch, heads, S, S, scale, st, mx);
 }
 
 extern "C" int qia_sage_attn_quantized(const void* workspace, void* out, int64_t batch, int64_t seq_q,

@@ -41,6 +41,9 @@ SIGNATURES: dict[str, list] = {
     "qia_sage_attention_split_mx": [_P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _P, _F, _P, _I, _P],
     "qia_sage_attention_noalloc": [_P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _F, _P],
     "qia_sage_quantize": [_P, _P, _P, _I, _I, _I, _I, _I, _P, _P, _I, _P],
+    "qia_sage_quantize_joint": [_P, _I, _P, _I, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _F, _P, _I, _P],
+    "qia_sage_attention_joint_mx": [_P, _I, _P, _I, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I,
+                                    _F, _F, _P, _I, _P],
     "qia_sage_attn_quantized": [_P, _P, _I, _I, _I, _I, _I, _P, _F, _P],
 }
 
@@ -91,9 +94,9 @@ def declared_symbols() -> list[str]:
 
 
 # kernels each entry point queues (for launch accounting); default 1
-KERNELS_PER_CALL = {"qia_sage_attention": 6, "qia_sage_attention_split": 6, "qia_sage_quantize": 5,
-                    "qia_sage_attention_split_mx": 6,
-                    "qia_sage_attention_noalloc": 6,
+KERNELS_PER_CALL = {"qia_sage_attention": 4, "qia_sage_attention_split": 4, "qia_sage_quantize": 3,
+                    "qia_sage_attention_split_mx": 4, "qia_sage_quantize_joint": 3, "qia_sage_attention_joint_mx": 4,
+                    "qia_sage_attention_noalloc": 4,
                     "qia_device_error": 0}
 launch_count = 0
 

@@ -10,8 +10,9 @@ state-dict names, so a checkpoint of that model loads as is.
 Per block and stream the hot path is:
   LN + (1+scale), +shift -> MXFP8         qia_ln_mod_quant
   fused Q|K|V GEMM (+bias)                 qia_mxfp8_gemm
-  QK-RMSNorm + RoPE + joint [txt, img]     qia_qknorm_rope_segment (x2 streams)
-  Sage INT8/FP8 joint attention -> MXFP8   qia_sage_attention_split_mx
+  QK-RMSNorm + RoPE + Sage quantization    qia_sage_attention_joint_mx (both
+    + joint [txt, img] INT8/FP8 attention    streams' projections in, per-stream
+    -> MXFP8                                 MXFP8 attention outputs back)
   out-proj GEMM + gate + residual          qia_mxfp8_gemm_gate_residual
   LN + (1+scale), +shift -> MXFP8          qia_ln_mod_quant
   FFN up GEMM + bias + GELU -> MXFP8       qia_mxfp8_gemm_gelu_quant
@@ -41,7 +42,8 @@ from .kernels.epilogue import layer_norm_scale_quantize
 from .kernels.layernorm import layer_norm_scale
 from .kernels.mxfp8 import quantize
 from .optimizations.mxfp8 import MXFP8Linear
-from .optimizations.sage_attention import sage_attention_split, sage_attention_split_quantized, workspace_bytes
+from .optimizations.sage_attention import (sage_attention_joint_quantized, sage_attention_split,
+                                           sage_attention_split_quantized, workspace_bytes)
 from .kernels.bf16 import gelu_tanh
 from .profiles import get_profile
 
@@ -269,6 +271,10 @@ class MMDiT:
         need = workspace_bytes(q.shape[0], q.shape[2], q.shape[1], k.shape[1])
         return torch.empty(need, device=q.device, dtype=torch.uint8)
 
+    def _attn_ws_joint(self, batch, seq):
+        need = workspace_bytes(batch, self.cfg.num_attention_heads, seq, seq)
+        return torch.empty(need, device=self.device, dtype=torch.uint8)
+
     # ------------------------------------------------------------------ block
     def block_forward(self, blk: DualStreamBlock, x: torch.Tensor, c: torch.Tensor, mod_img, mod_txt,
                       freqs_img, freqs_txt):
@@ -288,23 +294,27 @@ class MMDiT:
         else:
             qkv_i = F.linear(layer_norm_scale(x, s1_i, self.ln, shift=sh1_i), blk.img_qkv.w, blk.img_qkv.b)
             qkv_t = F.linear(layer_norm_scale(c, s1_t, self.ln, shift=sh1_t), blk.txt_qkv.w, blk.txt_qkv.b)
-        # ---- QK-RMSNorm + RoPE into the joint [text, image] sequence
         S = Lt + Li
-        q = torch.empty(B, S, H, hd, device=x.device, dtype=torch.bfloat16)
-        k = torch.empty_like(q)
-        v = torch.empty_like(q)
-        joint_qk_norm_rope(qkv_t.view(B, Lt, 3 * D), blk.norm_added_q, blk.norm_added_k, freqs_txt, q, k, v, 0,
-                           cfg.eps)
-        joint_qk_norm_rope(qkv_i.view(B, Li, 3 * D), blk.norm_q, blk.norm_k, freqs_img, q, k, v, Lt, cfg.eps)
-        # ---- joint attention, written back per stream (as MXFP8 straight from
-        # the attention epilogue when the output projections are MXFP8 GEMMs)
         if self.quantized and self.sage:
-            qa_t, qa_i = sage_attention_split_quantized(q, k, v, Lt, workspace=self._attn_ws(q, k))
-            del q, k, v
+            # ---- QK-RMSNorm + RoPE + Sage quantization straight from the two
+            # projections, joint attention, per-stream MXFP8 outputs for the
+            # output projections (no bf16 Q/K/V or attention output in memory)
+            qa_t, qa_i = sage_attention_joint_quantized(
+                qkv_t.view(B, Lt, 3 * D), qkv_i.view(B, Li, 3 * D), (blk.norm_added_q, blk.norm_added_k),
+                (blk.norm_q, blk.norm_k), freqs_txt, freqs_img, H, cfg.eps, workspace=self._attn_ws_joint(B, S))
+            del qkv_t, qkv_i
             blk.img_out.mx.matmul_gate_residual(qa_i, g1_i, x, out=x)
             blk.txt_out.mx.matmul_gate_residual(qa_t, g1_t, c, out=c)
             del qa_t, qa_i
         else:
+            # ---- QK-RMSNorm + RoPE into the joint [text, image] sequence
+            q = torch.empty(B, S, H, hd, device=x.device, dtype=torch.bfloat16)
+            k = torch.empty_like(q)
+            v = torch.empty_like(q)
+            joint_qk_norm_rope(qkv_t.view(B, Lt, 3 * D), blk.norm_added_q, blk.norm_added_k, freqs_txt, q, k, v, 0,
+                               cfg.eps)
+            joint_qk_norm_rope(qkv_i.view(B, Li, 3 * D), blk.norm_q, blk.norm_k, freqs_img, q, k, v, Lt, cfg.eps)
+            # ---- joint attention, written back per stream
             a_t = torch.empty(B, Lt, H, hd, device=x.device, dtype=torch.bfloat16)
             a_i = torch.empty(B, Li, H, hd, device=x.device, dtype=torch.bfloat16)
             self._attention(q, k, v, Lt, a_t, a_i)

@@ -47,8 +47,9 @@ def workspace_views(ws: torch.Tensor, batch: int, heads: int, seq_q: int, seq_kv
                ("v_scale", bh * 128 * 4, torch.float32, (bh, 128)),
                ("k_mean", bh * 128 * 2, torch.bfloat16, (bh, 128)),
                ("v_recp", bh * 128 * 4, torch.float32, (bh, 128)),
-               ("k_part", bh * (skp // 128) * 128 * 4, torch.float32, (bh, skp // 128, 128)),
-               ("v_part", bh * (skp // 128) * 128 * 4, torch.float32, (bh, skp // 128, 128))]
+               ("k_part", bh * (skp // 64) * 128 * 4, torch.float32, (bh, skp // 64, 128)),
+               ("v_part", bh * (skp // 64) * 128 * 4, torch.float32, (bh, skp // 64, 128)),
+               ("kn", bh * skp * 128 * 2, torch.bfloat16, (bh, skp, 128))]
     out, off = {}, 0
     for name, nbytes, dtype, shape in regions:
         out[name] = ws[off:off + nbytes].view(dtype).view(shape)
@@ -131,6 +132,73 @@ def sage_attention_split_quantized(q: torch.Tensor, k: torch.Tensor, v: torch.Te
               _lib.ptr(qa.scales), _lib.ptr(qb.values), _lib.ptr(qb.scales), split, b, sq, skv, h, d,
               _strides(q, k, v), float(sm_scale or 0.0), _lib.ptr(workspace), workspace.numel(),
               _lib.stream(q.device))
+    return qa, qb
+
+
+def _joint_args(qkv0, qkv1, weights0, weights1, freqs0, freqs1, heads):
+    """Pointer/size arguments of the joint entries (see sage_quantize_joint)."""
+    _lib.require_cuda(qkv0, qkv1, *weights0, *weights1, freqs0, freqs1)
+    for t in (qkv0, qkv1):
+        if t.ndim != 3 or t.dtype != torch.bfloat16 or t.stride(-1) != 1 or t.stride(0) != t.shape[1] * t.stride(1):
+            raise NotImplementedError("qkv projections must be (B, L, >= 3*H*128) bf16 with evenly strided rows")
+        if t.shape[2] < 3 * heads * 128:
+            raise ValueError("qkv projection narrower than 3*heads*128")
+    if qkv0.shape[0] != qkv1.shape[0]:
+        raise ValueError("the two streams' batch sizes differ")
+    for f, t in ((freqs0, qkv0), (freqs1, qkv1)):
+        if f.dtype != torch.float32 or not f.is_contiguous() or f.numel() < t.shape[1] * 128:
+            raise NotImplementedError("freqs must be contiguous float32 (L, 64, 2)")
+    for w in (*weights0, *weights1):
+        if w.dtype != torch.bfloat16 or w.numel() != 128 or not w.is_contiguous():
+            raise NotImplementedError("norm weights must be contiguous bf16 [128]")
+    return [_lib.ptr(qkv0), qkv0.stride(1), _lib.ptr(qkv1), qkv1.stride(1), _lib.ptr(weights0[0]),
+            _lib.ptr(weights0[1]), _lib.ptr(weights1[0]), _lib.ptr(weights1[1]), _lib.ptr(freqs0), _lib.ptr(freqs1)]
+
+
+def sage_quantize_joint(qkv0: torch.Tensor, qkv1: torch.Tensor, weights0, weights1, freqs0: torch.Tensor,
+                        freqs1: torch.Tensor, heads: int, eps: float = 1e-6) -> dict:
+    """The quantization half for the joint [stream 0, stream 1] sequence, read
+    straight from the streams' fused q|k|v projections (B, L_i, 3*H*128) with
+    each stream's QK-RMSNorm (weights_i = (norm_q, norm_k)) and RoPE (freqs_i
+    float32 (L_i, 64, 2)) applied on load. The workspace equals
+    joint_qk_norm_rope on both streams followed by sage_quantize."""
+    b, l0, l1 = qkv0.shape[0], qkv0.shape[1], qkv1.shape[1]
+    args = _joint_args(qkv0, qkv1, weights0, weights1, freqs0, freqs1, heads)
+    s = l0 + l1
+    need = workspace_bytes(b, heads, s, s)
+    ws = torch.empty(need, device=qkv0.device, dtype=torch.uint8)
+    _lib.call("qia_sage_quantize_joint", *args, b, l0, l1, heads, 128, float(eps), _lib.ptr(ws), need,
+              _lib.stream(qkv0.device))
+    views = workspace_views(ws, b, heads, s, s)
+    views["_workspace"] = ws
+    return views
+
+
+def sage_attention_joint_quantized(qkv0: torch.Tensor, qkv1: torch.Tensor, weights0, weights1,
+                                   freqs0: torch.Tensor, freqs1: torch.Tensor, heads: int, eps: float = 1e-6,
+                                   sm_scale: float | None = None, workspace: torch.Tensor | None = None):
+    """Joint attention of the dual-stream block from the two streams' fused
+    q|k|v projections (QK-RMSNorm + RoPE + Sage quantization fused), with the
+    per-stream outputs as MXFP8 activations (Quantized, rows = batch * L_i,
+    K = heads * 128): equal to joint_qk_norm_rope on both streams followed by
+    sage_attention_split_quantized(q, k, v, L_0)."""
+    from ..kernels.mxfp8 import empty_quantized
+    _check_settings()
+    b, l0, l1 = qkv0.shape[0], qkv0.shape[1], qkv1.shape[1]
+    args = _joint_args(qkv0, qkv1, weights0, weights1, freqs0, freqs1, heads)
+    s = l0 + l1
+    need = workspace_bytes(b, heads, s, s)
+    if workspace is None or workspace.numel() < need:
+        workspace = torch.empty(need, device=qkv0.device, dtype=torch.uint8)
+    qa = empty_quantized(b * l0, heads * 128, qkv0.device)
+    qb = empty_quantized(b * l1, heads * 128, qkv0.device)
+    for t in (qa, qb):             # rows past the live ones (padding to 128) stay zero
+        if t.values.shape[0] > t.rows:
+            t.values[t.rows:].view(torch.uint8).zero_()
+            t.scales.view(torch.uint8).zero_()
+    _lib.call("qia_sage_attention_joint_mx", *args, _lib.ptr(qa.values), _lib.ptr(qa.scales), _lib.ptr(qb.values),
+              _lib.ptr(qb.scales), b, l0, l1, heads, 128, float(eps), float(sm_scale or 0.0), _lib.ptr(workspace),
+              workspace.numel(), _lib.stream(qkv0.device))
     return qa, qb
 
 

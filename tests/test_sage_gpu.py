@@ -138,3 +138,82 @@ def test_split_attention_mxfp8_outputs_match_quantize(b, lt, li, h):
         assert got.rows == ref.rows and got.values.shape == ref.values.shape
         assert torch.equal(got.values.view(torch.uint8), ref.values.view(torch.uint8))
         assert torch.equal(got.scales.view(torch.uint8), ref.scales.view(torch.uint8))
+
+
+def _joint_inputs(b, lt, li, h, pad_cols, seed):
+    """Two streams' fused q|k|v projections (row stride 3*h*128 + pad_cols),
+    their QK-norm weights and RoPE tables."""
+    from qwen_image_accel_b200.mmdit import rope_tables
+    g = torch.Generator(device=DEV).manual_seed(seed)
+    cols = 3 * h * 128
+
+    def proj(n):
+        full = torch.randn(b, n, cols + pad_cols, device=DEV, dtype=torch.bfloat16, generator=g) * 2.0
+        full[..., h * 128:2 * h * 128] += 0.75        # a non-zero K mean exercises the smoothing
+        return full[..., :cols] if pad_cols else full
+
+    def weights():
+        return tuple((1.0 + 0.1 * torch.randn(128, device=DEV, generator=g)).to(torch.bfloat16) for _ in range(2))
+
+    img, txt = rope_tables(1, li, 1, lt)               # image tokens as one column of li rows
+    ft = torch.view_as_real(txt).to(DEV).contiguous()
+    fi = torch.view_as_real(img).to(DEV).contiguous()
+    return proj(lt), proj(li), weights(), weights(), ft, fi
+
+
+@pytest.mark.parametrize("b,lt,li,h,pad", [(1, 40, 192, 4, 0), (2, 77, 300, 2, 64), (1, 256, 4096, 24, 0),
+                                           (2, 130, 1, 1, 8)])
+def test_joint_quantize_matches_norm_rope_then_quantize(b, lt, li, h, pad):
+    """QK-RMSNorm + RoPE + quantization straight from the two projections fill
+    the workspace byte for byte as joint_qk_norm_rope on both streams followed
+    by sage_quantize on the bf16 joint Q/K/V."""
+    from qwen_image_accel_b200.kernels.attention import joint_qk_norm_rope
+    from qwen_image_accel_b200.optimizations.sage_attention import sage_quantize, sage_quantize_joint
+    qkv_t, qkv_i, w_t, w_i, ft, fi = _joint_inputs(b, lt, li, h, pad, 31)
+    s = lt + li
+    q, k, v = (torch.empty(b, s, h, 128, device=DEV, dtype=torch.bfloat16) for _ in range(3))
+    joint_qk_norm_rope(qkv_t, w_t[0], w_t[1], ft, q, k, v, 0, 1e-6)
+    joint_qk_norm_rope(qkv_i, w_i[0], w_i[1], fi, q, k, v, lt, 1e-6)
+    ref = sage_quantize(q, k, v)
+    got = sage_quantize_joint(qkv_t, qkv_i, w_t, w_i, ft, fi, h, 1e-6)
+    torch.cuda.synchronize()
+    for name in ("q8", "k8", "v8", "q_scale", "k_scale", "v_scale", "k_mean", "v_recp"):
+        assert torch.equal(got[name].view(torch.uint8), ref[name].view(torch.uint8)), name
+    tiles = (s + 63) // 64                     # partial-sum tiles that hold rows
+    for name in ("k_part", "v_part"):
+        assert torch.equal(got[name][:, :tiles], ref[name][:, :tiles]), name
+
+
+@pytest.mark.parametrize("b,lt,li,h,pad", [(1, 40, 192, 4, 0), (2, 77, 300, 2, 64), (2, 256, 4096, 24, 0)])
+def test_joint_attention_mx_matches_split(b, lt, li, h, pad):
+    """The fused joint entry gives the same per-stream MXFP8 attention outputs
+    as the two-stage path (norm + RoPE kernel, then the split attention)."""
+    from qwen_image_accel_b200 import _lib
+    from qwen_image_accel_b200.kernels.attention import joint_qk_norm_rope
+    from qwen_image_accel_b200.optimizations.sage_attention import (sage_attention_joint_quantized,
+                                                                    sage_attention_split_quantized)
+    qkv_t, qkv_i, w_t, w_i, ft, fi = _joint_inputs(b, lt, li, h, pad, 32)
+    s = lt + li
+    q, k, v = (torch.empty(b, s, h, 128, device=DEV, dtype=torch.bfloat16) for _ in range(3))
+    joint_qk_norm_rope(qkv_t, w_t[0], w_t[1], ft, q, k, v, 0, 1e-6)
+    joint_qk_norm_rope(qkv_i, w_i[0], w_i[1], fi, q, k, v, lt, 1e-6)
+    ra, rb = sage_attention_split_quantized(q, k, v, lt)
+    ga, gb = sage_attention_joint_quantized(qkv_t, qkv_i, w_t, w_i, ft, fi, h, 1e-6)
+    torch.cuda.synchronize()
+    assert _lib.device_error() == 0
+    for got, ref in ((ga, ra), (gb, rb)):
+        assert got.rows == ref.rows
+        assert torch.equal(got.values.view(torch.uint8), ref.values.view(torch.uint8))
+        assert torch.equal(got.scales.view(torch.uint8), ref.scales.view(torch.uint8))
+
+
+def test_joint_entry_rejects_bad_arguments():
+    from qwen_image_accel_b200 import _lib
+    from qwen_image_accel_b200.optimizations.sage_attention import sage_quantize_joint
+    qkv_t, qkv_i, w_t, w_i, ft, fi = _joint_inputs(1, 40, 192, 4, 0, 33)
+    with pytest.raises(ValueError):
+        sage_quantize_joint(qkv_t, qkv_i, w_t, w_i, ft, fi, 8)          # projection too narrow for 8 heads
+    with pytest.raises(_lib.QiaError):
+        _lib.call("qia_sage_quantize_joint", _lib.ptr(qkv_t), qkv_t.stride(1), _lib.ptr(qkv_i), qkv_i.stride(1),
+                  _lib.ptr(w_t[0]), _lib.ptr(w_t[1]), _lib.ptr(w_i[0]), _lib.ptr(w_i[1]), _lib.ptr(ft),
+                  _lib.ptr(fi), 1, 40, 0, 4, 128, 1e-6, 0, 0, _lib.stream(qkv_t.device))
