@@ -326,19 +326,33 @@ def sage_quant_q(q: np.ndarray, blk: int = 32):
 def sage_k_mean(k: np.ndarray) -> np.ndarray:
     """Per-(batch, head, channel) mean of K over the sequence, rounded to bf16
     (SAGE:sageattention/core.py:773, k.mean(dim=seq) on a bf16 tensor), in the
-    kernel's order: per 64-row tile, sixteen fp32 row-group sums (rows g,
-    g+16, g+32, g+48 of the tile in order), added in group order; tile sums
-    added in order; times fp32(1/S)."""
+    kernel's order: per 32-row tile, sixteen fp32 row-group sums (rows g and
+    g+16 of the tile, in order, added to 0.0); the groups paired (g + (g+1)
+    for even g); the eight pair sums added in order to 0.0 (the tile sum);
+    the tile sums as eight interleaved sub-sums (tiles j, j+8, j+16, ... in
+    order, from 0.0), added in sub order to 0.0; times fp32(1/S)."""
     b, s, h, d = k.shape
-    total = np.zeros((b, h, d), np.float32)
-    for t0 in range(0, s, 64):
-        part = np.zeros((b, h, d), np.float32)
+    parts = []
+    for t0 in range(0, s, 32):
+        grp = []
         for g in range(16):
-            grp = np.zeros((b, h, d), np.float32)
-            for i in range(t0 + g, min(s, t0 + 64), 16):
-                grp += k[:, i].astype(np.float32)
-            part += grp
-        total += part
+            acc = np.zeros((b, h, d), np.float32)
+            for i in range(t0 + g, min(s, t0 + 32), 16):
+                acc += k[:, i].astype(np.float32)
+            grp.append(acc)
+        part = np.zeros((b, h, d), np.float32)
+        for w in range(8):
+            part += (grp[2 * w] + grp[2 * w + 1]).astype(np.float32)
+        parts.append(part)
+    subs = []
+    for j in range(8):
+        acc = np.zeros((b, h, d), np.float32)
+        for part in parts[j::8]:
+            acc += part
+        subs.append(acc)
+    total = np.zeros((b, h, d), np.float32)
+    for acc in subs:
+        total += acc
     mean = (total * np.float32(1.0 / s)).astype(np.float32)
     return bf16_bits_to_f32(f32_to_bf16_bits(mean))
 

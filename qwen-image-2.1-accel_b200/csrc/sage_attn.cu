@@ -28,8 +28,8 @@
 // padded to a multiple of 128 with zeros): q8/k8 int8 [B*H, S_pad, 128],
 // v8 e4m3 [B*H, S_pad, 128], q_scale f32 [B*H, S_pad/32], k_scale f32
 // [B*H, S_pad/64], v_scale f32 [B*H, 128], k_mean bf16 [B*H, 128]; scratch:
-// v_recp f32 [B*H, 128], per-64-row-tile K sums and |V| maxima f32
-// [B*H, S_pad/64, 128] each, normalised K bf16 [B*H, S_pad, 128] (joint
+// v_recp f32 [B*H, 128], per-32-row-tile K sums and |V| maxima f32
+// [B*H, S_pad/32, 128] each, normalised K bf16 [B*H, S_pad, 128] (joint
 // entry points only).
 #include <cudaTypedefs.h>
 
@@ -50,30 +50,33 @@ constexpr float kFp8Offset = 8.807f;  // log2(448): P = 2^(s - m) <= 448
 
 // ------------------------------------------------------------------ quantizers
 // Three launches fill the workspace.
-//  1. sage_quant_q_stats_kernel, per (b, h, 64-row tile), 256 threads: Q codes
-//     and scales; per tile the column sums of K and column maxima of |V|; for
-//     a source that normalises Q/K on load, also the normalised K (bf16, in
-//     the workspace) for launch 3. Sixteen lanes per row (eight channels
-//     each), sixteen rows per pass, four passes (row p*16 + t/16 of the tile in
-//     pass p). Every thread first stages all the 16-byte pieces it will read
-//     (its Q/K/V row pieces and, with RoPE, its 32 bytes of each row's RoPE
-//     table) into shared memory with cp.async, so the tile's loads are all in
-//     flight at once, then reads back only its own pieces. A thread sums its
-//     four K rows in pass order from 0.0; the sixteen row-group sums are then
-//     added in group order (0.0 + g0 + ... + g15).
-//  2. sage_quant_finalize_kernel, per (b, h): the tile partials reduced in
-//     tile order: k_mean = bf16(sum * (1/S)); v_scale = amax/448 and
+//  1. sage_quant_q_stats_kernel, per (b, h, 32-row tile), 256 threads: Q codes
+//     and scales (the tile is one Q block); per tile the column sums of K and
+//     column maxima of |V|; for a source that normalises Q/K on load, also the
+//     normalised K (bf16, in the workspace) for launch 3. Sixteen lanes per
+//     row (eight channels each), sixteen rows per pass, two passes (row
+//     p*16 + t/16 of the tile in pass p). Every thread first stages all the
+//     16-byte pieces it will read (its Q/K/V row pieces and, with RoPE, its
+//     32 bytes of each row's RoPE table) into shared memory with cp.async, so
+//     the tile's loads are all in flight at once, then reads back only its own
+//     pieces. K column sums: a thread adds its two rows in pass order to 0.0;
+//     the two row groups of a warp (rows g and g+1 for even g) are added
+//     (g + (g+1)); the eight warp sums are added in warp order to 0.0.
+//  2. sage_quant_finalize_kernel, per (b, h): the tile partials reduced as
+//     eight interleaved sub-sums (tiles j, j + 8, j + 16, ... in order), added
+//     in sub order: k_mean = bf16(sum * (1/S)); v_scale = amax/448 and
 //     v_recp = 448/amax (0 for an all-zero channel).
 //  3. sage_quant_kv_kernel, per (b, h, 64-row tile) and z (0: K, 1: V): K
 //     codes of k - k_mean in one 64-row block, or V E4M3 codes of
-//     v * 448/amax, staged the same way.
+//     v * 448/amax, staged the same way (four passes).
 // INT8 blocks: scale = amax/127 (amax floored at 1e-7), codes =
 // rint_sat(x * 127/amax); rows past S are zeros. The rows come from a source:
 // strided [B, S, H, 128] bf16 tensors (PlainQKV), or the fused q|k|v
 // projection outputs of the two streams of the joint [text, image] sequence
 // (JointQKV), whose Q and K are normalised (per-head RMSNorm) and rotated
 // (RoPE) on load with the roundings of the separate attention-input kernel.
-constexpr int kQTile = 64;
+constexpr int kQTile = 64;    // rows per K/V-quantization CTA (one K block)
+constexpr int kQBlock = 32;   // rows per Q-statistics CTA (one Q block)
 
 __device__ __forceinline__ void cp_async16(void* smem, const void* gmem, bool valid) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(smem)), "l"(gmem),
@@ -201,17 +204,22 @@ __device__ __forceinline__ float row_amax(float v) {
 }
 __device__ __forceinline__ float pair_amax(float v) { return fmaxf(v, __shfl_xor_sync(0xffffffffu, v, 16)); }
 
-// INT8 codes rint_sat(x * inv) of a bf16 row piece (minus mf when SUB_MEAN),
-// four codes per 32-bit word.
+// INT8 codes rint(x * inv) of a bf16 row piece (minus mf when SUB_MEAN), four
+// codes per 32-bit word. |x * inv| <= 127 * (1 + 2^-24)^2 < 127.5 because inv
+// = 127/amax rounded and |x| <= amax, so no saturation is needed, and the
+// rounding to an integer is done on the FMA pipe: adding 1.5 * 2^23 leaves
+// round-to-nearest-even(x * inv) in the low mantissa bits (the same integer
+// cvt.rni gives), whose low byte is the two's-complement code.
 template <bool SUB_MEAN>
 __device__ __forceinline__ uint2 int8_piece(const uint4& x, const float (&mf)[8], float inv) {
+  constexpr float kMagic = 12582912.0f;
   float f[8];
   unpack8(x, f);
-  int c[8];
+  uint32_t c[8];
 #pragma unroll
   for (int e = 0; e < 8; ++e) {
-    const float v = SUB_MEAN ? f[e] - mf[e] : f[e];
-    asm("cvt.rni.sat.s8.f32 %0, %1;" : "=r"(c[e]) : "f"(v * inv));
+    const float v = SUB_MEAN ? __fsub_rn(f[e], mf[e]) : f[e];
+    c[e] = __float_as_uint(__fadd_rn(__fmul_rn(v, inv), kMagic));
   }
   const uint32_t lo = __byte_perm(__byte_perm(c[0], c[1], 0x0040), __byte_perm(c[2], c[3], 0x0040), 0x5410);
   const uint32_t hi = __byte_perm(__byte_perm(c[4], c[5], 0x0040), __byte_perm(c[6], c[7], 0x0040), 0x5410);
@@ -221,32 +229,33 @@ __device__ __forceinline__ uint2 int8_piece(const uint4& x, const float (&mf)[8]
 // Dynamic shared memory of the staged kernels (16-byte slots, one per thread).
 template <class Src>
 constexpr int q_stats_smem() {
-  return (3 + (Src::kNormRope ? 2 : 0)) * 4 * 256 * 16;
+  return (3 + (Src::kNormRope ? 2 : 0)) * 2 * 256 * 16;
 }
 constexpr int kKvSmem = 4 * 256 * 16;
 
-// Grid (B*H, max(Sq_pad/64, ceil(Skv/64))), 256 threads.
+// Grid (B*H, max(Sq_pad/32, ceil(Skv/32))), 256 threads: one 32-row tile,
+// two passes.
 template <class Src>
-__global__ void __launch_bounds__(256, 2) sage_quant_q_stats_kernel(Src src, int Sq, int Sq_pad, int Skv, int H,
+__global__ void __launch_bounds__(256, 4) sage_quant_q_stats_kernel(Src src, int Sq, int Sq_pad, int Skv, int H,
                                                                     int kv_tiles, int part_stride,
                                                                     int8_t* __restrict__ q8,
                                                                     float* __restrict__ q_scale,
                                                                     float* __restrict__ k_part,
                                                                     float* __restrict__ v_part) {
   extern __shared__ __align__(16) uint4 q_stage[];
-  __shared__ __align__(16) float s_k[16][kD];
-  __shared__ __align__(16) float s_v[16][kD];
-  __shared__ __align__(16) float s_wmax[2][8];
+  __shared__ __align__(16) float s_k[8][kD];
+  __shared__ __align__(16) float s_v[8][kD];
+  __shared__ __align__(16) float s_wmax[8];
   const int bh = blockIdx.x, b = bh / H, h = bh % H, tile = blockIdx.y, t = threadIdx.x;
   const int cg = t & 15, rs = t >> 4, warp = t >> 5;
-  const bool do_q = tile * kQTile < Sq_pad, do_kv = tile < kv_tiles;
+  const bool do_q = tile * kQBlock < Sq_pad, do_kv = tile < kv_tiles;
   // slots: x[c][p][t] (c = q, k, v), then the rows' RoPE pieces f[half][p][t]
   // (Q and K of a row share them; a source with RoPE has Sq == Skv)
-  auto sx = [&](int c, int p) { return q_stage + (c * 4 + p) * 256 + t; };
-  auto sf = [&](int half, int p) { return q_stage + 3 * 4 * 256 + (half * 4 + p) * 256 + t; };
+  auto sx = [&](int c, int p) { return q_stage + (c * 2 + p) * 256 + t; };
+  auto sf = [&](int half, int p) { return q_stage + 3 * 2 * 256 + (half * 2 + p) * 256 + t; };
 #pragma unroll
-  for (int p = 0; p < 4; ++p) {
-    const int row = tile * kQTile + p * 16 + rs;
+  for (int p = 0; p < 2; ++p) {
+    const int row = tile * kQBlock + p * 16 + rs;
     const bool vq = row < Sq, vkv = row < Skv;
     cp_async16(sx(0, p), (vq ? src.row(0, b, h, row) : src.row(0, 0, 0, 0)) + cg * 8, vq);
     cp_async16(sx(1, p), (vkv ? src.row(1, b, h, row) : src.row(1, 0, 0, 0)) + cg * 8, vkv);
@@ -257,37 +266,29 @@ __global__ void __launch_bounds__(256, 2) sage_quant_q_stats_kernel(Src src, int
       cp_async16(sf(1, p), f + 4, vq);
     }
   }
-  uint4 wq[2], wk[2];
-  if (Src::kNormRope) {
-    wq[0] = src.weight(0, 0);
-    wq[1] = src.weight(0, 1);
-    wk[0] = src.weight(1, 0);
-    wk[1] = src.weight(1, 1);
-  }
   cp_async_wait_all();
-  uint4 qx[4];
-  float rmax[4];
+  uint4 qx[2];
   float ks[8];
   uint32_t vm2[4] = {0u, 0u, 0u, 0u};
+  float amax = 1e-7f;
 #pragma unroll
   for (int e = 0; e < 8; ++e) ks[e] = 0.0f;
 #pragma unroll
-  for (int p = 0; p < 4; ++p) {
-    const int row = tile * kQTile + p * 16 + rs;
+  for (int p = 0; p < 2; ++p) {
+    const int row = tile * kQBlock + p * 16 + rs;
     float cs[8];
-    const bool first = src.first(row);
+    const int stream = src.first(row) ? 0 : 1;
     if (Src::kNormRope) load_cs(sf(0, p), sf(1, p), cs);
-    float amax = 1e-7f;
     qx[p] = make_uint4(0u, 0u, 0u, 0u);
     if (row < Sq) {
       qx[p] = *sx(0, p);
-      if (Src::kNormRope) qx[p] = norm_rope_piece(qx[p], first ? wq[0] : wq[1], cs, src.eps);
+      if (Src::kNormRope) qx[p] = norm_rope_piece(qx[p], src.weight(0, stream), cs, src.eps);
       amax = piece_amax(qx[p], amax);
     }
     if (row < Skv) {
       uint4 y = *sx(1, p);
       if (Src::kNormRope) {
-        y = norm_rope_piece(y, first ? wk[0] : wk[1], cs, src.eps);
+        y = norm_rope_piece(y, src.weight(1, stream), cs, src.eps);
         *reinterpret_cast<uint4*>(src.knrow(b, h, row) + cg * 8) = y;
       }
       float f[8];
@@ -300,71 +301,105 @@ __global__ void __launch_bounds__(256, 2) sage_quant_q_stats_kernel(Src src, int
       vm2[2] = max_bf16x2(vm2[2], abs_bf16x2(v.z));
       vm2[3] = max_bf16x2(vm2[3], abs_bf16x2(v.w));
     }
-    rmax[p] = row_amax(amax);
   }
-  // 32-row Q blocks: passes {0, 1} and {2, 3}; per warp, then across warps
-  const float w0 = pair_amax(fmaxf(rmax[0], rmax[1])), w1 = pair_amax(fmaxf(rmax[2], rmax[3]));
-  if ((t & 31) == 0) {
-    s_wmax[0][warp] = w0;
-    s_wmax[1][warp] = w1;
+  // the tile is one 32-row Q block: per warp (both half-warps), then across warps
+  amax = pair_amax(row_amax(amax));
+  if ((t & 31) == 0) s_wmax[warp] = amax;
+  // K sums / |V| maxima: the two row groups of a warp combined (one add), then
+  // the eight warps in order through shared memory
+  float vm[8];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    vm[2 * i] = bf16_lo(vm2[i]);
+    vm[2 * i + 1] = bf16_hi(vm2[i]);
   }
-  float4* sk = reinterpret_cast<float4*>(&s_k[rs][cg * 8]);
-  float4* sv = reinterpret_cast<float4*>(&s_v[rs][cg * 8]);
-  sk[0] = make_float4(ks[0], ks[1], ks[2], ks[3]);
-  sk[1] = make_float4(ks[4], ks[5], ks[6], ks[7]);
-  sv[0] = make_float4(bf16_lo(vm2[0]), bf16_hi(vm2[0]), bf16_lo(vm2[1]), bf16_hi(vm2[1]));
-  sv[1] = make_float4(bf16_lo(vm2[2]), bf16_hi(vm2[2]), bf16_lo(vm2[3]), bf16_hi(vm2[3]));
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
+    ks[e] += __shfl_xor_sync(0xffffffffu, ks[e], 16);
+    vm[e] = fmaxf(vm[e], __shfl_xor_sync(0xffffffffu, vm[e], 16));
+  }
+  if (rs % 2 == 0) {
+    float4* sk = reinterpret_cast<float4*>(&s_k[warp][cg * 8]);
+    float4* sv = reinterpret_cast<float4*>(&s_v[warp][cg * 8]);
+    sk[0] = make_float4(ks[0], ks[1], ks[2], ks[3]);
+    sk[1] = make_float4(ks[4], ks[5], ks[6], ks[7]);
+    sv[0] = make_float4(vm[0], vm[1], vm[2], vm[3]);
+    sv[1] = make_float4(vm[4], vm[5], vm[6], vm[7]);
+  }
   __syncthreads();
   if (t < kD && do_kv) {
-    float sum = 0.0f, amax = 0.0f;
+    float sum = 0.0f, vmax = 0.0f;
 #pragma unroll
-    for (int g = 0; g < 16; ++g) {
-      sum += s_k[g][t];
-      amax = fmaxf(amax, s_v[g][t]);
+    for (int w = 0; w < 8; ++w) {
+      sum += s_k[w][t];
+      vmax = fmaxf(vmax, s_v[w][t]);
     }
     const int64_t o = (int64_t(bh) * part_stride + tile) * kD + t;
     k_part[o] = sum;
-    v_part[o] = amax;
+    v_part[o] = vmax;
   }
   if (!do_q) return;
-  float bm[2];
-#pragma unroll
-  for (int i = 0; i < 2; ++i) {
-    const float4 a = *reinterpret_cast<const float4*>(&s_wmax[i][0]);
-    const float4 c = *reinterpret_cast<const float4*>(&s_wmax[i][4]);
-    bm[i] = fmaxf(fmaxf(fmaxf(a.x, a.y), fmaxf(a.z, a.w)), fmaxf(fmaxf(c.x, c.y), fmaxf(c.z, c.w)));
-  }
-  if (t < 2) q_scale[int64_t(bh) * (Sq_pad / 32) + tile * 2 + t] = __fdiv_rn(t == 0 ? bm[0] : bm[1], 127.0f);
-  const float inv0 = __fdiv_rn(127.0f, bm[0]), inv1 = __fdiv_rn(127.0f, bm[1]);
+  const float4 a = *reinterpret_cast<const float4*>(&s_wmax[0]);
+  const float4 c = *reinterpret_cast<const float4*>(&s_wmax[4]);
+  const float bm = fmaxf(fmaxf(fmaxf(a.x, a.y), fmaxf(a.z, a.w)), fmaxf(fmaxf(c.x, c.y), fmaxf(c.z, c.w)));
+  if (t == 0) q_scale[int64_t(bh) * (Sq_pad / 32) + tile] = __fdiv_rn(bm, 127.0f);
+  const float inv = __fdiv_rn(127.0f, bm);
   const float none[8] = {};
-  int8_t* dst = q8 + (int64_t(bh) * Sq_pad + tile * kQTile) * kD + cg * 8;
+  int8_t* dst = q8 + (int64_t(bh) * Sq_pad + tile * kQBlock) * kD + cg * 8;
 #pragma unroll
-  for (int p = 0; p < 4; ++p) {
+  for (int p = 0; p < 2; ++p) {
     const int r = p * 16 + rs;
-    const uint2 code = tile * kQTile + r < Sq ? int8_piece<false>(qx[p], none, p < 2 ? inv0 : inv1)
-                                              : make_uint2(0u, 0u);
+    const uint2 code = tile * kQBlock + r < Sq ? int8_piece<false>(qx[p], none, inv) : make_uint2(0u, 0u);
     *reinterpret_cast<uint2*>(dst + int64_t(r) * kD) = code;
   }
 }
 
-// Grid (B*H), 128 threads: the tile partials reduced in tile order.
-__global__ void __launch_bounds__(128) sage_quant_finalize_kernel(const float* __restrict__ k_part,
+// Grid (B*H, 4), 256 threads: 32 channels per CTA, eight sub-sums per
+// channel. Thread (sub, channel) adds the partials of tiles sub, sub + 8,
+// sub + 16, ... in order to 0.0 (all its loads in flight at once, 16 at a
+// time); the eight sub-sums are then added in sub order to 0.0. |V| maxima
+// the same way.
+__global__ void __launch_bounds__(256) sage_quant_finalize_kernel(const float* __restrict__ k_part,
                                                                   const float* __restrict__ v_part, int tiles,
                                                                   int part_stride, int S,
                                                                   __nv_bfloat16* __restrict__ k_mean,
                                                                   float* __restrict__ v_scale,
                                                                   float* __restrict__ v_recp) {
-  const int bh = blockIdx.x, d = threadIdx.x;
+  __shared__ float s_sum[8][32], s_max[8][32];
+  const int bh = blockIdx.x, t = threadIdx.x, ch = t & 31, sub = t >> 5, d = blockIdx.y * 32 + ch;
   const int64_t base = int64_t(bh) * part_stride * kD + d;
   float sum = 0.0f, amax = 0.0f;
-#pragma unroll 8
-  for (int i = 0; i < tiles; ++i) {
-    sum += k_part[base + int64_t(i) * kD];
-    amax = fmaxf(amax, v_part[base + int64_t(i) * kD]);
+  for (int i0 = sub; i0 < tiles; i0 += 8 * 16) {
+    float kv[16], vv[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const int i = i0 + 8 * j;
+      kv[j] = i < tiles ? __ldg(k_part + base + int64_t(i) * kD) : 0.0f;
+      vv[j] = i < tiles ? __ldg(v_part + base + int64_t(i) * kD) : 0.0f;
+    }
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      if (i0 + 8 * j < tiles) {
+        sum += kv[j];
+        amax = fmaxf(amax, vv[j]);
+      }
+    }
   }
-  k_mean[int64_t(bh) * kD + d] = __float2bfloat16_rn(sum * (1.0f / float(S)));
-  v_scale[int64_t(bh) * kD + d] = amax / 448.0f;
-  v_recp[int64_t(bh) * kD + d] = amax > 0.0f ? 448.0f / amax : 0.0f;
+  s_sum[sub][ch] = sum;
+  s_max[sub][ch] = amax;
+  __syncthreads();
+  if (t < 32) {
+    float total = 0.0f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) total += s_sum[j][ch];
+    k_mean[int64_t(bh) * kD + d] = __float2bfloat16_rn(total * (1.0f / float(S)));
+  } else if (t < 64) {
+    float m = 0.0f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) m = fmaxf(m, s_max[j][ch]);
+    v_scale[int64_t(bh) * kD + d] = m / 448.0f;
+    v_recp[int64_t(bh) * kD + d] = m > 0.0f ? 448.0f / m : 0.0f;
+  }
 }
 
 // Grid (B*H, S_pad/64, 2), 256 threads. z = 0: K codes of k - k_mean (one
@@ -926,8 +961,8 @@ struct Workspace {
   float* v_scale;
   __nv_bfloat16* k_mean;
   float* v_recp;
-  float* k_part;   // [B*H, S_kv_pad/64, 128] per-64-row-tile K column sums
-  float* v_part;   // [B*H, S_kv_pad/64, 128] per-64-row-tile |V| column maxima
+  float* k_part;   // [B*H, S_kv_pad/32, 128] per-32-row-tile K column sums
+  float* v_part;   // [B*H, S_kv_pad/32, 128] per-32-row-tile |V| column maxima
   __nv_bfloat16* kn;  // [B*H, S_kv_pad, 128] normalised K (joint-sequence entry points)
 };
 
@@ -947,8 +982,8 @@ int64_t workspace_layout(int64_t B, int64_t H, int64_t Sq, int64_t Skv, uint8_t*
   uint8_t* vs = take(bh * kD * 4);
   uint8_t* km = take(bh * kD * 2);
   uint8_t* vr = take(bh * kD * 4);
-  uint8_t* kpart = take(bh * (skp / 64) * kD * 4);
-  uint8_t* vpart = take(bh * (skp / 64) * kD * 4);
+  uint8_t* kpart = take(bh * (skp / 32) * kD * 4);
+  uint8_t* vpart = take(bh * (skp / 32) * kD * 4);
   uint8_t* kn = take(bh * skp * kD * 2);
   if (ws) {
     ws->q8 = (int8_t*)q8;
@@ -1001,14 +1036,14 @@ int quant_rows(const Src& src, int64_t B, int64_t H, int64_t Sq, int64_t Skv, co
   int rc = quant_smem_attrs<Src>();
   if (rc) return rc;
   const int64_t sqp = pad128(Sq), skp = pad128(Skv);
-  const unsigned bh = unsigned(B * H), q_tiles = unsigned(sqp / kQTile);
-  const unsigned kv_tiles = unsigned((Skv + kQTile - 1) / kQTile);
-  const int part_stride = int(skp / kQTile);
+  const unsigned bh = unsigned(B * H), q_tiles = unsigned(sqp / kQBlock);
+  const unsigned kv_tiles = unsigned((Skv + kQBlock - 1) / kQBlock);
+  const int part_stride = int(skp / kQBlock);
   sage_quant_q_stats_kernel<Src><<<dim3(bh, q_tiles > kv_tiles ? q_tiles : kv_tiles), 256, q_stats_smem<Src>(), st>>>(
       src, int(Sq), int(sqp), int(Skv), int(H), int(kv_tiles), part_stride, ws.q8, ws.q_scale, ws.k_part, ws.v_part);
   rc = check_launch("sage_quant_q_stats_kernel");
   if (rc) return rc;
-  sage_quant_finalize_kernel<<<bh, kD, 0, st>>>(ws.k_part, ws.v_part, int(kv_tiles), part_stride, int(Skv), ws.k_mean,
+  sage_quant_finalize_kernel<<<dim3(bh, kD / 32), 256, 0, st>>>(ws.k_part, ws.v_part, int(kv_tiles), part_stride, int(Skv), ws.k_mean,
                                                  ws.v_scale, ws.v_recp);
   rc = check_launch("sage_quant_finalize_kernel");
   if (rc) return rc;

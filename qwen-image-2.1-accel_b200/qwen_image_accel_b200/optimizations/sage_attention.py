@@ -47,8 +47,8 @@ def workspace_views(ws: torch.Tensor, batch: int, heads: int, seq_q: int, seq_kv
                ("v_scale", bh * 128 * 4, torch.float32, (bh, 128)),
                ("k_mean", bh * 128 * 2, torch.bfloat16, (bh, 128)),
                ("v_recp", bh * 128 * 4, torch.float32, (bh, 128)),
-               ("k_part", bh * (skp // 64) * 128 * 4, torch.float32, (bh, skp // 64, 128)),
-               ("v_part", bh * (skp // 64) * 128 * 4, torch.float32, (bh, skp // 64, 128)),
+               ("k_part", bh * (skp // 32) * 128 * 4, torch.float32, (bh, skp // 32, 128)),
+               ("v_part", bh * (skp // 32) * 128 * 4, torch.float32, (bh, skp // 32, 128)),
                ("kn", bh * skp * 128 * 2, torch.bfloat16, (bh, skp, 128))]
     out, off = {}, 0
     for name, nbytes, dtype, shape in regions:
