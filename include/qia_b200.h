@@ -202,6 +202,45 @@ int qia_mxfp8_gemm_gate_residual(const void* a_values, const void* a_scales,
                                  int64_t n, int64_t k, int64_t ldo,
                                  int64_t rows_per_batch, void* stream);
 
+/* One GEMM of a grouped launch. The fields an epilogue does not use are
+ * ignored: out/ldo for QIA_EPI_GELU_QUANT, q_values/q_scales for the others,
+ * gate/resid/rows_per_batch outside QIA_EPI_GATE_RESIDUAL. */
+typedef struct qia_mxfp8_gemm_problem {
+  const void* a_values;
+  const void* a_scales;
+  const void* b_values;
+  const void* b_scales;
+  const void* bias;       /* [n] bf16 or NULL */
+  const void* gate;       /* [m / rows_per_batch, n] bf16 */
+  const void* resid;      /* [m, ldo] bf16, may be out */
+  void* out;              /* [m, ldo] bf16 */
+  int64_t ldo;
+  void* q_values;         /* [ceil(m/128)*128, n] e4m3 */
+  void* q_scales;         /* blocked E8M0 */
+  int64_t m;
+  int64_t rows_per_batch;
+} qia_mxfp8_gemm_problem;
+
+enum qia_epilogue {
+  QIA_EPI_BF16 = 0,          /* qia_mxfp8_gemm */
+  QIA_EPI_GELU_QUANT = 1,    /* qia_mxfp8_gemm_gelu_quant */
+  QIA_EPI_GATE_RESIDUAL = 2, /* qia_mxfp8_gemm_gate_residual */
+  QIA_EPI_GELU_BF16 = 3      /* qia_mxfp8_gemm_gelu */
+};
+
+/* One or two GEMMs with the same n, k and epilogue in one persistent launch
+ * (count = 1 or 2): output tiles of problem 0 first, then problem 1's, so a
+ * small GEMM (the text stream's, m = batch * text tokens) fills the larger
+ * one's last wave instead of running as a separate launch that leaves most
+ * SMs idle. Each problem's results equal its single-GEMM entry point's.
+ * Replaces: the image- and text-stream MXFP8Linear.matmul pair of each
+ * projection of the dual-stream block (src/qwen_image_accel/optimizations/
+ * mxfp8.py:229-233, called per stream by QwenDoubleStreamAttnProcessor2_0 and
+ * the two MLPs, WHL:diffusers/models/transformers/transformer_qwenimage.py:
+ * 540-600, 741-767). */
+int qia_mxfp8_gemm_grouped(int epilogue, const qia_mxfp8_gemm_problem* problems,
+                           int count, int64_t n, int64_t k, void* stream);
+
 /* ---------------------------------------------------------------------------
  * Sage-style quantized attention (tcgen05: INT8 Q.K^T, FP8 P.V)
  *

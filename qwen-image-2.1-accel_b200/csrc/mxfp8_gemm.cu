@@ -57,6 +57,21 @@ struct EpiParams {
   int wide;                    // out/resid/q_values rows allow 32-byte accesses
 };
 
+// One or two GEMMs with the same N, K, tile width and epilogue kind run as
+// one persistent launch (the dual-stream block's image and text projections):
+// output tiles [0, tiles0) belong to problem 0, [tiles0, num_tiles) to
+// problem 1, so the small text GEMM fills the image GEMM's last wave instead
+// of running as a separate, mostly idle launch.
+struct GemmGroup {
+  const uint8_t* sfa0;
+  const uint8_t* sfb0;
+  const uint8_t* sfa1;
+  const uint8_t* sfb1;
+  EpiParams ep0, ep1;
+  int M0, M1;
+  int tiles0, num_tiles;
+};
+
 constexpr int kEpiWarps = 8;
 constexpr int kGemmThreads = 64 + 32 * kEpiWarps;
 
@@ -206,9 +221,9 @@ __device__ __forceinline__ void epilogue_chunk(float (&v)[32], const EpiParams& 
 
 template <int BN, int EPI>
 __global__ void __launch_bounds__(kGemmThreads, 1)
-mxfp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
-                  const uint8_t* __restrict__ sfa, const uint8_t* __restrict__ sfb, EpiParams ep, int M, int N,
-                  int K, int* err) {
+mxfp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a0, const __grid_constant__ CUtensorMap tmap_b0,
+                  const __grid_constant__ CUtensorMap tmap_a1, const __grid_constant__ CUtensorMap tmap_b1,
+                  const GemmGroup g, int N, int K, int* err) {
   using C = Cfg<BN>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -221,8 +236,8 @@ mxfp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_const
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int m_tiles = (M + 127) / 128, n_tiles = N / BN, k_blocks = K / 128;
-  const int num_tiles = m_tiles * n_tiles;
+  const int n_tiles = N / BN, k_blocks = K / 128;
+  const int num_tiles = g.num_tiles;
   const int kb_tiles = K / 128;  // 512-byte scale chunks per 128 rows
 
   if (threadIdx.x == 0) {
@@ -236,8 +251,12 @@ mxfp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_const
     }
     mbar_init(smem_u32(drain), 1);
     fence_barrier_init();
-    prefetch_tmap(&tmap_a);
-    prefetch_tmap(&tmap_b);
+    prefetch_tmap(&tmap_a0);
+    prefetch_tmap(&tmap_b0);
+    if (g.num_tiles > g.tiles0) {
+      prefetch_tmap(&tmap_a1);
+      prefetch_tmap(&tmap_b1);
+    }
   }
   if (warp == 1) tmem_alloc(smem_u32(tmem_slot), C::TMEM_COLS);
   tc_fence_before();
@@ -253,17 +272,21 @@ mxfp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_const
       int issued = 0;
       bool ok = true;
       for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
-        const int m_blk = tile / n_tiles, n_blk = tile % n_tiles;
+        const bool second = tile >= g.tiles0;
+        const int lt = second ? tile - g.tiles0 : tile;
+        const int m_blk = lt / n_tiles, n_blk = lt % n_tiles;
         const int m0 = m_blk * 128, n0 = n_blk * BN;
-        const uint8_t* sfa_tile = sfa + int64_t(m_blk) * kb_tiles * 512;
-        const uint8_t* sfb_tile = sfb + int64_t(n0 >> 7) * kb_tiles * 512;
+        const CUtensorMap* tmap_a = second ? &tmap_a1 : &tmap_a0;
+        const CUtensorMap* tmap_b = second ? &tmap_b1 : &tmap_b0;
+        const uint8_t* sfa_tile = (second ? g.sfa1 : g.sfa0) + int64_t(m_blk) * kb_tiles * 512;
+        const uint8_t* sfb_tile = (second ? g.sfb1 : g.sfb0) + int64_t(n0 >> 7) * kb_tiles * 512;
         for (int kb = 0; kb < k_blocks; ++kb) {
           if (!mbar_wait(smem_u32(&empty[s]), phase ^ 1, err)) { ok = false; break; }
           uint8_t* st = smem + s * C::STAGE_BYTES;
           const uint32_t fb = smem_u32(&full[s]);
           mbar_arrive_expect_tx(fb, C::A_BYTES + C::B_BYTES + C::SF_BYTES);
-          tma_load_2d(smem_u32(st), &tmap_a, fb, kb * 128, m0);
-          tma_load_2d(smem_u32(st + C::A_BYTES), &tmap_b, fb, kb * 128, n0);
+          tma_load_2d(smem_u32(st), tmap_a, fb, kb * 128, m0);
+          tma_load_2d(smem_u32(st + C::A_BYTES), tmap_b, fb, kb * 128, n0);
           bulk_load(smem_u32(st + C::A_BYTES + C::B_BYTES), sfa_tile + kb * 512, 512, fb);
 #pragma unroll
           for (int c = 0; c < C::SFB_CHUNKS; ++c)
@@ -304,7 +327,7 @@ mxfp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_const
         const uint32_t acc_phase = (C::NACC == 2) ? ((it >> 1) & 1) : (it & 1);
         if (!mbar_wait(smem_u32(&acc_empty[a]), acc_phase ^ 1, err)) { ok = false; break; }
         tc_fence_after();
-        const int n0 = (tile % n_tiles) * BN;
+        const int n0 = ((tile >= g.tiles0 ? tile - g.tiles0 : tile) % n_tiles) * BN;
         const uint32_t d_tmem = tmem_base + uint32_t(a * BN);
         // BN=192 tiles at odd multiples of 64 start 2 columns into the chunk
         const uint32_t sfb_shift = uint32_t(C::SFB_OFF + ((n0 & 127) >> 5));
@@ -349,9 +372,12 @@ mxfp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_const
       const bool got = __all_sync(0xffffffffu, mbar_wait(smem_u32(&acc_full[a]), acc_phase, err));
       if (!got) break;
       tc_fence_after();
-      const int m0 = (tile / n_tiles) * 128, n0 = (tile % n_tiles) * BN;
+      const bool second = tile >= g.tiles0;
+      const int lt = second ? tile - g.tiles0 : tile;
+      const int m0 = (lt / n_tiles) * 128, n0 = (lt % n_tiles) * BN;
+      const EpiParams& ep = second ? g.ep1 : g.ep0;
       const int64_t row = m0 + row_in_tile;
-      const bool live = row < M;
+      const bool live = row < (second ? g.M1 : g.M0);
       const uint32_t t_row = tmem_base + (uint32_t(sub * 32) << 16) + uint32_t(a * BN);
       if constexpr (C::NACC == 1) {
         // one accumulator: the next tile's MMAs wait for it, so take all of
@@ -680,9 +706,18 @@ int make_tmap(CUtensorMap* map, const void* base, int64_t rows, int64_t cols, in
   return QIA_OK;
 }
 
+// One GEMM of a group as the host sees it.
+struct Problem {
+  const void* a;
+  const void* sa;
+  const void* b;
+  const void* sb;
+  EpiParams ep;
+  int64_t M;
+};
+
 template <int BN, int EPI>
-int launch_gemm(const void* a, const void* sa, const void* b, const void* sb, const EpiParams& ep, int64_t M,
-                int64_t N, int64_t K, cudaStream_t st) {
+int launch_gemm(const Problem* pr, int count, int64_t N, int64_t K, cudaStream_t st) {
   using C = Cfg<BN>;
   static bool attr_done[64] = {false};
   static std::mutex mu;
@@ -697,17 +732,36 @@ int launch_gemm(const void* a, const void* sa, const void* b, const void* sb, co
       attr_done[dev] = true;
     }
   }
-  const int64_t m_pad = (M + 127) / 128 * 128;
-  CUtensorMap ta, tb;
-  int rc = make_tmap(&ta, a, m_pad, K, 128);
-  if (rc) return rc;
-  rc = make_tmap(&tb, b, N, K, BN);
-  if (rc) return rc;
-  const int64_t tiles = (m_pad / 128) * (N / BN);
+  CUtensorMap ta[2], tb[2];
+  int64_t tiles[2] = {0, 0};
+  for (int i = 0; i < count; ++i) {
+    const int64_t m_pad = (pr[i].M + 127) / 128 * 128;
+    int rc = make_tmap(&ta[i], pr[i].a, m_pad, K, 128);
+    if (rc) return rc;
+    rc = make_tmap(&tb[i], pr[i].b, N, K, BN);
+    if (rc) return rc;
+    tiles[i] = (m_pad / 128) * (N / BN);
+  }
+  if (count == 1) {
+    ta[1] = ta[0];
+    tb[1] = tb[0];
+  }
+  GemmGroup g;
+  g.sfa0 = (const uint8_t*)pr[0].sa;
+  g.sfb0 = (const uint8_t*)pr[0].sb;
+  g.ep0 = pr[0].ep;
+  g.M0 = int(pr[0].M);
+  const Problem& p1 = pr[count - 1];
+  g.sfa1 = (const uint8_t*)p1.sa;
+  g.sfb1 = (const uint8_t*)p1.sb;
+  g.ep1 = p1.ep;
+  g.M1 = int(p1.M);
+  g.tiles0 = int(tiles[0]);
+  g.num_tiles = int(tiles[0] + tiles[1]);
   int64_t grid = sm_count();
-  if (grid > tiles) grid = tiles;
-  mxfp8_gemm_kernel<BN, EPI><<<unsigned(grid), kGemmThreads, C::SMEM, st>>>(
-      ta, tb, (const uint8_t*)sa, (const uint8_t*)sb, ep, int(M), int(N), int(K), device_error_word());
+  if (grid > g.num_tiles) grid = g.num_tiles;
+  mxfp8_gemm_kernel<BN, EPI><<<unsigned(grid), kGemmThreads, C::SMEM, st>>>(ta[0], tb[0], ta[1], tb[1], g, int(N),
+                                                                            int(K), device_error_word());
   return check_launch("mxfp8_gemm_kernel");
 }
 
@@ -854,34 +908,51 @@ int pick_bn_pair(int64_t M, int64_t N) {
 }
 
 template <int EPI>
-int dispatch(const void* a, const void* sa, const void* b, const void* sb, const EpiParams& ep, int64_t M, int64_t N,
-             int64_t K, void* stream, const char* who) {
-  if (!a || !sa || !b || !sb) return set_error(QIA_ERR_INVALID, "%s: null operand", who);
-  if (M <= 0 || N <= 0 || K <= 0) return set_error(QIA_ERR_INVALID, "%s: M=%lld N=%lld K=%lld", who, (long long)M,
-                                                   (long long)N, (long long)K);
+int dispatch(const Problem* in, int count, int64_t N, int64_t K, void* stream, const char* who) {
+  if (count < 1 || count > 2) return set_error(QIA_ERR_INVALID, "%s: 1 or 2 problems per launch", who);
+  if (N <= 0 || K <= 0) return set_error(QIA_ERR_INVALID, "%s: N=%lld K=%lld", who, (long long)N, (long long)K);
   if (K % 128 || N % 128) return set_error(QIA_ERR_UNSUPPORTED, "%s: K and N must be multiples of 128", who);
-  if (M > (1LL << 30) || K > (1LL << 20) || N > (1LL << 20)) return set_error(QIA_ERR_UNSUPPORTED, "%s: too large", who);
-  if (!aligned(a, 16) || !aligned(b, 16) || !aligned(sa, 16) || !aligned(sb, 16))
-    return set_error(QIA_ERR_ALIGNMENT, "%s: operands must be 16-byte aligned", who);
-  EpiParams epw = ep;
-  epw.wide = (!ep.out || (aligned(ep.out, 32) && ep.ldo % 16 == 0)) && (!ep.resid || aligned(ep.resid, 32)) &&
-             (!ep.q_values || aligned(ep.q_values, 32));
+  if (K > (1LL << 20) || N > (1LL << 20)) return set_error(QIA_ERR_UNSUPPORTED, "%s: too large", who);
+  Problem pr[2];
+  int64_t m_tiles = 0;
+  for (int i = 0; i < count; ++i) {
+    const Problem& p = in[i];
+    if (!p.a || !p.sa || !p.b || !p.sb) return set_error(QIA_ERR_INVALID, "%s: null operand", who);
+    if (p.M <= 0 || p.M > (1LL << 30)) return set_error(QIA_ERR_INVALID, "%s: M=%lld", who, (long long)p.M);
+    if (!aligned(p.a, 16) || !aligned(p.b, 16) || !aligned(p.sa, 16) || !aligned(p.sb, 16))
+      return set_error(QIA_ERR_ALIGNMENT, "%s: operands must be 16-byte aligned", who);
+    pr[i] = p;
+    const EpiParams& ep = p.ep;
+    pr[i].ep.wide = (!ep.out || (aligned(ep.out, 32) && ep.ldo % 16 == 0)) && (!ep.resid || aligned(ep.resid, 32)) &&
+                    (!ep.q_values || aligned(ep.q_values, 32));
+    m_tiles += (p.M + 127) / 128;
+  }
+  if (m_tiles * 128 > (1LL << 30)) return set_error(QIA_ERR_UNSUPPORTED, "%s: too large", who);
   cudaStream_t st = as_stream(stream);
-  if (use_pair(M)) {
-    switch (pick_bn_pair(M, N)) {
-      case 128: return launch_gemm_pair<128, EPI>(a, sa, b, sb, epw, M, N, K, st);
-      case 192: return launch_gemm_pair<192, EPI>(a, sa, b, sb, epw, M, N, K, st);
-      case 256: return launch_gemm_pair<256, EPI>(a, sa, b, sb, epw, M, N, K, st);
+  if (count == 1 && use_pair(pr[0].M)) {
+    const Problem& p = pr[0];
+    switch (pick_bn_pair(p.M, N)) {
+      case 128: return launch_gemm_pair<128, EPI>(p.a, p.sa, p.b, p.sb, p.ep, p.M, N, K, st);
+      case 192: return launch_gemm_pair<192, EPI>(p.a, p.sa, p.b, p.sb, p.ep, p.M, N, K, st);
+      case 256: return launch_gemm_pair<256, EPI>(p.a, p.sa, p.b, p.sb, p.ep, p.M, N, K, st);
       default: return set_error(QIA_ERR_UNSUPPORTED, "%s: N=%lld has no supported tile width", who, (long long)N);
     }
   }
-  const int bn = pick_bn(M, N, EPI == kEpiGeluQuant || EPI == kEpiGeluBf16);
+  // the tile width is chosen for the group's total M tiles
+  const int bn = pick_bn(m_tiles * 128, N, EPI == kEpiGeluQuant || EPI == kEpiGeluBf16);
   switch (bn) {
-    case 128: return launch_gemm<128, EPI>(a, sa, b, sb, epw, M, N, K, st);
-    case 192: return launch_gemm<192, EPI>(a, sa, b, sb, epw, M, N, K, st);
-    case 256: return launch_gemm<256, EPI>(a, sa, b, sb, epw, M, N, K, st);
+    case 128: return launch_gemm<128, EPI>(pr, count, N, K, st);
+    case 192: return launch_gemm<192, EPI>(pr, count, N, K, st);
+    case 256: return launch_gemm<256, EPI>(pr, count, N, K, st);
     default: return set_error(QIA_ERR_UNSUPPORTED, "%s: N=%lld has no supported tile width", who, (long long)N);
   }
+}
+
+template <int EPI>
+int dispatch(const void* a, const void* sa, const void* b, const void* sb, const EpiParams& ep, int64_t M, int64_t N,
+             int64_t K, void* stream, const char* who) {
+  Problem p{a, sa, b, sb, ep, M};
+  return dispatch<EPI>(&p, 1, N, K, stream, who);
 }
 
 int check_out(const void* out, int64_t ldo, int64_t N, const char* who) {
@@ -955,4 +1026,44 @@ extern "C" int qia_mxfp8_gemm_gate_residual(const void* a_values, const void* a_
   ep.rows_per_batch = rows_per_batch;
   return dispatch<kEpiGateResidual>(a_values, a_scales, b_values, b_scales, ep, m, n, k, stream,
                                     "qia_mxfp8_gemm_gate_residual");
+}
+
+extern "C" int qia_mxfp8_gemm_grouped(int epilogue, const qia_mxfp8_gemm_problem* problems, int count, int64_t n,
+                                      int64_t k, void* stream) {
+  const char* who = "qia_mxfp8_gemm_grouped";
+  if (!problems || count < 1 || count > 2) return set_error(QIA_ERR_INVALID, "%s: 1 or 2 problems", who);
+  Problem pr[2];
+  for (int i = 0; i < count; ++i) {
+    const qia_mxfp8_gemm_problem& q = problems[i];
+    if (q.bias && !aligned(q.bias, 16)) return set_error(QIA_ERR_ALIGNMENT, "%s: bias alignment", who);
+    EpiParams ep{};
+    ep.bias = (const __nv_bfloat16*)q.bias;
+    if (epilogue == kEpiGeluQuant) {
+      if (!q.q_values || !q.q_scales) return set_error(QIA_ERR_INVALID, "%s: null MXFP8 output", who);
+      if (!aligned(q.q_values, 16)) return set_error(QIA_ERR_ALIGNMENT, "%s: output alignment", who);
+      ep.q_values = (uint8_t*)q.q_values;
+      ep.q_scales = (uint8_t*)q.q_scales;
+    } else {
+      int rc = check_out(q.out, q.ldo, n, who);
+      if (rc) return rc;
+      ep.out = (__nv_bfloat16*)q.out;
+      ep.ldo = q.ldo;
+    }
+    if (epilogue == kEpiGateResidual) {
+      if (!q.gate || !q.resid || q.rows_per_batch <= 0)
+        return set_error(QIA_ERR_INVALID, "%s: gate/resid/rows_per_batch", who);
+      if (!aligned(q.gate, 16) || !aligned(q.resid, 16)) return set_error(QIA_ERR_ALIGNMENT, "%s: alignment", who);
+      ep.gate = (const __nv_bfloat16*)q.gate;
+      ep.resid = (const __nv_bfloat16*)q.resid;
+      ep.rows_per_batch = q.rows_per_batch;
+    }
+    pr[i] = Problem{q.a_values, q.a_scales, q.b_values, q.b_scales, ep, q.m};
+  }
+  switch (epilogue) {
+    case kEpiBf16: return dispatch<kEpiBf16>(pr, count, n, k, stream, who);
+    case kEpiGeluQuant: return dispatch<kEpiGeluQuant>(pr, count, n, k, stream, who);
+    case kEpiGateResidual: return dispatch<kEpiGateResidual>(pr, count, n, k, stream, who);
+    case kEpiGeluBf16: return dispatch<kEpiGeluBf16>(pr, count, n, k, stream, who);
+    default: return set_error(QIA_ERR_INVALID, "%s: unknown epilogue %d", who, epilogue);
+  }
 }

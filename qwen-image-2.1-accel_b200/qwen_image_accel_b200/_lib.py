@@ -17,8 +17,20 @@ _P = ctypes.c_void_p
 _I = ctypes.c_int64
 _F = ctypes.c_float
 
+
+
+class GemmProblem(ctypes.Structure):
+    """qia_mxfp8_gemm_problem: one GEMM of a qia_mxfp8_gemm_grouped launch."""
+    _fields_ = [("a_values", _P), ("a_scales", _P), ("b_values", _P), ("b_scales", _P), ("bias", _P),
+                ("gate", _P), ("resid", _P), ("out", _P), ("ldo", _I), ("q_values", _P), ("q_scales", _P),
+                ("m", _I), ("rows_per_batch", _I)]
+
+
+EPI_BF16, EPI_GELU_QUANT, EPI_GATE_RESIDUAL, EPI_GELU_BF16 = 0, 1, 2, 3
+
 # name -> argument types (all return int status)
 SIGNATURES: dict[str, list] = {
+    "qia_mxfp8_gemm_grouped": [ctypes.c_int, _P, ctypes.c_int, _I, _I, _P],
     "qia_ln_mod": [_P, _P, _P, _P, _I, _I, _I, _F, _P],
     "qia_ln_mod_quant": [_P, _P, _P, _P, _P, _I, _I, _I, _F, _P],
     "qia_gated_residual": [_P, _P, _P, _P, _I, _I, _I, _P],

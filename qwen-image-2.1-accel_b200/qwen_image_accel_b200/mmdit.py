@@ -7,16 +7,17 @@ QwenImageTransformer2DModel / QwenImageTransformerBlock, :633-790, :859-1031):
 biases, AdaLN shift/scale/gate, text 3584 -> 3072. Weights use the Diffusers
 state-dict names, so a checkpoint of that model loads as is.
 
-Per block and stream the hot path is:
-  LN + (1+scale), +shift -> MXFP8         qia_ln_mod_quant
-  fused Q|K|V GEMM (+bias)                 qia_mxfp8_gemm
+Per block the hot path is (the image and text streams' GEMMs of each
+projection share N and K and run as one grouped launch, text tiles last):
+  LN + (1+scale), +shift -> MXFP8         qia_ln_mod_quant (per stream)
+  fused Q|K|V GEMM (+bias)                 qia_mxfp8_gemm_grouped (bf16)
   QK-RMSNorm + RoPE + Sage quantization    qia_sage_attention_joint_mx (both
     + joint [txt, img] INT8/FP8 attention    streams' projections in, per-stream
     -> MXFP8                                 MXFP8 attention outputs back)
-  out-proj GEMM + gate + residual          qia_mxfp8_gemm_gate_residual
-  LN + (1+scale), +shift -> MXFP8          qia_ln_mod_quant
-  FFN up GEMM + bias + GELU -> MXFP8       qia_mxfp8_gemm_gelu_quant
-  FFN down GEMM + gate + residual          qia_mxfp8_gemm_gate_residual
+  out-proj GEMM + gate + residual          qia_mxfp8_gemm_grouped (gate-residual)
+  LN + (1+scale), +shift -> MXFP8          qia_ln_mod_quant (per stream)
+  FFN up GEMM + bias + GELU -> MXFP8       qia_mxfp8_gemm_grouped (GELU-quant)
+  FFN down GEMM + gate + residual          qia_mxfp8_gemm_grouped (gate-residual)
 The prologue/epilogue layers outside the blocks (img_in, txt_norm/txt_in, the
 timestep embedding, the AdaLN modulation linears, norm_out's linear and
 proj_out) stay BF16 torch ops, as in the reference, where
@@ -41,7 +42,8 @@ from .kernels.elementwise import residual
 from .kernels.epilogue import layer_norm_scale_quantize
 from .kernels.layernorm import layer_norm_scale
 from .kernels.mxfp8 import quantize
-from .optimizations.mxfp8 import MXFP8Linear
+from .optimizations.mxfp8 import (MXFP8Linear, matmul_gate_residual_grouped, matmul_gelu_quantize_grouped,
+                                  matmul_grouped)
 from .optimizations.sage_attention import (sage_attention_joint_quantized, sage_attention_split,
                                            sage_attention_split_quantized, workspace_bytes)
 from .kernels.bf16 import gelu_tanh
@@ -289,8 +291,10 @@ class MMDiT:
         sh1_t, s1_t, g1_t, sh2_t, s2_t, g2_t = mod_txt
         # ---- norm1 + modulation + Q|K|V projections
         if self.quantized:
-            qkv_i = blk.img_qkv.mx.matmul(layer_norm_scale_quantize(x, s1_i, self.ln, shift=sh1_i))
-            qkv_t = blk.txt_qkv.mx.matmul(layer_norm_scale_quantize(c, s1_t, self.ln, shift=sh1_t))
+            # image and text projections share N and K: one grouped launch
+            qkv_i, qkv_t = matmul_grouped([
+                (blk.img_qkv.mx, layer_norm_scale_quantize(x, s1_i, self.ln, shift=sh1_i)),
+                (blk.txt_qkv.mx, layer_norm_scale_quantize(c, s1_t, self.ln, shift=sh1_t))])
         else:
             qkv_i = F.linear(layer_norm_scale(x, s1_i, self.ln, shift=sh1_i), blk.img_qkv.w, blk.img_qkv.b)
             qkv_t = F.linear(layer_norm_scale(c, s1_t, self.ln, shift=sh1_t), blk.txt_qkv.w, blk.txt_qkv.b)
@@ -303,8 +307,7 @@ class MMDiT:
                 qkv_t.view(B, Lt, 3 * D), qkv_i.view(B, Li, 3 * D), (blk.norm_added_q, blk.norm_added_k),
                 (blk.norm_q, blk.norm_k), freqs_txt, freqs_img, H, cfg.eps, workspace=self._attn_ws_joint(B, S))
             del qkv_t, qkv_i
-            blk.img_out.mx.matmul_gate_residual(qa_i, g1_i, x, out=x)
-            blk.txt_out.mx.matmul_gate_residual(qa_t, g1_t, c, out=c)
+            matmul_gate_residual_grouped([(blk.img_out.mx, qa_i, g1_i, x), (blk.txt_out.mx, qa_t, g1_t, c)])
             del qa_t, qa_i
         else:
             # ---- QK-RMSNorm + RoPE into the joint [text, image] sequence
@@ -323,17 +326,17 @@ class MMDiT:
         if self.quantized and self.sage:
             pass
         elif self.quantized:
-            blk.img_out.mx.matmul_gate_residual(quantize(a_i.view(B * Li, D)), g1_i, x, out=x)
-            blk.txt_out.mx.matmul_gate_residual(quantize(a_t.view(B * Lt, D)), g1_t, c, out=c)
+            matmul_gate_residual_grouped([(blk.img_out.mx, quantize(a_i.view(B * Li, D)), g1_i, x),
+                                          (blk.txt_out.mx, quantize(a_t.view(B * Lt, D)), g1_t, c)])
         else:
             x = residual(x, F.linear(a_i.view(B, Li, D), blk.img_out.w, blk.img_out.b), g1_i)
             c = residual(c, F.linear(a_t.view(B, Lt, D), blk.txt_out.w, blk.txt_out.b), g1_t)
         # ---- norm2 + modulation + GELU-tanh MLP + gated residual
         if self.quantized:
-            hi = blk.img_up.mx.matmul_gelu_quantize(layer_norm_scale_quantize(x, s2_i, self.ln, shift=sh2_i))
-            blk.img_down.mx.matmul_gate_residual(hi, g2_i, x, out=x)
-            ht = blk.txt_up.mx.matmul_gelu_quantize(layer_norm_scale_quantize(c, s2_t, self.ln, shift=sh2_t))
-            blk.txt_down.mx.matmul_gate_residual(ht, g2_t, c, out=c)
+            hi, ht = matmul_gelu_quantize_grouped([
+                (blk.img_up.mx, layer_norm_scale_quantize(x, s2_i, self.ln, shift=sh2_i)),
+                (blk.txt_up.mx, layer_norm_scale_quantize(c, s2_t, self.ln, shift=sh2_t))])
+            matmul_gate_residual_grouped([(blk.img_down.mx, hi, g2_i, x), (blk.txt_down.mx, ht, g2_t, c)])
         else:
             hi = gelu_tanh(F.linear(layer_norm_scale(x, s2_i, self.ln, shift=sh2_i), blk.img_up.w, blk.img_up.b))
             x = residual(x, F.linear(hi, blk.img_down.w, blk.img_down.b), g2_i)

@@ -9,6 +9,7 @@ MXFP8 requantization, gate + residual).
 """
 from __future__ import annotations
 
+import ctypes
 import os
 
 import torch
@@ -96,6 +97,64 @@ class MXFP8Linear(nn.Module):
         flat = x.reshape(-1, x.shape[-1])
         activation = quantize(flat if flat.stride(-1) == 1 else flat.contiguous())
         return self.matmul(activation, x.dtype).reshape(*x.shape[:-1], self.out_features)
+
+
+def _grouped(epilogue: int, problems: list) -> None:
+    """One qia_mxfp8_gemm_grouped launch over one or two (linear, activation,
+    fields) problems sharing N, K and the epilogue."""
+    lins = [p[0] for p in problems]
+    n, k = lins[0].out_features, lins[0].in_features
+    if any(l.out_features != n or l.in_features != k for l in lins):
+        raise ValueError("grouped GEMMs must share N and K")
+    arr = (_lib.GemmProblem * len(problems))()
+    for slot, (lin, act, fields) in zip(arr, problems):
+        a_v, a_s, b_v, b_s, bias = lin._args(act)
+        slot.a_values, slot.a_scales, slot.b_values, slot.b_scales, slot.bias = a_v, a_s, b_v, b_s, bias
+        slot.m = act.rows
+        for name, value in fields.items():
+            setattr(slot, name, value)
+    device = problems[0][1].values.device
+    _lib.call("qia_mxfp8_gemm_grouped", epilogue, ctypes.addressof(arr), len(problems), n, k, _lib.stream(device))
+
+
+def matmul_grouped(pairs) -> list:
+    """[(linear, activation), ...] (one or two, same N and K) -> their bf16
+    matmuls (+ bias) in one launch."""
+    outs, problems = [], []
+    for lin, act in pairs:
+        out = torch.empty((act.rows, lin.out_features), device=act.values.device, dtype=torch.bfloat16)
+        outs.append(out)
+        problems.append((lin, act, {"out": _lib.ptr(out), "ldo": out.stride(0)}))
+    _grouped(_lib.EPI_BF16, problems)
+    return outs
+
+
+def matmul_gelu_quantize_grouped(pairs) -> list:
+    """[(linear, activation), ...] -> MXFP8 gelu_tanh(activation @ W^T + bias)
+    per problem, in one launch."""
+    outs, problems = [], []
+    for lin, act in pairs:
+        q = empty_quantized(act.rows, lin.out_features, act.values.device)
+        outs.append(q)
+        problems.append((lin, act, {"q_values": _lib.ptr(q.values), "q_scales": _lib.ptr(q.scales)}))
+    _grouped(_lib.EPI_GELU_QUANT, problems)
+    return outs
+
+
+def matmul_gate_residual_grouped(items) -> None:
+    """[(linear, activation, gate, residual), ...]: residual += gate * (activation
+    @ W^T + bias) in place for each, in one launch (the rules of
+    MXFP8Linear.matmul_gate_residual)."""
+    problems = []
+    for lin, act, gate, residual in items:
+        n = lin.out_features
+        res2 = residual.reshape(-1, n)
+        if res2.shape[0] != act.rows or not res2.is_contiguous():
+            raise ValueError("residual must be contiguous with the activation's rows")
+        rows_per_batch = act.rows // gate.reshape(-1, n).shape[0]
+        problems.append((lin, act, {"gate": _lib.ptr(gate), "resid": _lib.ptr(res2), "out": _lib.ptr(res2),
+                                    "ldo": n, "rows_per_batch": rows_per_batch}))
+    _grouped(_lib.EPI_GATE_RESIDUAL, problems)
 
 
 # Which of a block's linears each selection converts. `attention` covers the

@@ -225,3 +225,40 @@ def test_gemm_output_row_stride(monkeypatch, bn, pad):
     assert bool((buf[:, :pad] == -7.0).all()) and bool((buf[:, pad + n:] == -7.0).all())
     from qwen_image_accel_b200 import _lib
     assert _lib.device_error() == 0
+
+
+@pytest.mark.parametrize("bn", ["128", "192", "256", None])
+@pytest.mark.parametrize("m0,m1,n,k", [(8192, 512, 768, 256), (300, 77, 384, 384), (128, 1000, 1536, 256)])
+def test_grouped_launch_matches_single_gemms(monkeypatch, bn, m0, m1, n, k):
+    """Two GEMMs in one grouped launch (each epilogue) give byte-identical
+    outputs to the single-GEMM entry points, including a group whose first
+    problem is the small one and rows that are not multiples of 128."""
+    from qwen_image_accel_b200.kernels.mxfp8 import quantize
+    from qwen_image_accel_b200.optimizations.mxfp8 import (MXFP8Linear, matmul_gate_residual_grouped,
+                                                            matmul_gelu_quantize_grouped, matmul_grouped)
+    if bn is not None:
+        monkeypatch.setenv("QIA_GEMM_BN", bn)
+    lins = [MXFP8Linear(make_linear(n, k, 40 + i)) for i in range(2)]
+    acts = [quantize(make_x(m, k, 50 + i)) for i, m in enumerate((m0, m1))]
+    got = matmul_grouped(list(zip(lins, acts)))
+    for lin, act, out in zip(lins, acts, got):
+        assert torch.equal(out, lin.matmul(act))
+    got_q = matmul_gelu_quantize_grouped(list(zip(lins, acts)))
+    for lin, act, q in zip(lins, acts, got_q):
+        ref = lin.matmul_gelu_quantize(act)
+        assert torch.equal(q.values.view(torch.uint8)[: q.rows], ref.values.view(torch.uint8)[: ref.rows])
+        assert torch.equal(q.scales.view(torch.uint8), ref.scales.view(torch.uint8))
+    g = torch.Generator(device=DEV).manual_seed(60)
+    items, refs = [], []
+    for lin, act, m in zip(lins, acts, (m0, m1)):
+        batch = 2 if m % 2 == 0 else 1
+        gate = torch.randn(batch, 1, n, device=DEV, dtype=torch.bfloat16, generator=g)
+        resid = torch.randn(m, n, device=DEV, dtype=torch.bfloat16, generator=g)
+        refs.append(lin.matmul_gate_residual(act, gate, resid.clone()))
+        items.append((lin, act, gate, resid))
+    matmul_gate_residual_grouped(items)
+    for (_, _, _, resid), ref in zip(items, refs):
+        assert torch.equal(resid, ref)
+    torch.cuda.synchronize()
+    from qwen_image_accel_b200 import _lib
+    assert _lib.device_error() == 0
