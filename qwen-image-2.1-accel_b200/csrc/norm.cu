@@ -111,33 +111,37 @@ ln_mod_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restri
 #pragma unroll
   for (int j = 0; j < NV; ++j) {
     const int c = t * 4 + j * 512;
-    float s[4], y[4];
-    unpack4(__ldg(reinterpret_cast<const uint2*>(scale + vec_row + c)), s);
-    float sh[4];
-    if (SHIFT) unpack4(__ldg(reinterpret_cast<const uint2*>(shift + vec_row + c)), sh);
-#pragma unroll
-    for (int ii = 0; ii < 4; ++ii) {
-      const float nrm = round_bf16(__fmul_rn(rstd, v[j * 4 + ii] - mean));
-      float m = round_bf16(__fmul_rn(nrm, s[ii]));
-      if (SHIFT) m = round_bf16(__fadd_rn(m, sh[ii]));
-      y[ii] = live ? m : 0.0f;
+    // bf16(rstd * (x - mean)), then bf16(. * scale) and bf16(. + shift): the
+    // operands of the last two are bf16 values, so the packed bf16x2 multiply
+    // and add (one rounding each) give the fp32-then-round results
+    const uint2 s2 = __ldg(reinterpret_cast<const uint2*>(scale + vec_row + c));
+    uint32_t y01 = cvt_bf16x2(__fmul_rn(rstd, v[j * 4] - mean), __fmul_rn(rstd, v[j * 4 + 1] - mean));
+    uint32_t y23 = cvt_bf16x2(__fmul_rn(rstd, v[j * 4 + 2] - mean), __fmul_rn(rstd, v[j * 4 + 3] - mean));
+    y01 = mul_bf16x2(y01, s2.x);
+    y23 = mul_bf16x2(y23, s2.y);
+    if (SHIFT) {
+      const uint2 h2 = __ldg(reinterpret_cast<const uint2*>(shift + vec_row + c));
+      y01 = add_bf16x2(y01, h2.x);
+      y23 = add_bf16x2(y23, h2.y);
     }
+    if (!live) y01 = y23 = 0u;
     if (MODE == kModBf16) {
-      *reinterpret_cast<uint2*>(out + row * D + c) = pack4(y);
+      *reinterpret_cast<uint2*>(out + row * D + c) = make_uint2(y01, y23);
     } else if (MODE == kAdalnResidual) {
-      float g[4], r[4];
-      unpack4(__ldg(reinterpret_cast<const uint2*>(gate + vec_row + c)), g);
-      unpack4(__ldg(reinterpret_cast<const uint2*>(resid + row * D + c)), r);
-#pragma unroll
-      for (int ii = 0; ii < 4; ++ii) y[ii] = __fadd_rn(r[ii], round_bf16(__fmul_rn(g[ii], y[ii])));
-      *reinterpret_cast<uint2*>(out + row * D + c) = pack4(y);
+      // r + bf16(gate * y), rounded: both steps on bf16 operands
+      const uint2 g2 = __ldg(reinterpret_cast<const uint2*>(gate + vec_row + c));
+      const uint2 r2 = __ldg(reinterpret_cast<const uint2*>(resid + row * D + c));
+      *reinterpret_cast<uint2*>(out + row * D + c) =
+          make_uint2(add_bf16x2(r2.x, mul_bf16x2(g2.x, y01)), add_bf16x2(r2.y, mul_bf16x2(g2.y, y23)));
     } else {
       // 32-element MX block = 8 consecutive threads (aligned groups of 8 lanes)
-      float amax = fmaxf(fmaxf(fabsf(y[0]), fabsf(y[1])), fmaxf(fabsf(y[2]), fabsf(y[3])));
+      const uint32_t m2 = max_bf16x2(abs_bf16x2(y01), abs_bf16x2(y23));
+      float amax = fmaxf(bf16_lo(m2), bf16_hi(m2));
       amax = warp_max_xor(amax, 4);
       const int e = mx_exponent(amax);
       const float inv = mx_inverse_scale(e);
-      const uint32_t codes = cvt_e4m3x4(y[0] * inv, y[1] * inv, y[2] * inv, y[3] * inv);
+      const uint32_t codes =
+          cvt_e4m3x4(bf16_lo(y01) * inv, bf16_hi(y01) * inv, bf16_lo(y23) * inv, bf16_hi(y23) * inv);
       *reinterpret_cast<uint32_t*>(q_values + row * D + c) = codes;
       if ((t & 7) == 0) q_scales[mx_scale_offset(row, c >> 5, D / 128)] = uint8_t(e);
     }

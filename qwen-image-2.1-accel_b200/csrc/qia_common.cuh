@@ -192,6 +192,38 @@ __device__ __forceinline__ void round_bf16_x2(float& lo, float& hi) {
   hi = __uint_as_float(b & 0xffff0000u);
 }
 
+// ---- packed bf16 pairs (low half = first element)
+__device__ __forceinline__ uint32_t cvt_bf16x2(float lo, float hi) {
+  uint32_t r;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+// Product of two bf16 pairs, rounded once to bf16: the exact product of two
+// bf16 values fits an fp32 mantissa, so this equals bf16(fp32(a) * fp32(b))
+// (for products down to 2^-135 in magnitude; smaller ones are zero or the
+// smallest bf16 subnormal either way).
+__device__ __forceinline__ uint32_t mul_bf16x2(uint32_t a, uint32_t b) {
+  uint32_t r;
+  asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+__device__ __forceinline__ uint32_t max_bf16x2(uint32_t a, uint32_t b) {
+  uint32_t r;
+  asm("max.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+__device__ __forceinline__ uint32_t abs_bf16x2(uint32_t a) { return a & 0x7fff7fffu; }
+
+// Sum of two bf16 pairs rounded once to bf16: equals bf16(fp32(a) + fp32(b))
+// (the fp32 sum is exact when the exponents differ by at most 16; beyond that
+// the smaller operand is below half a bf16 ulp of the larger and both round to
+// the larger).
+__device__ __forceinline__ uint32_t add_bf16x2(uint32_t a, uint32_t b) {
+  uint32_t r;
+  asm("add.rn.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+
 // gelu_tanh_fast on a pair: the same operations in the same order (so the
 // same results), with the FMA-pipe steps issued as f32x2 instructions.
 __device__ __forceinline__ void gelu_tanh_fast_x2(float& x0, float& x1) {

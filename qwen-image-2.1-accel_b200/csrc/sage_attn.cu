@@ -141,27 +141,6 @@ struct JointQKV {
   }
 };
 
-__device__ __forceinline__ uint32_t cvt_bf16x2(float lo, float hi) {
-  uint32_t r;
-  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
-  return r;
-}
-// Product of two bf16 pairs, rounded once to bf16: the exact product of two
-// bf16 values fits an fp32 mantissa, so this equals bf16(fp32(a) * fp32(b))
-// (for products down to 2^-135 in magnitude; smaller ones are zero or the
-// smallest bf16 subnormal either way).
-__device__ __forceinline__ uint32_t mul_bf16x2(uint32_t a, uint32_t b) {
-  uint32_t r;
-  asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
-  return r;
-}
-__device__ __forceinline__ uint32_t max_bf16x2(uint32_t a, uint32_t b) {
-  uint32_t r;
-  asm("max.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
-  return r;
-}
-__device__ __forceinline__ uint32_t abs_bf16x2(uint32_t a) { return a & 0x7fff7fffu; }
-
 // max(floor, |x_i|) over the eight bf16 values of a row piece.
 __device__ __forceinline__ float piece_amax(const uint4& x, float floor) {
   const uint32_t m = max_bf16x2(max_bf16x2(abs_bf16x2(x.x), abs_bf16x2(x.y)),
