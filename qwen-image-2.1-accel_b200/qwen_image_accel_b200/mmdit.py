@@ -362,8 +362,9 @@ class MMDiT:
         sh1_t, s1_t, g1_t, sh2_t, s2_t, g2_t = mod_txt
         if not self.quantized:
             raise NotImplementedError("the sharded step runs the MXFP8 profiles")
-        qkv_i = blk.img_qkv.mx.matmul(layer_norm_scale_quantize(x, s1_i, self.ln, shift=sh1_i))
-        qkv_t = blk.txt_qkv.mx.matmul(layer_norm_scale_quantize(c, s1_t, self.ln, shift=sh1_t))
+        qkv_i, qkv_t = matmul_grouped([
+            (blk.img_qkv.mx, layer_norm_scale_quantize(x, s1_i, self.ln, shift=sh1_i)),
+            (blk.txt_qkv.mx, layer_norm_scale_quantize(c, s1_t, self.ln, shift=sh1_t))])
         # local Q/K/V: image tokens (all heads), text tokens (all heads)
         qi, ki, vi = (torch.empty(B, Sl, H, hd, device=x.device, dtype=torch.bfloat16) for _ in range(3))
         qt, kt, vt = (torch.empty(B, Lt, H, hd, device=x.device, dtype=torch.bfloat16) for _ in range(3))
@@ -386,12 +387,12 @@ class MMDiT:
             a_i[b] = head_to_seq(o_i[0], plan)
             a_t[b] = gather_heads(o_t[0], plan)
         del qi, ki, vi, qt, kt, vt
-        blk.img_out.mx.matmul_gate_residual(quantize(a_i.view(B * Sl, D)), g1_i, x, out=x)
-        blk.txt_out.mx.matmul_gate_residual(quantize(a_t.view(B * Lt, D)), g1_t, c, out=c)
-        hi = blk.img_up.mx.matmul_gelu_quantize(layer_norm_scale_quantize(x, s2_i, self.ln, shift=sh2_i))
-        blk.img_down.mx.matmul_gate_residual(hi, g2_i, x, out=x)
-        ht = blk.txt_up.mx.matmul_gelu_quantize(layer_norm_scale_quantize(c, s2_t, self.ln, shift=sh2_t))
-        blk.txt_down.mx.matmul_gate_residual(ht, g2_t, c, out=c)
+        matmul_gate_residual_grouped([(blk.img_out.mx, quantize(a_i.view(B * Sl, D)), g1_i, x),
+                                      (blk.txt_out.mx, quantize(a_t.view(B * Lt, D)), g1_t, c)])
+        hi, ht = matmul_gelu_quantize_grouped([
+            (blk.img_up.mx, layer_norm_scale_quantize(x, s2_i, self.ln, shift=sh2_i)),
+            (blk.txt_up.mx, layer_norm_scale_quantize(c, s2_t, self.ln, shift=sh2_t))])
+        matmul_gate_residual_grouped([(blk.img_down.mx, hi, g2_i, x), (blk.txt_down.mx, ht, g2_t, c)])
         return x, c
 
     # ------------------------------------------------------------------ model
