@@ -67,6 +67,27 @@ int qia_ln_mod_quant(const void* x, const void* scale, const void* shift,
                      void* q_values, void* q_scales, int64_t rows, int64_t dim,
                      int64_t rows_per_batch, float eps, void* stream);
 
+/* One qia_ln_mod_quant problem of a grouped launch. */
+typedef struct qia_ln_mod_quant_problem {
+  const void* x;           /* [rows, dim] bf16 */
+  const void* scale;       /* [rows / rows_per_batch, dim] bf16 */
+  const void* shift;       /* same shape, or NULL (all problems alike) */
+  void* q_values;          /* [ceil(rows/128)*128, dim] e4m3 */
+  void* q_scales;          /* blocked E8M0 */
+  int64_t rows;
+  int64_t rows_per_batch;
+} qia_ln_mod_quant_problem;
+
+/* One or two qia_ln_mod_quant problems with the same dim and eps in one
+ * launch (count = 1 or 2): the dual-stream block's text rows (a few hundred)
+ * run inside the image rows' launch instead of as a separate, latency-bound
+ * launch. Each problem's outputs equal qia_ln_mod_quant's.
+ * Replaces: the image- and text-stream layer_norm_scale_quantize pair
+ * (src/qwen_image_accel/kernels/epilogue.py:304) of norm1 / norm2 of the v1
+ * block (WHL:diffusers/models/transformers/transformer_qwenimage.py:683-717). */
+int qia_ln_mod_quant_grouped(const qia_ln_mod_quant_problem* problems,
+                             int count, int64_t dim, float eps, void* stream);
+
 /* Gated residual: out = bf16(h + bf16(x * gate[b])). h, x, out: [rows, dim];
  * gate: [rows / rows_per_batch, dim].
  * Replaces: residual (src/qwen_image_accel/kernels/elementwise.py:26). */

@@ -92,15 +92,39 @@ __device__ __forceinline__ void row_stats(const __nv_bfloat16* __restrict__ xrow
   rstd = rsqrtf(s_stat[1] + eps);
 }
 
+// The arguments of one LayerNorm problem; a launch may hold two (the dual-
+// stream block's image and text rows): CTAs [0, split) take problem 0's rows,
+// the rest problem 1's, so the small text problem rides in the image launch.
+struct LnArgs {
+  const __nv_bfloat16* x;
+  const __nv_bfloat16* resid;
+  const __nv_bfloat16* scale;
+  const __nv_bfloat16* shift;
+  const __nv_bfloat16* gate;
+  __nv_bfloat16* out;
+  uint8_t* q_values;
+  uint8_t* q_scales;
+  int64_t rows;
+  int rows_per_batch;
+};
+
 template <int NV, int MODE, bool SHIFT>
 __global__ void __launch_bounds__(kThreads)
-ln_mod_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ resid,
-              const __nv_bfloat16* __restrict__ scale, const __nv_bfloat16* __restrict__ shift,
-              const __nv_bfloat16* __restrict__ gate, __nv_bfloat16* __restrict__ out,
-              uint8_t* __restrict__ q_values, uint8_t* __restrict__ q_scales,
-              int64_t rows, int rows_per_batch, float eps) {
+ln_mod_kernel(const LnArgs a0, const LnArgs a1, int64_t split, float eps) {
   constexpr int D = NV * 512;
-  const int64_t row = blockIdx.x;
+  const bool second = blockIdx.x >= split;
+  const LnArgs& a = second ? a1 : a0;
+  const __nv_bfloat16* __restrict__ x = a.x;
+  const __nv_bfloat16* __restrict__ resid = a.resid;
+  const __nv_bfloat16* __restrict__ scale = a.scale;
+  const __nv_bfloat16* __restrict__ shift = a.shift;
+  const __nv_bfloat16* __restrict__ gate = a.gate;
+  __nv_bfloat16* __restrict__ out = a.out;
+  uint8_t* __restrict__ q_values = a.q_values;
+  uint8_t* __restrict__ q_scales = a.q_scales;
+  const int64_t rows = a.rows;
+  const int rows_per_batch = a.rows_per_batch;
+  const int64_t row = second ? int64_t(blockIdx.x) - split : int64_t(blockIdx.x);
   const bool live = row < rows;
   const int t = threadIdx.x;
   float v[NV * 4];
@@ -148,16 +172,15 @@ ln_mod_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restri
   }
 }
 
+// grid0 (grid1) CTAs for problem 0 (1): its rows, or its rows padded to 128
+// for the MXFP8 output.
 template <int MODE, bool SHIFT>
-int launch_ln(int nv, dim3 grid, cudaStream_t st, const void* x, const void* resid, const void* scale,
-              const void* shift, const void* gate, void* out, void* qv, void* qs, int64_t rows,
-              int rows_per_batch, float eps) {
-#define QIA_LN_CASE(N)                                                                                 \
-  case N:                                                                                              \
-    ln_mod_kernel<N, MODE, SHIFT><<<grid, kThreads, 0, st>>>(                                          \
-        (const __nv_bfloat16*)x, (const __nv_bfloat16*)resid, (const __nv_bfloat16*)scale,             \
-        (const __nv_bfloat16*)shift, (const __nv_bfloat16*)gate, (__nv_bfloat16*)out, (uint8_t*)qv,    \
-        (uint8_t*)qs, rows, rows_per_batch, eps);                                                      \
+int launch_ln(int nv, cudaStream_t st, const LnArgs& a0, int64_t grid0, const LnArgs& a1, int64_t grid1,
+              float eps) {
+  const dim3 grid{unsigned(grid0 + grid1)};
+#define QIA_LN_CASE(N)                                                             \
+  case N:                                                                          \
+    ln_mod_kernel<N, MODE, SHIFT><<<grid, kThreads, 0, st>>>(a0, a1, grid0, eps);  \
     break;
   switch (nv) {
     QIA_LN_CASE(1) QIA_LN_CASE(2) QIA_LN_CASE(3) QIA_LN_CASE(4) QIA_LN_CASE(5) QIA_LN_CASE(6)
@@ -168,6 +191,22 @@ int launch_ln(int nv, dim3 grid, cudaStream_t st, const void* x, const void* res
   }
 #undef QIA_LN_CASE
   return check_launch("ln_mod_kernel");
+}
+
+LnArgs ln_args(const void* x, const void* resid, const void* scale, const void* shift, const void* gate, void* out,
+               void* qv, void* qs, int64_t rows, int64_t rows_per_batch) {
+  LnArgs a;
+  a.x = (const __nv_bfloat16*)x;
+  a.resid = (const __nv_bfloat16*)resid;
+  a.scale = (const __nv_bfloat16*)scale;
+  a.shift = (const __nv_bfloat16*)shift;
+  a.gate = (const __nv_bfloat16*)gate;
+  a.out = (__nv_bfloat16*)out;
+  a.q_values = (uint8_t*)qv;
+  a.q_scales = (uint8_t*)qs;
+  a.rows = rows;
+  a.rows_per_batch = int(rows_per_batch);
+  return a;
 }
 
 int validate_ln(const void* x, const void* scale, const void* out, int64_t rows, int64_t dim,
@@ -216,12 +255,9 @@ extern "C" int qia_ln_mod(const void* x, const void* scale, const void* shift, v
   if (rc) return rc;
   if (shift && !aligned(shift, 8)) return set_error(QIA_ERR_ALIGNMENT, "qia_ln_mod: shift misaligned");
   const int nv = int(dim / 512);
-  const dim3 grid{unsigned(rows)};
-  if (shift)
-    return launch_ln<kModBf16, true>(nv, grid, as_stream(stream), x, nullptr, scale, shift, nullptr, out, nullptr,
-                                     nullptr, rows, int(rows_per_batch), eps);
-  return launch_ln<kModBf16, false>(nv, grid, as_stream(stream), x, nullptr, scale, nullptr, nullptr, out, nullptr,
-                                    nullptr, rows, int(rows_per_batch), eps);
+  const LnArgs a = ln_args(x, nullptr, scale, shift, nullptr, out, nullptr, nullptr, rows, rows_per_batch);
+  if (shift) return launch_ln<kModBf16, true>(nv, as_stream(stream), a, rows, a, 0, eps);
+  return launch_ln<kModBf16, false>(nv, as_stream(stream), a, rows, a, 0, eps);
 }
 
 extern "C" int qia_ln_mod_quant(const void* x, const void* scale, const void* shift, void* q_values,
@@ -233,12 +269,34 @@ extern "C" int qia_ln_mod_quant(const void* x, const void* scale, const void* sh
   if (shift && !aligned(shift, 8)) return set_error(QIA_ERR_ALIGNMENT, "qia_ln_mod_quant: shift misaligned");
   const int64_t padded = (rows + 127) / 128 * 128;
   const int nv = int(dim / 512);
-  const dim3 grid{unsigned(padded)};
-  if (shift)
-    return launch_ln<kModQuant, true>(nv, grid, as_stream(stream), x, nullptr, scale, shift, nullptr, nullptr,
-                                      q_values, q_scales, rows, int(rows_per_batch), eps);
-  return launch_ln<kModQuant, false>(nv, grid, as_stream(stream), x, nullptr, scale, nullptr, nullptr, nullptr,
-                                     q_values, q_scales, rows, int(rows_per_batch), eps);
+  const LnArgs a = ln_args(x, nullptr, scale, shift, nullptr, nullptr, q_values, q_scales, rows, rows_per_batch);
+  if (shift) return launch_ln<kModQuant, true>(nv, as_stream(stream), a, padded, a, 0, eps);
+  return launch_ln<kModQuant, false>(nv, as_stream(stream), a, padded, a, 0, eps);
+}
+
+extern "C" int qia_ln_mod_quant_grouped(const qia_ln_mod_quant_problem* problems, int count, int64_t dim,
+                                        float eps, void* stream) {
+  const char* who = "qia_ln_mod_quant_grouped";
+  if (!problems || count < 1 || count > 2) return set_error(QIA_ERR_INVALID, "%s: 1 or 2 problems", who);
+  LnArgs a[2];
+  int64_t grid[2] = {0, 0};
+  const bool shift = problems[0].shift != nullptr;
+  for (int i = 0; i < count; ++i) {
+    const qia_ln_mod_quant_problem& p = problems[i];
+    int rc = validate_ln(p.x, p.scale, p.q_values, p.rows, dim, p.rows_per_batch, who);
+    if (rc) return rc;
+    if (!p.q_scales) return set_error(QIA_ERR_INVALID, "%s: null q_scales", who);
+    if ((p.shift != nullptr) != shift) return set_error(QIA_ERR_INVALID, "%s: shift on some problems only", who);
+    if (p.shift && !aligned(p.shift, 8)) return set_error(QIA_ERR_ALIGNMENT, "%s: shift misaligned", who);
+    a[i] = ln_args(p.x, nullptr, p.scale, p.shift, nullptr, nullptr, p.q_values, p.q_scales, p.rows,
+                   p.rows_per_batch);
+    grid[i] = (p.rows + 127) / 128 * 128;
+  }
+  if (grid[0] + grid[1] > 0x7fffffffLL) return set_error(QIA_ERR_UNSUPPORTED, "%s: too many rows", who);
+  if (count == 1) a[1] = a[0];
+  const int nv = int(dim / 512);
+  if (shift) return launch_ln<kModQuant, true>(nv, as_stream(stream), a[0], grid[0], a[1], grid[1], eps);
+  return launch_ln<kModQuant, false>(nv, as_stream(stream), a[0], grid[0], a[1], grid[1], eps);
 }
 
 extern "C" int qia_adaln_residual(const void* x, const void* r, const void* scale, const void* shift,
@@ -250,8 +308,8 @@ extern "C" int qia_adaln_residual(const void* x, const void* r, const void* scal
   if (!aligned(r, 8) || !aligned(shift, 8) || !aligned(gate, 8))
     return set_error(QIA_ERR_ALIGNMENT, "qia_adaln_residual: pointers must be 8-byte aligned");
   const int nv = int(dim / 512);
-  return launch_ln<kAdalnResidual, true>(nv, dim3(unsigned(rows)), as_stream(stream), x, r, scale, shift, gate,
-                                         out, nullptr, nullptr, rows, int(rows_per_batch), eps);
+  const LnArgs a = ln_args(x, r, scale, shift, gate, out, nullptr, nullptr, rows, rows_per_batch);
+  return launch_ln<kAdalnResidual, true>(nv, as_stream(stream), a, rows, a, 0, eps);
 }
 
 extern "C" int qia_gated_residual(const void* h, const void* x, const void* gate, void* out, int64_t rows,

@@ -28,9 +28,16 @@ class GemmProblem(ctypes.Structure):
 
 EPI_BF16, EPI_GELU_QUANT, EPI_GATE_RESIDUAL, EPI_GELU_BF16 = 0, 1, 2, 3
 
+
+class LnProblem(ctypes.Structure):
+    """qia_ln_mod_quant_problem: one problem of a qia_ln_mod_quant_grouped launch."""
+    _fields_ = [("x", _P), ("scale", _P), ("shift", _P), ("q_values", _P), ("q_scales", _P), ("rows", _I),
+                ("rows_per_batch", _I)]
+
 # name -> argument types (all return int status)
 SIGNATURES: dict[str, list] = {
     "qia_mxfp8_gemm_grouped": [ctypes.c_int, _P, ctypes.c_int, _I, _I, _P],
+    "qia_ln_mod_quant_grouped": [_P, ctypes.c_int, _I, _F, _P],
     "qia_ln_mod": [_P, _P, _P, _P, _I, _I, _I, _F, _P],
     "qia_ln_mod_quant": [_P, _P, _P, _P, _P, _I, _I, _I, _F, _P],
     "qia_gated_residual": [_P, _P, _P, _P, _I, _I, _I, _P],

@@ -7,15 +7,16 @@ QwenImageTransformer2DModel / QwenImageTransformerBlock, :633-790, :859-1031):
 biases, AdaLN shift/scale/gate, text 3584 -> 3072. Weights use the Diffusers
 state-dict names, so a checkpoint of that model loads as is.
 
-Per block the hot path is (the image and text streams' GEMMs of each
-projection share N and K and run as one grouped launch, text tiles last):
-  LN + (1+scale), +shift -> MXFP8         qia_ln_mod_quant (per stream)
+Per block the hot path is (the image and text streams' LayerNorms and the
+GEMMs of each projection share their shapes' inner dimensions and run as one
+grouped launch each, text rows/tiles last):
+  LN + (1+scale), +shift -> MXFP8         qia_ln_mod_quant_grouped
   fused Q|K|V GEMM (+bias)                 qia_mxfp8_gemm_grouped (bf16)
   QK-RMSNorm + RoPE + Sage quantization    qia_sage_attention_joint_mx (both
     + joint [txt, img] INT8/FP8 attention    streams' projections in, per-stream
     -> MXFP8                                 MXFP8 attention outputs back)
   out-proj GEMM + gate + residual          qia_mxfp8_gemm_grouped (gate-residual)
-  LN + (1+scale), +shift -> MXFP8          qia_ln_mod_quant (per stream)
+  LN + (1+scale), +shift -> MXFP8          qia_ln_mod_quant_grouped
   FFN up GEMM + bias + GELU -> MXFP8       qia_mxfp8_gemm_grouped (GELU-quant)
   FFN down GEMM + gate + residual          qia_mxfp8_gemm_grouped (gate-residual)
 The prologue/epilogue layers outside the blocks (img_in, txt_norm/txt_in, the
@@ -39,7 +40,7 @@ import torch.nn.functional as F
 
 from .kernels.attention import joint_qk_norm_rope
 from .kernels.elementwise import residual
-from .kernels.epilogue import layer_norm_scale_quantize
+from .kernels.epilogue import layer_norm_scale_quantize_grouped
 from .kernels.layernorm import layer_norm_scale
 from .kernels.mxfp8 import quantize
 from .optimizations.mxfp8 import (MXFP8Linear, matmul_gate_residual_grouped, matmul_gelu_quantize_grouped,
@@ -292,9 +293,9 @@ class MMDiT:
         # ---- norm1 + modulation + Q|K|V projections
         if self.quantized:
             # image and text projections share N and K: one grouped launch
-            qkv_i, qkv_t = matmul_grouped([
-                (blk.img_qkv.mx, layer_norm_scale_quantize(x, s1_i, self.ln, shift=sh1_i)),
-                (blk.txt_qkv.mx, layer_norm_scale_quantize(c, s1_t, self.ln, shift=sh1_t))])
+            a_i, a_t = layer_norm_scale_quantize_grouped([(x, s1_i, sh1_i), (c, s1_t, sh1_t)], self.ln)
+            qkv_i, qkv_t = matmul_grouped([(blk.img_qkv.mx, a_i), (blk.txt_qkv.mx, a_t)])
+            del a_i, a_t
         else:
             qkv_i = F.linear(layer_norm_scale(x, s1_i, self.ln, shift=sh1_i), blk.img_qkv.w, blk.img_qkv.b)
             qkv_t = F.linear(layer_norm_scale(c, s1_t, self.ln, shift=sh1_t), blk.txt_qkv.w, blk.txt_qkv.b)
@@ -333,9 +334,9 @@ class MMDiT:
             c = residual(c, F.linear(a_t.view(B, Lt, D), blk.txt_out.w, blk.txt_out.b), g1_t)
         # ---- norm2 + modulation + GELU-tanh MLP + gated residual
         if self.quantized:
-            hi, ht = matmul_gelu_quantize_grouped([
-                (blk.img_up.mx, layer_norm_scale_quantize(x, s2_i, self.ln, shift=sh2_i)),
-                (blk.txt_up.mx, layer_norm_scale_quantize(c, s2_t, self.ln, shift=sh2_t))])
+            n_i, n_t = layer_norm_scale_quantize_grouped([(x, s2_i, sh2_i), (c, s2_t, sh2_t)], self.ln)
+            hi, ht = matmul_gelu_quantize_grouped([(blk.img_up.mx, n_i), (blk.txt_up.mx, n_t)])
+            del n_i, n_t
             matmul_gate_residual_grouped([(blk.img_down.mx, hi, g2_i, x), (blk.txt_down.mx, ht, g2_t, c)])
         else:
             hi = gelu_tanh(F.linear(layer_norm_scale(x, s2_i, self.ln, shift=sh2_i), blk.img_up.w, blk.img_up.b))
@@ -362,9 +363,9 @@ class MMDiT:
         sh1_t, s1_t, g1_t, sh2_t, s2_t, g2_t = mod_txt
         if not self.quantized:
             raise NotImplementedError("the sharded step runs the MXFP8 profiles")
-        qkv_i, qkv_t = matmul_grouped([
-            (blk.img_qkv.mx, layer_norm_scale_quantize(x, s1_i, self.ln, shift=sh1_i)),
-            (blk.txt_qkv.mx, layer_norm_scale_quantize(c, s1_t, self.ln, shift=sh1_t))])
+        a_i, a_t = layer_norm_scale_quantize_grouped([(x, s1_i, sh1_i), (c, s1_t, sh1_t)], self.ln)
+        qkv_i, qkv_t = matmul_grouped([(blk.img_qkv.mx, a_i), (blk.txt_qkv.mx, a_t)])
+        del a_i, a_t
         # local Q/K/V: image tokens (all heads), text tokens (all heads)
         qi, ki, vi = (torch.empty(B, Sl, H, hd, device=x.device, dtype=torch.bfloat16) for _ in range(3))
         qt, kt, vt = (torch.empty(B, Lt, H, hd, device=x.device, dtype=torch.bfloat16) for _ in range(3))
@@ -389,9 +390,9 @@ class MMDiT:
         del qi, ki, vi, qt, kt, vt
         matmul_gate_residual_grouped([(blk.img_out.mx, quantize(a_i.view(B * Sl, D)), g1_i, x),
                                       (blk.txt_out.mx, quantize(a_t.view(B * Lt, D)), g1_t, c)])
-        hi, ht = matmul_gelu_quantize_grouped([
-            (blk.img_up.mx, layer_norm_scale_quantize(x, s2_i, self.ln, shift=sh2_i)),
-            (blk.txt_up.mx, layer_norm_scale_quantize(c, s2_t, self.ln, shift=sh2_t))])
+        n_i, n_t = layer_norm_scale_quantize_grouped([(x, s2_i, sh2_i), (c, s2_t, sh2_t)], self.ln)
+        hi, ht = matmul_gelu_quantize_grouped([(blk.img_up.mx, n_i), (blk.txt_up.mx, n_t)])
+        del n_i, n_t
         matmul_gate_residual_grouped([(blk.img_down.mx, hi, g2_i, x), (blk.txt_down.mx, ht, g2_t, c)])
         return x, c
 

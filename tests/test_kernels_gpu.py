@@ -320,3 +320,25 @@ def test_quantize_strided_rows():
     b = quantize(sub.contiguous())
     assert torch.equal(a.values.view(torch.uint8), b.values.view(torch.uint8))
     assert torch.equal(a.scales.view(torch.uint8), b.scales.view(torch.uint8))
+
+
+@pytest.mark.parametrize("shift", [True, False])
+def test_ln_mod_quant_grouped_matches_single(shift):
+    """Image (B x 4096 rows) and text (B x 77 rows) LayerNorm+modulate+MXFP8 in
+    one grouped launch: byte-identical to the two single launches."""
+    from qwen_image_accel_b200.kernels.epilogue import (layer_norm_scale_quantize,
+                                                         layer_norm_scale_quantize_grouped)
+    g = torch.Generator(device="cuda").manual_seed(70)
+    norm = torch.nn.LayerNorm(3072, elementwise_affine=False, eps=1e-6)
+    items = []
+    for s in (4096, 77):
+        x = torch.randn(2, s, 3072, device="cuda", dtype=torch.bfloat16, generator=g) * 3 + 0.5
+        sc = (1 + 0.1 * torch.randn(2, 1, 3072, device="cuda", generator=g)).to(torch.bfloat16)
+        sh = (0.1 * torch.randn(2, 1, 3072, device="cuda", generator=g)).to(torch.bfloat16) if shift else None
+        items.append((x, sc, sh))
+    got = layer_norm_scale_quantize_grouped(items, norm)
+    for (x, sc, sh), q in zip(items, got):
+        ref = layer_norm_scale_quantize(x, sc, norm, shift=sh)
+        assert q.rows == ref.rows
+        assert torch.equal(q.values.view(torch.uint8), ref.values.view(torch.uint8))
+        assert torch.equal(q.scales.view(torch.uint8), ref.scales.view(torch.uint8))
