@@ -455,7 +455,10 @@ def profile_case(name: str):
     ffn_up  - the FFN-up GEMM with the GELU+MXFP8 epilogue, M=8192 (one launch)
     attn    - Sage attention B=1, H=24, S=4352 (three calls)
     step8   - an 8-block 1024^2 step: two warm-up steps, then one inside an NVTX
-              range named `step` (for `ncu --nvtx --nvtx-include step/`)."""
+              range named `step` (for `ncu --nvtx --nvtx-include step/`)
+    quant   - the fused QK-norm/RoPE + Sage quantization of one block (B=2, 256
+              text + 4096 image tokens, 24 heads, from the two streams' q|k|v
+              projections), twice (three launches each)."""
     device = torch.device("cuda", 0)
     torch.cuda.set_device(device)
     g = torch.Generator(device=device).manual_seed(0)
@@ -471,6 +474,17 @@ def profile_case(name: str):
                    for _ in range(3))
         for _ in range(3):
             sage_attention(q, k, v)
+    elif name == "quant":
+        from qwen_image_accel_b200.mmdit import rope_tables
+        from qwen_image_accel_b200.optimizations.sage_attention import sage_quantize_joint
+        qkv = [torch.randn(2, n, 3 * HEADS * 128, device=device, dtype=torch.bfloat16, generator=g)
+               for n in (TXT_LEN, IMG_LEN)]
+        w = [tuple((1 + 0.1 * torch.randn(128, device=device, generator=g)).to(torch.bfloat16) for _ in range(2))
+             for _ in range(2)]
+        img, txt = rope_tables(1, GRID[1], GRID[2], TXT_LEN)
+        ft, fi = (torch.view_as_real(t).to(device).contiguous() for t in (txt, img))
+        for _ in range(2):
+            sage_quantize_joint(qkv[0], qkv[1], w[0], w[1], ft, fi, HEADS)
     elif name == "step8":
         from qwen_image_accel_b200.mmdit import MMDiT, MMDiTConfig, random_parameters
         cfg = MMDiTConfig(num_layers=8)
@@ -499,7 +513,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--config", default="c4", choices=["c4", "c5"],
                     help="c4: 1024^2 step (replicas for N>1); c5: 2048^2 step, CFG split x Ulysses for N>1")
-    ap.add_argument("--profile-case", choices=["ffn_up", "attn", "step8"],
+    ap.add_argument("--profile-case", choices=["ffn_up", "attn", "step8", "quant"],
                     help="run one small fixed case for an ncu capture and exit")
     args = ap.parse_args()
     if args.profile_case:
