@@ -26,19 +26,39 @@ struct Welford {
   float mean, m2, count;
 };
 
-// cuWelfordCombine(dataB = own, dataA = other) as used by PyTorch's warp and
-// block reductions.
-__device__ __forceinline__ Welford welford_combine(const Welford own, const Welford other) {
+// cuWelfordCombine(dataB = own, dataA = other) as PyTorch's warp and block
+// reductions use it -- delta = own.mean - other.mean, coef = 1/count,
+// mean = fma(other.count*coef, other.mean, own.count*coef * own.mean),
+// m2 = fma(delta^2 * other.count, own.count*coef, other.m2 + own.m2) -- for two
+// partials over the same known number of elements CNT (every merge of the
+// row reduction pairs equal counts: 4*NV per thread, doubling with each
+// merge), so the count-only terms (1/count and count*coef, both correctly
+// rounded) are folded at compile time.
+template <int CNT>
+__device__ __forceinline__ Welford welford_combine_eq(const Welford own, const Welford other) {
+  constexpr float count = float(2 * CNT);
+  constexpr float coef = 1.0f / count;
+  constexpr float n_ab = float(CNT) * coef;
   const float delta = own.mean - other.mean;
-  const float count = other.count + own.count;
-  const float coef = 1.0f / count;
-  const float n_a = other.count * coef;
-  const float n_b = own.count * coef;
   Welford r;
-  r.mean = __fmaf_rn(n_a, other.mean, __fmul_rn(n_b, own.mean));
-  r.m2 = __fmaf_rn(__fmul_rn(__fmul_rn(delta, delta), other.count), n_b, other.m2 + own.m2);
+  r.mean = __fmaf_rn(n_ab, other.mean, __fmul_rn(n_ab, own.mean));
+  r.m2 = __fmaf_rn(__fmul_rn(__fmul_rn(delta, delta), float(CNT)), n_ab, other.m2 + own.m2);
   r.count = count;
   return r;
+}
+
+template <int NV, int LEVEL>
+__device__ __forceinline__ Welford shuffle_merges(Welford w) {
+  // five shuffle-down merges (offsets 16, 8, 4, 2, 1); partial counts 4*NV * 2^LEVEL
+  if constexpr (LEVEL < 5) {
+    Welford o;
+    o.mean = __shfl_down_sync(0xffffffffu, w.mean, 16 >> LEVEL);
+    o.m2 = __shfl_down_sync(0xffffffffu, w.m2, 16 >> LEVEL);
+    o.count = w.count;
+    return shuffle_merges<NV, LEVEL + 1>(welford_combine_eq<(4 * NV) << LEVEL>(w, o));
+  } else {
+    return w;
+  }
 }
 
 template <int NV>
@@ -65,25 +85,18 @@ __device__ __forceinline__ void row_stats(const __nv_bfloat16* __restrict__ xrow
       w.m2 = __fmaf_rn(delta, x - w.mean, w.m2);
     }
   }
-#pragma unroll
-  for (int off = 16; off > 0; off >>= 1) {
-    Welford o;
-    o.mean = __shfl_down_sync(0xffffffffu, w.mean, off);
-    o.m2 = __shfl_down_sync(0xffffffffu, w.m2, off);
-    o.count = __shfl_down_sync(0xffffffffu, w.count, off);
-    w = welford_combine(w, o);
-  }
+  w = shuffle_merges<NV, 0>(w);
   __shared__ Welford s_w[2];
   const int warp = t >> 5, lane = t & 31;
   // upper half of the warps hands its partial to the lower half (offset 2, then 1)
   if (lane == 0 && warp >= 2) s_w[warp - 2] = w;
   __syncthreads();
-  if (lane == 0 && warp < 2) w = welford_combine(w, s_w[warp]);
+  if (lane == 0 && warp < 2) w = welford_combine_eq<(4 * NV) << 5>(w, s_w[warp]);
   __syncthreads();
   if (lane == 0 && warp == 1) s_w[0] = w;
   __syncthreads();
   if (t == 0) {
-    w = welford_combine(w, s_w[0]);
+    w = welford_combine_eq<(4 * NV) << 6>(w, s_w[0]);
     s_stat[0] = w.mean;
     s_stat[1] = __fdiv_rn(w.m2, float(dim));
   }
