@@ -111,6 +111,20 @@ int qia_adaln_residual(const void* x, const void* r, const void* scale,
 int qia_rms_norm(const void* x, const void* weight, void* out, int64_t rows,
                  int64_t dim, float eps, void* stream);
 
+/* AdaLN modulation vectors of one dual-stream block: out[r] =
+ * bf16(W[r] . x + bias[r]) for the block's stacked img_mod / txt_mod linears
+ * (weight [n, k] bf16, n = 12 * unit: each stream's shift1, scale1, gate1,
+ * shift2, scale2, gate2 chunks of width unit), with the scale chunks (1 and 4
+ * of every six) returned as bf16(1 + scale). x: SiLU(temb) [k] bf16. fp32
+ * accumulation, one warp per output row. `ctas` bounds the grid: a small grid
+ * (one CTA per SM) keeps the launch light enough to run beside the previous
+ * block's kernels on another stream.
+ * Replaces: img_mod / txt_mod Linear(SiLU(temb)) and the 1 + scale of
+ * _modulate (WHL:diffusers/models/transformers/transformer_qwenimage.py:683-717). */
+int qia_adaln_modulation(const void* x, const void* weight, const void* bias,
+                         void* out, int64_t n, int64_t k, int64_t unit,
+                         int64_t ctas, void* stream);
+
 /* ---------------------------------------------------------------------------
  * Attention input preparation
  * ------------------------------------------------------------------------ */

@@ -242,6 +242,7 @@ class MMDiT:
         del mod_w, mod_b
         self.ln = _LNParams(cfg.dim, cfg.eps)
         self._rope_cache = {}
+        self._mod_stream = None
 
     # ------------------------------------------------------------------ helpers
     def rope(self, img_shape, txt_len):
@@ -421,6 +422,36 @@ class MMDiT:
             out.append(per)
         return out
 
+    def modulations_overlapped(self, temb: torch.Tensor):
+        """modulations() for a single temb row, block by block with
+        qia_adaln_modulation: block 0's on the current stream (full grid),
+        blocks 1.. on a side stream with one CTA per SM, so that they run
+        beside the earlier blocks' kernels instead of as one weight-read-bound
+        GEMV before block 0. Returns (mods, events): block i must wait for
+        events[i] (None for block 0) on the stream that runs it."""
+        from .kernels.modulation import adaln_modulation
+        D, L = self.cfg.dim, self.cfg.num_layers
+        n = 12 * D
+        x = F.silu(temb).reshape(-1).contiguous()
+        buf = torch.empty(L, n, device=temb.device, dtype=torch.bfloat16)
+        adaln_modulation(x, self.mod_w[:n], self.mod_b[:n], D, out=buf[0])
+        if self._mod_stream is None:
+            self._mod_stream = torch.cuda.Stream(device=temb.device)
+        side, main = self._mod_stream, torch.cuda.current_stream(temb.device)
+        sms = torch.cuda.get_device_properties(temb.device).multi_processor_count
+        side.wait_stream(main)
+        events = [None]
+        with torch.cuda.stream(side):
+            for i in range(1, L):
+                adaln_modulation(x, self.mod_w[i * n:(i + 1) * n], self.mod_b[i * n:(i + 1) * n], D, out=buf[i],
+                                 ctas=sms)
+                ev = torch.cuda.Event()
+                ev.record(side)
+                events.append(ev)
+        v = buf.view(L, 2, 6, D)
+        mods = [[tuple(v[i, s, j].view(1, 1, D) for j in range(6)) for s in range(2)] for i in range(L)]
+        return mods, events
+
     def forward(self, hidden_states: torch.Tensor, encoder_hidden_states: torch.Tensor, timestep: torch.Tensor,
                 img_shape, shared_timestep: bool = False) -> torch.Tensor:
         """hidden_states [B, Li, 64] bf16 (packed latents), encoder_hidden_states
@@ -435,9 +466,15 @@ class MMDiT:
         c = F.linear(rms_norm_eager(encoder_hidden_states, self.txt_norm_w, cfg.eps), *self.txt_in)
         temb = self.time_embed(t[:1] if shared_timestep else t)
         freqs_img, freqs_txt = self.rope(img_shape, c.shape[1])
-        mods = self.modulations(temb)
+        if temb.shape[0] == 1:
+            mods, events = self.modulations_overlapped(temb)
+        else:
+            mods, events = self.modulations(temb), [None] * cfg.num_layers
         x, c = x.contiguous(), c.contiguous()
-        for blk, (m_img, m_txt) in zip(self.blocks, mods):
+        main = torch.cuda.current_stream(x.device)
+        for blk, (m_img, m_txt), ev in zip(self.blocks, mods, events):
+            if ev is not None:
+                main.wait_event(ev)
             x, c = self.block_forward(blk, x, c, m_img, m_txt, freqs_img, freqs_txt)
         emb = F.linear(F.silu(temb), *self.norm_out)
         scale, shift = emb.chunk(2, dim=1)
@@ -476,9 +513,12 @@ class MMDiT:
         freqs_img, freqs_txt = self.rope(img_shape, c.shape[1])
         lo, hi = plan.image_slice(freqs_img.shape[0])
         freqs_loc = freqs_img[lo:hi].contiguous()
-        mods = self.modulations(temb)
+        mods, events = self.modulations_overlapped(temb)
         x, c = x.contiguous(), c.contiguous()
-        for blk, (m_img, m_txt) in zip(self.blocks, mods):
+        main = torch.cuda.current_stream(x.device)
+        for blk, (m_img, m_txt), ev in zip(self.blocks, mods, events):
+            if ev is not None:
+                main.wait_event(ev)
             x, c = self.block_forward_sharded(blk, x, c, m_img, m_txt, freqs_loc, freqs_txt, plan)
         emb = F.linear(F.silu(temb), *self.norm_out)
         scale, shift = emb.chunk(2, dim=1)

@@ -342,3 +342,34 @@ def test_ln_mod_quant_grouped_matches_single(shift):
         assert q.rows == ref.rows
         assert torch.equal(q.values.view(torch.uint8), ref.values.view(torch.uint8))
         assert torch.equal(q.scales.view(torch.uint8), ref.scales.view(torch.uint8))
+
+
+def test_adaln_modulation_vs_linear():
+    """qia_adaln_modulation against the exact (fp64) Linear(SiLU(temb)) with
+    1 + scale on the scale chunks: within half a bf16 ulp of the linear output
+    plus, on the scale chunks, half an ulp of 1 + scale (the eager double
+    rounding), plus a small absolute slack for near-cancelling sums; mostly
+    equal to F.linear; identical for a light (one CTA per SM) and a full grid."""
+    from qwen_image_accel_b200.kernels.modulation import adaln_modulation
+    g = torch.Generator(device="cuda").manual_seed(80)
+    d = 3072
+    w = (0.02 * torch.randn(12 * d, d, device="cuda", generator=g)).to(torch.bfloat16)
+    b = (0.02 * torch.randn(12 * d, device="cuda", generator=g)).to(torch.bfloat16)
+    x = F.silu(torch.randn(1, d, device="cuda", generator=g).to(torch.bfloat16)).reshape(-1)
+    full = adaln_modulation(x, w, b, d)
+    light = adaln_modulation(x, w, b, d, ctas=torch.cuda.get_device_properties(0).multi_processor_count)
+    assert torch.equal(full, light)
+    ref = F.linear(x[None], w, b).view(2, 6, d)
+    ref[:, 1] += 1
+    ref[:, 4] += 1
+    got = full.view(2, 6, d).float()
+    lin = F.linear(x[None].double(), w.double(), b.double()).view(2, 6, d)
+    exact = lin.clone()
+    exact[:, 1] += 1
+    exact[:, 4] += 1
+    # one bf16 rounding of the linear output, a second one after the +1
+    bound = ((lin.abs() + exact.abs()) * 2.0 ** -8).float() + 1e-4
+    err = (got - exact.float()).abs()
+    assert bool((err <= bound).all()), float((err - bound).max())
+    # cuBLAS may reduce in reduced precision for bf16 GEMMs: agreement, not equality
+    assert (got == ref.float()).float().mean().item() > 0.8
