@@ -125,6 +125,18 @@ int qia_adaln_modulation(const void* x, const void* weight, const void* bias,
                          void* out, int64_t n, int64_t k, int64_t unit,
                          int64_t ctas, void* stream);
 
+/* True-CFG combine with norm rescaling and the flow-match Euler update, one
+ * launch: per row of dim channels, comb = neg + s*(cond - neg),
+ * v = comb * (||cond|| / ||comb||), out = latents + dt * v, with every eager
+ * bf16 boundary a bf16 rounding (fp32 sums of squares; the last add in fp32).
+ * cond, neg, latents, out: [rows, dim] bf16 (out may be latents).
+ * Replaces: the CFG combine of the v1 pipeline and the scheduler step
+ * (WHL:diffusers/pipelines/qwenimage/pipeline_qwenimage.py:643-681;
+ * WHL:diffusers/schedulers/scheduling_flow_match_euler_discrete.py:483-517). */
+int qia_cfg_euler(const void* cond, const void* neg, const void* latents,
+                  void* out, int64_t rows, int64_t dim, float cfg_scale,
+                  float dt, void* stream);
+
 /* ---------------------------------------------------------------------------
  * Attention input preparation
  * ------------------------------------------------------------------------ */

@@ -43,6 +43,7 @@ from .kernels.elementwise import residual
 from .kernels.epilogue import layer_norm_scale_quantize_grouped
 from .kernels.layernorm import layer_norm_scale
 from .kernels.mxfp8 import quantize
+from .kernels.scheduler import cfg_euler
 from .optimizations.mxfp8 import (MXFP8Linear, matmul_gate_residual_grouped, matmul_gelu_quantize_grouped,
                                   matmul_grouped)
 from .optimizations.sage_attention import (sage_attention_joint_quantized, sage_attention_split,
@@ -492,11 +493,7 @@ class MMDiT:
         t = torch.full((2 * b,), sigma, device=latents.device, dtype=latents.dtype)
         v = self.forward(x_in, enc, t, img_shape, shared_timestep=True)
         cond, neg = v[:b], v[b:]
-        comb = neg + cfg_scale * (cond - neg)
-        cond_norm = torch.norm(cond, dim=-1, keepdim=True)
-        comb_norm = torch.norm(comb, dim=-1, keepdim=True)
-        v = comb * (cond_norm / comb_norm)
-        return (latents.to(torch.float32) + (sigma_next - sigma) * v).to(latents.dtype)
+        return cfg_euler(cond.contiguous(), neg.contiguous(), latents.contiguous(), cfg_scale, sigma_next - sigma)
 
 
     def forward_sharded(self, hidden_local: torch.Tensor, encoder_hidden_states: torch.Tensor,
@@ -539,11 +536,8 @@ class MMDiT:
         t = torch.full((b,), sigma, device=latents_local.device, dtype=latents_local.dtype)
         v = self.forward_sharded(latents_local, enc, t, img_shape, plan)
         cond, neg = exchange_cfg(v, plan)
-        comb = neg + cfg_scale * (cond - neg)
-        cond_norm = torch.norm(cond, dim=-1, keepdim=True)
-        comb_norm = torch.norm(comb, dim=-1, keepdim=True)
-        v = comb * (cond_norm / comb_norm)
-        return (latents_local.to(torch.float32) + (sigma_next - sigma) * v).to(latents_local.dtype)
+        return cfg_euler(cond.contiguous(), neg.contiguous(), latents_local.contiguous(), cfg_scale,
+                         sigma_next - sigma)
 
 
 def parameter_shapes_block_names() -> list[str]:

@@ -373,3 +373,24 @@ def test_adaln_modulation_vs_linear():
     assert bool((err <= bound).all()), float((err - bound).max())
     # cuBLAS may reduce in reduced precision for bf16 GEMMs: agreement, not equality
     assert (got == ref.float()).float().mean().item() > 0.8
+
+
+def test_cfg_euler_vs_eager():
+    """The fused CFG combine + norm rescale + Euler update against the eager
+    torch sequence of the pipeline: the bf16 roundings are the same; the fp32
+    sums of squares of torch.norm may run in another order, so the updated
+    latents are equal for almost every element and within one bf16 ulp
+    elsewhere."""
+    from qwen_image_accel_b200.kernels.scheduler import cfg_euler
+    g = torch.Generator(device="cuda").manual_seed(90)
+    cond, neg = (torch.randn(1, 4096, 64, device="cuda", generator=g).to(torch.bfloat16) for _ in range(2))
+    lat = torch.randn(1, 4096, 64, device="cuda", generator=g).to(torch.bfloat16)
+    s, sigma, sigma_next = 4.0, 0.9, 0.875
+    comb = neg + s * (cond - neg)
+    v = comb * (torch.norm(cond, dim=-1, keepdim=True) / torch.norm(comb, dim=-1, keepdim=True))
+    ref = (lat.to(torch.float32) + (sigma_next - sigma) * v).to(lat.dtype)
+    got = cfg_euler(cond, neg, lat, s, sigma_next - sigma)
+    diff = (got.float() - ref.float()).abs()
+    ulp = ref.float().abs() * 2.0 ** -7 + 1e-30
+    assert bool((diff <= ulp).all())
+    assert (got == ref).float().mean().item() > 0.99
