@@ -434,8 +434,9 @@ def c5_arm(args, rank, world, local_rank):
                 "config": {"workload": "config5: 60-block dual-stream MMDiT denoise step, 2048^2 "
                                        "(16384 img + 256 txt tokens), CFG batch 2, profile mxfp8_sage",
                            "global_batch": 2, "seq_len": img_len + TXT_LEN,
-                           "parallelism": (f"CFG split x Ulysses {plan.ulysses} (NCCL all-to-all)" if plan
-                                           else "single GPU"),
+                           "parallelism": ((f"CFG split x Ulysses {plan.ulysses} (NCCL all-to-all)"
+                                            if plan.ulysses > 1 else "CFG split (one NCCL exchange per step)")
+                                           if plan else "single GPU"),
                            "cuda_graph": used_graph,
                            "l2": "working set >> L2; no flush"},
                 "e2e": {"value": round(e2e_ms, 3), "unit": "ms/step",

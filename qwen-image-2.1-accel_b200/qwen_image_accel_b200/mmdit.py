@@ -516,7 +516,12 @@ class MMDiT:
         for blk, (m_img, m_txt), ev in zip(self.blocks, mods, events):
             if ev is not None:
                 main.wait_event(ev)
-            x, c = self.block_forward_sharded(blk, x, c, m_img, m_txt, freqs_loc, freqs_txt, plan)
+            if plan.ulysses == 1:
+                # CFG split only: this rank holds every token of its half, so
+                # the fused single-GPU block applies unchanged
+                x, c = self.block_forward(blk, x, c, m_img, m_txt, freqs_loc, freqs_txt)
+            else:
+                x, c = self.block_forward_sharded(blk, x, c, m_img, m_txt, freqs_loc, freqs_txt, plan)
         emb = F.linear(F.silu(temb), *self.norm_out)
         scale, shift = emb.chunk(2, dim=1)
         y = layer_norm_scale(x, (1 + scale)[:, None].contiguous(), self.ln, shift=shift[:, None].contiguous())
