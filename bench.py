@@ -451,6 +451,139 @@ def c5_arm(args, rank, world, local_rank):
         print(json.dumps(line), flush=True)
 
 
+PREFILL_RUNS = (("t", 113), ("i", 4096), ("t", 20), ("i", 4096))   # text, condition image, text, target
+PREFILL_HEADS = 32                                                   # Qwen-Image 2.1: 32 x 128 heads
+
+
+def _prefill_inputs(device):
+    runs = PREFILL_RUNS
+    ids, blk = [], 0
+    for kind, n in runs:
+        ids += [-1] * n if kind == "t" else [blk] * n
+        blk += kind == "i"
+    image_ids = torch.tensor(ids, device=device)
+    g = torch.Generator(device=device).manual_seed(3)
+    s = image_ids.shape[0]
+    q, k, v = (torch.randn(1, s, PREFILL_HEADS, 128, device=device, dtype=torch.bfloat16, generator=g)
+               for _ in range(3))
+    return image_ids, q, k, v
+
+
+def _segment_prefill(q, k, v, image_ids):
+    """The reference's default prefill (QwenImage21AttnProcessor,
+    transformer_qwenimage21.py:502-543): one bf16 SDPA per prefix segment over
+    keys [0, end), text segments with their causal triangle, then one for the
+    target image over every key. Segments are host-side (as the reference
+    derives them once per forward)."""
+    import torch.nn.functional as F
+    ids = image_ids.tolist()
+    target = ids[-1]
+    prefix_len = next(i for i, x in enumerate(ids) if x == target)
+    segs, start = [], 0
+    for i in range(1, prefix_len + 1):
+        if i == prefix_len or ids[i] != ids[start]:
+            segs.append((start, i, ids[start] < 0))
+            start = i
+    qt, kt, vt = (t.transpose(1, 2) for t in (q, k, v))
+    outs = []
+    for a, b, is_text in segs:
+        mask = None
+        if is_text:
+            n = b - a
+            mask = torch.cat([torch.ones(n, a, dtype=torch.bool, device=q.device),
+                              torch.tril(torch.ones(n, n, dtype=torch.bool, device=q.device))], dim=1)
+        outs.append(F.scaled_dot_product_attention(qt[:, :, a:b], kt[:, :, :b], vt[:, :, :b], attn_mask=mask))
+    outs.append(F.scaled_dot_product_attention(qt[:, :, prefix_len:], kt, vt))
+    return torch.cat(outs, dim=2).transpose(1, 2)
+
+
+def prefill_arm(args, rank, world, local_rank):
+    """`--config prefill`: the Qwen-Image 2.1 block-causal prefill attention
+    (text 113, condition image 4096, text 20, target image 4096 tokens; B=1,
+    32 heads x 128) through prefill_attention (Sage quantizers + the tcgen05
+    kernel with per-query key limits). Beside it, on the same inputs: the
+    same kernel without limits (full attention) and the reference's per-
+    segment bf16 SDPA prefill. One replica per GPU for N > 1."""
+    from qwen_image_accel_b200 import _lib
+    from qwen_image_accel_b200.optimizations.prefill import block_causal_kv_limits, prefill_attention
+    from qwen_image_accel_b200.optimizations.sage_attention import (sage_attention, sage_attention_prefill,
+                                                                    workspace_bytes)
+    device = torch.device("cuda", local_rank)
+    torch.cuda.set_device(device)
+    image_ids, q, k, v = _prefill_inputs(device)
+    s = q.shape[1]
+    ws = torch.empty(workspace_bytes(1, PREFILL_HEADS, s, s), device=device, dtype=torch.uint8)
+    out = torch.empty_like(q)
+    limits = block_causal_kv_limits(image_ids)
+    visible = int(limits.to(torch.int64).sum())
+    tops_call = 4.0 * 128 * PREFILL_HEADS * visible / 1e12      # QK^T + PV over the visible pairs
+    stream = torch.cuda.current_stream(device)
+
+    def timed(fn):
+        for _ in range(args.warmup):
+            fn()
+        if world > 1:
+            torch.distributed.barrier()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(args.steps):
+            fn()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / args.steps
+        if world > 1:
+            t = torch.tensor([ms], device=device)
+            torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+            ms = float(t.item())
+        return ms
+
+    _lib.launch_count = 0
+    clk = ClockSampler(local_rank)
+    # per layer: the limits are derived once per forward and shared by every block
+    ms = timed(lambda: sage_attention_prefill(q, k, v, limits, out=out, workspace=ws))
+    clocks = clk.stop()
+    launches = _lib.launch_count // (args.warmup + args.steps)
+    ms_full = timed(lambda: sage_attention(q, k, v, out=out, workspace=ws))
+    ms_ref = timed(lambda: _segment_prefill(q, k, v, image_ids))
+    # end to end through the public prefill API (limits derived from image_ids
+    # each call): q, k, v from pinned host memory, the output back to the host
+    host = [t.cpu().pin_memory() for t in (q, k, v)]
+    host_out = torch.empty(q.shape, dtype=q.dtype).pin_memory()
+    dq, dk, dv = (torch.empty_like(q) for _ in range(3))
+
+    def e2e():
+        for h, d in zip(host, (dq, dk, dv)):
+            d.copy_(h, non_blocking=True)
+        host_out.copy_(prefill_attention(dq, dk, dv, image_ids, workspace=ws), non_blocking=True)
+
+    ms_e2e = timed(e2e)
+    _, bf16_tf, peak_kind = load_peaks()
+    if rank == 0:
+        achieved = tops_call / (ms * 1e-3)
+        line = {"metric": "ms per Qwen-Image 2.1 block-causal prefill attention (1024^2 edit: 113 + 4096 + 20 + "
+                          "4096 tokens, 32 heads)", "value": round(ms, 4), "unit": "ms/call", "n_gpus": world,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
+                "higher_is_better": False, "scaling": "weak", "vs_baseline": None, "dtype": "int8/fp8 attn",
+                "data": "synthetic (seeded N(0,1) q, k, v)",
+                "config": {"workload": "prefill: block-causal joint attention of the 2.1 prefix-KV path, "
+                                       f"S={s}, B=1, H={PREFILL_HEADS}, d=128",
+                           "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
+                           "visible_pairs_frac": round(visible / (s * s), 4),
+                           "l2": "inputs (204 MB) > L2; no flush"},
+                "compare": {"full_attention_same_kernel_ms": round(ms_full, 4),
+                            "reference_segment_sdpa_bf16_ms": round(ms_ref, 4)},
+                "e2e": {"value": round(ms_e2e, 4), "unit": "ms/call", "h2d_bytes_per_step": 3 * q.numel() * 2,
+                        "d2h_bytes_per_step": q.numel() * 2},
+                "gpu_launches": launches * args.steps,
+                "roofline": {"bound": "tensor", "kernel": "prefill call (quantizers + attention), visible pairs "
+                                                          f"{tops_call * 1e3:.1f} GOP", "achieved": round(achieved, 1),
+                             "peak": round(2 * bf16_tf, 1), "unit": "TOP/s", "frac": round(achieved / (2 * bf16_tf), 3),
+                             "traffic": None, "peak_kind": f"2x {peak_kind} cuBLAS bf16 burst"},
+                "cpu_baseline": None, "clocks": clocks}
+        print(json.dumps(line), flush=True)
+
+
 def profile_case(name: str):
     """Small fixed cases for ncu captures (no timing, no JSON line):
     ffn_up  - the FFN-up GEMM with the GELU+MXFP8 epilogue, M=8192 (one launch)
@@ -512,8 +645,9 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--config", default="c4", choices=["c4", "c5"],
-                    help="c4: 1024^2 step (replicas for N>1); c5: 2048^2 step, CFG split x Ulysses for N>1")
+    ap.add_argument("--config", default="c4", choices=["c4", "c5", "prefill"],
+                    help="c4: 1024^2 step (replicas for N>1); c5: 2048^2 step, CFG split x Ulysses for N>1; "
+                         "prefill: the 2.1 block-causal prefill attention")
     ap.add_argument("--profile-case", choices=["ffn_up", "attn", "step8", "quant"],
                     help="run one small fixed case for an ncu capture and exit")
     args = ap.parse_args()
@@ -533,6 +667,8 @@ def main():
     try:
         if args.config == "c5":
             c5_arm(args, rank, world, local_rank)
+        elif args.config == "prefill":
+            prefill_arm(args, rank, world, local_rank)
         else:
             our_arm(args, rank, world, local_rank)
     finally:

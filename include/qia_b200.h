@@ -310,6 +310,27 @@ int qia_sage_attention(const void* q, const void* k, const void* v, void* out,
                        float sm_scale, void* workspace, int64_t workspace_bytes,
                        void* stream);
 
+/* Block-causal prefill: qia_sage_attention where query token t of batch b
+ * attends to keys [0, kv_limit[b * kv_limit_stride_b + t]) only (int32,
+ * clamped to [0, seq_kv]; kv_limit_stride_b 0 shares one row of limits across
+ * the batch). The 2.1 prefill mask -- text tokens causal, every image block
+ * bidirectional inside itself and causal towards what precedes it -- is one
+ * such limit per query: t + 1 for a text token, the end of its image block
+ * for an image token. Key tiles past a query tile's largest limit are not
+ * visited. A row whose limit is 0 is written as zeros.
+ * Replaces: the prefill branch of QwenImage21AttnProcessor (one SDPA call per
+ * prefix segment plus one for the target image,
+ * WHL:diffusers/models/transformers/transformer_qwenimage21.py:499-543) and
+ * the flex_attention BlockMask of QwenImage21FlexAttnProcessor
+ * (transformer_qwenimage21.py:257-306, 410-440). */
+int qia_sage_attention_prefill(const void* q, const void* k, const void* v,
+                               void* out, const int32_t* kv_limit,
+                               int64_t kv_limit_stride_b, int64_t batch,
+                               int64_t seq_q, int64_t seq_kv, int64_t heads,
+                               int64_t head_dim, const int64_t* strides,
+                               float sm_scale, void* workspace,
+                               int64_t workspace_bytes, void* stream);
+
 /* The joint [text, image] sequence written back as two streams: query tokens
  * [0, split) go to out_a ([batch, split, heads, 128]) and [split, seq_q) to
  * out_b ([batch, seq_q - split, heads, 128]); strides: q, k, v, out_a, out_b

@@ -377,12 +377,53 @@ def sage_quant_v(v: np.ndarray, scale_max: float = 448.0):
     return codes, scale
 
 
-def sage_attention(q: np.ndarray, k: np.ndarray, v: np.ndarray, sm_scale: float | None = None) -> np.ndarray:
+def block_causal_mask(image_ids: np.ndarray, key_valid: np.ndarray | None = None) -> np.ndarray:
+    """The Qwen-Image 2.1 prefill mask, densely: query q may see key kv when
+    kv <= q or both are tokens of the same image block, and kv is a valid key
+    (WHL:diffusers/models/transformers/transformer_qwenimage21.py:291-296,
+    `mask_mod` of build_qwenimage21_block_causal_mask). image_ids: int [S],
+    -1 at text tokens; key_valid: bool [B, S] or None. Returns bool [B, S, S]
+    (B = 1 without key_valid)."""
+    ids = np.asarray(image_ids, np.int64)
+    s = ids.shape[0]
+    q = np.arange(s)[:, None]
+    kv = np.arange(s)[None, :]
+    same = (ids[:, None] == ids[None, :]) & (ids[:, None] >= 0)
+    allowed = (q >= kv) | same
+    if key_valid is None:
+        return allowed[None]
+    return allowed[None] & np.asarray(key_valid, bool)[:, None, :]
+
+
+def block_causal_kv_limits(image_ids: np.ndarray) -> np.ndarray:
+    """One key limit per query that reproduces block_causal_mask without a key
+    mask when every image block is one contiguous run (as
+    QwenImage21Transformer2DModel.build_token_metadata assigns them,
+    transformer_qwenimage21.py:808-844): q + 1 for a text token, the end of
+    its run for an image token -- the `[0, end)` keys each prefix segment sees
+    in QwenImage21AttnProcessor (transformer_qwenimage21.py:502-541). Plain
+    loop restatement; int32 [S]."""
+    ids = [int(x) for x in np.asarray(image_ids).ravel()]
+    s = len(ids)
+    out = np.zeros(s, np.int32)
+    end = s
+    for i in range(s - 1, -1, -1):
+        if i == s - 1 or ids[i + 1] != ids[i]:
+            end = i + 1
+        out[i] = i + 1 if ids[i] < 0 else end
+    return out
+
+
+def sage_attention(q: np.ndarray, k: np.ndarray, v: np.ndarray, sm_scale: float | None = None,
+                   kv_limit: np.ndarray | None = None) -> np.ndarray:
     """Sage-style attention (SAGE:sageattention/core.py:725-828): INT8 Q/K with
     K smoothing, fp32 softmax in base 2 with the +log2(448) offset so that P
     lands in [0, 448], P rounded to E4M3, FP8 V with per-channel scales, output
     divided by the row sum of the unrounded P. Inputs fp32 [B, S, H, D];
-    returns fp32 [B, Sq, H, D]."""
+    returns fp32 [B, Sq, H, D]. kv_limit (int [B, Sq] or [Sq]): query t sees
+    keys [0, limit) only -- the row max and the row sum run over those keys,
+    the others get P = 0; the quantization is unchanged (K's mean still runs
+    over all keys). A row with no visible key is zero."""
     b, sq, h, d = q.shape
     if sm_scale is None:
         sm_scale = d ** -0.5
@@ -398,18 +439,28 @@ def sage_attention(q: np.ndarray, k: np.ndarray, v: np.ndarray, sm_scale: float 
             qscale = np.repeat(qs[bi, hi], 32)[:sq]
             kscale = np.repeat(ks[bi, hi], 64)[: k.shape[1]]
             sc = s_int.astype(np.float32) * (qscale[:, None] * kscale[None, :]) * np.float32(sm_scale * log2e)
-            m = sc.max(axis=1, keepdims=True) - np.float32(8.807)
-            p = np.exp2(sc - m).astype(np.float32)
+            if kv_limit is None:
+                m = sc.max(axis=1, keepdims=True) - np.float32(8.807)
+                p = np.exp2(sc - m).astype(np.float32)
+            else:
+                lim = np.asarray(kv_limit).reshape(-1, sq)[bi if np.asarray(kv_limit).ndim > 1 else 0]
+                seen = np.arange(k.shape[1])[None, :] < np.clip(lim, 0, k.shape[1])[:, None]
+                m = np.where(seen, sc, -np.inf).max(axis=1, keepdims=True) - np.float32(8.807)
+                m = np.where(np.isfinite(m), m, 0.0).astype(np.float32)
+                p = np.where(seen, np.exp2(sc - m), 0.0).astype(np.float32)
             denom = p.sum(axis=1, keepdims=True)
             p8 = table[_encode_e4m3(p)]
             vv = table[vc[bi, :, hi, :]]
             o = (p8.astype(np.float64) @ vv.astype(np.float64)).astype(np.float32)
-            out[bi, :, hi, :] = o / denom * vs[bi, hi][None, :]
+            safe = np.where(denom > 0, denom, 1.0)
+            out[bi, :, hi, :] = np.where(denom > 0, o / safe, 0.0) * vs[bi, hi][None, :]
     return out
 
 
-def attention_fp32(q, k, v, sm_scale=None):
-    """Exact softmax attention in fp64 (reference for cosine checks)."""
+def attention_fp32(q, k, v, sm_scale=None, mask=None):
+    """Exact softmax attention in fp64 (reference for cosine checks). mask:
+    bool [B, Sq, Skv] (or [1, Sq, Skv]) of visible keys, or None; a row with
+    no visible key is zero."""
     b, sq, h, d = q.shape
     if sm_scale is None:
         sm_scale = d ** -0.5
@@ -417,8 +468,11 @@ def attention_fp32(q, k, v, sm_scale=None):
     for bi in range(b):
         for hi in range(h):
             s = q[bi, :, hi, :].astype(np.float64) @ k[bi, :, hi, :].astype(np.float64).T * sm_scale
-            s -= s.max(axis=1, keepdims=True)
-            p = np.exp(s)
-            p /= p.sum(axis=1, keepdims=True)
+            if mask is not None:
+                s = np.where(mask[bi if mask.shape[0] > 1 else 0], s, -np.inf)
+            mx = s.max(axis=1, keepdims=True)
+            p = np.exp(s - np.where(np.isfinite(mx), mx, 0.0))
+            den = p.sum(axis=1, keepdims=True)
+            p = np.where(den > 0, p / np.where(den > 0, den, 1.0), 0.0)
             out[bi, :, hi, :] = (p @ v[bi, :, hi, :].astype(np.float64)).astype(np.float32)
     return out

@@ -507,6 +507,11 @@ struct AttnParams {
   uint8_t* qa_scales;
   uint8_t* qb_values;
   uint8_t* qb_scales;
+  // Optional per-query key limit (block-causal prefill): query token t of
+  // batch b attends to keys [0, kv_limit[b * kv_limit_stride_b + t]) only,
+  // clamped to [0, Skv]. Null: every query sees all Skv keys.
+  const int* kv_limit;
+  int64_t kv_limit_stride_b;
 };
 
 // Two CTAs share an SM (98 KB of shared memory and 256 TMEM columns each), so
@@ -566,11 +571,11 @@ sage_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
   uint64_t* o_full = pb_full + 2;           // all P.V done
   uint64_t* drain = o_full + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  int* kv_extent = reinterpret_cast<int*>(tmem_slot + 1);   // largest key limit of this query tile
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int q_tile = blockIdx.x, bh = blockIdx.y;
-  const int nkv = p.Skv_pad / kTile;
-  const int nh = 2 * nkv;                   // 64-key halves in the P pass
+  int nkv = p.Skv_pad / kTile;
   const int q_row0 = bh * p.Sq_pad + q_tile * kTile;
   const int kv_row0 = bh * p.Skv_pad;
 
@@ -592,6 +597,7 @@ sage_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
     }
     mbar_init(smem_u32(o_full), 1);
     mbar_init(smem_u32(drain), 1);
+    *kv_extent = 0;
     fence_barrier_init();
     prefetch_tmap(&tm_q);
     prefetch_tmap(&tm_k);
@@ -602,6 +608,20 @@ sage_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  // this thread's key limit when it is a softmax thread (one query row each)
+  int kv_lim = p.Skv;
+  if (p.kv_limit) {
+    // the tile visits only the key tiles its rows may see
+    if (warp >= 2) {
+      const int q_tok = q_tile * kTile + (warp & 3) * 32 + lane;
+      kv_lim = q_tok < p.Sq ? min(max(__ldg(p.kv_limit + (bh / p.H) * p.kv_limit_stride_b + q_tok), 0), p.Skv) : 0;
+      const int wmax = __reduce_max_sync(0xffffffffu, kv_lim);
+      if (lane == 0) atomicMax(kv_extent, wmax);
+    }
+    __syncthreads();
+    nkv = max(1, (*kv_extent + kTile - 1) / kTile);
+  }
+  const int nh = 2 * nkv;                   // 64-key halves in the P pass
 
   if (warp == 0) {
     if (lane == 0) {
@@ -724,7 +744,7 @@ sage_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
       ks_next = make_float2(__ldg(ks_head + 2 * jn), __ldg(ks_head + 2 * jn + 1));
       if (!__all_sync(0xffffffffu, mbar_wait(smem_u32(&sa_full[j & 1]), (j >> 1) & 1, err))) { ok = false; break; }
       tc_fence_after();
-      const int valid = p.Skv - j * kTile;
+      const int valid = kv_lim - j * kTile;
       uint32_t sv[128];
 #pragma unroll
       for (int c = 0; c < 4; ++c)
@@ -775,7 +795,7 @@ sage_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
       ks_cur = __ldg(ks_head + (i + 1 < nh ? i + 1 : 0));
       if (!__all_sync(0xffffffffu, mbar_wait(smem_u32(&sb_full[h]), (i >> 1) & 1, err))) { ok = false; break; }
       tc_fence_after();
-      const int valid = p.Skv - i * kHalf;
+      const int valid = kv_lim - i * kHalf;
       uint32_t sv[64];
       tc_ld_32x32b_x32(tmem + t_lane + uint32_t(h * kHalf), *reinterpret_cast<uint32_t(*)[32]>(&sv[0]));
       tc_ld_32x32b_x32(tmem + t_lane + uint32_t(h * kHalf + 32), *reinterpret_cast<uint32_t(*)[32]>(&sv[32]));
@@ -829,7 +849,8 @@ sage_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
     const float dsum = (ds[0] + ds[1]) + (ds[2] + ds[3]);
     if (ok && __all_sync(0xffffffffu, mbar_wait(smem_u32(o_full), 0, err))) {
       tc_fence_after();
-      const float rinv = 1.0f / dsum;
+      // a row that may see no key at all (a key limit of 0) writes zeros
+      const float rinv = dsum > 0.0f ? 1.0f / dsum : 0.0f;
       const float* vs = p.v_scale + int64_t(bh) * kD;
       const int b = bh / p.H, h = bh % p.H;
       if (p.qa_values) {
@@ -1055,7 +1076,8 @@ struct MxOut {
 };
 
 int launch_attn(const Workspace& ws, void* out, Strides os, void* out2, Strides os2, int64_t split, int64_t B,
-                int64_t H, int64_t Sq, int64_t Skv, float sm_scale, cudaStream_t st, const MxOut& mx = MxOut()) {
+                int64_t H, int64_t Sq, int64_t Skv, float sm_scale, cudaStream_t st, const MxOut& mx = MxOut(),
+                const int* kv_limit = nullptr, int64_t kv_limit_stride_b = 0) {
   static bool attr_done[64] = {false};
   static std::mutex mu;
   int dev = 0;
@@ -1100,6 +1122,8 @@ int launch_attn(const Workspace& ws, void* out, Strides os, void* out2, Strides 
   p.qa_scales = (uint8_t*)mx.a_scales;
   p.qb_values = (uint8_t*)mx.b_values;
   p.qb_scales = (uint8_t*)mx.b_scales;
+  p.kv_limit = kv_limit;
+  p.kv_limit_stride_b = kv_limit_stride_b;
   sage_attn_kernel<<<dim3(unsigned(sqp / 128), unsigned(B * H)), 192, kAttnSmem, st>>>(tq, tk, tv, p,
                                                                                         device_error_word());
   return check_launch("sage_attn_kernel");
@@ -1207,6 +1231,40 @@ extern "C" int qia_sage_attention(const void* q, const void* k, const void* v, v
   rc = quant_qkv(q, sq, k, sk, v, sv, batch, heads, seq_q, seq_kv, ws, st);
   if (rc) return rc;
   return launch_attn(ws, out, so, nullptr, so, 0, batch, heads, seq_q, seq_kv, scale, st);
+}
+
+extern "C" int qia_sage_attention_prefill(const void* q, const void* k, const void* v, void* out,
+                                          const int32_t* kv_limit, int64_t kv_limit_stride_b, int64_t batch,
+                                          int64_t seq_q, int64_t seq_kv, int64_t heads, int64_t head_dim,
+                                          const int64_t* strides, float sm_scale, void* workspace,
+                                          int64_t workspace_bytes, void* stream) {
+  int rc = check_sizes(batch, heads, seq_q, seq_kv, head_dim, "qia_sage_attention_prefill");
+  if (rc) return rc;
+  if (!strides) return set_error(QIA_ERR_INVALID, "qia_sage_attention_prefill: null strides");
+  if (!kv_limit) return set_error(QIA_ERR_INVALID, "qia_sage_attention_prefill: null kv_limit");
+  if (kv_limit_stride_b < 0 || (batch > 1 && kv_limit_stride_b != 0 && kv_limit_stride_b < seq_q))
+    return set_error(QIA_ERR_INVALID, "qia_sage_attention_prefill: kv_limit_stride_b must be 0 or >= seq_q");
+  if (!aligned(kv_limit, 4)) return set_error(QIA_ERR_ALIGNMENT, "qia_sage_attention_prefill: kv_limit alignment 4");
+  const Strides sq{strides[0], strides[1], strides[2]}, sk{strides[3], strides[4], strides[5]},
+      sv{strides[6], strides[7], strides[8]}, so{strides[9], strides[10], strides[11]};
+  if ((rc = check_nhd(q, sq, "qia_sage_attention_prefill q")) ||
+      (rc = check_nhd(k, sk, "qia_sage_attention_prefill k")) ||
+      (rc = check_nhd(v, sv, "qia_sage_attention_prefill v")) ||
+      (rc = check_nhd(out, so, "qia_sage_attention_prefill out")))
+    return rc;
+  const int64_t need = workspace_layout(batch, heads, seq_q, seq_kv, nullptr, nullptr);
+  if (!workspace || workspace_bytes < need)
+    return set_error(QIA_ERR_INVALID, "qia_sage_attention_prefill: workspace of %lld bytes needed", (long long)need);
+  if (!aligned(workspace, 256))
+    return set_error(QIA_ERR_ALIGNMENT, "qia_sage_attention_prefill: workspace alignment 256");
+  Workspace ws;
+  workspace_layout(batch, heads, seq_q, seq_kv, (uint8_t*)workspace, &ws);
+  const float scale = sm_scale > 0.0f ? sm_scale : 1.0f / sqrtf(float(head_dim));
+  cudaStream_t st = as_stream(stream);
+  rc = quant_qkv(q, sq, k, sk, v, sv, batch, heads, seq_q, seq_kv, ws, st);
+  if (rc) return rc;
+  return launch_attn(ws, out, so, nullptr, so, 0, batch, heads, seq_q, seq_kv, scale, st, MxOut(), kv_limit,
+                     kv_limit_stride_b);
 }
 
 extern "C" int qia_sage_attention_split(const void* q, const void* k, const void* v, void* out_a, void* out_b,

@@ -58,6 +58,7 @@ SIGNATURES: dict[str, list] = {
     "qia_mxfp8_gemm_gate_residual": [_P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _P],
     "qia_device_error": [_P],
     "qia_sage_attention": [_P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _F, _P, _I, _P],
+    "qia_sage_attention_prefill": [_P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _P, _F, _P, _I, _P],
     "qia_sage_attention_split": [_P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _P, _F, _P, _I, _P],
     "qia_sage_attention_split_mx": [_P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _P, _F, _P, _I, _P],
     "qia_sage_attention_noalloc": [_P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _F, _P],
@@ -117,7 +118,7 @@ def declared_symbols() -> list[str]:
 # kernels each entry point queues (for launch accounting); default 1
 KERNELS_PER_CALL = {"qia_sage_attention": 4, "qia_sage_attention_split": 4, "qia_sage_quantize": 3,
                     "qia_sage_attention_split_mx": 4, "qia_sage_quantize_joint": 3, "qia_sage_attention_joint_mx": 4,
-                    "qia_sage_attention_noalloc": 4,
+                    "qia_sage_attention_noalloc": 4, "qia_sage_attention_prefill": 4,
                     "qia_device_error": 0}
 launch_count = 0
 

@@ -92,6 +92,32 @@ def sage_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, sm_scale: 
     return out
 
 
+def sage_attention_prefill(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, kv_limit: torch.Tensor,
+                           sm_scale: float | None = None, out: torch.Tensor | None = None,
+                           workspace: torch.Tensor | None = None) -> torch.Tensor:
+    """sage_attention where query token t sees keys [0, kv_limit[t]) only
+    (kv_limit int32 [Sq], shared by the batch, or [B, Sq]); the block-causal
+    prefill of the 2.1 prefix-KV path (see prefill.prefill_attention)."""
+    _check_settings()
+    _validate(q, k, v)
+    b, sq, h, d = q.shape
+    skv = k.shape[1]
+    _lib.require_cuda(kv_limit)
+    if kv_limit.dtype != torch.int32 or kv_limit.shape[-1] != sq or kv_limit.ndim not in (1, 2) \
+            or kv_limit.stride(-1) != 1 or (kv_limit.ndim == 2 and kv_limit.shape[0] != b):
+        raise NotImplementedError("kv_limit must be int32 [Sq] or [B, Sq] with a contiguous last dim")
+    stride_b = 0 if kv_limit.ndim == 1 or b == 1 else kv_limit.stride(0)
+    if out is None:
+        out = torch.empty_like(q)
+    need = workspace_bytes(b, h, sq, skv)
+    if workspace is None or workspace.numel() < need:
+        workspace = torch.empty(need, device=q.device, dtype=torch.uint8)
+    _lib.call("qia_sage_attention_prefill", _lib.ptr(q), _lib.ptr(k), _lib.ptr(v), _lib.ptr(out), _lib.ptr(kv_limit),
+              stride_b, b, sq, skv, h, d, _strides(q, k, v, out), float(sm_scale or 0.0), _lib.ptr(workspace),
+              workspace.numel(), _lib.stream(q.device))
+    return out
+
+
 def sage_attention_split(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, split: int, out_a: torch.Tensor,
                          out_b: torch.Tensor, sm_scale: float | None = None,
                          workspace: torch.Tensor | None = None) -> None:

@@ -17,6 +17,9 @@ modified). Sources of truth, per fixture:
   from the pinned wheel (the oracle of tests/gpu/check_attention_ops.py:264-267),
   with freqs from QwenEmbedRope for a (1, 4, 4) grid and 16 text tokens.
 * activations.npz -- eager F.silu(g) * v and F.gelu(x, approximate="tanh").
+* block_causal.npz -- the Qwen-Image 2.1 prefill mask (token metadata,
+  prefix segments and the flex mask_mod evaluated densely, with a key-padding
+  mask) from WHL:diffusers/models/transformers/transformer_qwenimage21.py.
 * mmdit_tiny.npz -- the Diffusers QwenImageTransformer2DModel (v1 dual-stream
   MMDiT, WHL:diffusers/models/transformers/transformer_qwenimage.py) at a tiny
   size (2 blocks, 4x128 heads, text dim 512) in bf16 on the CPU, weights from
@@ -180,6 +183,48 @@ def make_mmdit(reference: Path):
                         keys=np.array(sorted(sd)))
 
 
+def make_block_causal(reference: Path):
+    """The 2.1 prefill mask from the pinned wheel: token metadata
+    (QwenImage21Transformer2DModel.build_token_metadata), the prefix segments
+    the default processor iterates (_qwenimage21_prefix_segments) and the
+    dense mask of the flex BlockMask's mask_mod
+    (build_qwenimage21_block_causal_mask), for a few sequence layouts."""
+    import torch
+    _import_diffusers(reference)
+    from diffusers.models.transformers import transformer_qwenimage21 as t21
+
+    # (runs of (kind, length) in sequence order, image shapes condition-first)
+    layouts = {
+        "t2i": ([("t", 7), ("i", 8)], [(1, 2, 4)]),
+        "edit": ([("t", 5), ("i", 6), ("t", 3), ("i", 8)], [(1, 2, 3), (1, 2, 4)]),
+        "adjacent": ([("t", 4), ("i", 4), ("i", 6), ("t", 2), ("i", 12)], [(1, 2, 2), (1, 2, 3), (1, 3, 4)]),
+        "long": ([("t", 37), ("i", 64), ("t", 11), ("i", 48), ("t", 5), ("i", 96)], [(1, 8, 8), (1, 6, 8), (1, 8, 12)]),
+    }
+    cases = {}
+    for name, (runs, shapes) in layouts.items():
+        pad = torch.cat([torch.full((n,), kind == "i") for kind, n in runs])
+        image_ids, target = t21.QwenImage21Transformer2DModel.build_token_metadata(pad, shapes)
+        s = pad.shape[0]
+        prefix_len = int((~target).sum())
+        segments = t21._qwenimage21_prefix_segments(image_ids, prefix_len)
+        g = torch.Generator().manual_seed(len(name))
+        key_valid = torch.ones(2, s, dtype=torch.bool)
+        text_pos = (~pad).nonzero(as_tuple=True)[0]
+        drop = text_pos[torch.randperm(text_pos.numel(), generator=g)[: max(1, text_pos.numel() // 4)]]
+        key_valid[1, drop] = False
+        key_valid[1, 0] = True
+        bm = t21.build_qwenimage21_block_causal_mask(image_ids, key_valid, 2, torch.device("cpu"))
+        qi = torch.arange(s)[:, None]
+        ki = torch.arange(s)[None, :]
+        dense = torch.stack([bm.mask_mod(torch.tensor(b), torch.tensor(0), qi, ki) for b in range(2)])
+        cases[f"image_ids_{name}"] = image_ids.numpy().astype(np.int64)
+        cases[f"target_{name}"] = target.numpy()
+        cases[f"segments_{name}"] = np.array([(a, b, int(t)) for a, b, t in segments], np.int64).reshape(-1, 3)
+        cases[f"key_valid_{name}"] = key_valid.numpy()
+        cases[f"mask_{name}"] = dense.numpy()
+    np.savez_compressed(OUT / "block_causal.npz", **cases)
+
+
 if __name__ == "__main__":
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default="/root/reference")
@@ -188,4 +233,5 @@ if __name__ == "__main__":
     make_mxfp8(ref)   # first: the interpreter flag must precede the first triton import
     make_eager(ref)
     make_mmdit(ref)
+    make_block_causal(ref)
     print("wrote", sorted(p.name for p in OUT.glob("*.npz")))
