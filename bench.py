@@ -592,7 +592,9 @@ def profile_case(name: str):
               range named `step` (for `ncu --nvtx --nvtx-include step/`)
     quant   - the fused QK-norm/RoPE + Sage quantization of one block (B=2, 256
               text + 4096 image tokens, 24 heads, from the two streams' q|k|v
-              projections), twice (three launches each)."""
+              projections), twice (three launches each).
+    prefill - the 2.1 block-causal prefill attention of `--config prefill`
+              (S=8325, 32 heads), three calls (four launches each)."""
     device = torch.device("cuda", 0)
     torch.cuda.set_device(device)
     g = torch.Generator(device=device).manual_seed(0)
@@ -608,6 +610,13 @@ def profile_case(name: str):
                    for _ in range(3))
         for _ in range(3):
             sage_attention(q, k, v)
+    elif name == "prefill":
+        from qwen_image_accel_b200.optimizations.prefill import block_causal_kv_limits
+        from qwen_image_accel_b200.optimizations.sage_attention import sage_attention_prefill
+        image_ids, q, k, v = _prefill_inputs(device)
+        limits = block_causal_kv_limits(image_ids)
+        for _ in range(3):
+            sage_attention_prefill(q, k, v, limits)
     elif name == "quant":
         from qwen_image_accel_b200.mmdit import rope_tables
         from qwen_image_accel_b200.optimizations.sage_attention import sage_quantize_joint
@@ -648,7 +657,7 @@ def main():
     ap.add_argument("--config", default="c4", choices=["c4", "c5", "prefill"],
                     help="c4: 1024^2 step (replicas for N>1); c5: 2048^2 step, CFG split x Ulysses for N>1; "
                          "prefill: the 2.1 block-causal prefill attention")
-    ap.add_argument("--profile-case", choices=["ffn_up", "attn", "step8", "quant"],
+    ap.add_argument("--profile-case", choices=["ffn_up", "attn", "step8", "quant", "prefill"],
                     help="run one small fixed case for an ncu capture and exit")
     args = ap.parse_args()
     if args.profile_case:

@@ -574,7 +574,10 @@ sage_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
   int* kv_extent = reinterpret_cast<int*>(tmem_slot + 1);   // largest key limit of this query tile
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int q_tile = blockIdx.x, bh = blockIdx.y;
+  // with key limits the grid is (B*H, query tiles) and the last query tiles,
+  // which see the most keys, are issued first (longest first shortens the tail)
+  const int q_tile = p.kv_limit ? int(gridDim.y - 1 - blockIdx.y) : int(blockIdx.x);
+  const int bh = p.kv_limit ? int(blockIdx.x) : int(blockIdx.y);
   int nkv = p.Skv_pad / kTile;
   const int q_row0 = bh * p.Sq_pad + q_tile * kTile;
   const int kv_row0 = bh * p.Skv_pad;
@@ -1124,8 +1127,8 @@ int launch_attn(const Workspace& ws, void* out, Strides os, void* out2, Strides 
   p.qb_scales = (uint8_t*)mx.b_scales;
   p.kv_limit = kv_limit;
   p.kv_limit_stride_b = kv_limit_stride_b;
-  sage_attn_kernel<<<dim3(unsigned(sqp / 128), unsigned(B * H)), 192, kAttnSmem, st>>>(tq, tk, tv, p,
-                                                                                        device_error_word());
+  const dim3 grid = kv_limit ? dim3(unsigned(B * H), unsigned(sqp / 128)) : dim3(unsigned(sqp / 128), unsigned(B * H));
+  sage_attn_kernel<<<grid, 192, kAttnSmem, st>>>(tq, tk, tv, p, device_error_word());
   return check_launch("sage_attn_kernel");
 }
 
@@ -1245,6 +1248,7 @@ extern "C" int qia_sage_attention_prefill(const void* q, const void* k, const vo
   if (kv_limit_stride_b < 0 || (batch > 1 && kv_limit_stride_b != 0 && kv_limit_stride_b < seq_q))
     return set_error(QIA_ERR_INVALID, "qia_sage_attention_prefill: kv_limit_stride_b must be 0 or >= seq_q");
   if (!aligned(kv_limit, 4)) return set_error(QIA_ERR_ALIGNMENT, "qia_sage_attention_prefill: kv_limit alignment 4");
+  if (pad128(seq_q) / 128 > 65535) return set_error(QIA_ERR_UNSUPPORTED, "qia_sage_attention_prefill: seq_q too large");
   const Strides sq{strides[0], strides[1], strides[2]}, sk{strides[3], strides[4], strides[5]},
       sv{strides[6], strides[7], strides[8]}, so{strides[9], strides[10], strides[11]};
   if ((rc = check_nhd(q, sq, "qia_sage_attention_prefill q")) ||
