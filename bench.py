@@ -469,34 +469,6 @@ def _prefill_inputs(device):
     return image_ids, q, k, v
 
 
-def _segment_prefill(q, k, v, image_ids):
-    """The reference's default prefill (QwenImage21AttnProcessor,
-    transformer_qwenimage21.py:502-543): one bf16 SDPA per prefix segment over
-    keys [0, end), text segments with their causal triangle, then one for the
-    target image over every key. Segments are host-side (as the reference
-    derives them once per forward)."""
-    import torch.nn.functional as F
-    ids = image_ids.tolist()
-    target = ids[-1]
-    prefix_len = next(i for i, x in enumerate(ids) if x == target)
-    segs, start = [], 0
-    for i in range(1, prefix_len + 1):
-        if i == prefix_len or ids[i] != ids[start]:
-            segs.append((start, i, ids[start] < 0))
-            start = i
-    qt, kt, vt = (t.transpose(1, 2) for t in (q, k, v))
-    outs = []
-    for a, b, is_text in segs:
-        mask = None
-        if is_text:
-            n = b - a
-            mask = torch.cat([torch.ones(n, a, dtype=torch.bool, device=q.device),
-                              torch.tril(torch.ones(n, n, dtype=torch.bool, device=q.device))], dim=1)
-        outs.append(F.scaled_dot_product_attention(qt[:, :, a:b], kt[:, :, :b], vt[:, :, :b], attn_mask=mask))
-    outs.append(F.scaled_dot_product_attention(qt[:, :, prefix_len:], kt, vt))
-    return torch.cat(outs, dim=2).transpose(1, 2)
-
-
 def prefill_arm(args, rank, world, local_rank):
     """`--config prefill`: the Qwen-Image 2.1 block-causal prefill attention
     (text 113, condition image 4096, text 20, target image 4096 tokens; B=1,
@@ -505,7 +477,8 @@ def prefill_arm(args, rank, world, local_rank):
     same kernel without limits (full attention) and the reference's per-
     segment bf16 SDPA prefill. One replica per GPU for N > 1."""
     from qwen_image_accel_b200 import _lib
-    from qwen_image_accel_b200.optimizations.prefill import block_causal_kv_limits, prefill_attention
+    from qwen_image_accel_b200.optimizations.prefill import (block_causal_kv_limits, prefill_attention,
+                                                             prefix_segments, segment_prefill_sdpa)
     from qwen_image_accel_b200.optimizations.sage_attention import (sage_attention, sage_attention_prefill,
                                                                     workspace_bytes)
     device = torch.device("cuda", local_rank)
@@ -545,7 +518,9 @@ def prefill_arm(args, rank, world, local_rank):
     clocks = clk.stop()
     launches = _lib.launch_count // (args.warmup + args.steps)
     ms_full = timed(lambda: sage_attention(q, k, v, out=out, workspace=ws))
-    ms_ref = timed(lambda: _segment_prefill(q, k, v, image_ids))
+    prefix_len = s - PREFILL_RUNS[-1][1]
+    segments = prefix_segments(image_ids, prefix_len)       # host-side, once per forward
+    ms_ref = timed(lambda: segment_prefill_sdpa(q, k, v, image_ids, prefix_len, segments=segments))
     # end to end through the public prefill API (limits derived from image_ids
     # each call): q, k, v from pinned host memory, the output back to the host
     host = [t.cpu().pin_memory() for t in (q, k, v)]
@@ -582,6 +557,155 @@ def prefill_arm(args, rank, world, local_rank):
                              "traffic": None, "peak_kind": f"2x {peak_kind} cuBLAS bf16 burst"},
                 "cpu_baseline": None, "clocks": clocks}
         print(json.dumps(line), flush=True)
+
+
+Q21_LAYERS, Q21_DIM, Q21_HEADS, Q21_PREFIX, Q21_TARGET = 32, 4096, 32, 113, 4096   # Qwen-Image 2.1, 1024^2 t2i
+
+
+def q21_arm(args, rank, world, local_rank):
+    """`--config q21`: the Qwen-Image 2.1 denoiser on the sm_100a kernels
+    (qwen21.Block21, profile mxfp8_sage): 32 single-stream blocks (D 4096,
+    32 x 128 heads, SwiGLU 12288), 1024^2 text-to-image (4096 target tokens,
+    a 113-token text prefix). value = one cached-decode step, captured in a
+    CUDA graph: img_in, the shared modulation GEMV, the 32 blocks over the
+    target tokens against the prefix KV cache, norm_out and proj_out. Not in
+    the step: the timestep embedder and the text projection (prompt-sized
+    work). Beside it, the prefill step (eager, the prefix K/V extracted) with
+    the reference's per-segment SDPA and with the tcgen05 block-causal
+    kernel. One replica per GPU for N > 1."""
+    import torch.nn.functional as F
+    from qwen_image_accel_b200 import _lib
+    from qwen_image_accel_b200.kernels.layernorm import layer_norm_scale
+    from qwen_image_accel_b200.mmdit import init_parameter
+    from qwen_image_accel_b200.qwen21 import (Block21, Block21Config, KVCache, _Norm, block21_parameter_shapes,
+                                              modulation_values)
+    device = torch.device("cuda", local_rank)
+    torch.cuda.set_device(device)
+    cfg = Block21Config(dim=Q21_DIM, heads=Q21_HEADS)
+    shapes = block21_parameter_shapes(cfg)
+    blocks = [Block21(lambda n, i=i: init_parameter(f"transformer_blocks.{i}.{n}", shapes[n], 42, device), cfg,
+                      device=device, profile="mxfp8_sage") for i in range(Q21_LAYERS)]
+    D, S, P = Q21_DIM, Q21_PREFIX + Q21_TARGET, Q21_PREFIX
+    w = {n: init_parameter(n, shp, 42, device) for n, shp in
+         (("img_in.weight", (D, 64)), ("modulation.1.weight", (4 * D, D)), ("norm_out.linear.weight", (D, D)),
+          ("proj_out.weight", (64, D)))}
+    g = torch.Generator(device=device).manual_seed(42)
+    lat = torch.randn(1, Q21_TARGET, 64, device=device, dtype=torch.bfloat16, generator=g)
+    temb = torch.randn(2, D, device=device, dtype=torch.bfloat16, generator=g)        # [sampled t, t = 0]
+    joint = torch.randn(1, S, D, device=device, dtype=torch.bfloat16, generator=g)     # img_in / txt_in output
+    phase = torch.rand(S, 64, device=device, generator=g) * 6.2831853
+    freqs = torch.polar(torch.ones_like(phase), phase)                               # complex64 [S, 64]
+    freqs_target = freqs[P:].contiguous()
+    image_ids = torch.cat([torch.full((P,), -1, device=device), torch.zeros(Q21_TARGET, device=device)]).long()
+    cache = KVCache(Q21_LAYERS)
+    ln = _Norm(None, cfg.eps, (D,))
+
+    def prefill():
+        mod = F.linear(F.silu(temb), w["modulation.1.weight"])
+        x = joint
+        for i, blk in enumerate(blocks):
+            x = blk.forward_prefill(x, mod, freqs, image_ids, P, layer_cache=cache.get_layer(i))
+        return x
+
+    def decode(latents):
+        x = F.linear(latents, w["img_in.weight"])
+        vals = modulation_values(F.linear(F.silu(temb), w["modulation.1.weight"]))
+        for i, blk in enumerate(blocks):
+            x = blk.forward_cached(x, vals, freqs_target, cache.get_layer(i))
+        scale = F.linear(F.silu(temb[:1]), w["norm_out.linear.weight"])
+        return F.linear(layer_norm_scale(x, (1 + scale)[:, None].contiguous(), ln), w["proj_out.weight"])
+
+    st = torch.cuda.current_stream()
+
+    def time_eager(fn, n):
+        for _ in range(2):
+            fn()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(st)
+        for _ in range(n):
+            fn()
+        e1.record(st)
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / n
+
+    ms_prefill_sage = None
+    for blk in blocks:
+        blk.sage_prefill = True
+    ms_prefill_sage = time_eager(prefill, 3)
+    for blk in blocks:
+        blk.sage_prefill = False
+    ms_prefill = time_eager(prefill, 3)             # leaves the reference-path prefix K/V in the cache
+
+    static_lat = lat.clone()
+    _lib.launch_count = 0
+    for _ in range(max(args.warmup, 3)):
+        decode(static_lat)
+    torch.cuda.synchronize()
+    launches = _lib.launch_count // max(args.warmup, 3)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        static_out = decode(static_lat)
+    for _ in range(2):
+        graph.replay()
+    torch.cuda.synchronize()
+    if world > 1:
+        torch.distributed.barrier()
+    sampler = ClockSampler(torch.cuda.current_device()) if rank == 0 else None
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    e0.record(st)
+    for _ in range(args.steps):
+        graph.replay()
+    e1.record(st)
+    torch.cuda.synchronize()
+    clocks = sampler.stop() if sampler else None
+    ms = e0.elapsed_time(e1) / args.steps
+    host_lat = lat.cpu().pin_memory()
+    host_out = torch.empty(static_out.shape, dtype=static_out.dtype).pin_memory()
+    torch.cuda.synchronize()
+    e0.record(st)
+    for _ in range(args.steps):
+        static_lat.copy_(host_lat, non_blocking=True)
+        graph.replay()
+        host_out.copy_(static_out, non_blocking=True)
+    e1.record(st)
+    torch.cuda.synchronize()
+    ms_e2e = e0.elapsed_time(e1) / args.steps
+    if world > 1:
+        t = torch.tensor([ms, ms_e2e], device=device)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        ms, ms_e2e = t.tolist()
+    assert _lib.device_error() == 0, "a device-side wait timed out"
+    _, bf16_tf, peak_kind = load_peaks()
+    T, F_ = Q21_TARGET, 3 * D
+    tflop = Q21_LAYERS * (2.0 * T * (4 * D * D + 3 * D * F_) + 4.0 * T * S * D) / 1e12
+    if rank == 0:
+        achieved = tflop / (ms * 1e-3)
+        line = {"metric": "ms per Qwen-Image 2.1 cached-decode denoiser step (32 blocks, 1024^2: 4096 target "
+                          "tokens, 113-token prefix KV)", "value": round(ms, 3), "unit": "ms/step", "n_gpus": world,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": False,
+                "scaling": "weak", "vs_baseline": None, "dtype": "mxfp8+int8/fp8 attn",
+                "data": "synthetic (random-init weights ~N(0,0.02), seeded latents/embeddings, random RoPE phases)",
+                "config": {"workload": "q21: Qwen-Image 2.1 denoiser decode step, profile mxfp8_sage (img_in, "
+                                       "modulation, 32 blocks, norm_out, proj_out; timestep embedder and text "
+                                       "projection not in the step)", "global_batch": 1, "seq_len": T,
+                           "prefix_len": P, "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
+                           "cuda_graph": True, "l2": "weights (7 GB MXFP8) >> L2; no flush"},
+                "compare": {"prefill_step_ms_segment_sdpa": round(ms_prefill, 2),
+                            "prefill_step_ms_sage_block_causal": round(ms_prefill_sage, 2),
+                            "reference_rtx5090_mxfp8_sage_decode_ms": 147.3,
+                            "reference_rtx5090_mxfp8_sage_prefill_ms": 186.5},
+                "e2e": {"value": round(ms_e2e, 3), "unit": "ms/step", "h2d_bytes_per_step": host_lat.numel() * 2,
+                        "d2h_bytes_per_step": host_out.numel() * 2},
+                "gpu_launches": launches * args.steps,
+                "roofline": {"bound": "tensor", "kernel": f"whole decode step ({tflop:.1f} TFLOP)",
+                             "achieved": round(achieved, 1), "peak": round(2 * bf16_tf, 1), "unit": "TFLOP/s",
+                             "frac": round(achieved / (2 * bf16_tf), 3), "traffic": None,
+                             "peak_kind": f"2x {peak_kind} cuBLAS bf16 burst"},
+                "cpu_baseline": None, "clocks": clocks}
+        print(json.dumps(line), flush=True)
+    del graph
 
 
 def profile_case(name: str):
@@ -654,9 +778,9 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--config", default="c4", choices=["c4", "c5", "prefill"],
+    ap.add_argument("--config", default="c4", choices=["c4", "c5", "prefill", "q21"],
                     help="c4: 1024^2 step (replicas for N>1); c5: 2048^2 step, CFG split x Ulysses for N>1; "
-                         "prefill: the 2.1 block-causal prefill attention")
+                         "prefill: the 2.1 block-causal prefill attention; q21: the 2.1 cached-decode step")
     ap.add_argument("--profile-case", choices=["ffn_up", "attn", "step8", "quant", "prefill"],
                     help="run one small fixed case for an ncu capture and exit")
     args = ap.parse_args()
@@ -678,6 +802,8 @@ def main():
             c5_arm(args, rank, world, local_rank)
         elif args.config == "prefill":
             prefill_arm(args, rank, world, local_rank)
+        elif args.config == "q21":
+            q21_arm(args, rank, world, local_rank)
         else:
             our_arm(args, rank, world, local_rank)
     finally:

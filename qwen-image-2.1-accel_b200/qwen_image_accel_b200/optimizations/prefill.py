@@ -25,6 +25,7 @@ keys each query sees is unchanged, so the result is the masked attention.
 from __future__ import annotations
 
 import torch
+import torch.nn.functional as F
 
 from .sage_attention import sage_attention_prefill
 
@@ -63,6 +64,46 @@ def compact_valid_keys(k: torch.Tensor, v: torch.Tensor, key_valid: torch.Tensor
     counted = torch.where(lim > 0, torch.gather(seen, 1, (lim - 1).clamp(min=0).expand(b, -1)),
                           torch.zeros_like(seen[:, :1]).expand(b, lim.shape[-1]))
     return k_c, v_c, counted.to(torch.int32).contiguous()
+
+
+def prefix_segments(image_ids: torch.Tensor, prefix_len: int) -> list[tuple[int, int, bool]]:
+    """(start, end, is_text) runs of equal image ids over the prefix, as the
+    reference derives them once per forward (one host sync;
+    _qwenimage21_prefix_segments, transformer_qwenimage21.py:309-323)."""
+    ids = image_ids[:prefix_len].tolist()
+    segs, start = [], 0
+    for i in range(1, prefix_len + 1):
+        if i == prefix_len or ids[i] != ids[start]:
+            segs.append((start, i, ids[start] < 0))
+            start = i
+    return segs
+
+
+def segment_prefill_sdpa(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, image_ids: torch.Tensor,
+                         prefix_len: int, key_valid: torch.Tensor | None = None,
+                         segments: list | None = None) -> torch.Tensor:
+    """The reference's default prefill attention, restated over torch SDPA
+    (QwenImage21AttnProcessor, transformer_qwenimage21.py:499-543): each
+    prefix segment's queries attend to keys [0, end) (text segments with
+    their causal triangle), the target's queries to every key; padded keys
+    (key_valid False) are dropped. NHD bf16 in and out. This is the bf16
+    library path the reference runs; prefill_attention is the tcgen05 one."""
+    segs = prefix_segments(image_ids, prefix_len) if segments is None else segments
+    qt, kt, vt = (t.transpose(1, 2) for t in (q, k, v))
+    outs = []
+    for a, b, is_text in segs:
+        mask = None
+        if is_text:
+            n = b - a
+            mask = torch.cat([torch.ones(n, a, dtype=torch.bool, device=q.device),
+                              torch.tril(torch.ones(n, n, dtype=torch.bool, device=q.device))], dim=1)[None, None]
+        if key_valid is not None:
+            kvm = key_valid[:, None, None, :b]
+            mask = kvm if mask is None else (mask & kvm)
+        outs.append(F.scaled_dot_product_attention(qt[:, :, a:b], kt[:, :, :b], vt[:, :, :b], attn_mask=mask))
+    mask = None if key_valid is None else key_valid[:, None, None, :]
+    outs.append(F.scaled_dot_product_attention(qt[:, :, prefix_len:], kt, vt, attn_mask=mask))
+    return torch.cat(outs, dim=2).transpose(1, 2)
 
 
 def prefill_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, image_ids: torch.Tensor,

@@ -1,0 +1,262 @@
+"""Qwen-Image 2.1 single-stream block on the sm_100a kernels, with its prefix KV cache.
+
+Mirrors QwenImage21TransformerBlock (WHL:diffusers/models/transformers/
+transformer_qwenimage21.py:584-650) in its two modes:
+
+* prefill (`kv_cache_mode="extract"`): the whole joint sequence (text,
+  condition images, target image) under the block-causal mask, storing the
+  prefix's post-RoPE K/V in a KVLayerCache (:343-353). Prefix tokens take the
+  modulation row of t = 0 (the trailing row), target tokens their sample's row
+  (_select_modulation_rows, :238-254).
+* cached decode (`kv_cache_mode="cached"`): only the target tokens, attending
+  to [cached prefix, target] without a mask; this is the reference's fused
+  decode block (src/qwen_image_accel/optimizations/fusion.py:38-60 for the
+  bf16 profiles, quantized_decode.py:108-137 for the MXFP8 ones): LN x (1+s)
+  (MXFP8 straight out of the LN when the projections are MXFP8), Q/K/V
+  projections sharing one quantized activation, fused QK-RMSNorm + RoPE +
+  prefix pack, Sage attention when the profile has it and nothing is masked,
+  gated residual, SwiGLU MLP whose gate/value projections share one
+  activation, SwiGLU fused with the MXFP8 quantization of the out projection's
+  operand.
+
+As in the reference (quantize_transformer swaps the linears, the MLP forward
+is replaced for both modes), the prefill uses the same MXFP8 linears and MLP;
+its attention is the reference's per-segment SDPA by default, or, with
+`sage_prefill=True`, the tcgen05 Sage kernel with per-query key limits
+(qia_sage_attention_prefill).
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+from typing import Callable
+
+import torch
+import torch.nn as nn
+import torch.nn.functional as F
+
+from . import _lib
+from .kernels.attention import prepare_attention_inputs
+from .kernels.bf16 import swiglu
+from .kernels.elementwise import residual
+from .kernels.epilogue import layer_norm_scale_quantize, swiglu_quantize
+from .kernels.layernorm import layer_norm_scale
+from .kernels.mxfp8 import quantize
+from .optimizations.mxfp8 import MXFP8Linear
+from .optimizations.prefill import prefill_attention, segment_prefill_sdpa
+from .optimizations.sage_attention import sage_attention
+from .profiles import get_profile
+
+
+@dataclass(frozen=True)
+class Block21Config:
+    dim: int = 4096
+    heads: int = 32
+    head_dim: int = 128
+    mlp_ratio: int = 3
+    eps: float = 1e-6
+
+
+def block21_parameter_shapes(cfg: Block21Config) -> dict[str, tuple]:
+    """Diffusers state-dict names and shapes of QwenImage21TransformerBlock
+    (transformer_qwenimage21.py:584-606; no biases anywhere in 2.1)."""
+    d, f, hd = cfg.dim, cfg.dim * cfg.mlp_ratio, cfg.head_dim
+    return {
+        "attn.to_q.weight": (d, d), "attn.to_k.weight": (d, d), "attn.to_v.weight": (d, d),
+        "attn.to_out.0.weight": (d, d), "attn.norm_q.weight": (hd,), "attn.norm_k.weight": (hd,),
+        "img_mlp.gate_layer.weight": (f, d), "img_mlp.proj.weight": (f, d), "img_mlp.out.weight": (d, f),
+    }
+
+
+class KVLayerCache:
+    """Post-RoPE K and V of the prefix tokens of one block, NHD bf16
+    [B, prefix, H, 128] (QwenImage21KVLayerCache, transformer_qwenimage21.py:56-74)."""
+
+    def __init__(self):
+        self.k: torch.Tensor | None = None
+        self.v: torch.Tensor | None = None
+
+    def store(self, k: torch.Tensor, v: torch.Tensor):
+        self.k, self.v = k, v
+
+    def get(self) -> tuple[torch.Tensor, torch.Tensor]:
+        if self.k is None:
+            raise RuntimeError("KV cache has not been populated yet.")
+        return self.k, self.v
+
+
+class KVCache:
+    """One KVLayerCache per block (QwenImage21KVCache, :77-84)."""
+
+    def __init__(self, num_layers: int):
+        self.layer_caches = [KVLayerCache() for _ in range(num_layers)]
+
+    def get_layer(self, layer_idx: int) -> KVLayerCache:
+        return self.layer_caches[layer_idx]
+
+
+def modulation_values(modulation: torch.Tensor):
+    """The cached decode's per-step vectors from the shared modulation
+    [B + 1, 4D] (rows [0, B): the sampled timestep; the trailing row: t = 0,
+    which belongs to the cached prefix): (1 + s1, tanh g1, 1 + s2, tanh g2),
+    each (B, 1, D) bf16 -- as the reference caches them per modulation tensor
+    (fusion.py:45-49)."""
+    s1, g1, s2, g2 = modulation[:-1].chunk(4, dim=-1)
+    return tuple(t.contiguous() for t in (1 + s1[:, None], g1[:, None].tanh(), 1 + s2[:, None], g2[:, None].tanh()))
+
+
+class _Norm:
+    """The attribute bundle the fused ops read from a norm module (weight, eps,
+    normalized_shape, elementwise_affine)."""
+
+    def __init__(self, weight, eps, shape=None):
+        self.weight = weight
+        self.bias = None
+        self.eps = eps
+        self.normalized_shape = shape if shape is not None else tuple(weight.shape)
+        self.elementwise_affine = False
+
+
+class Block21:
+    """One 2.1 block (params: a name -> tensor mapping or callable with the
+    Diffusers names of block21_parameter_shapes)."""
+
+    def __init__(self, params: Callable[[str], torch.Tensor] | dict, cfg: Block21Config = Block21Config(),
+                 device="cuda", profile: str = "mxfp8_sage", sage_prefill: bool = False):
+        prof = get_profile(profile)
+        if not prof.fused:
+            raise ValueError(f"profile {profile!r} has no fused decode path")
+        get = params if callable(params) else params.__getitem__
+        self.cfg = cfg
+        self.quantized, self.sage, self.sage_prefill = prof.quantized, prof.sage, sage_prefill
+        dev = torch.device(device)
+
+        def linear(name):
+            w = get(name).to(dev, torch.bfloat16).contiguous()
+            lin = nn.Linear(w.shape[1], w.shape[0], bias=False, device=dev, dtype=torch.bfloat16)
+            with torch.no_grad():
+                lin.weight.copy_(w)
+            return MXFP8Linear(lin) if self.quantized else lin
+
+        self.to_q, self.to_k, self.to_v = (linear(f"attn.to_{n}.weight") for n in "qkv")
+        self.to_out = linear("attn.to_out.0.weight")
+        self.gate_layer, self.proj, self.out = (linear(f"img_mlp.{n}.weight") for n in ("gate_layer", "proj", "out"))
+        self.norm_q = _Norm(get("attn.norm_q.weight").to(dev, torch.bfloat16).contiguous(), cfg.eps)
+        self.norm_k = _Norm(get("attn.norm_k.weight").to(dev, torch.bfloat16).contiguous(), cfg.eps)
+        self.norm = _Norm(None, cfg.eps, (cfg.dim,))          # img_norm1 / img_norm2: no affine
+
+    # ------------------------------------------------------------------ helpers
+    def _normalized(self, h, scale):
+        """LN(h) x scale, as MXFP8 straight out of the LN when the consumers
+        are MXFP8 linears (quantized_decode.py:99-105)."""
+        if not self.quantized:
+            return layer_norm_scale(h, scale, self.norm)
+        x = layer_norm_scale_quantize(h, scale, self.norm)
+        if x is None:
+            raise NotImplementedError(f"LN + MXFP8: unsupported input {tuple(h.shape)}")
+        return x
+
+    def _project(self, x, lead):
+        """Q, K, V [*lead, H, 128] from the LN output (bf16 tensor or MXFP8
+        Quantized shared by the three projections)."""
+        h, hd = self.cfg.heads, self.cfg.head_dim
+        if self.quantized:
+            a = x if not isinstance(x, torch.Tensor) else quantize(x.reshape(-1, x.shape[-1]))
+            return tuple(p.matmul(a).view(*lead, h, hd) for p in (self.to_q, self.to_k, self.to_v))
+        return tuple(F.linear(x, p.weight).unflatten(-1, (h, hd)) for p in (self.to_q, self.to_k, self.to_v))
+
+    def _out_proj(self, attn):
+        flat = attn.flatten(2, 3)
+        if self.quantized:
+            return self.to_out(flat.contiguous())
+        return F.linear(flat, self.to_out.weight)
+
+    def _mlp(self, x, lead):
+        """SwiGLU MLP; x is the LN output (bf16) or its MXFP8 quantization."""
+        if self.quantized:
+            a = x if not isinstance(x, torch.Tensor) else quantize(x.reshape(-1, x.shape[-1]))
+            gate, value = self.gate_layer.matmul(a), self.proj.matmul(a)
+            act = swiglu_quantize(gate, value)
+            return self.out.matmul(act).view(*lead, -1)
+        return F.linear(swiglu(F.linear(x, self.gate_layer.weight), F.linear(x, self.proj.weight)),
+                        self.out.weight)
+
+    def _rows(self, name, x, vectors, prefix_len, other=None):
+        """LN x (1+s) (name "ln") or the gated residual (name "res") with the
+        prefix rows of every sample using vector row B (t = 0) and the target
+        rows vector row b: one launch per row range, into one output."""
+        b, s, d = x.shape
+        out = torch.empty_like(x)
+        xf, of = x.view(-1, d), out.view(-1, d)
+        yf = other.view(-1, d) if other is not None else None
+        st = _lib.stream(x.device)
+        for bi in range(b):
+            for r0, r1, vec in ((0, prefix_len, b), (prefix_len, s, bi)):
+                n = r1 - r0
+                if n <= 0:
+                    continue
+                lo = bi * s + r0
+                v = vectors[vec:vec + 1]
+                if name == "ln":
+                    _lib.call("qia_ln_mod", _lib.ptr(xf[lo:lo + n]), _lib.ptr(v), None, _lib.ptr(of[lo:lo + n]), n, d,
+                              n, float(self.cfg.eps), st)
+                else:
+                    _lib.call("qia_gated_residual", _lib.ptr(xf[lo:lo + n]), _lib.ptr(yf[lo:lo + n]), _lib.ptr(v),
+                              _lib.ptr(of[lo:lo + n]), n, d, n, st)
+        return out
+
+    # ------------------------------------------------------------------ modes
+    def forward_cached(self, h: torch.Tensor, values, freqs: torch.Tensor, layer_cache: KVLayerCache,
+                       key_valid: torch.Tensor | None = None) -> torch.Tensor:
+        """Cached decode of the target tokens h [B, St, D]; values =
+        modulation_values(modulation); freqs complex64 [St, 64] (the target's
+        rows of the RoPE table); key_valid bool [B, prefix + St] or None."""
+        s1, g1, s2, g2 = values
+        b, st, _ = h.shape
+        h = h.contiguous()
+        x = self._normalized(h, s1)
+        q, k, v = self._project(x, (b, st))
+        cached_k, cached_v = layer_cache.get()
+        prepared = prepare_attention_inputs(q.contiguous(), k.contiguous(), v.contiguous(), self.norm_q, self.norm_k,
+                                            freqs.contiguous(), cached_k, cached_v)
+        if prepared is None:
+            raise NotImplementedError("cached decode: unsupported Q/K/V or cache layout")
+        q, k, v = prepared
+        if self.sage and key_valid is None:
+            attn = sage_attention(q, k, v)
+        else:
+            mask = None if key_valid is None else key_valid[:, None, None, :]
+            attn = F.scaled_dot_product_attention(q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2),
+                                                  attn_mask=mask).transpose(1, 2)
+        h = residual(h, self._out_proj(attn).contiguous(), g1)
+        x = self._normalized(h, s2)
+        return residual(h, self._mlp(x, (b, st)).contiguous(), g2)
+
+    def forward_prefill(self, h: torch.Tensor, modulation: torch.Tensor, freqs: torch.Tensor,
+                        image_ids: torch.Tensor, prefix_len: int, layer_cache: KVLayerCache | None = None,
+                        key_valid: torch.Tensor | None = None) -> torch.Tensor:
+        """Prefill of the joint sequence h [B, S, D] (target image = the last
+        S - prefix_len tokens); modulation [B + 1, 4D]; freqs complex64
+        [S, 64]; image_ids int [S] (-1 at text tokens). Stores the prefix's
+        post-RoPE K/V in layer_cache when given (kv_cache_mode="extract")."""
+        b, s, _ = h.shape
+        h = h.contiguous()
+        s1, g1, s2, g2 = modulation.chunk(4, dim=-1)
+        one_s1, tanh_g1, one_s2, tanh_g2 = ((1 + s1).contiguous(), g1.tanh().contiguous(),
+                                            (1 + s2).contiguous(), g2.tanh().contiguous())
+        x = self._rows("ln", h, one_s1, prefix_len)
+        q, k, v = self._project(x, (b, s))
+        empty = torch.empty((b, 0) + tuple(q.shape[2:]), device=q.device, dtype=q.dtype)
+        prepared = prepare_attention_inputs(q.contiguous(), k.contiguous(), v.contiguous(), self.norm_q, self.norm_k,
+                                            freqs.contiguous(), empty, empty)
+        if prepared is None:
+            raise NotImplementedError("prefill: unsupported Q/K/V layout")
+        q, k, v = prepared
+        if layer_cache is not None:
+            layer_cache.store(k[:, :prefix_len].clone(), v[:, :prefix_len].clone())
+        if self.sage_prefill:
+            attn = prefill_attention(q, k, v, image_ids, key_valid=key_valid)
+        else:
+            attn = segment_prefill_sdpa(q, k, v, image_ids, prefix_len, key_valid=key_valid)
+        h = self._rows("res", h, tanh_g1, prefix_len, other=self._out_proj(attn).contiguous())
+        x = self._rows("ln", h, one_s2, prefix_len)
+        return self._rows("res", h, tanh_g2, prefix_len, other=self._mlp(x, (b, s)).contiguous())

@@ -20,6 +20,9 @@ modified). Sources of truth, per fixture:
 * block_causal.npz -- the Qwen-Image 2.1 prefill mask (token metadata,
   prefix segments and the flex mask_mod evaluated densely, with a key-padding
   mask) from WHL:diffusers/models/transformers/transformer_qwenimage21.py.
+* block21_tiny.npz -- one Qwen-Image 2.1 single-stream block (Diffusers
+  QwenImage21TransformerBlock, tiny dims, seeded weights): prefill with the
+  prefix K/V extracted, then a cached decode of new target tokens.
 * mmdit_tiny.npz -- the Diffusers QwenImageTransformer2DModel (v1 dual-stream
   MMDiT, WHL:diffusers/models/transformers/transformer_qwenimage.py) at a tiny
   size (2 blocks, 4x128 heads, text dim 512) in bf16 on the CPU, weights from
@@ -225,6 +228,55 @@ def make_block_causal(reference: Path):
     np.savez_compressed(OUT / "block_causal.npz", **cases)
 
 
+BLOCK21_RUNS = [("t", 20), ("i", 48), ("t", 6), ("i", 64)]      # text, condition image, text, target
+BLOCK21_SHAPES = [(1, 6, 8), (1, 8, 8)]
+
+
+def make_block21(reference: Path):
+    """One Diffusers QwenImage21TransformerBlock (dim 512, 4 x 128 heads, SwiGLU
+    1536) in bf16 on the CPU, weights from the package's seeded recipe
+    (mmdit.init_parameter, seed 11): the prefill of a condition-image edit
+    sequence with the prefix K/V extracted into a QwenImage21KVLayerCache
+    (kv_cache_mode="extract", the default per-segment processor), then one
+    cached decode of new target tokens (kv_cache_mode="cached")."""
+    import torch
+    _import_diffusers(reference)
+    from diffusers.models.transformers import transformer_qwenimage21 as t21
+    sys.path.insert(0, str(OUT.parents[1] / "qwen-image-2.1-accel_b200"))
+    from qwen_image_accel_b200.mmdit import init_parameter
+
+    dim, heads = 512, 4
+    block = t21.QwenImage21TransformerBlock(dim, heads, 128).to(torch.bfloat16)
+    sd = block.state_dict()
+    block.load_state_dict({n: init_parameter(n, tuple(t.shape), seed=11) for n, t in sd.items()})
+    block.eval()
+    pad = torch.cat([torch.full((n,), kind == "i") for kind, n in BLOCK21_RUNS])
+    image_ids, target = t21.QwenImage21Transformer2DModel.build_token_metadata(pad, BLOCK21_SHAPES)
+    prefix_len = int((~target).sum())
+    segments = t21._qwenimage21_prefix_segments(image_ids, prefix_len)
+    rope = t21.QwenImage21Rope(theta=10000, axes_dim=[16, 56, 56])(BLOCK21_SHAPES, pad, torch.device("cpu"))
+    g = torch.Generator().manual_seed(21)
+    s = pad.shape[0]
+    h = torch.randn(1, s, dim, generator=g).to(torch.bfloat16)
+    modulation = (0.5 * torch.randn(2, 4 * dim, generator=g)).to(torch.bfloat16)   # [real row, t = 0 row]
+    h_target = torch.randn(1, s - prefix_len, dim, generator=g).to(torch.bfloat16)
+    cache = t21.QwenImage21KVLayerCache()
+    with torch.no_grad():
+        out_prefill = block(hidden_states=h, modulation=modulation, rotary_emb=rope, attention_mask=None,
+                            target_token_mask=target, layer_cache=cache, kv_cache_mode="extract",
+                            cache_write_slice=slice(0, prefix_len), segments=segments, key_valid=None)
+        cached_k, cached_v = cache.get()
+        out_cached = block(hidden_states=h_target, modulation=modulation, rotary_emb=rope[prefix_len:],
+                           attention_mask=None, target_token_mask=target[prefix_len:], layer_cache=cache,
+                           kv_cache_mode="cached", cache_write_slice=None, segments=None, key_valid=None)
+    np.savez_compressed(OUT / "block21_tiny.npz", h=_bits(h), modulation=_bits(modulation),
+                        h_target=_bits(h_target), out_prefill=_bits(out_prefill), out_cached=_bits(out_cached),
+                        cached_k=_bits(cached_k), cached_v=_bits(cached_v), image_ids=image_ids.numpy(),
+                        target=target.numpy(), rope=torch.view_as_real(rope).numpy().copy(),
+                        prefix_len=np.int64(prefix_len), dims=np.array([dim, heads]),
+                        keys=np.array(sorted(sd)))
+
+
 if __name__ == "__main__":
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default="/root/reference")
@@ -234,4 +286,5 @@ if __name__ == "__main__":
     make_eager(ref)
     make_mmdit(ref)
     make_block_causal(ref)
+    make_block21(ref)
     print("wrote", sorted(p.name for p in OUT.glob("*.npz")))
