@@ -562,25 +562,16 @@ def prefill_arm(args, rank, world, local_rank):
 Q21_LAYERS, Q21_DIM, Q21_HEADS, Q21_PREFIX, Q21_TARGET = 32, 4096, 32, 113, 4096   # Qwen-Image 2.1, 1024^2 t2i
 
 
-def q21_arm(args, rank, world, local_rank):
-    """`--config q21`: the Qwen-Image 2.1 denoiser on the sm_100a kernels
-    (qwen21.Block21, profile mxfp8_sage): 32 single-stream blocks (D 4096,
-    32 x 128 heads, SwiGLU 12288), 1024^2 text-to-image (4096 target tokens,
-    a 113-token text prefix). value = one cached-decode step, captured in a
-    CUDA graph: img_in, the shared modulation GEMV, the 32 blocks over the
-    target tokens against the prefix KV cache, norm_out and proj_out. Not in
-    the step: the timestep embedder and the text projection (prompt-sized
-    work). Beside it, the prefill step (eager, the prefix K/V extracted) with
-    the reference's per-segment SDPA and with the tcgen05 block-causal
-    kernel. One replica per GPU for N > 1."""
+def _q21_setup(device):
+    """The Qwen-Image 2.1 denoiser of `--config q21` on `device`: 32 Block21
+    (mxfp8_sage) with seeded random weights, the embedders around them, the
+    inputs, and its prefill / decode closures (see q21_arm)."""
+    import types
     import torch.nn.functional as F
-    from qwen_image_accel_b200 import _lib
     from qwen_image_accel_b200.kernels.layernorm import layer_norm_scale
     from qwen_image_accel_b200.mmdit import init_parameter
     from qwen_image_accel_b200.qwen21 import (Block21, Block21Config, KVCache, _Norm, block21_parameter_shapes,
                                               modulation_values)
-    device = torch.device("cuda", local_rank)
-    torch.cuda.set_device(device)
     cfg = Block21Config(dim=Q21_DIM, heads=Q21_HEADS)
     shapes = block21_parameter_shapes(cfg)
     blocks = [Block21(lambda n, i=i: init_parameter(f"transformer_blocks.{i}.{n}", shapes[n], 42, device), cfg,
@@ -615,6 +606,25 @@ def q21_arm(args, rank, world, local_rank):
         scale = F.linear(F.silu(temb[:1]), w["norm_out.linear.weight"])
         return F.linear(layer_norm_scale(x, (1 + scale)[:, None].contiguous(), ln), w["proj_out.weight"])
 
+    return types.SimpleNamespace(blocks=blocks, lat=lat, prefill=prefill, decode=decode, D=D, S=S, P=P)
+
+
+def q21_arm(args, rank, world, local_rank):
+    """`--config q21`: the Qwen-Image 2.1 denoiser on the sm_100a kernels
+    (qwen21.Block21, profile mxfp8_sage): 32 single-stream blocks (D 4096,
+    32 x 128 heads, SwiGLU 12288), 1024^2 text-to-image (4096 target tokens,
+    a 113-token text prefix). value = one cached-decode step, captured in a
+    CUDA graph: img_in, the shared modulation GEMV, the 32 blocks over the
+    target tokens against the prefix KV cache, norm_out and proj_out. Not in
+    the step: the timestep embedder and the text projection (prompt-sized
+    work). Beside it, the prefill step (eager, the prefix K/V extracted) with
+    the reference's per-segment SDPA and with the tcgen05 block-causal
+    kernel. One replica per GPU for N > 1."""
+    from qwen_image_accel_b200 import _lib
+    device = torch.device("cuda", local_rank)
+    torch.cuda.set_device(device)
+    m = _q21_setup(device)
+    blocks, lat, prefill, decode, D, S, P = m.blocks, m.lat, m.prefill, m.decode, m.D, m.S, m.P
     st = torch.cuda.current_stream()
 
     def time_eager(fn, n):
@@ -718,7 +728,9 @@ def profile_case(name: str):
               text + 4096 image tokens, 24 heads, from the two streams' q|k|v
               projections), twice (three launches each).
     prefill - the 2.1 block-causal prefill attention of `--config prefill`
-              (S=8325, 32 heads), three calls (four launches each)."""
+              (S=8325, 32 heads), three calls (four launches each).
+    q21step - the `--config q21` denoiser: prefill, two decode steps, then one
+              decode step inside an NVTX range named `step`."""
     device = torch.device("cuda", 0)
     torch.cuda.set_device(device)
     g = torch.Generator(device=device).manual_seed(0)
@@ -741,6 +753,15 @@ def profile_case(name: str):
         limits = block_causal_kv_limits(image_ids)
         for _ in range(3):
             sage_attention_prefill(q, k, v, limits)
+    elif name == "q21step":
+        m = _q21_setup(device)
+        m.prefill()
+        for _ in range(2):
+            m.decode(m.lat)
+        torch.cuda.synchronize()
+        torch.cuda.nvtx.range_push("step")
+        m.decode(m.lat)
+        torch.cuda.nvtx.range_pop()
     elif name == "quant":
         from qwen_image_accel_b200.mmdit import rope_tables
         from qwen_image_accel_b200.optimizations.sage_attention import sage_quantize_joint
@@ -781,7 +802,7 @@ def main():
     ap.add_argument("--config", default="c4", choices=["c4", "c5", "prefill", "q21"],
                     help="c4: 1024^2 step (replicas for N>1); c5: 2048^2 step, CFG split x Ulysses for N>1; "
                          "prefill: the 2.1 block-causal prefill attention; q21: the 2.1 cached-decode step")
-    ap.add_argument("--profile-case", choices=["ffn_up", "attn", "step8", "quant", "prefill"],
+    ap.add_argument("--profile-case", choices=["ffn_up", "attn", "step8", "quant", "prefill", "q21step"],
                     help="run one small fixed case for an ncu capture and exit")
     args = ap.parse_args()
     if args.profile_case:

@@ -351,7 +351,8 @@ int qia_sage_attention_split(const void* q, const void* k, const void* v,
  * seq_q); rows padded to 128 are not written) with E8M0 scales in the 128x4
  * blocked layout -- byte-identical to qia_mxfp8_quantize of the bf16 outputs
  * and the A operand of the output-projection GEMMs (strides: q, k, v -- 9
- * values; values 32-byte, scales 4-byte aligned).
+ * values; values 32-byte, scales 4-byte aligned). split == seq_q gives one
+ * stream: every query token goes to a_*, and b_values / b_scales may be null.
  * Replaces: the attention output -> MXFP8 quantize step of MXFusedProcessor
  * (src/qwen_image_accel/optimizations/quantized_decode.py:31-78). */
 int qia_sage_attention_split_mx(const void* q, const void* k, const void* v,

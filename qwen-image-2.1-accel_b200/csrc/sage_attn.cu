@@ -1308,11 +1308,13 @@ extern "C" int qia_sage_attention_split_mx(const void* q, const void* k, const v
   int rc = check_sizes(batch, heads, seq_q, seq_kv, head_dim, "qia_sage_attention_split_mx");
   if (rc) return rc;
   if (!strides) return set_error(QIA_ERR_INVALID, "qia_sage_attention_split_mx: null strides");
-  if (split <= 0 || split >= seq_q)
-    return set_error(QIA_ERR_INVALID, "qia_sage_attention_split_mx: 0 < split < seq_q");
-  if (!a_values || !a_scales || !b_values || !b_scales)
+  // split == seq_q: one stream (every query token goes to a_*; b_* unused)
+  if (split <= 0 || split > seq_q)
+    return set_error(QIA_ERR_INVALID, "qia_sage_attention_split_mx: 0 < split <= seq_q");
+  const bool two = split < seq_q;
+  if (!a_values || !a_scales || (two && (!b_values || !b_scales)))
     return set_error(QIA_ERR_INVALID, "qia_sage_attention_split_mx: null output");
-  if (!aligned(a_values, 32) || !aligned(b_values, 32) || !aligned(a_scales, 4) || !aligned(b_scales, 4))
+  if (!aligned(a_values, 32) || !aligned(a_scales, 4) || (two && (!aligned(b_values, 32) || !aligned(b_scales, 4))))
     return set_error(QIA_ERR_ALIGNMENT, "qia_sage_attention_split_mx: values 32-byte, scales 4-byte aligned");
   const Strides sq{strides[0], strides[1], strides[2]}, sk{strides[3], strides[4], strides[5]},
       sv{strides[6], strides[7], strides[8]};

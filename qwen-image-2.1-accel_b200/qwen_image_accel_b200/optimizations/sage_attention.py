@@ -161,6 +161,31 @@ def sage_attention_split_quantized(q: torch.Tensor, k: torch.Tensor, v: torch.Te
     return qa, qb
 
 
+def sage_attention_quantized(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, sm_scale: float | None = None,
+                             workspace: torch.Tensor | None = None):
+    """sage_attention whose output comes back as one MXFP8 activation
+    (Quantized, rows = batch * Sq, K = heads * 128) for the output projection:
+    byte-identical to quantize() of the bf16 output (qia_sage_attention_split_mx
+    with split = Sq). q may be a strided view (e.g. the target rows of a joint
+    [prefix, target] buffer)."""
+    from ..kernels.mxfp8 import empty_quantized
+    _check_settings()
+    _validate(q, k, v)
+    b, sq, h, d = q.shape
+    skv = k.shape[1]
+    need = workspace_bytes(b, h, sq, skv)
+    if workspace is None or workspace.numel() < need:
+        workspace = torch.empty(need, device=q.device, dtype=torch.uint8)
+    qa = empty_quantized(b * sq, h * d, q.device)
+    if qa.values.shape[0] > qa.rows:      # rows past the live ones (padding to 128) stay zero
+        qa.values[qa.rows:].view(torch.uint8).zero_()
+        qa.scales.view(torch.uint8).zero_()
+    _lib.call("qia_sage_attention_split_mx", _lib.ptr(q), _lib.ptr(k), _lib.ptr(v), _lib.ptr(qa.values),
+              _lib.ptr(qa.scales), None, None, sq, b, sq, skv, h, d, _strides(q, k, v), float(sm_scale or 0.0),
+              _lib.ptr(workspace), workspace.numel(), _lib.stream(q.device))
+    return qa
+
+
 def _joint_args(qkv0, qkv1, weights0, weights1, freqs0, freqs1, heads):
     """Pointer/size arguments of the joint entries (see sage_quantize_joint)."""
     _lib.require_cuda(qkv0, qkv1, *weights0, *weights1, freqs0, freqs1)

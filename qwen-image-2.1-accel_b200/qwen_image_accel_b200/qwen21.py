@@ -19,6 +19,16 @@ transformer_qwenimage21.py:584-650) in its two modes:
   activation, SwiGLU fused with the MXFP8 quantization of the out projection's
   operand.
 
+Where the reference runs three Q/K/V projections, this runs one over the
+stacked [W_q; W_k; W_v] (per-row MXFP8 weight scales, so the codes and every
+output are those of the three), normalises and rotates its rows straight into
+the joint [prefix, target] K/V buffers behind the copied cache
+(qia_qknorm_rope_segment, the same arithmetic as the pack kernel), and in the
+MXFP8 profiles takes the attention output as MXFP8 from the attention
+epilogue, the gated residuals from the output-projection GEMM epilogues, and
+the gate/value projections as one grouped launch -- each byte-identical to
+the unfused op it replaces.
+
 As in the reference (quantize_transformer swaps the linears, the MLP forward
 is replaced for both modes), the prefill uses the same MXFP8 linears and MLP;
 its attention is the reference's per-segment SDPA by default, or, with
@@ -35,15 +45,15 @@ import torch.nn as nn
 import torch.nn.functional as F
 
 from . import _lib
-from .kernels.attention import prepare_attention_inputs
+from .kernels.attention import joint_qk_norm_rope
 from .kernels.bf16 import swiglu
 from .kernels.elementwise import residual
 from .kernels.epilogue import layer_norm_scale_quantize, swiglu_quantize
 from .kernels.layernorm import layer_norm_scale
 from .kernels.mxfp8 import quantize
-from .optimizations.mxfp8 import MXFP8Linear
+from .optimizations.mxfp8 import MXFP8Linear, matmul_grouped
 from .optimizations.prefill import prefill_attention, segment_prefill_sdpa
-from .optimizations.sage_attention import sage_attention
+from .optimizations.sage_attention import sage_attention, sage_attention_quantized
 from .profiles import get_profile
 
 
@@ -130,14 +140,15 @@ class Block21:
         self.quantized, self.sage, self.sage_prefill = prof.quantized, prof.sage, sage_prefill
         dev = torch.device(device)
 
-        def linear(name):
-            w = get(name).to(dev, torch.bfloat16).contiguous()
+        def linear(name_or_weight):
+            w = get(name_or_weight) if isinstance(name_or_weight, str) else name_or_weight
+            w = w.to(dev, torch.bfloat16).contiguous()
             lin = nn.Linear(w.shape[1], w.shape[0], bias=False, device=dev, dtype=torch.bfloat16)
             with torch.no_grad():
                 lin.weight.copy_(w)
             return MXFP8Linear(lin) if self.quantized else lin
 
-        self.to_q, self.to_k, self.to_v = (linear(f"attn.to_{n}.weight") for n in "qkv")
+        self.qkv = linear(torch.cat([get(f"attn.to_{n}.weight") for n in "qkv"]))
         self.to_out = linear("attn.to_out.0.weight")
         self.gate_layer, self.proj, self.out = (linear(f"img_mlp.{n}.weight") for n in ("gate_layer", "proj", "out"))
         self.norm_q = _Norm(get("attn.norm_q.weight").to(dev, torch.bfloat16).contiguous(), cfg.eps)
@@ -155,14 +166,21 @@ class Block21:
             raise NotImplementedError(f"LN + MXFP8: unsupported input {tuple(h.shape)}")
         return x
 
-    def _project(self, x, lead):
-        """Q, K, V [*lead, H, 128] from the LN output (bf16 tensor or MXFP8
-        Quantized shared by the three projections)."""
-        h, hd = self.cfg.heads, self.cfg.head_dim
+    def _qkv_into(self, x, b, s, freqs, oq, ok, ov, offset):
+        """q|k|v projection of the LN output x (bf16 tensor, or MXFP8 Quantized
+        in the quantized profiles) for s tokens per sample, RMS-normalised and
+        rotated into rows [offset, offset + s) of the joint NHD buffers."""
         if self.quantized:
             a = x if not isinstance(x, torch.Tensor) else quantize(x.reshape(-1, x.shape[-1]))
-            return tuple(p.matmul(a).view(*lead, h, hd) for p in (self.to_q, self.to_k, self.to_v))
-        return tuple(F.linear(x, p.weight).unflatten(-1, (h, hd)) for p in (self.to_q, self.to_k, self.to_v))
+            qkv = self.qkv.matmul(a).view(b, s, -1)
+        else:
+            qkv = F.linear(x, self.qkv.weight).view(b, s, -1)
+        joint_qk_norm_rope(qkv, self.norm_q.weight, self.norm_k.weight, torch.view_as_real(freqs).contiguous(),
+                           oq, ok, ov, offset, eps=self.cfg.eps)
+
+    def _joint(self, b, total, device):
+        shape = (b, total, self.cfg.heads, self.cfg.head_dim)
+        return tuple(torch.empty(shape, device=device, dtype=torch.bfloat16) for _ in range(3))
 
     def _out_proj(self, attn):
         flat = attn.flatten(2, 3)
@@ -170,13 +188,18 @@ class Block21:
             return self.to_out(flat.contiguous())
         return F.linear(flat, self.to_out.weight)
 
+    def _swiglu_act(self, x):
+        """MXFP8 SwiGLU activation of the MLP (quantized profiles): the gate and
+        value projections of one shared activation in one grouped launch, then
+        SwiGLU + quantization in one pass."""
+        a = x if not isinstance(x, torch.Tensor) else quantize(x.reshape(-1, x.shape[-1]))
+        gate, value = matmul_grouped([(self.gate_layer, a), (self.proj, a)])
+        return swiglu_quantize(gate, value)
+
     def _mlp(self, x, lead):
         """SwiGLU MLP; x is the LN output (bf16) or its MXFP8 quantization."""
         if self.quantized:
-            a = x if not isinstance(x, torch.Tensor) else quantize(x.reshape(-1, x.shape[-1]))
-            gate, value = self.gate_layer.matmul(a), self.proj.matmul(a)
-            act = swiglu_quantize(gate, value)
-            return self.out.matmul(act).view(*lead, -1)
+            return self.out.matmul(self._swiglu_act(x)).view(*lead, -1)
         return F.linear(swiglu(F.linear(x, self.gate_layer.weight), F.linear(x, self.proj.weight)),
                         self.out.weight)
 
@@ -213,22 +236,28 @@ class Block21:
         s1, g1, s2, g2 = values
         b, st, _ = h.shape
         h = h.contiguous()
-        x = self._normalized(h, s1)
-        q, k, v = self._project(x, (b, st))
         cached_k, cached_v = layer_cache.get()
-        prepared = prepare_attention_inputs(q.contiguous(), k.contiguous(), v.contiguous(), self.norm_q, self.norm_k,
-                                            freqs.contiguous(), cached_k, cached_v)
-        if prepared is None:
-            raise NotImplementedError("cached decode: unsupported Q/K/V or cache layout")
-        q, k, v = prepared
-        if self.sage and key_valid is None:
-            attn = sage_attention(q, k, v)
+        p = cached_k.shape[1]
+        if cached_k.shape[0] != b or cached_v.shape != cached_k.shape:
+            raise ValueError("cached decode: the cache does not match the batch")
+        oq, ok, ov = self._joint(b, p + st, h.device)
+        ok[:, :p].copy_(cached_k)
+        ov[:, :p].copy_(cached_v)
+        self._qkv_into(self._normalized(h, s1), b, st, freqs, oq, ok, ov, p)
+        q = oq[:, p:]
+        if self.sage and key_valid is None and self.quantized:
+            h = self.to_out.matmul_gate_residual(sage_attention_quantized(q, ok, ov), g1, h)
         else:
-            mask = None if key_valid is None else key_valid[:, None, None, :]
-            attn = F.scaled_dot_product_attention(q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2),
-                                                  attn_mask=mask).transpose(1, 2)
-        h = residual(h, self._out_proj(attn).contiguous(), g1)
+            if self.sage and key_valid is None:
+                attn = sage_attention(q, ok, ov)
+            else:
+                mask = None if key_valid is None else key_valid[:, None, None, :]
+                attn = F.scaled_dot_product_attention(q.transpose(1, 2), ok.transpose(1, 2), ov.transpose(1, 2),
+                                                      attn_mask=mask).transpose(1, 2)
+            h = residual(h, self._out_proj(attn).contiguous(), g1)
         x = self._normalized(h, s2)
+        if self.quantized:
+            return self.out.matmul_gate_residual(self._swiglu_act(x), g2, h)
         return residual(h, self._mlp(x, (b, st)).contiguous(), g2)
 
     def forward_prefill(self, h: torch.Tensor, modulation: torch.Tensor, freqs: torch.Tensor,
@@ -244,13 +273,8 @@ class Block21:
         one_s1, tanh_g1, one_s2, tanh_g2 = ((1 + s1).contiguous(), g1.tanh().contiguous(),
                                             (1 + s2).contiguous(), g2.tanh().contiguous())
         x = self._rows("ln", h, one_s1, prefix_len)
-        q, k, v = self._project(x, (b, s))
-        empty = torch.empty((b, 0) + tuple(q.shape[2:]), device=q.device, dtype=q.dtype)
-        prepared = prepare_attention_inputs(q.contiguous(), k.contiguous(), v.contiguous(), self.norm_q, self.norm_k,
-                                            freqs.contiguous(), empty, empty)
-        if prepared is None:
-            raise NotImplementedError("prefill: unsupported Q/K/V layout")
-        q, k, v = prepared
+        q, k, v = self._joint(b, s, h.device)
+        self._qkv_into(x, b, s, freqs, q, k, v, 0)
         if layer_cache is not None:
             layer_cache.store(k[:, :prefix_len].clone(), v[:, :prefix_len].clone())
         if self.sage_prefill:

@@ -103,3 +103,49 @@ def test_bf16_decode_on_golden_cache_is_tight():
     out = blk.forward_cached(ht, modulation_values(mod), freqs[p:], cache).float().cpu()
     ref = t_bf16(g["out_cached"]).float()
     assert psnr(out, ref) >= 45.0 and cosine(out, ref) >= 0.99999
+
+
+def test_fused_decode_equals_reference_op_composition():
+    """MXFP8 + Sage decode: the fused block (stacked Q|K|V GEMM, segment
+    norm/RoPE into the joint buffers, MXFP8 attention output, gate-residual
+    epilogues, grouped gate/value GEMMs) is byte-identical to the reference's
+    op sequence on the same kernels (quantized_decode.py:31-137: three
+    projections of one activation, prepare_attention_inputs, sage_decode,
+    to_out, residual, _mx_mlp_forward, residual)."""
+    import torch.nn as nn
+    from qwen_image_accel_b200.kernels.attention import prepare_attention_inputs
+    from qwen_image_accel_b200.kernels.elementwise import residual
+    from qwen_image_accel_b200.kernels.epilogue import layer_norm_scale_quantize, swiglu_quantize
+    from qwen_image_accel_b200.mmdit import init_parameter
+    from qwen_image_accel_b200.optimizations.mxfp8 import MXFP8Linear
+    from qwen_image_accel_b200.optimizations.sage_attention import sage_attention
+    from qwen_image_accel_b200.qwen21 import KVLayerCache, block21_parameter_shapes, Block21Config, modulation_values
+    blk, g = build("mxfp8_sage")
+    dim, heads = g["dims"].tolist()
+    shapes = block21_parameter_shapes(Block21Config(dim=dim, heads=heads))
+
+    def mx(name):
+        w = init_parameter(name, shapes[name], seed=11).cuda()
+        lin = nn.Linear(w.shape[1], w.shape[0], bias=False, device="cuda", dtype=torch.bfloat16)
+        with torch.no_grad():
+            lin.weight.copy_(w)
+        return MXFP8Linear(lin)
+
+    to_q, to_k, to_v = (mx(f"attn.to_{n}.weight") for n in "qkv")
+    mod, ht = t_bf16(g["modulation"]).cuda(), t_bf16(g["h_target"]).cuda()
+    freqs = torch.view_as_complex(torch.from_numpy(g["rope"]).contiguous()).cuda()
+    p = int(g["prefix_len"])
+    ck, cv = t_bf16(g["cached_k"]).cuda(), t_bf16(g["cached_v"]).cuda()
+    s1, g1, s2, g2 = vals = modulation_values(mod)
+    b, st, d = ht.shape
+    a = layer_norm_scale_quantize(ht, s1, blk.norm)
+    q, k, v = (lin.matmul(a).view(b, st, heads, 128) for lin in (to_q, to_k, to_v))
+    q, k, v = prepare_attention_inputs(q, k, v, blk.norm_q, blk.norm_k, freqs[p:].contiguous(), ck, cv)
+    h1 = residual(ht, blk.to_out(sage_attention(q, k, v).flatten(2, 3).contiguous()), g1)
+    a2 = layer_norm_scale_quantize(h1, s2, blk.norm)
+    act = swiglu_quantize(blk.gate_layer.matmul(a2), blk.proj.matmul(a2))
+    want = residual(h1, blk.out.matmul(act).view(b, st, d), g2)
+    cache = KVLayerCache()
+    cache.store(ck, cv)
+    got = blk.forward_cached(ht, vals, freqs[p:].contiguous(), cache)
+    assert torch.equal(got, want)
