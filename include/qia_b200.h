@@ -239,6 +239,21 @@ int qia_mxfp8_gemm_gelu_quant(const void* a_values, const void* a_scales,
                               const void* bias, void* q_values, void* q_scales,
                               int64_t m, int64_t n, int64_t k, void* stream);
 
+/* The SwiGLU MLP's gate and value projections and the SwiGLU itself, one GEMM:
+ * B stacks the two weights interleaved every 32 rows (rows [64 j, 64 j + 32)
+ * = gate rows [32 j, 32 j + 32), the next 32 = value rows [32 j, 32 j + 32);
+ * n = 2 * the MLP width, a multiple of 256). The epilogue rounds each gate and
+ * value sum to bf16, forms bf16(silu(g) * v) with silu = bf16(g / (1 +
+ * exp(-g))), and writes it as MXFP8 q_values [ceil(m/128)*128, n/2] + blocked
+ * E8M0 q_scales (padding rows zero): byte-identical to qia_mxfp8_gemm of the
+ * two projections followed by qia_swiglu_quant, without their bf16 outputs.
+ * Replaces: _mx_mlp_forward's gate_layer.matmul + proj.matmul + swiglu_quantize
+ * (src/qwen_image_accel/optimizations/quantized_decode.py:81-96). */
+int qia_mxfp8_gemm_swiglu_quant(const void* a_values, const void* a_scales,
+                                const void* b_values, const void* b_scales,
+                                void* q_values, void* q_scales, int64_t m,
+                                int64_t n, int64_t k, void* stream);
+
 /* Gated residual epilogue: out = bf16(resid + bf16(gate[b] * bf16(A . B^T + bias)))
  * with b = row / rows_per_batch; gate: [m / rows_per_batch, n]; resid and out
  * share the row stride ldo and may be the same buffer (in-place update). */

@@ -20,7 +20,6 @@
 namespace qia {
 namespace {
 
-__device__ __forceinline__ float silu_ref(float g) { return round_bf16(__fdiv_rn(g, 1.0f + expf(-g))); }
 
 
 // Quantize 8 values (one quarter of an MX block) held by this lane; the 4 lanes

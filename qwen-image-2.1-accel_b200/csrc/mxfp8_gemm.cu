@@ -43,7 +43,7 @@
 namespace qia {
 namespace {
 
-enum Epi { kEpiBf16 = 0, kEpiGeluQuant = 1, kEpiGateResidual = 2, kEpiGeluBf16 = 3 };
+enum Epi { kEpiBf16 = 0, kEpiGeluQuant = 1, kEpiGateResidual = 2, kEpiGeluBf16 = 3, kEpiSwigluQuant = 4 };
 
 struct EpiParams {
   __nv_bfloat16* out;          // [M, ldo] bf16 (kEpiBf16 / kEpiGeluBf16 / kEpiGateResidual)
@@ -52,8 +52,8 @@ struct EpiParams {
   const __nv_bfloat16* gate;   // [M / rows_per_batch, N] (kEpiGateResidual)
   const __nv_bfloat16* resid;  // [M, ldo] (kEpiGateResidual; may alias out)
   int64_t rows_per_batch;
-  uint8_t* q_values;           // [Mpad, N] e4m3 (kEpiGeluQuant)
-  uint8_t* q_scales;           // blocked E8M0 (kEpiGeluQuant)
+  uint8_t* q_values;           // [Mpad, N] e4m3 (kEpiGeluQuant); [Mpad, N/2] (kEpiSwigluQuant)
+  uint8_t* q_scales;           // blocked E8M0 (kEpiGeluQuant, kEpiSwigluQuant)
   int wide;                    // out/resid/q_values rows allow 32-byte accesses
 };
 
@@ -183,6 +183,8 @@ __device__ __forceinline__ void epilogue_chunk(float (&v)[32], const EpiParams& 
         for (int q = 0; q < 4; ++q) op[q] = ov[q];
       }
     }
+  } else if (EPI == kEpiSwigluQuant) {
+    // handled per chunk pair (epilogue_swiglu_pair)
   } else {  // kEpiGeluQuant: the 32 columns are exactly one MX block of the next GEMM's K
     // bf16 round -> GELU -> bf16 round -> |max|, on lane pairs (f32x2)
     float amax = 0.0f;
@@ -217,6 +219,46 @@ __device__ __forceinline__ void epilogue_chunk(float (&v)[32], const EpiParams& 
     }
     ep.q_scales[mx_scale_offset(row, col >> 5, N >> 7)] = uint8_t(e);
   }
+}
+
+// SwiGLU epilogue of one chunk pair: the B operand stacks the gate and value
+// projections interleaved every 32 rows, so output columns [64 j, 64 j + 32)
+// are gate columns [32 j, 32 j + 32) and the next 32 the matching value
+// columns. Both are rounded to bf16 (the GEMMs' bf16 outputs), combined as
+// bf16(silu(g) * v) and quantized as one MX block of column block j of the
+// [Mpad, N/2] activation -- the arithmetic of a bf16 GEMM pair followed by
+// the SwiGLU + MXFP8 quantizer.
+__device__ __forceinline__ void epilogue_swiglu_pair(const float (&vg)[32], const float (&vv)[32],
+                                                     const EpiParams& ep, int64_t row, int out_col, bool live,
+                                                     int n_out) {
+  float y[32];
+  float amax = 0.0f;
+#pragma unroll
+  for (int i = 0; i < 32; ++i) {
+    const float g = round_bf16(vg[i]), v = round_bf16(vv[i]);
+    y[i] = live ? round_bf16(__fmul_rn(silu_ref(g), v)) : 0.0f;
+    amax = fmaxf(amax, fabsf(y[i]));
+  }
+  const int e = mx_exponent(amax);
+  const float inv = mx_inverse_scale(e);
+  const uint64_t inv2 = f2_pack(inv, inv);
+  uint32_t w[8];
+#pragma unroll
+  for (int q = 0; q < 8; ++q) {
+    float y0, y1, y2, y3;
+    f2_unpack(f2_mul(f2_pack(y[4 * q], y[4 * q + 1]), inv2), y0, y1);
+    f2_unpack(f2_mul(f2_pack(y[4 * q + 2], y[4 * q + 3]), inv2), y2, y3);
+    w[q] = cvt_e4m3x4(y0, y1, y2, y3);
+  }
+  uint4 c0 = make_uint4(w[0], w[1], w[2], w[3]), c1 = make_uint4(w[4], w[5], w[6], w[7]);
+  uint4* qp = reinterpret_cast<uint4*>(ep.q_values + row * int64_t(n_out) + out_col);
+  if (ep.wide) {
+    st_global_v8(qp, c0, c1);
+  } else {
+    qp[0] = c0;
+    qp[1] = c1;
+  }
+  ep.q_scales[mx_scale_offset(row, out_col >> 5, n_out >> 7)] = uint8_t(e);
 }
 
 template <int BN, int EPI>
@@ -364,6 +406,7 @@ mxfp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a0, const __grid_cons
     const int half = (warp - 2) / 4;  // which half of the tile's columns
     const int row_in_tile = sub * 32 + lane;
     constexpr int kChunks = BN / 64;  // 32-column chunks per warp
+    static_assert(EPI != kEpiSwigluQuant || kChunks % 2 == 0, "SwiGLU pairs need an even chunk count");
     int it = 0;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++it) {
       const int a = (C::NACC == 2) ? (it & 1) : 0;
@@ -389,12 +432,47 @@ mxfp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a0, const __grid_cons
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(smem_u32(&acc_empty[a]));
+        if constexpr (EPI == kEpiSwigluQuant) {
 #pragma unroll
-        for (int jj = 0; jj < kChunks; ++jj) {
-          float v[32];
+          for (int jj = 0; jj < kChunks; jj += 2) {
+            float vg[32], vv[32];
 #pragma unroll
-          for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[jj][i]);
-          epilogue_chunk<EPI>(v, ep, row, n0 + (half * kChunks + jj) * 32, live, N);
+            for (int i = 0; i < 32; ++i) {
+              vg[i] = __uint_as_float(r[jj][i]);
+              vv[i] = __uint_as_float(r[jj + 1][i]);
+            }
+            epilogue_swiglu_pair(vg, vv, ep, row, (n0 + (half * kChunks + jj) * 32) / 2, live, N / 2);
+          }
+        } else {
+#pragma unroll
+          for (int jj = 0; jj < kChunks; ++jj) {
+            float v[32];
+#pragma unroll
+            for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[jj][i]);
+            epilogue_chunk<EPI>(v, ep, row, n0 + (half * kChunks + jj) * 32, live, N);
+          }
+        }
+      } else if constexpr (EPI == kEpiSwigluQuant) {
+#pragma unroll 1
+        for (int jj = 0; jj < kChunks; jj += 2) {
+          const int j = half * kChunks + jj;
+          uint32_t rg[32], rv[32];
+          tc_ld_32x32b_x32(t_row + uint32_t(j * 32), rg);
+          tc_ld_32x32b_x32(t_row + uint32_t((j + 1) * 32), rv);
+          tc_wait_ld();
+          if (jj == kChunks - 2) {
+            // all columns of this accumulator are in registers: hand it back
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(smem_u32(&acc_empty[a]));
+          }
+          float vg[32], vv[32];
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            vg[i] = __uint_as_float(rg[i]);
+            vv[i] = __uint_as_float(rv[i]);
+          }
+          epilogue_swiglu_pair(vg, vv, ep, row, (n0 + j * 32) / 2, live, N / 2);
         }
       } else {
 #pragma unroll 1
@@ -856,11 +934,11 @@ int launch_gemm_pair(const void* a, const void* sa, const void* b, const void* s
   return check_launch("mxfp8_gemm_pair_kernel");
 }
 
-int pick_bn(int64_t M, int64_t N, bool heavy_epilogue) {
+int pick_bn(int64_t M, int64_t N, bool heavy_epilogue, bool even_chunks = false) {
   // QIA_GEMM_BN (128, 192 or 256) pins the tile width, for tuning and tests.
   const char* env = getenv("QIA_GEMM_BN");
   const int forced = env ? atoi(env) : 0;
-  if ((forced == 128 || forced == 192 || forced == 256) && N % forced == 0) return forced;
+  if ((forced == 128 || (forced == 192 && !even_chunks) || forced == 256) && N % forced == 0) return forced;
   (void)heavy_epilogue;   // the f32x2 GELU epilogues keep up with BN=256 main loops
   // Prefer the tile width with the best last-wave occupancy over the SMs.
   const int64_t m_tiles = (M + 127) / 128;
@@ -868,7 +946,7 @@ int pick_bn(int64_t M, int64_t N, bool heavy_epilogue) {
   int best = 0;
   double best_eff = -1.0;
   for (int bn : {192, 256, 128}) {
-    if (N % bn) continue;
+    if (N % bn || (even_chunks && bn == 192)) continue;   // the SwiGLU epilogue pairs 32-column chunks
     const int64_t tiles = m_tiles * (N / bn);
     const int64_t waves = (tiles + sms - 1) / sms;
     // measured per-tile efficiency on B200: BN=256 (one accumulator, released
@@ -929,23 +1007,28 @@ int dispatch(const Problem* in, int count, int64_t N, int64_t K, void* stream, c
   }
   if (m_tiles * 128 > (1LL << 30)) return set_error(QIA_ERR_UNSUPPORTED, "%s: too large", who);
   cudaStream_t st = as_stream(stream);
-  if (count == 1 && use_pair(pr[0].M)) {
-    const Problem& p = pr[0];
-    switch (pick_bn_pair(p.M, N)) {
-      case 128: return launch_gemm_pair<128, EPI>(p.a, p.sa, p.b, p.sb, p.ep, p.M, N, K, st);
-      case 192: return launch_gemm_pair<192, EPI>(p.a, p.sa, p.b, p.sb, p.ep, p.M, N, K, st);
-      case 256: return launch_gemm_pair<256, EPI>(p.a, p.sa, p.b, p.sb, p.ep, p.M, N, K, st);
-      default: return set_error(QIA_ERR_UNSUPPORTED, "%s: N=%lld has no supported tile width", who, (long long)N);
+  if constexpr (EPI != kEpiSwigluQuant) {   // the CTA-pair kernel has no SwiGLU epilogue
+    if (count == 1 && use_pair(pr[0].M)) {
+      const Problem& p = pr[0];
+      switch (pick_bn_pair(p.M, N)) {
+        case 128: return launch_gemm_pair<128, EPI>(p.a, p.sa, p.b, p.sb, p.ep, p.M, N, K, st);
+        case 192: return launch_gemm_pair<192, EPI>(p.a, p.sa, p.b, p.sb, p.ep, p.M, N, K, st);
+        case 256: return launch_gemm_pair<256, EPI>(p.a, p.sa, p.b, p.sb, p.ep, p.M, N, K, st);
+        default: return set_error(QIA_ERR_UNSUPPORTED, "%s: N=%lld has no supported tile width", who, (long long)N);
+      }
     }
   }
   // the tile width is chosen for the group's total M tiles
-  const int bn = pick_bn(m_tiles * 128, N, EPI == kEpiGeluQuant || EPI == kEpiGeluBf16);
+  const int bn = pick_bn(m_tiles * 128, N, EPI == kEpiGeluQuant || EPI == kEpiGeluBf16, EPI == kEpiSwigluQuant);
   switch (bn) {
     case 128: return launch_gemm<128, EPI>(pr, count, N, K, st);
-    case 192: return launch_gemm<192, EPI>(pr, count, N, K, st);
+    case 192:
+      if constexpr (EPI != kEpiSwigluQuant) return launch_gemm<192, EPI>(pr, count, N, K, st);
+      break;
     case 256: return launch_gemm<256, EPI>(pr, count, N, K, st);
-    default: return set_error(QIA_ERR_UNSUPPORTED, "%s: N=%lld has no supported tile width", who, (long long)N);
+    default: break;
   }
+  return set_error(QIA_ERR_UNSUPPORTED, "%s: N=%lld has no supported tile width", who, (long long)N);
 }
 
 template <int EPI>
@@ -1005,6 +1088,19 @@ extern "C" int qia_mxfp8_gemm_gelu_quant(const void* a_values, const void* a_sca
   ep.q_scales = (uint8_t*)q_scales;
   return dispatch<kEpiGeluQuant>(a_values, a_scales, b_values, b_scales, ep, m, n, k, stream,
                                  "qia_mxfp8_gemm_gelu_quant");
+}
+
+extern "C" int qia_mxfp8_gemm_swiglu_quant(const void* a_values, const void* a_scales, const void* b_values,
+                                           const void* b_scales, void* q_values, void* q_scales, int64_t m,
+                                           int64_t n, int64_t k, void* stream) {
+  if (!q_values || !q_scales) return set_error(QIA_ERR_INVALID, "qia_mxfp8_gemm_swiglu_quant: null output");
+  if (n % 256) return set_error(QIA_ERR_UNSUPPORTED, "qia_mxfp8_gemm_swiglu_quant: n must be a multiple of 256");
+  if (!aligned(q_values, 16)) return set_error(QIA_ERR_ALIGNMENT, "qia_mxfp8_gemm_swiglu_quant: q_values alignment");
+  EpiParams ep{};
+  ep.q_values = (uint8_t*)q_values;
+  ep.q_scales = (uint8_t*)q_scales;
+  return dispatch<kEpiSwigluQuant>(a_values, a_scales, b_values, b_scales, ep, m, n, k, stream,
+                                   "qia_mxfp8_gemm_swiglu_quant");
 }
 
 extern "C" int qia_mxfp8_gemm_gate_residual(const void* a_values, const void* a_scales, const void* b_values,

@@ -47,6 +47,11 @@ __device__ __forceinline__ __nv_bfloat16 f32_to_bf16(float v) { return __float2b
 // Round an fp32 value through bf16 and back (the eager bf16 tensor boundary).
 __device__ __forceinline__ float round_bf16(float v) { return __bfloat162float(__float2bfloat16_rn(v)); }
 
+// SiLU of a bf16 value as the reference's SwiGLU computes it
+// (src/qwen_image_accel/kernels/bf16.py:12-24): div.rn(g, 1 + exp(-g)),
+// rounded to bf16.
+__device__ __forceinline__ float silu_ref(float g) { return round_bf16(__fdiv_rn(g, 1.0f + expf(-g))); }
+
 __device__ __forceinline__ float bf16_lo(uint32_t packed) { return __uint_as_float(packed << 16); }
 __device__ __forceinline__ float bf16_hi(uint32_t packed) { return __uint_as_float(packed & 0xffff0000u); }
 

@@ -58,6 +58,7 @@ SIGNATURES: dict[str, list] = {
     "qia_mxfp8_gemm_gate_residual": [_P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _P],
     "qia_device_error": [_P],
     "qia_sage_attention": [_P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _F, _P, _I, _P],
+    "qia_mxfp8_gemm_swiglu_quant": [_P, _P, _P, _P, _P, _P, _I, _I, _I, _P],
     "qia_sage_attention_prefill": [_P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _P, _F, _P, _I, _P],
     "qia_sage_attention_split": [_P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _P, _F, _P, _I, _P],
     "qia_sage_attention_split_mx": [_P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _P, _F, _P, _I, _P],

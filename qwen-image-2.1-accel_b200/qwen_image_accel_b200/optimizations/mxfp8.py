@@ -76,6 +76,18 @@ class MXFP8Linear(nn.Module):
                   self.in_features, _lib.stream(q.values.device))
         return q
 
+    def matmul_swiglu_quantize(self, activation: Quantized) -> Quantized:
+        """MXFP8 SwiGLU activation bf16(silu(g) * v) of the gate/value pair
+        this linear stacks (interleaved_gate_value), quantized in the GEMM
+        epilogue: [rows, out_features / 2]."""
+        if self.bias is not None:
+            raise NotImplementedError("the SwiGLU epilogue takes no bias")
+        m, n = activation.rows, self.out_features
+        q = empty_quantized(m, n // 2, activation.values.device)
+        _lib.call("qia_mxfp8_gemm_swiglu_quant", *self._args(activation)[:4], _lib.ptr(q.values), _lib.ptr(q.scales),
+                  m, n, self.in_features, _lib.stream(q.values.device))
+        return q
+
     def matmul_gate_residual(self, activation: Quantized, gate: torch.Tensor, residual: torch.Tensor,
                              out: torch.Tensor | None = None) -> torch.Tensor:
         """residual + gate * (activation @ W^T + bias), each step rounded to bf16.
@@ -97,6 +109,15 @@ class MXFP8Linear(nn.Module):
         flat = x.reshape(-1, x.shape[-1])
         activation = quantize(flat if flat.stride(-1) == 1 else flat.contiguous())
         return self.matmul(activation, x.dtype).reshape(*x.shape[:-1], self.out_features)
+
+
+def interleaved_gate_value(gate_weight: torch.Tensor, value_weight: torch.Tensor) -> torch.Tensor:
+    """[2F, K] stack of the SwiGLU gate and value weights ([F, K] each),
+    interleaved every 32 rows -- the B operand of matmul_swiglu_quantize."""
+    f, k = gate_weight.shape
+    if value_weight.shape != (f, k) or f % 32:
+        raise ValueError("gate and value weights must be [F, K] with F a multiple of 32")
+    return torch.stack([gate_weight.reshape(f // 32, 32, k), value_weight.reshape(f // 32, 32, k)], dim=1).reshape(2 * f, k)
 
 
 def _grouped(epilogue: int, problems: list) -> None:

@@ -27,7 +27,7 @@ the joint [prefix, target] K/V buffers behind the copied cache
 MXFP8 profiles takes the attention output as MXFP8 from the attention
 epilogue, the gated residuals from the output-projection GEMM epilogues, and
 the gate/value projections as one grouped launch -- each byte-identical to
-the unfused op it replaces.
+the unfused op sequence it replaces.
 
 As in the reference (quantize_transformer swaps the linears, the MLP forward
 is replaced for both modes), the prefill uses the same MXFP8 linears and MLP;
@@ -191,7 +191,10 @@ class Block21:
     def _swiglu_act(self, x):
         """MXFP8 SwiGLU activation of the MLP (quantized profiles): the gate and
         value projections of one shared activation in one grouped launch, then
-        SwiGLU + quantization in one pass."""
+        SwiGLU + quantization in one pass. (The single-GEMM form with the
+        SwiGLU in the epilogue, MXFP8Linear.matmul_swiglu_quantize, gives the
+        same bytes but measured slower here: its per-element IEEE divide and
+        exp hold the accumulator hand-off of the GEMM.)"""
         a = x if not isinstance(x, torch.Tensor) else quantize(x.reshape(-1, x.shape[-1]))
         gate, value = matmul_grouped([(self.gate_layer, a), (self.proj, a)])
         return swiglu_quantize(gate, value)

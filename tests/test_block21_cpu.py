@@ -48,3 +48,16 @@ def test_kv_cache_container():
     k = torch.zeros(1, 4, 2, 128)
     cache.get_layer(1).store(k, k)
     assert cache.get_layer(1).get()[0] is k
+
+
+def test_interleaved_gate_value_layout():
+    from qwen_image_accel_b200.optimizations.mxfp8 import interleaved_gate_value
+    g = torch.arange(96 * 4, dtype=torch.float32).view(96, 4)
+    v = -g - 1
+    s = interleaved_gate_value(g, v)
+    assert s.shape == (192, 4)
+    for j in range(3):
+        assert torch.equal(s[64 * j:64 * j + 32], g[32 * j:32 * j + 32])
+        assert torch.equal(s[64 * j + 32:64 * j + 64], v[32 * j:32 * j + 32])
+    with pytest.raises(ValueError):
+        interleaved_gate_value(g[:40], v[:40])

@@ -262,3 +262,30 @@ def test_grouped_launch_matches_single_gemms(monkeypatch, bn, m0, m1, n, k):
     torch.cuda.synchronize()
     from qwen_image_accel_b200 import _lib
     assert _lib.device_error() == 0
+
+
+@pytest.mark.parametrize("bn", ["128", "256", None])
+@pytest.mark.parametrize("m,f,k", [(300, 384, 256), (4096, 1536, 512), (130, 128, 384)])
+def test_swiglu_epilogue_matches_gemm_pair_then_swiglu_quantize(monkeypatch, bn, m, f, k):
+    """qia_mxfp8_gemm_swiglu_quant over the interleaved [W_gate; W_value]
+    stack is byte-identical to the two bf16 GEMMs followed by
+    swiglu_quantize (codes, scales and the zero padding rows)."""
+    import torch.nn as nn
+    from qwen_image_accel_b200.kernels.epilogue import swiglu_quantize
+    from qwen_image_accel_b200.kernels.mxfp8 import quantize
+    from qwen_image_accel_b200.optimizations.mxfp8 import MXFP8Linear, interleaved_gate_value
+    if bn:
+        monkeypatch.setenv("QIA_GEMM_BN", bn)
+    else:
+        monkeypatch.delenv("QIA_GEMM_BN", raising=False)
+    gate, value = make_linear(f, k, 5, bias=False), make_linear(f, k, 6, bias=False)
+    stacked = nn.Linear(k, 2 * f, bias=False, device="cuda", dtype=torch.bfloat16)
+    with torch.no_grad():
+        stacked.weight.copy_(interleaved_gate_value(gate.weight, value.weight))
+    mg, mv, ms = MXFP8Linear(gate), MXFP8Linear(value), MXFP8Linear(stacked)
+    a = quantize(make_x(m, k, 7))
+    want = swiglu_quantize(mg.matmul(a), mv.matmul(a))
+    got = ms.matmul_swiglu_quantize(a)
+    assert got.rows == want.rows and got.values.shape == want.values.shape
+    assert torch.equal(got.values.view(torch.uint8), want.values.view(torch.uint8))
+    assert torch.equal(got.scales.view(torch.uint8), want.scales.view(torch.uint8))
