@@ -17,6 +17,8 @@
 
 #include <math.h>
 
+#include <mutex>
+
 namespace qia {
 namespace {
 
@@ -90,6 +92,58 @@ __global__ void swiglu_quant_kernel(const __nv_bfloat16* __restrict__ g, const _
   }
 }
 
+// SwiGLU + quantizer for large inputs: the gate is bf16, so silu(g) takes one
+// of 65,536 values. Each CTA first tabulates silu_ref over every bf16 bit
+// pattern in shared memory (128 KB, the same device function, so every entry
+// is exactly what the direct kernel computes) and then looks it up, which
+// leaves the kernel bound by HBM instead of by the IEEE divide and exp of
+// every element. Two 16-byte loads of gate and value per thread are in flight
+// per trip.
+constexpr int kSiluTableThreads = 1024;
+constexpr int kSiluTableBytes = 65536 * 2;
+
+__device__ __forceinline__ void swiglu_table8(const uint4& g, const uint4& v, const uint16_t* __restrict__ tab,
+                                              float (&y)[8]) {
+  const uint32_t gw[4] = {g.x, g.y, g.z, g.w};
+  float fv[8];
+  unpack8(v, fv);
+#pragma unroll
+  for (int m = 0; m < 4; ++m) {
+    const float s0 = __uint_as_float(uint32_t(tab[gw[m] & 0xffffu]) << 16);
+    const float s1 = __uint_as_float(uint32_t(tab[gw[m] >> 16]) << 16);
+    y[2 * m] = round_bf16(__fmul_rn(s0, fv[2 * m]));
+    y[2 * m + 1] = round_bf16(__fmul_rn(s1, fv[2 * m + 1]));
+  }
+}
+
+__global__ void __launch_bounds__(kSiluTableThreads, 1)
+swiglu_quant_table_kernel(const uint4* __restrict__ g, const uint4* __restrict__ v, uint8_t* __restrict__ qv,
+                          uint8_t* __restrict__ qs, int64_t rows, int64_t k, int64_t n8) {
+  extern __shared__ uint16_t silu_tab[];
+  for (int i = threadIdx.x; i < 65536; i += blockDim.x)
+    silu_tab[i] = __bfloat16_as_ushort(__float2bfloat16_rn(silu_ref(__uint_as_float(uint32_t(i) << 16))));
+  __syncthreads();
+  // rows past `rows` (the padding up to 128) read as zero gate and value:
+  // bf16(silu(0) * 0) = 0, the zero codes the direct kernel writes
+  const uint4 zero = make_uint4(0u, 0u, 0u, 0u);
+  const int64_t stride = int64_t(gridDim.x) * blockDim.x;
+  for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < n8; i += 2 * stride) {
+    const int64_t i2 = i + stride;
+    const bool has2 = i2 < n8;                  // uniform in each aligned 4-lane MX group
+    const int64_t row0 = (i * 8) / k, row1 = (i2 * 8) / k;
+    const bool live0 = row0 < rows, live1 = has2 && row1 < rows;
+    const uint4 g0 = live0 ? __ldg(g + i) : zero, v0 = live0 ? __ldg(v + i) : zero;
+    const uint4 g1 = live1 ? __ldg(g + i2) : zero, v1 = live1 ? __ldg(v + i2) : zero;
+    float y[8];
+    swiglu_table8(g0, v0, silu_tab, y);
+    mx_quant8(y, qv, qs, row0, i * 8 - row0 * k, k);
+    if (has2) {
+      swiglu_table8(g1, v1, silu_tab, y);
+      mx_quant8(y, qv, qs, row1, i2 * 8 - row1 * k, k);
+    }
+  }
+}
+
 __global__ void gelu_tanh_kernel(const uint4* __restrict__ x, uint4* __restrict__ out, int64_t n8) {
   for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < n8; i += int64_t(gridDim.x) * blockDim.x) {
     float f[8];
@@ -146,6 +200,27 @@ extern "C" int qia_swiglu_quant(const void* gate, const void* value, void* q_val
     return set_error(QIA_ERR_ALIGNMENT, "qia_swiglu_quant: 16-byte alignment");
   const int64_t padded = (rows + 127) / 128 * 128;
   const int64_t n8 = padded * width / 8;
+  // above ~8M elements the table's set-up (65,536 silu per CTA) is repaid
+  if (n8 >= (int64_t(1) << 20)) {
+    static bool attr_done[64] = {false};
+    static std::mutex mu;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    {
+      std::lock_guard<std::mutex> lock(mu);
+      if (dev >= 0 && dev < 64 && !attr_done[dev]) {
+        cudaError_t e = cudaFuncSetAttribute(swiglu_quant_table_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             kSiluTableBytes);
+        if (e != cudaSuccess) return set_error(QIA_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+        attr_done[dev] = true;
+      }
+    }
+    int64_t blocks = (n8 + 2 * kSiluTableThreads - 1) / (2 * kSiluTableThreads);
+    if (blocks > sm_count()) blocks = sm_count();
+    swiglu_quant_table_kernel<<<unsigned(blocks), kSiluTableThreads, kSiluTableBytes, as_stream(stream)>>>(
+        (const uint4*)gate, (const uint4*)value, (uint8_t*)q_values, (uint8_t*)q_scales, rows, width, n8);
+    return check_launch("swiglu_quant_table_kernel");
+  }
   swiglu_quant_kernel<<<flat_grid(n8, 256), 256, 0, as_stream(stream)>>>(
       (const __nv_bfloat16*)gate, (const __nv_bfloat16*)value, (uint8_t*)q_values, (uint8_t*)q_scales, rows, width,
       n8);

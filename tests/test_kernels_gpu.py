@@ -271,6 +271,27 @@ def test_swiglu_and_quant(rows, width):
         assert close_bf16(bits(out), ref).all()
 
 
+def test_swiglu_quant_table_covers_every_bf16_gate():
+    """Above ~8M elements swiglu_quantize looks silu up in a per-CTA table of
+    all 65,536 bf16 patterns: feed every finite bf16 gate value with
+    |g| < 1e4 (all exponents, subnormals, both signs) and compare with the
+    direct SiLU (swiglu) followed by quantize, byte for byte."""
+    from qwen_image_accel_b200.kernels.bf16 import swiglu
+    from qwen_image_accel_b200.kernels.epilogue import swiglu_quantize
+    from qwen_image_accel_b200.kernels.mxfp8 import quantize
+    pats = torch.arange(65536, dtype=torch.int32).to(torch.int16).view(torch.bfloat16)
+    keep = torch.isfinite(pats.float()) & (pats.float().abs() < 1e4)
+    vals = pats[keep]
+    rows, width = 1024, 12288
+    reps = rows * width // vals.numel() + 1
+    gt = vals.repeat(reps)[: rows * width].view(rows, width).to(DEV)
+    g = torch.Generator(device=DEV).manual_seed(3)
+    v = torch.randn(rows, width, device=DEV, dtype=torch.bfloat16, generator=g)
+    fused = swiglu_quantize(gt, v)
+    sep = quantize(swiglu(gt, v))
+    assert np.array_equal(u8(fused.values), u8(sep.values)) and np.array_equal(u8(fused.scales), u8(sep.scales))
+
+
 def test_gelu_tanh_equals_torch():
     from qwen_image_accel_b200.kernels.bf16 import gelu_tanh
     g = torch.Generator(device=DEV).manual_seed(4)
