@@ -149,3 +149,26 @@ def test_fused_decode_equals_reference_op_composition():
     cache.store(ck, cv)
     got = blk.forward_cached(ht, vals, freqs[p:].contiguous(), cache)
     assert torch.equal(got, want)
+
+
+@pytest.mark.parametrize("sage_prefill", [False, True])
+def test_batch_of_two_equals_single_samples(sage_prefill):
+    """B = 2 (the golden sample twice, one shared modulation row set) gives
+    each sample the B = 1 result bit for bit, in the prefill (per-sample
+    modulation rows, extracted K/V) and in the cached decode (joint K/V
+    buffers, gate-residual epilogue rows per sample)."""
+    from qwen_image_accel_b200.qwen21 import KVLayerCache, modulation_values
+    blk, g = build("mxfp8_sage", sage_prefill)
+    h, mod, ht = (t_bf16(g[n]).cuda() for n in ("h", "modulation", "h_target"))
+    freqs = torch.view_as_complex(torch.from_numpy(g["rope"]).contiguous()).cuda()
+    ids = torch.from_numpy(g["image_ids"]).cuda()
+    p = int(g["prefix_len"])
+    mod2 = torch.cat([mod[:1], mod[:1], mod[1:]])             # two sampled rows + the t = 0 row
+    c1, c2 = KVLayerCache(), KVLayerCache()
+    one = blk.forward_prefill(h, mod, freqs, ids, p, layer_cache=c1)
+    two = blk.forward_prefill(torch.cat([h, h]), mod2, freqs, ids, p, layer_cache=c2)
+    assert torch.equal(two[0], one[0]) and torch.equal(two[1], one[0])
+    assert torch.equal(c2.k[1], c1.k[0]) and torch.equal(c2.v[0], c1.v[0])
+    d1 = blk.forward_cached(ht, modulation_values(mod), freqs[p:].contiguous(), c1)
+    d2 = blk.forward_cached(torch.cat([ht, ht]), modulation_values(mod2), freqs[p:].contiguous(), c2)
+    assert torch.equal(d2[0], d1[0]) and torch.equal(d2[1], d1[0])

@@ -143,3 +143,14 @@ def test_prefill_entry_rejects_bad_arguments():
                                         1, 128, strides, 0.0, None, 0, None)
     assert rc != 0 and b"kv_limit" in lib.qia_last_error_string()
     assert _lib.device_error() == 0
+
+
+def test_all_valid_keys_equal_unmasked():
+    """key_valid with every key valid leaves the key order and the limits
+    unchanged (recounted per sample), so the result is the unmasked call's."""
+    from qwen_image_accel_b200.optimizations.prefill import prefill_attention
+    ids = torch.from_numpy(GOLD["image_ids_long"]).to(DEV)
+    s = ids.shape[0]
+    q, k, v = make_qkv(2, s, 2, 71)
+    kv = torch.ones(2, s, dtype=torch.bool, device=DEV)
+    assert torch.equal(prefill_attention(q, k, v, ids, key_valid=kv), prefill_attention(q, k, v, ids))
