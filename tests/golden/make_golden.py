@@ -23,6 +23,9 @@ modified). Sources of truth, per fixture:
 * block21_tiny.npz -- one Qwen-Image 2.1 single-stream block (Diffusers
   QwenImage21TransformerBlock, tiny dims, seeded weights): prefill with the
   prefix K/V extracted, then a cached decode of new target tokens.
+* model21_tiny.npz -- the whole Qwen-Image 2.1 transformer (Diffusers
+  QwenImage21Transformer2DModel, 2 blocks, tiny dims, seeded weights):
+  prefill with KV extract, then one cached step.
 * mmdit_tiny.npz -- the Diffusers QwenImageTransformer2DModel (v1 dual-stream
   MMDiT, WHL:diffusers/models/transformers/transformer_qwenimage.py) at a tiny
   size (2 blocks, 4x128 heads, text dim 512) in bf16 on the CPU, weights from
@@ -277,6 +280,45 @@ def make_block21(reference: Path):
                         keys=np.array(sorted(sd)))
 
 
+def make_model21(reference: Path):
+    """The whole Diffusers QwenImage21Transformer2DModel at a tiny size (2
+    blocks, 4 x 128 heads, text dim 256) in bf16 on the CPU, weights from the
+    package's seeded recipe (seed 13): a condition-image edit in the
+    vision-language slot layout (text 10, condition image (1, 4, 4) as 4
+    slots, text 3, target (1, 4, 6) as 6 slots), prefill with kv_cache_mode
+    "extract" at t = 0.8, then a cached step at t = 0.6 with new target
+    latents."""
+    import torch
+    _import_diffusers(reference)
+    from diffusers.models.transformers import transformer_qwenimage21 as t21
+    sys.path.insert(0, str(OUT.parents[1] / "qwen-image-2.1-accel_b200"))
+    from qwen_image_accel_b200.mmdit import init_parameter
+
+    model = t21.QwenImage21Transformer2DModel(num_layers=2, num_attention_heads=4, context_in_dim=256).to(torch.bfloat16)
+    sd = model.state_dict()
+    model.load_state_dict({n: init_parameter(n, tuple(t.shape), seed=13) for n, t in sd.items()})
+    model.eval()
+    shapes = [(1, 4, 4), (1, 4, 6)]
+    img_mask = torch.tensor([[False] * 10 + [True] * 4 + [False] * 3 + [True] * 6])
+    g = torch.Generator().manual_seed(31)
+    enc = torch.randn(1, img_mask.shape[1] - 6, 256, generator=g).to(torch.bfloat16)
+    lat = torch.randn(1, 16 + 24, 64, generator=g).to(torch.bfloat16)
+    lat2 = lat.clone()
+    lat2[:, 16:] = torch.randn(1, 24, 64, generator=g).to(torch.bfloat16)
+    cache = t21.QwenImage21KVCache(2)
+    with torch.no_grad():
+        out_prefill = model(hidden_states=lat, encoder_hidden_states=enc, timestep=torch.tensor([0.8]),
+                            img_shapes=[shapes], img_mask=img_mask, kv_cache=cache, kv_cache_mode="extract",
+                            return_dict=False)[0]
+        out_cached = model(hidden_states=lat2, encoder_hidden_states=enc, timestep=torch.tensor([0.6]),
+                           img_shapes=[shapes], img_mask=img_mask, kv_cache=cache, kv_cache_mode="cached",
+                           return_dict=False)[0]
+    np.savez_compressed(OUT / "model21_tiny.npz", lat=_bits(lat), lat2=_bits(lat2), enc=_bits(enc),
+                        img_mask=img_mask.numpy(), shapes=np.array(shapes), out_prefill=_bits(out_prefill),
+                        out_cached=_bits(out_cached), cached_k0=_bits(cache.get_layer(0).k),
+                        keys=np.array(sorted(sd)), t=np.array([0.8, 0.6], np.float32))
+
+
 if __name__ == "__main__":
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default="/root/reference")
@@ -287,4 +329,5 @@ if __name__ == "__main__":
     make_mmdit(ref)
     make_block_causal(ref)
     make_block21(ref)
+    make_model21(ref)
     print("wrote", sorted(p.name for p in OUT.glob("*.npz")))
