@@ -560,66 +560,77 @@ def prefill_arm(args, rank, world, local_rank):
 
 
 Q21_LAYERS, Q21_DIM, Q21_HEADS, Q21_PREFIX, Q21_TARGET = 32, 4096, 32, 113, 4096   # Qwen-Image 2.1, 1024^2 t2i
+Q21_CTX = 4096                                                                        # text embedding width
 
 
 def _q21_setup(device):
-    """The Qwen-Image 2.1 denoiser of `--config q21` on `device`: 32 Block21
-    (mxfp8_sage) with seeded random weights, the embedders around them, the
-    inputs, and its prefill / decode closures (see q21_arm)."""
+    """The Qwen-Image 2.1 transformer of `--config q21` on `device`
+    (qwen21_model.Qwen21Transformer, 32 Block21, mxfp8_sage, seeded random
+    weights), a 1024^2 text-to-image input in the vision-language slot layout
+    (113 text slots + 1024 target slots of 2x2 latent tokens), and closures:
+    prefill() = the public forward with kv_cache_mode="extract"; forward(lat)
+    = the public forward with kv_cache_mode="cached"; decode(lat) = the same
+    cached step without its host-side glue (RoPE table, metadata, slot
+    layout, and the text projection the cached step discards), so that it can
+    be captured in a CUDA graph (see q21_arm)."""
     import types
     import torch.nn.functional as F
     from qwen_image_accel_b200.kernels.layernorm import layer_norm_scale
     from qwen_image_accel_b200.mmdit import init_parameter
-    from qwen_image_accel_b200.qwen21 import (Block21, Block21Config, KVCache, _Norm, block21_parameter_shapes,
-                                              modulation_values)
+    from qwen_image_accel_b200.qwen21 import Block21Config, KVCache, modulation_values
+    from qwen_image_accel_b200.qwen21_model import Qwen21Transformer, model21_parameter_shapes, rope_table
     cfg = Block21Config(dim=Q21_DIM, heads=Q21_HEADS)
-    shapes = block21_parameter_shapes(cfg)
-    blocks = [Block21(lambda n, i=i: init_parameter(f"transformer_blocks.{i}.{n}", shapes[n], 42, device), cfg,
-                      device=device, profile="mxfp8_sage") for i in range(Q21_LAYERS)]
+    shapes = model21_parameter_shapes(Q21_LAYERS, cfg, context_in_dim=Q21_CTX)
+    model = Qwen21Transformer(lambda n: init_parameter(n, shapes[n], 42, device), num_layers=Q21_LAYERS, cfg=cfg,
+                              context_in_dim=Q21_CTX, device=device, profile="mxfp8_sage")
     D, S, P = Q21_DIM, Q21_PREFIX + Q21_TARGET, Q21_PREFIX
-    w = {n: init_parameter(n, shp, 42, device) for n, shp in
-         (("img_in.weight", (D, 64)), ("modulation.1.weight", (4 * D, D)), ("norm_out.linear.weight", (D, D)),
-          ("proj_out.weight", (64, D)))}
+    side = int(round(Q21_TARGET ** 0.5))
+    img_shapes = [[(1, side, side)]]
+    img_mask = torch.tensor([[False] * P + [True] * (Q21_TARGET // 4)], device=device)
     g = torch.Generator(device=device).manual_seed(42)
     lat = torch.randn(1, Q21_TARGET, 64, device=device, dtype=torch.bfloat16, generator=g)
-    temb = torch.randn(2, D, device=device, dtype=torch.bfloat16, generator=g)        # [sampled t, t = 0]
-    joint = torch.randn(1, S, D, device=device, dtype=torch.bfloat16, generator=g)     # img_in / txt_in output
-    phase = torch.rand(S, 64, device=device, generator=g) * 6.2831853
-    freqs = torch.polar(torch.ones_like(phase), phase)                               # complex64 [S, 64]
-    freqs_target = freqs[P:].contiguous()
-    image_ids = torch.cat([torch.full((P,), -1, device=device), torch.zeros(Q21_TARGET, device=device)]).long()
+    enc = torch.randn(1, P, Q21_CTX, device=device, dtype=torch.bfloat16, generator=g)
+    t0, t1 = torch.tensor([0.9], device=device), torch.tensor([0.8], device=device)
     cache = KVCache(Q21_LAYERS)
-    ln = _Norm(None, cfg.eps, (D,))
+    pad = torch.cat([torch.zeros(P, dtype=torch.bool), torch.ones(Q21_TARGET, dtype=torch.bool)])
+    freqs_target = rope_table(img_shapes[0], pad)[P:].contiguous().to(device)
 
     def prefill():
-        mod = F.linear(F.silu(temb), w["modulation.1.weight"])
-        x = joint
-        for i, blk in enumerate(blocks):
-            x = blk.forward_prefill(x, mod, freqs, image_ids, P, layer_cache=cache.get_layer(i))
-        return x
+        return model.forward(lat, enc, t0, img_shapes, img_mask, kv_cache=cache, kv_cache_mode="extract")
+
+    def forward(latents):
+        return model.forward(latents, enc, t1, img_shapes, img_mask, kv_cache=cache, kv_cache_mode="cached")
+
+    t = t1.to(torch.bfloat16)
+    temb_in = torch.cat([t, t.new_zeros(1)])
 
     def decode(latents):
-        x = F.linear(latents, w["img_in.weight"])
-        vals = modulation_values(F.linear(F.silu(temb), w["modulation.1.weight"]))
-        for i, blk in enumerate(blocks):
+        x = F.linear(latents, model.w["img_in.weight"])
+        temb = model.time_embed(temb_in)
+        vals = modulation_values(F.linear(F.silu(temb), model.w["modulation.1.weight"]))
+        for i, blk in enumerate(model.blocks):
             x = blk.forward_cached(x, vals, freqs_target, cache.get_layer(i))
-        scale = F.linear(F.silu(temb[:1]), w["norm_out.linear.weight"])
-        return F.linear(layer_norm_scale(x, (1 + scale)[:, None].contiguous(), ln), w["proj_out.weight"])
+        scale = F.linear(F.silu(temb[:1]), model.w["norm_out.linear.weight"])
+        return F.linear(layer_norm_scale(x, (1 + scale)[:, None].contiguous(), model.ln), model.w["proj_out.weight"])
 
-    return types.SimpleNamespace(blocks=blocks, lat=lat, prefill=prefill, decode=decode, D=D, S=S, P=P)
+    return types.SimpleNamespace(model=model, blocks=model.blocks, lat=lat, enc=enc, prefill=prefill, forward=forward,
+                                 decode=decode, D=D, S=S, P=P, t1=t1, img_shapes=img_shapes, img_mask=img_mask,
+                                 cache=cache)
 
 
 def q21_arm(args, rank, world, local_rank):
-    """`--config q21`: the Qwen-Image 2.1 denoiser on the sm_100a kernels
-    (qwen21.Block21, profile mxfp8_sage): 32 single-stream blocks (D 4096,
-    32 x 128 heads, SwiGLU 12288), 1024^2 text-to-image (4096 target tokens,
-    a 113-token text prefix). value = one cached-decode step, captured in a
-    CUDA graph: img_in, the shared modulation GEMV, the 32 blocks over the
-    target tokens against the prefix KV cache, norm_out and proj_out. Not in
-    the step: the timestep embedder and the text projection (prompt-sized
-    work). Beside it, the prefill step (eager, the prefix K/V extracted) with
-    the reference's per-segment SDPA and with the tcgen05 block-causal
-    kernel. One replica per GPU for N > 1."""
+    """`--config q21`: the Qwen-Image 2.1 transformer on the sm_100a kernels
+    (qwen21_model.Qwen21Transformer, profile mxfp8_sage): 32 single-stream
+    blocks (D 4096, 32 x 128 heads, SwiGLU 12288), 1024^2 text-to-image (4096
+    target tokens, a 113-token text prefix). value = one cached-decode step,
+    captured in a CUDA graph: img_in, the timestep embedder, the shared
+    modulation, the 32 blocks over the target tokens against the prefix KV
+    cache, norm_out and proj_out (the text projection, which the cached step
+    discards, and the host-side RoPE/metadata glue are left out of the graph).
+    e2e = the public forward(kv_cache_mode="cached") from pinned host buffers,
+    eager, glue included. Beside it, the prefill step (the public forward with
+    kv_cache_mode="extract") with the reference's per-segment SDPA and with
+    the tcgen05 block-causal kernel. One replica per GPU for N > 1."""
     from qwen_image_accel_b200 import _lib
     device = torch.device("cuda", local_rank)
     torch.cuda.set_device(device)
@@ -671,14 +682,24 @@ def q21_arm(args, rank, world, local_rank):
     torch.cuda.synchronize()
     clocks = sampler.stop() if sampler else None
     ms = e0.elapsed_time(e1) / args.steps
-    host_lat = lat.cpu().pin_memory()
+    # end to end through the public model API (Qwen21Transformer.forward,
+    # kv_cache_mode="cached", eager with its host-side glue): latents and
+    # prompt embeddings from pinned host memory, the velocity back to the host
+    host_lat, host_enc = lat.cpu().pin_memory(), m.enc.cpu().pin_memory()
+    dev_lat, dev_enc = torch.empty_like(lat), torch.empty_like(m.enc)
     host_out = torch.empty(static_out.shape, dtype=static_out.dtype).pin_memory()
+
+    def e2e_step():
+        dev_lat.copy_(host_lat, non_blocking=True)
+        dev_enc.copy_(host_enc, non_blocking=True)
+        host_out.copy_(m.model.forward(dev_lat, dev_enc, m.t1, m.img_shapes, m.img_mask, kv_cache=m.cache,
+                                       kv_cache_mode="cached"), non_blocking=True)
+
+    e2e_step()
     torch.cuda.synchronize()
     e0.record(st)
     for _ in range(args.steps):
-        static_lat.copy_(host_lat, non_blocking=True)
-        graph.replay()
-        host_out.copy_(static_out, non_blocking=True)
+        e2e_step()
     e1.record(st)
     torch.cuda.synchronize()
     ms_e2e = e0.elapsed_time(e1) / args.steps
@@ -697,16 +718,18 @@ def q21_arm(args, rank, world, local_rank):
                 "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": False,
                 "scaling": "weak", "vs_baseline": None, "dtype": "mxfp8+int8/fp8 attn",
                 "data": "synthetic (random-init weights ~N(0,0.02), seeded latents/embeddings, random RoPE phases)",
-                "config": {"workload": "q21: Qwen-Image 2.1 denoiser decode step, profile mxfp8_sage (img_in, "
-                                       "modulation, 32 blocks, norm_out, proj_out; timestep embedder and text "
-                                       "projection not in the step)", "global_batch": 1, "seq_len": T,
+                "config": {"workload": "q21: Qwen-Image 2.1 transformer cached-decode step, profile mxfp8_sage "
+                                       "(img_in, timestep embedder, modulation, 32 blocks, norm_out, proj_out in "
+                                       "a CUDA graph; e2e = the eager public forward)", "global_batch": 1,
+                           "seq_len": T,
                            "prefix_len": P, "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
                            "cuda_graph": True, "l2": "weights (7 GB MXFP8) >> L2; no flush"},
                 "compare": {"prefill_step_ms_segment_sdpa": round(ms_prefill, 2),
                             "prefill_step_ms_sage_block_causal": round(ms_prefill_sage, 2),
                             "reference_rtx5090_mxfp8_sage_decode_ms": 147.3,
                             "reference_rtx5090_mxfp8_sage_prefill_ms": 186.5},
-                "e2e": {"value": round(ms_e2e, 3), "unit": "ms/step", "h2d_bytes_per_step": host_lat.numel() * 2,
+                "e2e": {"value": round(ms_e2e, 3), "unit": "ms/step",
+                        "h2d_bytes_per_step": host_lat.numel() * 2 + host_enc.numel() * 2,
                         "d2h_bytes_per_step": host_out.numel() * 2},
                 "gpu_launches": launches * args.steps,
                 "roofline": {"bound": "tensor", "kernel": f"whole decode step ({tflop:.1f} TFLOP)",
