@@ -128,6 +128,7 @@ class Qwen21Transformer:
         self.blocks = [Block21(lambda n, i=i: get(f"transformer_blocks.{i}.{n}"), cfg, device=dev, profile=profile,
                                sage_prefill=sage_prefill) for i in range(num_layers)]
         self.ln = _Norm(None, cfg.eps, (cfg.dim,))
+        self._layouts: dict = {}
         # QwenImage21TemporalTimesteps(256): frequencies built once in fp32 on the CPU
         self.t_freqs = torch.exp(-math.log(10000) * torch.arange(0, 128, dtype=torch.float32) / 128).to(dev)
 
@@ -149,6 +150,29 @@ class Qwen21Transformer:
         y = F.gelu(F.linear(y, self.w["txt_in.in_layer.weight"]), approximate="tanh")
         return F.linear(y, self.w["txt_in.out_layer.weight"])
 
+    def layout(self, img_shapes, img_mask: torch.Tensor, device) -> dict:
+        """The layout-only tensors of a forward -- per-slot repeats, the image
+        token mask, the RoPE table, the token metadata and the prefix length
+        -- memoised per (image shapes, slot mask): every denoising step of a
+        generation shares them, and the reference rebuilds them each forward
+        (the RoPE table alone is a host loop over the sequence). The key reads
+        the slot mask on the host, where the reference's RoPE already syncs."""
+        key = (tuple(tuple(int(v) for v in s) for s in img_shapes[0]), bytes(img_mask[0].cpu().numpy().tobytes()),
+               str(device))
+        hit = self._layouts.get(key)
+        if hit is not None:
+            return hit
+        repeats = torch.where(img_mask, 4, 1)[0]
+        image_pad_mask = torch.repeat_interleave(img_mask[0], repeats)
+        image_ids, target = token_metadata(image_pad_mask.to(device), img_shapes[0])
+        lay = {"repeats": repeats.to(device), "pad": image_pad_mask.to(device), "pad_cpu": image_pad_mask.cpu(),
+               "rope": rope_table(img_shapes[0], image_pad_mask, self.axes).to(device), "image_ids": image_ids,
+               "target": target, "prefix_len": int((~target).sum())}
+        if len(self._layouts) >= 8:
+            self._layouts.pop(next(iter(self._layouts)))
+        self._layouts[key] = lay
+        return lay
+
     # ---------------------------------------------------------------- forward
     def forward(self, hidden_states: torch.Tensor, encoder_hidden_states: torch.Tensor, timestep: torch.Tensor,
                 img_shapes, img_mask: torch.Tensor, encoder_hidden_states_mask: torch.Tensor | None = None,
@@ -167,24 +191,22 @@ class Qwen21Transformer:
         x = F.linear(hidden_states, self.w["img_in.weight"])
         c = self.text_projection(encoder_hidden_states)
         # every image slot stands for 2x2 latent tokens; samples share a layout
-        repeats = torch.where(img_mask, 4, 1)[0]
-        image_pad_mask = torch.repeat_interleave(img_mask[0], repeats)
+        lay = self.layout(img_shapes, img_mask, dev)
+        image_pad_mask, rope, image_ids = lay["pad"], lay["rope"], lay["image_ids"]
         target_tokens = math.prod(img_shapes[0][-1])
         joint = torch.cat([c, c.new_zeros(b, target_tokens // 4, c.shape[2])], dim=1)
-        joint = joint.repeat_interleave(repeats.to(dev), dim=1)
-        joint[:, image_pad_mask.to(dev)] = x
-        rope = rope_table(img_shapes[0], image_pad_mask, self.axes).to(dev)
-        image_ids, target = token_metadata(image_pad_mask.to(dev), img_shapes[0])
+        joint = joint.repeat_interleave(lay["repeats"], dim=1)
+        joint[:, image_pad_mask] = x
         t = timestep.to(torch.bfloat16)
         temb = self.time_embed(torch.cat([t, t.new_zeros(1)]))          # [sampled rows, t = 0]
         modulation = F.linear(F.silu(temb), self.w["modulation.1.weight"])
         key_valid = None
         if encoder_hidden_states_mask is not None:
             key_valid = torch.ones(b, image_pad_mask.shape[0], dtype=torch.bool, device=dev)
-            text_pos = (~image_pad_mask).nonzero(as_tuple=True)[0].to(dev)
+            text_pos = (~lay["pad_cpu"]).nonzero(as_tuple=True)[0].to(dev)
             vlm_text = ~img_mask[0][: encoder_hidden_states_mask.shape[1]]
             key_valid[:, text_pos] = encoder_hidden_states_mask.bool()[:, vlm_text.to(encoder_hidden_states_mask.device)].to(dev)
-        prefix_len = int((~target).sum())
+        prefix_len = lay["prefix_len"]
         scale = F.linear(F.silu(temb), self.w["norm_out.linear.weight"])   # [B + 1, D]
         if kv_cache_mode == "cached":
             h = joint[:, prefix_len:].contiguous()
