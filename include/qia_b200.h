@@ -62,7 +62,7 @@ int qia_ln_mod(const void* x, const void* scale, const void* shift, void* out,
 /* qia_ln_mod followed by MXFP8 quantization of the bf16 result, in one pass.
  * q_values: [padded_rows, dim] e4m3; q_scales: padded_rows*dim/32 bytes.
  * padded_rows = ceil(rows/128)*128; rows past `rows` are written as zeros.
- * Replaces: layer_norm_scale_quantize (src/qwen_image_accel/kernels/epilogue.py:304). */
+ * Replaces: layer_norm_scale_quantize (src/qwen_image_accel/kernels/epilogue.py:76). */
 int qia_ln_mod_quant(const void* x, const void* scale, const void* shift,
                      void* q_values, void* q_scales, int64_t rows, int64_t dim,
                      int64_t rows_per_batch, float eps, void* stream);
@@ -83,7 +83,7 @@ typedef struct qia_ln_mod_quant_problem {
  * run inside the image rows' launch instead of as a separate, latency-bound
  * launch. Each problem's outputs equal qia_ln_mod_quant's.
  * Replaces: the image- and text-stream layer_norm_scale_quantize pair
- * (src/qwen_image_accel/kernels/epilogue.py:304) of norm1 / norm2 of the v1
+ * (src/qwen_image_accel/kernels/epilogue.py:76) of norm1 / norm2 of the v1
  * block (WHL:diffusers/models/transformers/transformer_qwenimage.py:683-717). */
 int qia_ln_mod_quant_grouped(const qia_ln_mod_quant_problem* problems,
                              int count, int64_t dim, float eps, void* stream);
@@ -184,12 +184,12 @@ int qia_qknorm_rope_segment(const void* qkv, int64_t ld_in,
  * ------------------------------------------------------------------------ */
 
 /* SwiGLU: out = bf16(bf16(silu(gate)) * value), silu = div.rn(g, 1 + exp(-g)).
- * Replaces: swiglu (src/qwen_image_accel/kernels/bf16.py:184). */
+ * Replaces: swiglu (src/qwen_image_accel/kernels/bf16.py:27). */
 int qia_swiglu(const void* gate, const void* value, void* out, int64_t n,
                void* stream);
 
 /* SwiGLU + MXFP8 quantization. gate, value: [rows, width], width % 128 == 0.
- * Replaces: swiglu_quantize (src/qwen_image_accel/kernels/epilogue.py:351). */
+ * Replaces: swiglu_quantize (src/qwen_image_accel/kernels/epilogue.py:123). */
 int qia_swiglu_quant(const void* gate, const void* value, void* q_values,
                      void* q_scales, int64_t rows, int64_t width, void* stream);
 
@@ -204,7 +204,7 @@ int qia_gelu_tanh(const void* x, void* out, int64_t n, void* stream);
 
 /* Quantize a bf16 [rows, k] matrix (row stride ld elements) to MXFP8.
  * k % 128 == 0. Outputs as described at the top of this file.
- * Replaces: quantize / _mx_quantize_kernel (src/qwen_image_accel/kernels/mxfp8.py:190-226). */
+ * Replaces: quantize / _mx_quantize_kernel (src/qwen_image_accel/kernels/mxfp8.py:31-67). */
 int qia_mxfp8_quantize(const void* x, int64_t ld, void* q_values, void* q_scales,
                        int64_t rows, int64_t k, void* stream);
 
@@ -215,7 +215,7 @@ int qia_mxfp8_quantize(const void* x, int64_t ld, void* q_values, void* q_scales
  * (the nn.Linear weight layout) + scales; fp32 accumulation; bias: bf16 [n] or
  * NULL. k and n multiples of 128. Rows past m are not written (bf16 outputs).
  * Replaces: MXFP8Linear.matmul / torch._scaled_mm
- * (src/qwen_image_accel/optimizations/mxfp8.py:229-233), with the epilogues
+ * (src/qwen_image_accel/optimizations/mxfp8.py:32-36), with the epilogues
  * of the dual-stream block's linears (WHL:diffusers/models/attention.py:1736,
  * activations.py:81-90, transformer_qwenimage.py:767-774).
  * ------------------------------------------------------------------------ */
@@ -297,7 +297,7 @@ enum qia_epilogue {
  * SMs idle. Each problem's results equal its single-GEMM entry point's.
  * Replaces: the image- and text-stream MXFP8Linear.matmul pair of each
  * projection of the dual-stream block (src/qwen_image_accel/optimizations/
- * mxfp8.py:229-233, called per stream by QwenDoubleStreamAttnProcessor2_0 and
+ * mxfp8.py:32-36, called per stream by QwenDoubleStreamAttnProcessor2_0 and
  * the two MLPs, WHL:diffusers/models/transformers/transformer_qwenimage.py:
  * 540-600, 741-767). */
 int qia_mxfp8_gemm_grouped(int epilogue, const qia_mxfp8_gemm_problem* problems,

@@ -297,7 +297,7 @@ def mx_dequantize(codes: np.ndarray, scales: np.ndarray, rows: int) -> np.ndarra
 
 def mxfp8_gemm(a_codes, a_scales, b_codes, b_scales, m: int, n: int, bias=None) -> np.ndarray:
     """Block-scaled GEMM restated as dequantize -> fp64 matmul -> fp32 [m, n]
-    (reference src/qwen_image_accel/optimizations/mxfp8.py:229-233, torch._scaled_mm)."""
+    (reference src/qwen_image_accel/optimizations/mxfp8.py:32-36, torch._scaled_mm)."""
     a = mx_dequantize(a_codes, a_scales, m).astype(np.float64)
     b = mx_dequantize(b_codes, b_scales, n).astype(np.float64)
     y = a @ b.T
@@ -310,7 +310,15 @@ def mxfp8_gemm(a_codes, a_scales, b_codes, b_scales, m: int, n: int, bias=None) 
 def sage_quant_q(q: np.ndarray, blk: int = 32):
     """Per-(32-token warp block, head) INT8 of Q (SAGE:csrc/fused/fused.cu:64-198
     with BLKQ=128, WARPQ=32): scale = amax/127 (amax floor 1e-7), codes =
-    rint(x * 127/amax) saturated to [-127, 127]. q: fp32 [B, S, H, D]."""
+    rint(x * 127/amax) saturated to [-127, 127]. q: fp32 [B, S, H, D].
+
+    The divides here are IEEE; the reference's extension is built with
+    --use_fast_math, whose approximate divide can land an ulp away, so a code
+    whose x * 127/amax sits within that of a rounding boundary can differ by
+    one (and a scale by an ulp or two). The kernels use the reference's
+    divide and are pinned bit for bit against the built reference on the GPU
+    (tests/test_sage_ref_gpu.py); against this restatement the tests count
+    and bound those differences."""
     b, s, h, d = q.shape
     nblk = (s + blk - 1) // blk
     qp = np.zeros((b, nblk * blk, h, d), np.float32)
@@ -325,8 +333,10 @@ def sage_quant_q(q: np.ndarray, blk: int = 32):
 
 def sage_k_mean(k: np.ndarray) -> np.ndarray:
     """Per-(batch, head, channel) mean of K over the sequence, rounded to bf16
-    (SAGE:sageattention/core.py:773, k.mean(dim=seq) on a bf16 tensor), in the
-    kernel's order: per 32-row tile, sixteen fp32 row-group sums (rows g and
+    (SAGE:sageattention/core.py:773, k.mean(dim=seq) on a bf16 tensor). The
+    reference sums in torch's reduction order; this restates the kernels' own
+    fp32 order (pinned against torch's k.mean on the GPU, where at most 1 in
+    500 elements may land one bf16 ulp apart: tests/test_sage_ref_gpu.py): per 32-row tile, sixteen fp32 row-group sums (rows g and
     g+16 of the tile, in order, added to 0.0); the groups paired (g + (g+1)
     for even g); the eight pair sums added in order to 0.0 (the tile sum);
     the tile sums as eight interleaved sub-sums (tiles j, j+8, j+16, ... in

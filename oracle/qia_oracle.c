@@ -78,7 +78,7 @@ uint8_t oracle_e4m3(float x) {
 }
 
 /* ---------------------------------------------------------------- MXFP8 */
-/* reference src/qwen_image_accel/kernels/mxfp8.py:201-209 */
+/* reference src/qwen_image_accel/kernels/mxfp8.py:46-50 */
 static inline int mx_exponent(float amax) {
   uint32_t b = bits_f(amax);
   int e = (int)((b >> 23) & 0xffu) - 8 + (((b & 0x7fffffu) > 6291456u) ? 1 : 0);
@@ -86,7 +86,7 @@ static inline int mx_exponent(float amax) {
   if (e > 254) e = 254;
   return amax == 0.0f ? 0 : e;
 }
-/* reference src/qwen_image_accel/kernels/mxfp8.py:212-215 */
+/* reference src/qwen_image_accel/kernels/mxfp8.py:53-56 */
 static inline int64_t mx_scale_offset(int64_t row, int64_t kb, int64_t kb_tiles) {
   return ((row >> 7) * kb_tiles + (kb >> 2)) * 512 + (row & 31) * 16 + ((row >> 5) & 3) * 4 + (kb & 3);
 }
@@ -101,7 +101,7 @@ static void mx_block(const float* y, uint8_t* qv, uint8_t* qs, int64_t row, int6
   qs[mx_scale_offset(row, kb, k >> 7)] = (uint8_t)e;
 }
 
-/* reference src/qwen_image_accel/kernels/mxfp8.py:190-226 (rows padded to 128) */
+/* reference src/qwen_image_accel/kernels/mxfp8.py:31-67 (rows padded to 128) */
 void oracle_mx_quantize(const uint16_t* x, int64_t ld, uint8_t* qv, uint8_t* qs, int64_t rows, int64_t k) {
   int64_t padded = (rows + 127) / 128 * 128;
   float y[32];
@@ -192,7 +192,7 @@ void oracle_ln_mod(const uint16_t* x, const uint16_t* scale, const uint16_t* shi
   free(y);
 }
 
-/* reference kernels/epilogue.py:252-301: LN-mod then the quantizer on the bf16 result */
+/* reference kernels/epilogue.py:24-73: LN-mod then the quantizer on the bf16 result */
 void oracle_ln_mod_quant(const uint16_t* x, const uint16_t* scale, const uint16_t* shift, uint8_t* qv, uint8_t* qs,
                          int64_t rows, int dim, int64_t rows_per_batch, float eps) {
   int64_t padded = (rows + 127) / 128 * 128;
@@ -341,7 +341,7 @@ void oracle_swiglu(const uint16_t* g, const uint16_t* v, uint16_t* out, int64_t 
   for (int64_t i = 0; i < n; ++i) out[i] = f2bf(silu_ref(bf2f(g[i])) * bf2f(v[i]));
 }
 
-/* reference kernels/epilogue.py:324-348 */
+/* reference kernels/epilogue.py:96-120 */
 void oracle_swiglu_quant(const uint16_t* g, const uint16_t* v, uint8_t* qv, uint8_t* qs, int64_t rows,
                          int64_t width) {
   uint16_t* tmp = (uint16_t*)malloc(sizeof(uint16_t) * rows * width);

@@ -1,6 +1,6 @@
 // MXFP8 activation quantizer, SwiGLU (+ quantize) and GELU-tanh.
 //
-// Quantizer numerics (reference src/qwen_image_accel/kernels/mxfp8.py:190-215):
+// Quantizer numerics (reference src/qwen_image_accel/kernels/mxfp8.py:31-56):
 // per 1x32 block along K, E8M0 exponent from the fp32 bits of the block amax,
 // codes = E4M3(x * 2^(127-e)) with round-to-nearest-even and saturation, and the
 // scale byte stored in the 128x4 blocked layout. Rows past `rows` (padding up

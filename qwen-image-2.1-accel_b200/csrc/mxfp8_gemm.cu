@@ -4,7 +4,7 @@
 //   scales per 1x32 block along K in the 128x4 blocked layout.
 //
 // Replaces torch._scaled_mm in MXFP8Linear.matmul (reference
-// src/qwen_image_accel/optimizations/mxfp8.py:229-233) and adds the epilogues
+// src/qwen_image_accel/optimizations/mxfp8.py:32-36) and adds the epilogues
 // the dual-stream block needs (bias, GELU-tanh + MXFP8 requantization, gate +
 // residual).
 //

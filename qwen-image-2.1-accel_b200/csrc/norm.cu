@@ -10,7 +10,7 @@
 //  * Every eager bf16 tensor boundary is kept as a bf16 rounding point
 //    (normalised, *scale, +shift, *gate, +residual).
 //  * The MXFP8 epilogue quantizes the bf16 result exactly as the standalone
-//    quantizer does (reference kernels/epilogue.py:252-301).
+//    quantizer does (reference kernels/epilogue.py:24-73).
 //
 // HBM layout: rows are contiguous [rows, dim] bf16; one 128-thread CTA per row
 // keeps the row in registers (dim/128 fp32 per thread), so x is read once.

@@ -102,7 +102,7 @@ __device__ __forceinline__ uint32_t cvt_e4m3x4(float a, float b, float c, float 
 }
 
 // MXFP8 (OCP MX, E8M0 scale, 32-element blocks) exponent selection used by the
-// reference quantizer (src/qwen_image_accel/kernels/mxfp8.py:201-209): the
+// reference quantizer (src/qwen_image_accel/kernels/mxfp8.py:46-50): the
 // smallest power of two 2^(e-127) with amax / 2^(e-127) <= 448, read from the
 // fp32 bits of amax; 0 when the block is all zeros; clamped to [0, 254].
 __device__ __forceinline__ int mx_exponent(float amax) {
@@ -118,7 +118,7 @@ __device__ __forceinline__ float mx_inverse_scale(int e) {
 }
 
 // Byte offset of the E8M0 scale of (row, k-block) in the 128x4 blocked layout
-// consumed by block-scaled tensor-core MMAs (reference kernels/mxfp8.py:212-215):
+// consumed by block-scaled tensor-core MMAs (reference kernels/mxfp8.py:53-56):
 // 512-byte tiles of 128 rows x 4 k-blocks, ordered (row % 32, row / 32 % 4, kb % 4).
 __host__ __device__ __forceinline__ int64_t mx_scale_offset(int64_t row, int64_t kb, int64_t kb_tiles) {
   return ((row >> 7) * kb_tiles + (kb >> 2)) * 512 + (row & 31) * 16 + ((row >> 5) & 3) * 4 + (kb & 3);

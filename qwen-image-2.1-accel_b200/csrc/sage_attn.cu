@@ -11,6 +11,12 @@
 //    (SAGE:csrc/fused/fused.cu:140-184);
 //  * V FP8 E4M3 per (batch, head, channel): scale = amax/448
 //    (SAGE:csrc/fused/fused.cu:316-427);
+//  * the four divides (amax/127, 127/amax, amax/448, 448/amax) are
+//    __fdividef: the reference extension is built with --use_fast_math
+//    (SAGE:setup.py:53-61), under which its `/` is that intrinsic (the two
+//    agree bit for bit on 4M quantizer-shaped divisions on a B200, and the
+//    IEEE divide differs in ~30 % of them), so codes and scales match the
+//    built reference bit for bit;
 //  * S = int32 Q.K^T, s = S * (sm_scale*log2e) * (q_scale*k_scale); running
 //    max m offset by log2(448) so P = 2^(s - m) lies in [0, 448]
 //    (SAGE:csrc/qattn/attn_utils.cuh:353-440); P rounded to E4M3 for the
@@ -70,7 +76,7 @@ constexpr float kFp8Offset = 8.807f;  // log2(448): P = 2^(s - m) <= 448
 //     codes of k - k_mean in one 64-row block, or V E4M3 codes of
 //     v * 448/amax, staged the same way (four passes).
 // INT8 blocks: scale = amax/127 (amax floored at 1e-7), codes =
-// rint_sat(x * 127/amax); rows past S are zeros. The rows come from a source:
+// rint_sat(x * 127/amax), both divides __fdividef; rows past S are zeros. The rows come from a source:
 // strided [B, S, H, 128] bf16 tensors (PlainQKV), or the fused q|k|v
 // projection outputs of the two streams of the joint [text, image] sequence
 // (JointQKV), whose Q and K are normalised (per-head RMSNorm) and rotated
@@ -321,8 +327,8 @@ __global__ void __launch_bounds__(256, 4) sage_quant_q_stats_kernel(Src src, int
   const float4 a = *reinterpret_cast<const float4*>(&s_wmax[0]);
   const float4 c = *reinterpret_cast<const float4*>(&s_wmax[4]);
   const float bm = fmaxf(fmaxf(fmaxf(a.x, a.y), fmaxf(a.z, a.w)), fmaxf(fmaxf(c.x, c.y), fmaxf(c.z, c.w)));
-  if (t == 0) q_scale[int64_t(bh) * (Sq_pad / 32) + tile] = __fdiv_rn(bm, 127.0f);
-  const float inv = __fdiv_rn(127.0f, bm);
+  if (t == 0) q_scale[int64_t(bh) * (Sq_pad / 32) + tile] = __fdividef(bm, 127.0f);
+  const float inv = __fdividef(127.0f, bm);
   const float none[8] = {};
   int8_t* dst = q8 + (int64_t(bh) * Sq_pad + tile * kQBlock) * kD + cg * 8;
 #pragma unroll
@@ -376,8 +382,8 @@ __global__ void __launch_bounds__(256) sage_quant_finalize_kernel(const float* _
     float m = 0.0f;
 #pragma unroll
     for (int j = 0; j < 8; ++j) m = fmaxf(m, s_max[j][ch]);
-    v_scale[int64_t(bh) * kD + d] = m / 448.0f;
-    v_recp[int64_t(bh) * kD + d] = m > 0.0f ? 448.0f / m : 0.0f;
+    v_scale[int64_t(bh) * kD + d] = __fdividef(m, 448.0f);
+    v_recp[int64_t(bh) * kD + d] = m > 0.0f ? __fdividef(448.0f, m) : 0.0f;
   }
 }
 
@@ -430,8 +436,8 @@ __global__ void __launch_bounds__(256, 4) sage_quant_kv_kernel(Src src, int S, i
     const float4 a = *reinterpret_cast<const float4*>(&s_wmax[0]);
     const float4 c = *reinterpret_cast<const float4*>(&s_wmax[4]);
     const float bm = fmaxf(fmaxf(fmaxf(a.x, a.y), fmaxf(a.z, a.w)), fmaxf(fmaxf(c.x, c.y), fmaxf(c.z, c.w)));
-    if (t == 0) k_scale[int64_t(bh) * (S_pad / 64) + tile] = __fdiv_rn(bm, 127.0f);
-    const float inv = __fdiv_rn(127.0f, bm);
+    if (t == 0) k_scale[int64_t(bh) * (S_pad / 64) + tile] = __fdividef(bm, 127.0f);
+    const float inv = __fdividef(127.0f, bm);
     int8_t* dst = k8 + (int64_t(bh) * S_pad + tile * kQTile) * kD + cg * 8;
 #pragma unroll
     for (int p = 0; p < 4; ++p) {

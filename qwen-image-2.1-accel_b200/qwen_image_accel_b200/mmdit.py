@@ -23,7 +23,7 @@ The prologue/epilogue layers outside the blocks (img_in, txt_norm/txt_in, the
 timestep embedding, the AdaLN modulation linears, norm_out's linear and
 proj_out) stay BF16 torch ops, as in the reference, where
 quantize_transformer never touches them
-(src/qwen_image_accel/optimizations/mxfp8.py:263-288). The modulation of all
+(src/qwen_image_accel/optimizations/mxfp8.py:66-91). The modulation of all
 blocks is one stacked GEMM per step.
 
 Profiles (flags of profiles.PROFILES): quantized -> MXFP8 block GEMMs, else
@@ -449,6 +449,11 @@ class MMDiT:
                 ev = torch.cuda.Event()
                 ev.record(side)
                 events.append(ev)
+        # x and buf were allocated on the main stream and are read / written by
+        # the side stream's launches: without these the caching allocator may
+        # hand their blocks to main-stream tensors while those launches run.
+        x.record_stream(side)
+        buf.record_stream(side)
         v = buf.view(L, 2, 6, D)
         mods = [[tuple(v[i, s, j].view(1, 1, D) for j in range(6)) for s in range(2)] for i in range(L)]
         return mods, events

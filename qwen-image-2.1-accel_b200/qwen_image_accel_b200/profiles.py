@@ -2,6 +2,9 @@
 
 Mirrors src/qwen_image_accel/profiles.py: the same PROFILES mapping, Profile
 fields and retired-name errors, so callers select the same behaviour by name.
+The profile names, flags and retired-name table are the reference's interface
+(Qwen-Image-2.1-Accel, Copyright (c) 2026 Devin Lai, CPAL-1.0; see its LICENSE
+and NOTICE for the attribution terms); the module here is written anew.
 """
 from dataclasses import dataclass
 from types import MappingProxyType

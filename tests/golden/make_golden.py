@@ -4,7 +4,7 @@ Runs only where the reference checkout is mounted (it is read, never
 modified). Sources of truth, per fixture:
 
 * mxfp8_quantize.npz -- E8M0 scales from the reference's own Triton kernel
-  `_mx_quantize_kernel` (src/qwen_image_accel/kernels/mxfp8.py:190) run by the
+  `_mx_quantize_kernel` (src/qwen_image_accel/kernels/mxfp8.py:31) run by the
   Triton interpreter on the CPU; codes from the reference's known-answer rule
   (tests/gpu/check_mxfp8.py:41-51): x * 2^(127-e) cast with torch's
   float8_e4m3fn. (The interpreter's own fp8/bf16 casts truncate, so its codes
@@ -32,7 +32,7 @@ modified). Sources of truth, per fixture:
   the package's seeded recipe (mmdit.init_parameter, torch CPU generator),
   seeded inputs; plus its RoPE tables and timestep embedding input.
 
-Usage: python tests/golden/make_golden.py [--reference /path/to/checkout]
+Usage: python tests/golden/make_golden.py --reference /path/to/checkout  (or QIA_REFERENCE=...)
 """
 from __future__ import annotations
 
@@ -321,8 +321,11 @@ def make_model21(reference: Path):
 
 if __name__ == "__main__":
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=os.environ.get("QIA_REFERENCE"),
+                    help="reference checkout (read only); or set QIA_REFERENCE")
     args = ap.parse_args()
+    if not args.reference:
+        ap.error("--reference (or QIA_REFERENCE) is required")
     ref = Path(args.reference)
     make_mxfp8(ref)   # first: the interpreter flag must precede the first triton import
     make_eager(ref)
