@@ -1,24 +1,39 @@
-"""Benchmark: ms per MMDiT denoise step (1024^2) on B200.
+"""Benchmark: ms per MMDiT denoise step at 2048^2 and 1024^2 on B200, with the
+kernels' roofline fractions (BASELINE.json metric and configs).
 
-One step = the 60-block dual-stream MMDiT forward on the CFG batch of 2
-(4096 image + 256 text tokens per sample) through the `mxfp8_sage` profile,
-plus the CFG combine and the flow-matching Euler update. Random-init weights
-(~N(0, 0.02)) and seeded synthetic latents / text embeddings of the BASELINE
-shapes stand in for the checkpoint and the prompts (no network).
+Default line (`python bench.py --gpus N`): BASELINE config 5, the 60-block
+dual-stream MMDiT denoise step at 2048^2 (16384 image + 256 text tokens per
+CFG row) through profile `mxfp8_sage` (blocks 0 and 31 in bf16, as the
+reference's default skip list), plus the CFG combine and the flow-match Euler
+update. N = 1: the CFG batch of 2 on one GPU. N >= 2 (torchrun): CFG split x
+Ulysses N/2 -- each CFG half a Ulysses group over NCCL (all-to-all Q/K/V and O
+per block, one velocity exchange per step); strong scaling (the same step at
+every N). At N = 1 the same line carries config 4 (the 1024^2 step, its
+FFN-up GEMM roofline and CPU baseline) and the kernel measurements of configs
+1-3 (AdaLN op vs HBM, the MXFP8 GEMM sweep beside torch._scaled_mm, the joint
+attention beside the reference's SageAttention built from its sources).
+Random-init weights (~N(0, 0.02)) and seeded synthetic latents / text
+embeddings of the BASELINE shapes stand in for the checkpoint and prompts.
 
-Timing: W untimed warm-up steps, then K steps replayed from one CUDA graph of
-the step, bracketed by barrier + synchronize, timed with CUDA events on the
-launching stream; max over ranks. The working set (27 GB of weights streamed
-per step) is far larger than L2, so no flush is needed between steps.
+Timing: W warm-up steps, the step captured once in a CUDA graph through the
+product API (optimizations/cuda_graph.DenoiseStepGraph), K replays bracketed
+by barrier + synchronize and timed with CUDA events on the launching stream,
+max over ranks. The step streams ~27 GB of weights (far above the 126 MB L2),
+so no flush is needed between steps; the kernel-level measurements of configs
+1-3 flush L2 (a 256 MiB write) before every timed launch. `e2e`: K steps of
+DenoiseStepGraph.step() with the latents and both prompt embeddings copied in
+from pinned host memory and the new latents copied back, every step.
 
-N > 1: replicas of the 1024^2 step (one per GPU, no collective on the data
-path), weak scaling; `value` = whole-job ms per step = max elapsed / (K * N).
-`--config c5`: the 2048^2 step, on N >= 2 GPUs split into CFG halves of
-Ulysses groups (NCCL all-to-all); strong scaling, `value` = ms per step.
+`--impl reference`: the reference's eager CPU path -- the Diffusers
+QwenImageTransformer2DModel of the pinned wheel (baseline/_ref) in bf16 on
+this host's cores, one whole sampled forward per step (img_in, text norm and
+projection, timestep embedding, one dual-stream block, norm_out, proj_out,
+then the CFG combine and the Euler update) at a bounded token count, scaled
+to the configured step by its FLOP ratio.
 
-`--impl reference` times the reference's eager CPU path (oracle/mmdit_cpu.py,
-a restatement of the Diffusers block) on this host's cores: one full-size
-block per step sample, scaled by 60 blocks.
+Other configurations: `--config c4` (1024^2 only; replicas for N > 1),
+`prefill` (the 2.1 block-causal prefill attention), `q21` (the Qwen-Image 2.1
+cached-decode step), and `--profile-case` small fixed cases for ncu.
 """
 from __future__ import annotations
 
@@ -38,10 +53,22 @@ for _p in (ROOT, ROOT / "qwen-image-2.1-accel_b200"):
 
 import torch  # noqa: E402
 
-METRIC = "ms per MMDiT denoise step at 1024^2 (60 blocks, CFG batch 2)"
-BLOCKS, HEADS, TXT_LEN, TXT_DIM = 60, 24, 256, 3584
+METRIC = "ms per MMDiT denoise step at 2048^2 (60 blocks, CFG batch 2; config 4 = 1024^2 alongside)"
+METRIC_C4 = "ms per MMDiT denoise step at 1024^2 (60 blocks, CFG batch 2)"
+BLOCKS, HEADS, TXT_LEN, TXT_DIM, DIM, FFN = 60, 24, 256, 3584, 3072, 12288
 GRID = (1, 64, 64)                   # 1024^2 latent 16ch x 128 x 128, 2x2 patches
 IMG_LEN = GRID[0] * GRID[1] * GRID[2]
+GRID_C5 = (1, 128, 128)              # 2048^2 latent 16ch x 256 x 256, 2x2 patches
+IMG_LEN_C5 = GRID_C5[0] * GRID_C5[1] * GRID_C5[2]
+SIGMAS = (1.0, 0.975)
+
+
+def step_flops(img_len: int, txt_len: int = TXT_LEN, blocks: int = BLOCKS) -> float:
+    """Algorithmic FLOPs of one CFG-batch-2 step: per block and CFG row,
+    2 T (4 D^2 + 2 D F) for the linears of both streams over T = image + text
+    tokens, and 4 T^2 D for the joint attention."""
+    t = img_len + txt_len
+    return blocks * 2 * (2.0 * t * (4 * DIM * DIM + 2 * DIM * FFN) + 4.0 * t * t * DIM)
 
 
 def log(*a):
@@ -56,11 +83,19 @@ def load_peaks():
     return 6650.0, 1590.0, "fallback"
 
 
+def max_over_ranks(vals, world, device):
+    if world == 1:
+        return list(vals)
+    t = torch.tensor(list(vals), device=device, dtype=torch.float64)
+    torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    return t.tolist()
+
+
 # ----------------------------------------------------------------------------- clocks
 class ClockSampler:
     def __init__(self, gpu_index: int):
         self.proc = None
-        self.path = Path(f"/tmp/qia_clocks_{os.getpid()}.csv")
+        self.path = Path(f"/tmp/qia_clocks_{os.getpid()}_{gpu_index}.csv")
         q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
@@ -101,274 +136,175 @@ class ClockSampler:
         return out
 
 
-# ----------------------------------------------------------------------------- reference arm
-def cpu_block_sample(repeats: int = 1):
-    """Time one full-size v1 block (B=2 CFG, 4096+256 tokens) of the eager CPU
-    restatement on this host; returns (ms per block, threads)."""
-    from oracle import mmdit_cpu
-    from qwen_image_accel_b200.mmdit import MMDiTConfig, init_parameter, parameter_shapes, rope_tables
+# ----------------------------------------------------------------------------- reference arm (CPU)
+REF_SAMPLE_IMG, REF_SAMPLE_TXT = 1024, 256     # tokens of one sampled forward (B = 2, one block)
+_CPU_MODEL: dict = {}
+
+
+def cpu_reference_sample():
+    """One bounded sample of the reference's eager CPU path: the Diffusers v1
+    QwenImageTransformer2DModel (pinned wheel) with one dual-stream block at
+    D 3072 / 24 heads / text 3584, bf16, the CFG batch of 2 with 1024 image +
+    256 text tokens per row, then the pipeline's CFG combine and the Euler
+    step. Returns (ms, threads, sample FLOPs)."""
+    from oracle import diffusers_ref
+    from qwen_image_accel_b200.mmdit import MMDiTConfig, init_parameter, parameter_shapes
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
-    cfg = MMDiTConfig(num_layers=1)
-    shapes = parameter_shapes(cfg)
-    p = {n: init_parameter(n, s, seed=42) for n, s in shapes.items() if n.startswith("transformer_blocks.0.")}
+    model = _CPU_MODEL.get("m")
+    if model is None:
+        tq = diffusers_ref.qwen_v1()
+        cfg = MMDiTConfig(num_layers=1)
+        model = tq.QwenImageTransformer2DModel(patch_size=2, in_channels=64, out_channels=16, num_layers=1,
+                                               attention_head_dim=128, num_attention_heads=HEADS,
+                                               joint_attention_dim=TXT_DIM, axes_dims_rope=(16, 56, 56))
+        model = model.to(torch.bfloat16)
+        shapes = parameter_shapes(cfg)
+        model.load_state_dict({n: init_parameter(n, shapes[n], 42) for n in model.state_dict()})
+        model.eval()
+        _CPU_MODEL["m"] = model
     g = torch.Generator().manual_seed(42)
-    D = cfg.dim
-    x = torch.randn(2, IMG_LEN, D, generator=g).to(torch.bfloat16)
-    c = torch.randn(2, TXT_LEN, D, generator=g).to(torch.bfloat16)
-    temb = torch.randn(2, D, generator=g).to(torch.bfloat16)
-    img_f, txt_f = rope_tables(*GRID, TXT_LEN)
-    times = []
-    with torch.no_grad():
-        for _ in range(repeats):
-            t0 = time.perf_counter()
-            mmdit_cpu.block_forward(p, "transformer_blocks.0.", x, c, temb, img_f, txt_f, HEADS)
-            times.append((time.perf_counter() - t0) * 1e3)
-    return min(times), threads
+    side = int(REF_SAMPLE_IMG ** 0.5)
+    lat = torch.randn(1, REF_SAMPLE_IMG, 64, generator=g).to(torch.bfloat16)
+    enc = torch.randn(2, REF_SAMPLE_TXT, TXT_DIM, generator=g).to(torch.bfloat16)
+    t = torch.full((2,), SIGMAS[0], dtype=torch.bfloat16)
+
+    def run():
+        with torch.no_grad():
+            v = model(hidden_states=torch.cat([lat, lat]), encoder_hidden_states=enc, timestep=t,
+                      img_shapes=[(1, side, side)] * 2, return_dict=False)[0]
+            cond, neg = v[:1], v[1:]
+            comb = neg + 4.0 * (cond - neg)
+            noise = comb * (torch.norm(cond, dim=-1, keepdim=True) / torch.norm(comb, dim=-1, keepdim=True))
+            return (lat.float() + (SIGMAS[1] - SIGMAS[0]) * noise).to(lat.dtype)
+
+    run()
+    t0 = time.perf_counter()
+    run()
+    ms = (time.perf_counter() - t0) * 1e3
+    return ms, threads, step_flops(REF_SAMPLE_IMG, REF_SAMPLE_TXT, blocks=1)
 
 
-def reference_arm(args, rank):
+def reference_arm(args, rank, world):
+    """--impl reference: rank 0 times the reference's eager CPU path (see
+    cpu_reference_sample) once per step and scales each sample to the
+    configured step by FLOPs; the other ranks exit without work."""
     if rank != 0:
         return
-    log("reference arm: eager CPU restatement of the v1 block, one block per step sample")
-    vals = []
+    from oracle import diffusers_ref
+    img = IMG_LEN if args.config == "c4" else IMG_LEN_C5
+    metric = METRIC_C4 if args.config == "c4" else METRIC
+    workload = ("config4: 60-block dual-stream MMDiT, 1024^2 (4096 img + 256 txt tokens), CFG batch 2"
+                if args.config == "c4" else
+                "config5: 60-block dual-stream MMDiT, 2048^2 (16384 img + 256 txt tokens), CFG batch 2")
+    if not diffusers_ref.available():
+        print(json.dumps({"impl": "reference", "unavailable": "the pinned Diffusers wheel is not installed under "
+                                                               "baseline/_ref"}), flush=True)
+        return
+    log("reference arm: the Diffusers v1 MMDiT of the pinned wheel, eager bf16 on the host CPU")
+    target = step_flops(img)
+    vals, sample_ms = [], []
+    threads = 1
     for i in range(args.warmup + args.steps):
-        ms_block, threads = cpu_block_sample(1)
+        ms, threads, flops = cpu_reference_sample()
         if i >= args.warmup:
-            vals.append(ms_block * BLOCKS)
+            sample_ms.append(ms)
+            vals.append(ms * target / flops)
     v = statistics.mean(vals)
-    line = {"impl": "reference", "metric": METRIC, "value": round(v, 1), "unit": "ms/step", "n_gpus": args.gpus,
+    sample = (f"one eager forward of the Diffusers model with 1 of 60 blocks (B=2 CFG rows, {REF_SAMPLE_IMG} img + "
+              f"{REF_SAMPLE_TXT} txt tokens) + CFG combine + Euler step per step, mean {statistics.mean(sample_ms):.0f}"
+              f" ms, scaled by the FLOP ratio {target / step_flops(REF_SAMPLE_IMG, REF_SAMPLE_TXT, 1):.0f}x "
+              "(extrapolated)")
+    line = {"impl": "reference", "metric": metric, "value": round(v, 1), "unit": "ms/step", "n_gpus": args.gpus,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(v, 1), "higher_is_better": False,
-            "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": "config4: 60-block dual-stream MMDiT, 1024^2 (4096 img + 256 txt tokens), "
-                                   "CFG batch 2", "global_batch": 2, "seq_len": IMG_LEN + TXT_LEN},
-            "cpu_baseline": {"value": round(v, 1), "unit": "ms/step", "cores": threads, "kind": "port",
-                             "sample": "one full-size block (B=2, 4352 tokens) of the eager bf16 CPU "
-                                       "restatement per step, x60 blocks"},
+            "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": workload, "global_batch": 2, "seq_len": img + TXT_LEN},
+            "cpu_baseline": {"value": round(v, 1), "unit": "ms/step", "cores": threads, "kind": "reference",
+                             "sample": sample},
             "e2e": {"value": round(v, 1), "unit": "ms/step", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
 
-# ----------------------------------------------------------------------------- our arm
+# ----------------------------------------------------------------------------- kernel timing helpers
+class L2Flush:
+    """Writes 256 MiB (twice the 126 MB L2) so the next launch reads cold."""
+
+    def __init__(self, device):
+        self.buf = torch.empty(256 << 20, dtype=torch.uint8, device=device)
+
+    def __call__(self):
+        self.buf.fill_(1)
+
+
+def time_launches(fn, flush: L2Flush, n: int = 20, warmup: int = 3) -> float:
+    """Mean device time (ms) of fn() over n launches, each preceded (outside
+    its event pair) by an L2 flush; CUDA events on the current stream."""
+    for _ in range(warmup):
+        fn()
+    st = torch.cuda.current_stream()
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(n)]
+    for e0, e1 in evs:
+        flush()
+        e0.record(st)
+        fn()
+        e1.record(st)
+    torch.cuda.synchronize()
+    return statistics.mean(e0.elapsed_time(e1) for e0, e1 in evs)
+
+
+def roofline_entry(kernel, achieved, peak, unit, bound, peak_kind, traffic=None, **extra):
+    d = {"bound": bound, "kernel": kernel, "achieved": round(achieved, 1), "peak": round(peak, 1), "unit": unit,
+         "frac": round(achieved / peak, 3), "traffic": traffic, "peak_kind": peak_kind}
+    d.update(extra)
+    return d
+
+
+def ncu_traffic(kernel: str, shape: str):
+    """dram__bytes_read.sum + dram__bytes_write.sum of one launch from the
+    committed ncu record (profiles/roofline_traffic.json, written from the
+    capture named there), or None when no capture of this kernel and shape
+    exists."""
+    p = ROOT / "profiles" / "roofline_traffic.json"
+    if not p.exists():
+        return None, None
+    rec = json.loads(p.read_text()).get(kernel)
+    if not rec or rec.get("shape") != shape:
+        return None, None
+    return int(rec["dram_read_bytes"]) + int(rec["dram_write_bytes"]), rec.get("source")
+
+
+# ----------------------------------------------------------------------------- our arm: the denoise step
 def build_model(device):
     from qwen_image_accel_b200.mmdit import MMDiT, MMDiTConfig, random_parameters
     cfg = MMDiTConfig(num_layers=BLOCKS)
     t0 = time.time()
     model = MMDiT(cfg, random_parameters(cfg, 42, device), device=device, profile="mxfp8_sage")
     torch.cuda.synchronize()
-    log(f"model built in {time.time() - t0:.1f} s, {torch.cuda.memory_allocated() / 2**30:.1f} GiB allocated")
+    log(f"model built in {time.time() - t0:.1f} s, {torch.cuda.memory_allocated() / 2**30:.1f} GiB allocated; "
+        f"bf16 blocks {sorted(model.skip_blocks)}")
     return model, cfg
 
 
-# dram__bytes_read.sum + dram__bytes_write.sum of one launch of this GEMM shape
-# (M=8192, 3072 -> 12288, GELU+MXFP8 epilogue) from `ncu --set full` on a B200:
-# 65.55 MB + 83.21 MB; algorithmic bytes are 168.7 MB (operands, scales, output).
-FFN_UP_TRAFFIC_BYTES = 148_761_344
-
-
-def gemm_roofline(model, device, peak_tflops_fp8, launches=20):
-    """Live timing of the dominant kernel class -- the FFN up-projection GEMM
-    (M = 8192 image rows, 3072 -> 12288, bias + GELU + MXFP8 requant epilogue),
-    exactly as launched in the step -- with CUDA events on its stream."""
-    from qwen_image_accel_b200.kernels.mxfp8 import quantize
-    blk = model.blocks[0]
-    g = torch.Generator(device=device).manual_seed(1)
-    x = torch.randn(2 * IMG_LEN, model.cfg.dim, device=device, dtype=torch.bfloat16, generator=g)
-    a = quantize(x)
-    for _ in range(3):
-        blk.img_up.mx.matmul_gelu_quantize(a)
-    st = torch.cuda.current_stream()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    torch.cuda.synchronize()
-    e0.record(st)
-    for _ in range(launches):
-        blk.img_up.mx.matmul_gelu_quantize(a)
-    e1.record(st)
-    torch.cuda.synchronize()
-    ms = e0.elapsed_time(e1) / launches
-    m, n, k = 2 * IMG_LEN, model.cfg.ffn_dim, model.cfg.dim
-    tflops = 2.0 * m * n * k / (ms * 1e-3) / 1e12
-    # library comparison on the same operands: cuBLASLt MXFP8 via torch._scaled_mm
-    lib_tflops = None
-    try:
-        w, ws = blk.img_up.mx.weight_fp8, blk.img_up.mx.weight_scale
-        for _ in range(3):
-            torch._scaled_mm(a.values, w, scale_a=a.scales, scale_b=ws, out_dtype=torch.bfloat16)
-        torch.cuda.synchronize()
-        e0.record(st)
-        for _ in range(launches):
-            torch._scaled_mm(a.values, w, scale_a=a.scales, scale_b=ws, out_dtype=torch.bfloat16)
-        e1.record(st)
-        torch.cuda.synchronize()
-        lib_tflops = 2.0 * m * n * k / (e0.elapsed_time(e1) / launches * 1e-3) / 1e12
-    except Exception as exc:  # noqa: BLE001
-        log(f"torch._scaled_mm comparison unavailable: {exc!r}")
-    return {"bound": "tensor", "kernel": "mxfp8_gemm_kernel (FFN up, M=8192 N=12288 K=3072, GELU+requant)",
-            "achieved": round(tflops, 1), "peak": round(peak_tflops_fp8, 1), "unit": "TFLOP/s",
-            "frac": round(tflops / peak_tflops_fp8, 3), "traffic": FFN_UP_TRAFFIC_BYTES,
-            "traffic_unit": "bytes per launch (dram read + write, one ncu capture of this shape: "
-                            "bench.py --profile-case ffn_up)", "ms_per_launch": round(ms, 4),
-            "cublaslt_mxfp8_tflops_same_operands": None if lib_tflops is None else round(lib_tflops, 1)}
-
-
-def our_arm(args, rank, world, local_rank):
+def time_step(model, grid, args, rank, world, device, plan=None):
+    """The denoise step through DenoiseStepGraph: device-timed K replays with
+    inputs resident, then K end-to-end steps from pinned host buffers."""
     from qwen_image_accel_b200 import _lib
-    device = torch.device("cuda", local_rank)
-    torch.cuda.set_device(device)
-    hbm, bf16_tf, peak_kind = load_peaks()
-    fp8_peak = 2.0 * bf16_tf   # FP8 tensor rate = 2x the bf16 rate; denominator = 2x measured cuBLAS bf16
-    model, cfg = build_model(device)
-    g = torch.Generator(device=device).manual_seed(42)
-    latents = torch.randn(1, IMG_LEN, 64, device=device, dtype=torch.bfloat16, generator=g)
-    pe = torch.randn(1, TXT_LEN, TXT_DIM, device=device, dtype=torch.bfloat16, generator=g)
-    ne = torch.randn(1, TXT_LEN, TXT_DIM, device=device, dtype=torch.bfloat16, generator=g)
-    sig, sig_next = 1.0, 0.975
-
-    static_in = latents.clone()
-    static_pe, static_ne = pe.clone(), ne.clone()
-
-    def step():
-        return model.denoise_step(static_in, static_pe, static_ne, sig, sig_next, GRID)
-
-    # warm-up (eager), then capture the step once
-    _lib.launch_count = 0
-    for _ in range(max(args.warmup, 3)):
-        out = step()
-        static_in.copy_(out)
-    torch.cuda.synchronize()
-    launches_per_step = _lib.launch_count // max(args.warmup, 3)
-    graph = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(graph):
-        static_out = step()
-    for _ in range(2):
-        graph.replay()
-    torch.cuda.synchronize()
-    if world > 1:
-        torch.distributed.barrier()
-
-    # ---------------------------------------------------------------- device-timed K steps
-    sampler = ClockSampler(torch.cuda.current_device()) if rank == 0 else None
-    st = torch.cuda.current_stream()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    if world > 1:
-        torch.distributed.barrier()
-    torch.cuda.synchronize()
-    e0.record(st)
-    for _ in range(args.steps):
-        graph.replay()
-        static_in.copy_(static_out)
-    e1.record(st)
-    torch.cuda.synchronize()
-    if world > 1:
-        torch.distributed.barrier()
-    elapsed = e0.elapsed_time(e1)
-    clocks = sampler.stop() if sampler else None
-    if world > 1:
-        t = torch.tensor([elapsed], device=device)
-        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-        elapsed = t.item()
-    ms_step = elapsed / args.steps
-
-    # ---------------------------------------------------------------- end to end through the API
-    host_lat = torch.empty_like(latents, device="cpu").pin_memory()
-    host_lat.copy_(latents.cpu())
-    host_pe = pe.cpu().pin_memory()
-    host_ne = ne.cpu().pin_memory()
-    host_out = torch.empty_like(host_lat).pin_memory()
-    torch.cuda.synchronize()
-    e0.record(st)
-    for _ in range(args.steps):
-        static_in.copy_(host_lat, non_blocking=True)
-        static_pe.copy_(host_pe, non_blocking=True)
-        static_ne.copy_(host_ne, non_blocking=True)
-        graph.replay()
-        host_out.copy_(static_out, non_blocking=True)
-    e1.record(st)
-    torch.cuda.synchronize()
-    e2e_ms = e0.elapsed_time(e1) / args.steps
-    if world > 1:
-        t = torch.tensor([e2e_ms], device=device)
-        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-        e2e_ms = t.item()
-    h2d = host_lat.numel() * 2 + host_pe.numel() * 2 + host_ne.numel() * 2
-    d2h = host_out.numel() * 2
-
-    roof = gemm_roofline(model, device, fp8_peak) if rank == 0 else None
-    if roof:
-        roof["peak_kind"] = f"2x {peak_kind} cuBLAS bf16 burst ({bf16_tf} TFLOP/s)"
-    assert _lib.device_error() == 0, "a device-side wait timed out"
-
-    del graph
-    cpu = None
-    if rank == 0 and not args.no_cpu_baseline:
-        ms_block, threads = cpu_block_sample(1)
-        cpu = {"value": round(ms_block * BLOCKS, 1), "unit": "ms/step", "cores": threads, "kind": "port",
-               "sample": "one full-size block (B=2, 4352 tokens) of the eager bf16 CPU restatement, x60 blocks"}
-
-    if rank == 0:
-        line = {"metric": METRIC, "value": round(ms_step / world, 3), "unit": "ms/step", "n_gpus": world,
-                "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 3),
-                "higher_is_better": False, "scaling": "weak", "vs_baseline": None, "dtype": "mxfp8+int8/fp8 attn",
-                "data": "synthetic (random-init weights ~N(0,0.02), seeded latents/text)",
-                "config": {"workload": "config4: 60-block dual-stream MMDiT denoise step, 1024^2 "
-                                       "(4096 img + 256 txt tokens), CFG batch 2, profile mxfp8_sage",
-                           "global_batch": 2 * world, "seq_len": IMG_LEN + TXT_LEN,
-                           "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
-                           "cuda_graph": True, "l2": "working set (27 GB weights/step) >> L2; no flush"},
-                "e2e": {"value": round(e2e_ms / world, 3), "unit": "ms/step", "h2d_bytes_per_step": h2d,
-                        "d2h_bytes_per_step": d2h},
-                "gpu_launches": launches_per_step * args.steps,
-                "roofline": roof, "cpu_baseline": cpu, "clocks": clocks}
-        print(json.dumps(line), flush=True)
-
-
-METRIC_C5 = "ms per MMDiT denoise step at 2048^2 (60 blocks, CFG batch 2)"
-GRID_C5 = (1, 128, 128)              # 2048^2 latent 16ch x 256 x 256, 2x2 patches
-FLOP_C5 = 860.5e12                   # per step (both CFG rows): linears + attention
-
-
-def c5_arm(args, rank, world, local_rank):
-    """the 2048^2 step (16384 image + 256 text tokens per CFG
-    row). One GPU runs the CFG batch of 2; N >= 2 GPUs split it into the two
-    CFG halves, each a Ulysses group of N/2 ranks over NCCL (all-to-all Q/K/V
-    and O per block, one velocity swap per step). Strong scaling: the same
-    step at every N."""
-    from qwen_image_accel_b200 import _lib
-    device = torch.device("cuda", local_rank)
-    torch.cuda.set_device(device)
-    model, cfg = build_model(device)
-    img_len = GRID_C5[0] * GRID_C5[1] * GRID_C5[2]
+    from qwen_image_accel_b200.optimizations.cuda_graph import DenoiseStepGraph
+    img_len = grid[0] * grid[1] * grid[2]
     g = torch.Generator(device=device).manual_seed(42)
     latents = torch.randn(1, img_len, 64, device=device, dtype=torch.bfloat16, generator=g)
     pe = torch.randn(1, TXT_LEN, TXT_DIM, device=device, dtype=torch.bfloat16, generator=g)
     ne = torch.randn(1, TXT_LEN, TXT_DIM, device=device, dtype=torch.bfloat16, generator=g)
-    sig, sig_next = 1.0, 0.975
-    plan = None
-    if world > 1:
-        from qwen_image_accel_b200.ulysses import make_plan
-        plan = make_plan(cfg_split=True)
+    if plan is not None:
         lo, hi = plan.image_slice(img_len)
-        static_in = latents[:, lo:hi].clone()
-        step = lambda: model.denoise_step_sharded(static_in, pe, ne, sig, sig_next, GRID_C5, plan)  # noqa: E731
-    else:
-        static_in = latents.clone()
-        step = lambda: model.denoise_step(static_in, pe, ne, sig, sig_next, GRID_C5)  # noqa: E731
+        latents = latents[:, lo:hi].contiguous()
     _lib.launch_count = 0
-    for _ in range(max(args.warmup, 3)):
-        static_in.copy_(step())
+    graph = DenoiseStepGraph(model, latents, pe, ne, grid, plan=plan, warmup=max(args.warmup, 3))
+    launches_per_step = _lib.launch_count // (max(args.warmup, 3) + 1)
+    sig = torch.tensor(SIGMAS, dtype=torch.float32, device=device)
+    for _ in range(2):
+        graph.step(graph.out, sig)
     torch.cuda.synchronize()
-    launches_per_step = _lib.launch_count // max(args.warmup, 3)
-    graph = None
-    try:
-        graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(graph):
-            static_out = step()
-        graph.replay()
-        torch.cuda.synchronize()
-    except Exception as exc:  # noqa: BLE001
-        log(f"CUDA graph capture of the sharded step failed ({exc!r}); timing eager steps")
-        graph = None
-        torch.cuda.synchronize()
     if world > 1:
         torch.distributed.barrier()
     sampler = ClockSampler(torch.cuda.current_device()) if rank == 0 else None
@@ -379,75 +315,324 @@ def c5_arm(args, rank, world, local_rank):
         torch.distributed.barrier()
     e0.record(st)
     for _ in range(args.steps):
-        if graph is not None:
-            graph.replay()
-            static_in.copy_(static_out)
-        else:
-            static_in.copy_(step())
+        graph.step(graph.out, sig)
     e1.record(st)
     torch.cuda.synchronize()
     if world > 1:
         torch.distributed.barrier()
-    elapsed = e0.elapsed_time(e1)
     clocks = sampler.stop() if sampler else None
-    if world > 1:
-        t = torch.tensor([elapsed], device=device)
-        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-        elapsed = t.item()
-    ms_step = elapsed / args.steps
-    # end to end: this rank's latent shard and its half's text in from pinned
-    # host memory, its updated shard back, every step
-    host_lat = static_in.cpu().pin_memory()
+    ms = e0.elapsed_time(e1) / args.steps
+    # end to end through the public step(): this rank's latents and both
+    # prompt embeddings from pinned host memory, the new latents back
+    host_lat = latents.cpu().pin_memory()
     host_pe, host_ne = pe.cpu().pin_memory(), ne.cpu().pin_memory()
-    host_out = torch.empty_like(host_lat).pin_memory()
+    host_sig = torch.tensor(SIGMAS, dtype=torch.float32).pin_memory()
+    host_out = torch.empty(host_lat.shape, dtype=host_lat.dtype).pin_memory()
     torch.cuda.synchronize()
     if world > 1:
         torch.distributed.barrier()
     e0.record(st)
     for _ in range(args.steps):
-        static_in.copy_(host_lat, non_blocking=True)
-        pe.copy_(host_pe, non_blocking=True)
-        ne.copy_(host_ne, non_blocking=True)
-        if graph is not None:
-            graph.replay()
-            host_out.copy_(static_out, non_blocking=True)
-        else:
-            host_out.copy_(step(), non_blocking=True)
+        host_out.copy_(graph.step(host_lat, host_sig.to(device, non_blocking=True), host_pe, host_ne),
+                       non_blocking=True)
     e1.record(st)
     torch.cuda.synchronize()
     e2e_ms = e0.elapsed_time(e1) / args.steps
-    if world > 1:
-        t = torch.tensor([e2e_ms], device=device)
-        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-        e2e_ms = t.item()
+    ms, e2e_ms = max_over_ranks([ms, e2e_ms], world, device)
     assert _lib.device_error() == 0, "a device-side wait timed out"
-    used_graph = graph is not None
-    del graph   # a graph holding NCCL calls must go before the process group
+    h2d = host_lat.numel() * 2 + host_pe.numel() * 2 + host_ne.numel() * 2 + host_sig.numel() * 4
+    d2h = host_out.numel() * 2
+    del graph
+    return {"ms": ms, "e2e_ms": e2e_ms, "launches_per_step": launches_per_step, "clocks": clocks, "h2d": h2d,
+            "d2h": d2h}
+
+
+def ffn_up_roofline(model, device, rows, peak_tflops_fp8, peak_kind, flush):
+    """Live timing of the step's dominant kernel class -- the image stream's
+    FFN up-projection (3072 -> 12288, bias + GELU + MXFP8 requant epilogue),
+    as launched in the step, at `rows` image rows -- and cuBLASLt's MXFP8
+    GEMM (torch._scaled_mm, the reference's GEMM) on the same operands."""
+    from qwen_image_accel_b200.kernels.mxfp8 import quantize
+    blk = model.blocks[1]
+    g = torch.Generator(device=device).manual_seed(1)
+    a = quantize(torch.randn(rows, DIM, device=device, dtype=torch.bfloat16, generator=g))
+    ms = time_launches(lambda: blk.img_up.mx.matmul_gelu_quantize(a), flush)
+    flops = 2.0 * rows * FFN * DIM
+    tflops = flops / (ms * 1e-3) / 1e12
+    w, ws = blk.img_up.mx.weight_fp8, blk.img_up.mx.weight_scale
+    ms_lib = time_launches(lambda: torch._scaled_mm(a.values, w, scale_a=a.scales, scale_b=ws,
+                                                    out_dtype=torch.bfloat16), flush)
+    shape = f"M={rows} N={FFN} K={DIM}"
+    traffic, source = ncu_traffic("mxfp8_gemm_kernel ffn_up gelu_quant", shape)
+    algo = rows * DIM + FFN * DIM + rows * DIM // 32 + FFN * DIM // 32 + rows * FFN * (1 + 1 / 32) + FFN * 2
+    return roofline_entry(f"mxfp8_gemm_kernel (FFN up, {shape}, GELU + MXFP8 requant)", tflops, peak_tflops_fp8,
+                          "TFLOP/s", "tensor", peak_kind, traffic=traffic, traffic_source=source,
+                          algorithmic_bytes=int(algo), ms_per_launch=round(ms, 4),
+                          cublaslt_mxfp8_tflops_same_operands=round(flops / (ms_lib * 1e-3) / 1e12, 1),
+                          vs_cublaslt=round(ms_lib / ms, 3))
+
+
+# ----------------------------------------------------------------------------- configs 1-3 (kernel level)
+def measure_c1(device, hbm, peak_kind, flush):
+    """r + gate * (LN(x) * (1 + scale) + shift) over
+    [1, 4096, 3072] bf16 (seed 0: x, shift, scale, r, gate) -- one launch of
+    qia_adaln_residual against HBM (read x, read r, write out: 75.5 MB), and
+    the eager bf16 op on this host's CPU (median of 10 after 2)."""
+    from qwen_image_accel_b200.kernels.adaln import adaln_residual
+    g = torch.Generator().manual_seed(0)
+    x = torch.randn(1, 4096, DIM, generator=g).to(torch.bfloat16)
+    shift = (0.1 * torch.randn(1, DIM, generator=g)).to(torch.bfloat16)
+    scale = (0.1 * torch.randn(1, DIM, generator=g)).to(torch.bfloat16)
+    r = torch.randn(1, 4096, DIM, generator=g).to(torch.bfloat16)
+    gate = (0.1 * torch.randn(1, DIM, generator=g)).to(torch.bfloat16)
+    xd, rd = x.to(device), r.to(device)
+    one_s = (1 + scale).to(device)[:, None].contiguous()
+    sh, ga = shift.to(device)[:, None].contiguous(), gate.to(device)[:, None].contiguous()
+    ms = time_launches(lambda: adaln_residual(xd, rd, one_s, sh, ga), flush)
+    nbytes = 3 * x.numel() * 2
+    gbs = nbytes / (ms * 1e-3) / 1e9
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    ln = torch.nn.LayerNorm(DIM, eps=1e-6, elementwise_affine=False)
+
+    def eager():
+        with torch.no_grad():
+            return r + gate * (ln(x) * (1 + scale) + shift)
+
+    for _ in range(2):
+        eager()
+    cpu = []
+    for _ in range(10):
+        t0 = time.perf_counter()
+        eager()
+        cpu.append((time.perf_counter() - t0) * 1e3)
+    traffic, source = ncu_traffic("adaln_residual_kernel", "[1,4096,3072]")
+    return {"workload": "config1: AdaLN composite r + gate*(LN(x)*(1+scale)+shift), x/r bf16 [1,4096,3072]",
+            "ms": round(ms, 4),
+            "roofline": roofline_entry("adaln_residual_kernel", gbs, hbm, "GB/s", "hbm", peak_kind, traffic=traffic,
+                                       traffic_source=source, algorithmic_bytes=nbytes),
+            "cpu_baseline": {"value": round(statistics.median(cpu), 2), "unit": "ms", "cores": threads,
+                             "kind": "reference", "sample": "the eager bf16 op at full size, median of 10 after 2"}}
+
+
+C2_SHAPES = (("qkv", 3072, 9216), ("out", 3072, 3072), ("ffn_up", 3072, 12288), ("ffn_down", 12288, 3072))
+
+
+def measure_c2(device, peak_fp8, hbm, peak_kind, hbm_kind, flush):
+    """the MXFP8 GEMM sweep. A bf16 [M, K] ~N(0,1),
+    M in {4352, 16640}; W bf16 [N, K] ~N(0,0.02), bias ~N(0,0.01), seed 1;
+    both quantized to E4M3 + 1x32 E8M0. Per shape: the tcgen05 GEMM with the
+    epilogue the block runs (bias; bias + GELU + MXFP8 requant on the
+    up-projection; gate + residual on the output and down projections) and
+    torch._scaled_mm (cuBLASLt, the reference's GEMM) on the same operands;
+    plus the activation quantizer against HBM (2 B in, 1.03125 B out per
+    element) and, per M, the CPU restatement (dequantize -> fp32 matmul) of
+    the out-projection on a 256-row sample scaled to M."""
+    from qwen_image_accel_b200.kernels.mxfp8 import quantize
+    from qwen_image_accel_b200.optimizations.mxfp8 import MXFP8Linear
+    import oracle
+    out = {"workload": "config2: MXFP8 GEMM sweep, M in {4352, 16640}", "shapes": []}
+    g = torch.Generator(device=device).manual_seed(1)
+    for m in (4352, 16640):
+        for name, k, n in C2_SHAPES:
+            a_bf = torch.randn(m, k, device=device, dtype=torch.bfloat16, generator=g)
+            lin = torch.nn.Linear(k, n, bias=True, device=device, dtype=torch.bfloat16)
+            with torch.no_grad():
+                lin.weight.copy_(0.02 * torch.randn(n, k, device=device, generator=g))
+                lin.bias.copy_(0.01 * torch.randn(n, device=device, generator=g))
+            mx = MXFP8Linear(lin)
+            a = quantize(a_bf)
+            if name == "ffn_up":
+                fn = lambda: mx.matmul_gelu_quantize(a)  # noqa: E731
+                epi = "bias+GELU+MXFP8"
+            elif name == "qkv":
+                fn = lambda: mx.matmul(a)  # noqa: E731
+                epi = "bias"
+            else:
+                res = torch.randn(m, n, device=device, dtype=torch.bfloat16, generator=g)
+                gate = (0.1 * torch.randn(1, n, device=device, generator=g)).to(torch.bfloat16)
+                fn = lambda: mx.matmul_gate_residual(a, gate, res, out=res)  # noqa: E731
+                epi = "bias+gate+residual"
+            ms = time_launches(fn, flush)
+            ms_lib = time_launches(lambda: torch._scaled_mm(a.values, mx.weight_fp8, scale_a=a.scales,
+                                                            scale_b=mx.weight_scale, out_dtype=torch.bfloat16),
+                                   flush)
+            flops = 2.0 * m * n * k
+            tf, tf_lib = flops / (ms * 1e-3) / 1e12, flops / (ms_lib * 1e-3) / 1e12
+            out["shapes"].append({"linear": name, "M": m, "K": k, "N": n, "epilogue": epi, "ms": round(ms, 4),
+                                  "tflops": round(tf, 1), "frac": round(tf / peak_fp8, 3),
+                                  "scaled_mm_ms": round(ms_lib, 4), "scaled_mm_tflops": round(tf_lib, 1),
+                                  "vs_scaled_mm": round(ms_lib / ms, 3)})
+            del a, a_bf, mx, lin
+        xq = torch.randn(m, DIM, device=device, dtype=torch.bfloat16, generator=g)
+        ms_q = time_launches(lambda: quantize(xq), flush)
+        nbytes = m * DIM * (2 + 1 + 1 / 32)
+        out.setdefault("quantizer", []).append(
+            roofline_entry(f"mx_quantize_kernel [{m},{DIM}]", nbytes / (ms_q * 1e-3) / 1e9, hbm, "GB/s", "hbm",
+                           hbm_kind, algorithmic_bytes=int(nbytes), ms=round(ms_q, 4)))
+    fr = [s["frac"] for s in out["shapes"]]
+    out["frac_min"], out["frac_mean"] = round(min(fr), 3), round(statistics.mean(fr), 3)
+    out["vs_scaled_mm_min"] = round(min(s["vs_scaled_mm"] for s in out["shapes"]), 3)
+    # CPU restatement sample: 256 rows of the out-projection, scaled to M rows
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    gc = torch.Generator().manual_seed(1)
+    w = (0.02 * torch.randn(DIM, DIM, generator=gc)).to(torch.bfloat16)
+    x = torch.randn(256, DIM, generator=gc).to(torch.bfloat16)
+    wq = oracle.mx_quantize_numpy(w.view(torch.int16).numpy().view("uint16"))
+    xq = oracle.mx_quantize_numpy(x.view(torch.int16).numpy().view("uint16"))
+    t0 = time.perf_counter()
+    oracle.mxfp8_gemm(xq[0], xq[1], wq[0], wq[1], 256, DIM)
+    cpu_ms = (time.perf_counter() - t0) * 1e3
+    out["cpu_baseline"] = {"value": {str(m): round(cpu_ms * m / 256, 1) for m in (4352, 16640)}, "unit": "ms",
+                           "cores": threads, "kind": "port",
+                           "sample": "out-projection (3072->3072) dequantize -> fp64 matmul on 256 rows, scaled "
+                                     "to M rows"}
+    return out
+
+
+def measure_c3(device, peak_fp8, peak_kind, flush):
+    """joint attention, B=2, H=24, d=128, 256 text + 4096
+    image tokens; q, k, v ~N(0,1) bf16 (seed 2), per-head QK-RMSNorm
+    (weight 1, eps 1e-6) and the v1 3D RoPE (axes 16/56/56, (1,64,64) grid,
+    text positions offset) applied with qia_qknorm_rope_segment; then the
+    Sage quantizers + tcgen05 attention (sage_attention) beside the
+    reference's SageAttention built from its pinned sources, on the same
+    inputs; plus the fused QK-norm/RoPE + quantizers of the dual-stream block
+    straight from the q|k|v projections. CPU: the restated Sage attention at
+    S = 544 (one head, B = 1), scaled by B H (S/544)^2."""
+    import numpy as np
+    from qwen_image_accel_b200.kernels.attention import joint_qk_norm_rope
+    from qwen_image_accel_b200.mmdit import rope_tables
+    from qwen_image_accel_b200.optimizations.sage_attention import (sage_attention, sage_quantize_joint,
+                                                                    workspace_bytes)
+    import oracle
+    from oracle import sage_ref
+    b, h, lt, li = 2, HEADS, TXT_LEN, IMG_LEN
+    s = lt + li
+    g = torch.Generator(device=device).manual_seed(2)
+    qkv = [torch.randn(b, n, 3 * h * 128, device=device, dtype=torch.bfloat16, generator=g) for n in (lt, li)]
+    ones = torch.ones(128, device=device, dtype=torch.bfloat16)
+    img, txt = rope_tables(*GRID, lt)
+    ft, fi = (torch.view_as_real(t).to(device).contiguous() for t in (txt, img))
+    q, k, v = (torch.empty(b, s, h, 128, device=device, dtype=torch.bfloat16) for _ in range(3))
+    joint_qk_norm_rope(qkv[0], ones, ones, ft, q, k, v, 0, 1e-6)
+    joint_qk_norm_rope(qkv[1], ones, ones, fi, q, k, v, lt, 1e-6)
+    ws = torch.empty(workspace_bytes(b, h, s, s), device=device, dtype=torch.uint8)
+    o = torch.empty_like(q)
+    ms = time_launches(lambda: sage_attention(q, k, v, out=o, workspace=ws), flush)
+    ms_quant = time_launches(lambda: sage_quantize_joint(qkv[0], qkv[1], (ones, ones), (ones, ones), ft, fi, h),
+                             flush)
+    ops = 4.0 * b * h * s * s * 128
+    out = {"workload": "config3: joint attention B=2 H=24 S=256+4096 d=128, QK-RMSNorm + 3D RoPE",
+           "ms": round(ms, 4), "fused_norm_rope_quantizers_ms": round(ms_quant, 4),
+           "roofline": roofline_entry("sage_quant_* + sage_attn_kernel", ops / (ms * 1e-3) / 1e12, peak_fp8,
+                                      "TOP/s", "tensor", peak_kind, algorithmic_ops=ops)}
+    if sage_ref.available():
+        ref = sage_ref.attention(q, k, v)
+        ms_ref = time_launches(lambda: sage_ref.attention(q, k, v), flush)
+        a, r = o.double().flatten(), ref.double().flatten()
+        out["reference_sageattention"] = {"ms": round(ms_ref, 4), "tops": round(ops / (ms_ref * 1e-3) / 1e12, 1),
+                                          "speedup": round(ms_ref / ms, 3),
+                                          "cosine": round(float(a @ r / (a.norm() * r.norm())), 6),
+                                          "kernel": "SageAttention 2.2.0 sm89 qk_int8_sv_f8_accum_f32_fuse_v_scale"
+                                                    "_attn_inst_buf + quantizers, built from the pinned tarball"}
+    threads = os.cpu_count() or 1
+    sc = 544
+    qs, ks, vs = (t[:1, :sc, :1].float().cpu().numpy() for t in (q, k, v))
+    t0 = time.perf_counter()
+    oracle.sage_attention(np.ascontiguousarray(qs), np.ascontiguousarray(ks), np.ascontiguousarray(vs))
+    cpu_ms = (time.perf_counter() - t0) * 1e3
+    out["cpu_baseline"] = {"value": round(cpu_ms * b * h * (s / sc) ** 2, 1), "unit": "ms", "cores": 1,
+                           "kind": "port", "sample": f"restated Sage attention (numpy) at S={sc}, one head, B=1, "
+                                                     "scaled by B*H*(S/544)^2"}
+    return out
+
+
+# ----------------------------------------------------------------------------- the default line
+def step_arm(args, rank, world, local_rank):
+    """BASELINE config 5 (2048^2) as the headline at every N; at N = 1 also
+    config 4 (1024^2) and the kernel measurements of configs 1-3. With
+    --config c4: the 1024^2 step alone (replicas for N > 1)."""
+    device = torch.device("cuda", local_rank)
+    torch.cuda.set_device(device)
+    hbm, bf16_tf, peak_kind = load_peaks()
+    fp8_peak = 2.0 * bf16_tf     # FP8 tensor rate = 2x the bf16 rate: the denominator is 2x measured cuBLAS bf16
+    fp8_kind = f"2x {peak_kind} cuBLAS bf16 burst ({bf16_tf} TFLOP/s)"
+    hbm_kind = f"{peak_kind} copy bandwidth"
+    model, cfg = build_model(device)
+    c4_only = args.config == "c4"
+    plan = None
+    if world > 1 and not c4_only:
+        from qwen_image_accel_b200.ulysses import make_plan
+        plan = make_plan(cfg_split=True)
+    grid = GRID if c4_only else GRID_C5
+    img = grid[0] * grid[1] * grid[2]
+    head = time_step(model, grid, args, rank, world, device, plan=plan)
+    flush = L2Flush(device)
+    extra = {}
+    roof = None
     if rank == 0:
-        hbm, bf16_tf, peak_kind = load_peaks()
-        per_gpu_tf = FLOP_C5 / (ms_step * 1e-3) / world / 1e12
-        line = {"metric": METRIC_C5, "value": round(ms_step, 3), "unit": "ms/step", "n_gpus": world,
-                "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 3),
-                "higher_is_better": False, "scaling": "strong", "vs_baseline": None,
-                "dtype": "mxfp8+int8/fp8 attn",
+        rows = 2 * img if plan is None else 2 * img // plan.world
+        roof = ffn_up_roofline(model, device, rows, fp8_peak, fp8_kind, flush)
+        per_gpu = step_flops(img) / (head["ms"] * 1e-3) / max(1, world) / 1e12
+        roof["step_tflops_per_gpu"] = round(per_gpu, 1)
+        roof["step_frac"] = round(per_gpu / fp8_peak, 3)
+    cpu = None
+    if world == 1 and not c4_only:
+        c4 = time_step(model, GRID, args, rank, world, device)
+        c4_roof = ffn_up_roofline(model, device, 2 * IMG_LEN, fp8_peak, fp8_kind, flush)
+        tf4 = step_flops(IMG_LEN) / (c4["ms"] * 1e-3) / 1e12
+        extra["config4"] = {"workload": "config4: 60-block dual-stream MMDiT, 1024^2 (4096 img + 256 txt tokens), "
+                                        "CFG batch 2, profile mxfp8_sage",
+                            "ms_per_step": round(c4["ms"], 3), "e2e_ms_per_step": round(c4["e2e_ms"], 3),
+                            "step_tflops": round(tf4, 1), "step_frac": round(tf4 / fp8_peak, 3),
+                            "gpu_launches_per_step": c4["launches_per_step"], "roofline": c4_roof,
+                            "clocks": c4["clocks"]}
+        del model
+        torch.cuda.empty_cache()
+        extra["config1"] = measure_c1(device, hbm, hbm_kind, flush)
+        extra["config2"] = measure_c2(device, fp8_peak, hbm, fp8_kind, hbm_kind, flush)
+        extra["config3"] = measure_c3(device, fp8_peak, fp8_kind, flush)
+    if rank == 0 and not args.no_cpu_baseline and world == 1:
+        try:
+            ms, threads, flops = cpu_reference_sample()
+            cpu = {"value": round(ms * step_flops(img) / flops, 1), "unit": "ms/step", "cores": threads,
+                   "kind": "reference",
+                   "sample": f"one eager forward of the pinned Diffusers v1 model with 1 of 60 blocks (B=2, "
+                             f"{REF_SAMPLE_IMG} img + {REF_SAMPLE_TXT} txt tokens) + CFG + Euler on the host CPU "
+                             f"({ms:.0f} ms), scaled by FLOPs to the step (extrapolated)"}
+            if "config4" in extra:
+                extra["config4"]["cpu_baseline"] = dict(cpu, value=round(ms * step_flops(IMG_LEN) / flops, 1))
+        except Exception as exc:  # noqa: BLE001
+            log(f"CPU baseline unavailable: {exc!r}")
+    if rank == 0:
+        if c4_only:
+            metric, workload = METRIC_C4, ("config4: 60-block dual-stream MMDiT denoise step, 1024^2 (4096 img + 256 "
+                                           "txt tokens), CFG batch 2, profile mxfp8_sage")
+            parallelism = f"replicas x{world}" if world > 1 else "single GPU"
+            value, scaling = head["ms"] / world, "weak"
+        else:
+            metric, workload = METRIC, ("config5: 60-block dual-stream MMDiT denoise step, 2048^2 (16384 img + 256 "
+                                        "txt tokens), CFG batch 2, profile mxfp8_sage")
+            parallelism = ("single GPU (CFG batch 2)" if plan is None else
+                           (f"CFG split x Ulysses {plan.ulysses} (NCCL all-to-all)" if plan.ulysses > 1
+                            else "CFG split (one NCCL exchange per step)"))
+            value, scaling = head["ms"], "strong"
+        line = {"metric": metric, "value": round(value, 3), "unit": "ms/step", "n_gpus": world,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(head["ms"], 3),
+                "higher_is_better": False, "scaling": scaling, "vs_baseline": None,
+                "dtype": "mxfp8+int8/fp8 attn (blocks 0 and 31 bf16)",
                 "data": "synthetic (random-init weights ~N(0,0.02), seeded latents/text)",
-                "config": {"workload": "config5: 60-block dual-stream MMDiT denoise step, 2048^2 "
-                                       "(16384 img + 256 txt tokens), CFG batch 2, profile mxfp8_sage",
-                           "global_batch": 2, "seq_len": img_len + TXT_LEN,
-                           "parallelism": ((f"CFG split x Ulysses {plan.ulysses} (NCCL all-to-all)"
-                                            if plan.ulysses > 1 else "CFG split (one NCCL exchange per step)")
-                                           if plan else "single GPU"),
-                           "cuda_graph": used_graph,
-                           "l2": "working set >> L2; no flush"},
-                "e2e": {"value": round(e2e_ms, 3), "unit": "ms/step",
-                        "h2d_bytes_per_step": host_lat.numel() * 2 + host_pe.numel() * 2 + host_ne.numel() * 2,
-                        "d2h_bytes_per_step": host_out.numel() * 2},
-                "gpu_launches": launches_per_step * args.steps,
-                "roofline": {"bound": "tensor", "kernel": "whole step (860.5 TFLOP)", "achieved": round(per_gpu_tf, 1),
-                             "peak": round(2 * bf16_tf, 1), "unit": "TFLOP/s",
-                             "frac": round(per_gpu_tf / (2 * bf16_tf), 3), "traffic": None,
-                             "peak_kind": f"2x {peak_kind} cuBLAS bf16 burst, per GPU"},
-                "cpu_baseline": None, "clocks": clocks}
+                "config": {"workload": workload, "global_batch": 2, "seq_len": img + TXT_LEN,
+                           "parallelism": parallelism, "cuda_graph": "DenoiseStepGraph (whole step)",
+                           "l2": "step working set (27 GB weights) >> L2, no flush; kernel lines flush L2 (256 MiB "
+                                 "write) before each timed launch"},
+                "e2e": {"value": round(head["e2e_ms"] / (world if c4_only else 1), 3), "unit": "ms/step",
+                        "h2d_bytes_per_step": head["h2d"], "d2h_bytes_per_step": head["d2h"]},
+                "gpu_launches": head["launches_per_step"] * args.steps,
+                "roofline": roof, "cpu_baseline": cpu, "clocks": head["clocks"]}
+        line.update(extra)
         print(json.dumps(line), flush=True)
 
 
@@ -747,13 +932,23 @@ def profile_case(name: str):
     attn    - Sage attention B=1, H=24, S=4352 (three calls)
     step8   - an 8-block 1024^2 step: two warm-up steps, then one inside an NVTX
               range named `step` (for `ncu --nvtx --nvtx-include step/`)
+    step8_c5 - the same at 2048^2 (config 5's shapes)
     quant   - the fused QK-norm/RoPE + Sage quantization of one block (B=2, 256
               text + 4096 image tokens, 24 heads, from the two streams' q|k|v
               projections), twice (three launches each).
     prefill - the 2.1 block-causal prefill attention of `--config prefill`
               (S=8325, 32 heads), three calls (four launches each).
     q21step - the `--config q21` denoiser: prefill, two decode steps, then one
-              decode step inside an NVTX range named `step`."""
+              decode step inside an NVTX range named `step`.
+    ffn_up_c5 - the FFN-up GEMM (GELU+MXFP8 epilogue) at config 5's M=32768.
+    kernels - one launch each of the memory-bound kernels at the step's
+              shapes: LN + modulation -> MXFP8 (image + text rows, grouped),
+              the AdaLN modulation GEMV (one block), the config-1 AdaLN
+              composite [1,4096,3072], the MXFP8 quantizer [8192,3072],
+              SwiGLU -> MXFP8 (table and direct forms, [4096,12288]), QK-norm +
+              RoPE of one stream segment (B=2, 4096 tokens, 24 heads), the
+              CFG/Euler update and the fused proj_out + CFG/Euler tail
+              (1024^2: 4096 tokens)."""
     device = torch.device("cuda", 0)
     torch.cuda.set_device(device)
     g = torch.Generator(device=device).manual_seed(0)
@@ -763,6 +958,14 @@ def profile_case(name: str):
         lin = torch.nn.Linear(3072, 12288, bias=True, device=device, dtype=torch.bfloat16)
         a = quantize(torch.randn(8192, 3072, device=device, dtype=torch.bfloat16, generator=g))
         MXFP8Linear(lin).matmul_gelu_quantize(a)
+    elif name == "ffn_up_c5":
+        from qwen_image_accel_b200.kernels.mxfp8 import quantize
+        from qwen_image_accel_b200.optimizations.mxfp8 import MXFP8Linear
+        lin = torch.nn.Linear(DIM, FFN, bias=True, device=device, dtype=torch.bfloat16)
+        a = quantize(torch.randn(2 * IMG_LEN_C5, DIM, device=device, dtype=torch.bfloat16, generator=g))
+        MXFP8Linear(lin).matmul_gelu_quantize(a)
+    elif name == "kernels":
+        profile_kernels(device, g)
     elif name == "attn":
         from qwen_image_accel_b200.optimizations.sage_attention import sage_attention
         q, k, v = (torch.randn(1, IMG_LEN + TXT_LEN, HEADS, 128, device=device, dtype=torch.bfloat16, generator=g)
@@ -796,23 +999,64 @@ def profile_case(name: str):
         ft, fi = (torch.view_as_real(t).to(device).contiguous() for t in (txt, img))
         for _ in range(2):
             sage_quantize_joint(qkv[0], qkv[1], w[0], w[1], ft, fi, HEADS)
-    elif name == "step8":
+    elif name in ("step8", "step8_c5"):
         from qwen_image_accel_b200.mmdit import MMDiT, MMDiTConfig, random_parameters
+        grid = GRID if name == "step8" else GRID_C5
         cfg = MMDiTConfig(num_layers=8)
+        # blocks 1-7 MXFP8 (block 0 bf16, as the 60-block step's blocks 0 and 31)
         model = MMDiT(cfg, random_parameters(cfg, 42, device), device=device, profile="mxfp8_sage")
-        lat = torch.randn(1, IMG_LEN, 64, device=device, dtype=torch.bfloat16, generator=g)
+        n = grid[0] * grid[1] * grid[2]
+        lat = torch.randn(1, n, 64, device=device, dtype=torch.bfloat16, generator=g)
         pe = torch.randn(1, TXT_LEN, TXT_DIM, device=device, dtype=torch.bfloat16, generator=g)
         ne = torch.randn(1, TXT_LEN, TXT_DIM, device=device, dtype=torch.bfloat16, generator=g)
         for _ in range(2):
-            model.denoise_step(lat, pe, ne, 1.0, 0.975, GRID)
+            model.denoise_step(lat, pe, ne, 1.0, 0.975, grid)
         torch.cuda.synchronize()
         torch.cuda.nvtx.range_push("step")
-        model.denoise_step(lat, pe, ne, 1.0, 0.975, GRID)
+        model.denoise_step(lat, pe, ne, 1.0, 0.975, grid)
         torch.cuda.nvtx.range_pop()
     else:
         raise SystemExit(f"unknown profile case {name!r}")
     torch.cuda.synchronize()
     log(f"profile case {name}: done")
+
+
+def profile_kernels(device, g):
+    """The `kernels` profile case (see profile_case)."""
+    from qwen_image_accel_b200.kernels.adaln import adaln_residual
+    from qwen_image_accel_b200.kernels.attention import joint_qk_norm_rope
+    from qwen_image_accel_b200.kernels.epilogue import layer_norm_scale_quantize_grouped, swiglu_quantize
+    from qwen_image_accel_b200.kernels.modulation import adaln_modulation
+    from qwen_image_accel_b200.kernels.mxfp8 import quantize
+    from qwen_image_accel_b200.kernels.scheduler import cfg_euler, proj_out_cfg_euler
+    from qwen_image_accel_b200.mmdit import _LNParams, rope_tables
+    bf = torch.bfloat16
+    rn = lambda *shape, s=1.0: (s * torch.randn(*shape, device=device, generator=g)).to(bf)  # noqa: E731
+    ln = _LNParams(DIM, 1e-6)
+    x, c = rn(2, IMG_LEN, DIM), rn(2, TXT_LEN, DIM)
+    sc, sh = 1 + rn(2, 1, DIM, s=0.1), rn(2, 1, DIM, s=0.1)
+    layer_norm_scale_quantize_grouped([(x, sc, sh), (c, sc, sh)], ln)
+    adaln_modulation(rn(DIM), rn(12 * DIM, DIM, s=0.02), rn(12 * DIM, s=0.01), DIM)
+    x1, r1 = rn(1, 4096, DIM), rn(1, 4096, DIM)
+    adaln_residual(x1, r1, 1 + rn(1, 1, DIM, s=0.1), rn(1, 1, DIM, s=0.1), rn(1, 1, DIM, s=0.1))
+    quantize(rn(8192, DIM))
+    gt, vt = rn(4096, 12288), rn(4096, 12288)
+    swiglu_quantize(gt, vt)
+    swiglu_quantize(gt[:512].contiguous(), vt[:512].contiguous())
+    img, _ = rope_tables(*GRID, TXT_LEN)
+    fi = torch.view_as_real(img).to(device).contiguous()
+    qkv = rn(2, IMG_LEN, 3 * DIM)
+    q, k, v = (torch.empty(2, IMG_LEN, HEADS, 128, device=device, dtype=bf) for _ in range(3))
+    w = 1 + rn(128, s=0.1)
+    joint_qk_norm_rope(qkv, w, w, fi, q, k, v, 0, 1e-6)
+    lat = rn(1, IMG_LEN, 64)
+    sig = torch.tensor(SIGMAS, device=device, dtype=torch.float32)
+    cfg_euler(rn(1, IMG_LEN, 64), rn(1, IMG_LEN, 64), lat, 4.0, sigmas=sig)
+    proj_out_cfg_euler(rn(2, IMG_LEN, DIM), rn(64, DIM, s=0.02), rn(64, s=0.01), lat, 4.0, sig)
+    from qwen_image_accel_b200.qwen21_model import rope_table_device
+    mask = torch.cat([torch.zeros(113, dtype=torch.bool), torch.ones(4096, dtype=torch.bool),
+                      torch.zeros(20, dtype=torch.bool), torch.ones(4096, dtype=torch.bool)]).to(device)
+    rope_table_device([(1, 64, 64), (1, 64, 64)], mask)
 
 
 def main():
@@ -822,10 +1066,12 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--config", default="c4", choices=["c4", "c5", "prefill", "q21"],
-                    help="c4: 1024^2 step (replicas for N>1); c5: 2048^2 step, CFG split x Ulysses for N>1; "
-                         "prefill: the 2.1 block-causal prefill attention; q21: the 2.1 cached-decode step")
-    ap.add_argument("--profile-case", choices=["ffn_up", "attn", "step8", "quant", "prefill", "q21step"],
+    ap.add_argument("--config", default="c5", choices=["c5", "c4", "prefill", "q21"],
+                    help="c5 (default): the 2048^2 step (CFG split x Ulysses for N>1), with config 4 and the "
+                         "configs 1-3 kernel lines at N=1; c4: the 1024^2 step (replicas for N>1); prefill: the "
+                         "2.1 block-causal prefill attention; q21: the 2.1 cached-decode step")
+    ap.add_argument("--profile-case", choices=["ffn_up", "ffn_up_c5", "kernels", "attn", "step8", "step8_c5",
+                                               "quant", "prefill", "q21step"],
                     help="run one small fixed case for an ncu capture and exit")
     args = ap.parse_args()
     if args.profile_case:
@@ -835,21 +1081,19 @@ def main():
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     if args.impl == "reference":
-        reference_arm(args, rank)
+        reference_arm(args, rank, world)
         return
     if world > 1:
         from datetime import timedelta
         torch.cuda.set_device(local_rank)
         torch.distributed.init_process_group("nccl", timeout=timedelta(seconds=300))
     try:
-        if args.config == "c5":
-            c5_arm(args, rank, world, local_rank)
-        elif args.config == "prefill":
+        if args.config == "prefill":
             prefill_arm(args, rank, world, local_rank)
         elif args.config == "q21":
             q21_arm(args, rank, world, local_rank)
         else:
-            our_arm(args, rank, world, local_rank)
+            step_arm(args, rank, world, local_rank)
     finally:
         if world > 1:
             torch.distributed.destroy_process_group()

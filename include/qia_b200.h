@@ -137,6 +137,48 @@ int qia_cfg_euler(const void* cond, const void* neg, const void* latents,
                   void* out, int64_t rows, int64_t dim, float cfg_scale,
                   float dt, void* stream);
 
+/* The Qwen-Image 2.1 joint-sequence RoPE table on the device: is_image
+ * uint8 [seq] (1 = image token), block_hw HOST int32 [n_blocks, 2] (height,
+ * width of each image block in sequence order, n_blocks <= 64), the three
+ * per-axis complex64 tables (float pairs, rows_pos rows for positions 0.. then
+ * rows_neg rows for positions -rows_neg..-1; pairs_* complex entries per row)
+ * -> out complex64 [seq, pairs_frame + pairs_h + pairs_w]. Text tokens advance
+ * one position on all axes; an image block freezes the frame axis and lays
+ * its tokens on a centred height/width grid, then advances the position by
+ * max(h, w). Bit-identical to the reference's table (an exact gather).
+ * Replaces: QwenImage21Rope.forward's host loop and .tolist() sync
+ * (WHL:diffusers/models/transformers/transformer_qwenimage21.py:677-710). */
+int qia_rope21_table(const void* is_image, int64_t seq, const int32_t* block_hw,
+                     int64_t n_blocks, const void* tab_frame, const void* tab_h,
+                     const void* tab_w, int64_t pairs_frame, int64_t pairs_h,
+                     int64_t pairs_w, int64_t rows_pos, int64_t rows_neg,
+                     void* out, void* stream);
+
+/* qia_cfg_euler with dt = sigmas[1] - sigmas[0] (fp32) read from device
+ * memory (sigmas: device float[2] = {sigma, sigma_next}), so a step captured
+ * in a CUDA graph replays with each step's schedule. Used by the CFG-split
+ * (multi-GPU) step after the two halves' velocities are exchanged.
+ * Replaces: the same reference sequence as qia_cfg_euler. */
+int qia_cfg_euler_sched(const void* cond, const void* neg, const void* latents,
+                        void* out, int64_t rows, int64_t dim, float cfg_scale,
+                        const void* sigmas, void* stream);
+
+/* The denoise step's tail as one tcgen05 kernel: proj_out of both CFG rows
+ * (bf16 GEMM + bias, y bf16 [2*rows, k] row-major: rows [0, rows) the
+ * conditional branch, [rows, 2*rows) the unconditional one; w bf16 [n, k];
+ * bias bf16 [n] or NULL), the true-CFG combine with norm rescaling and the
+ * Euler update into out [rows, n] (may be latents), with the roundings of
+ * qia_cfg_euler; dt = sigmas[1] - sigmas[0] from device memory.
+ * n must be 64 and k a multiple of 64; y, w, latents, out 16-byte aligned.
+ * Replaces: proj_out + the CFG combine + FlowMatchEulerDiscreteScheduler.step
+ * (WHL:diffusers/models/transformers/transformer_qwenimage.py:1007-1012;
+ * WHL:diffusers/pipelines/qwenimage/pipeline_qwenimage.py:643-681;
+ * WHL:diffusers/schedulers/scheduling_flow_match_euler_discrete.py:483-517). */
+int qia_proj_out_cfg_euler(const void* y, const void* w, const void* bias,
+                           const void* latents, void* out, int64_t rows,
+                           int64_t k, int64_t n, float cfg_scale,
+                           const void* sigmas, void* stream);
+
 /* ---------------------------------------------------------------------------
  * Attention input preparation
  * ------------------------------------------------------------------------ */

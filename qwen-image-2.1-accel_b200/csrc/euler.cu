@@ -11,7 +11,9 @@
 //   v     = bf16(comb * ratio)
 //   out   = bf16(float(latent) + float(bf16(dt * v)))
 // One warp per row; the sums of squares are a per-lane sum over the lane's
-// channels (c = lane, lane + 32, ...) and a xor-shuffle tree.
+// channels (c = lane, lane + 32, ...) and a xor-shuffle tree. dt is a launch
+// argument (qia_cfg_euler) or sigma_next - sigma from device memory
+// (qia_cfg_euler_sched, so a captured step replays with each step's schedule).
 #include "qia_common.cuh"
 
 namespace qia {
@@ -21,8 +23,9 @@ __global__ void __launch_bounds__(256) cfg_euler_kernel(const __nv_bfloat16* __r
                                                         const __nv_bfloat16* __restrict__ neg,
                                                         const __nv_bfloat16* __restrict__ lat,
                                                         __nv_bfloat16* __restrict__ out, int64_t rows, int dim,
-                                                        float s, float dt) {
+                                                        float s, float dt, const float* __restrict__ sigmas) {
   const int lane = threadIdx.x & 31;
+  if (sigmas) dt = __fsub_rn(sigmas[1], sigmas[0]);   // the schedule's fp32 step, read on the device
   const int64_t warps = int64_t(gridDim.x) * (blockDim.x / 32);
   for (int64_t row = int64_t(blockIdx.x) * (blockDim.x / 32) + (threadIdx.x >> 5); row < rows; row += warps) {
     const int64_t base = row * dim;
@@ -54,17 +57,32 @@ __global__ void __launch_bounds__(256) cfg_euler_kernel(const __nv_bfloat16* __r
 
 using namespace qia;
 
-extern "C" int qia_cfg_euler(const void* cond, const void* neg, const void* latents, void* out, int64_t rows,
-                             int64_t dim, float cfg_scale, float dt, void* stream) {
-  if (!cond || !neg || !latents || !out) return set_error(QIA_ERR_INVALID, "qia_cfg_euler: null pointer");
-  if (rows <= 0 || dim <= 0) return set_error(QIA_ERR_INVALID, "qia_cfg_euler: rows=%lld dim=%lld",
+namespace {
+int launch_cfg_euler(const void* cond, const void* neg, const void* latents, void* out, int64_t rows, int64_t dim,
+                     float cfg_scale, float dt, const float* sigmas, void* stream, const char* name) {
+  if (!cond || !neg || !latents || !out) return set_error(QIA_ERR_INVALID, "%s: null pointer", name);
+  if (rows <= 0 || dim <= 0) return set_error(QIA_ERR_INVALID, "%s: rows=%lld dim=%lld", name,
                                               (long long)rows, (long long)dim);
-  if (dim > 65536) return set_error(QIA_ERR_UNSUPPORTED, "qia_cfg_euler: dim too large");
+  if (dim > 65536) return set_error(QIA_ERR_UNSUPPORTED, "%s: dim too large", name);
   int64_t blocks = (rows + 7) / 8;
   const int64_t cap = int64_t(sm_count()) * 16;
   if (blocks > cap) blocks = cap;
   cfg_euler_kernel<<<unsigned(blocks), 256, 0, as_stream(stream)>>>(
       (const __nv_bfloat16*)cond, (const __nv_bfloat16*)neg, (const __nv_bfloat16*)latents, (__nv_bfloat16*)out,
-      rows, int(dim), cfg_scale, dt);
+      rows, int(dim), cfg_scale, dt, sigmas);
   return check_launch("cfg_euler_kernel");
+}
+}  // namespace
+
+extern "C" int qia_cfg_euler(const void* cond, const void* neg, const void* latents, void* out, int64_t rows,
+                             int64_t dim, float cfg_scale, float dt, void* stream) {
+  return launch_cfg_euler(cond, neg, latents, out, rows, dim, cfg_scale, dt, nullptr, stream, "qia_cfg_euler");
+}
+
+extern "C" int qia_cfg_euler_sched(const void* cond, const void* neg, const void* latents, void* out, int64_t rows,
+                                   int64_t dim, float cfg_scale, const void* sigmas, void* stream) {
+  if (!sigmas) return set_error(QIA_ERR_INVALID, "qia_cfg_euler_sched: null sigmas");
+  if (!aligned(sigmas, 4)) return set_error(QIA_ERR_ALIGNMENT, "qia_cfg_euler_sched: misaligned sigmas");
+  return launch_cfg_euler(cond, neg, latents, out, rows, dim, cfg_scale, 0.0f, (const float*)sigmas, stream,
+                          "qia_cfg_euler_sched");
 }

@@ -40,6 +40,9 @@ SIGNATURES: dict[str, list] = {
     "qia_ln_mod_quant_grouped": [_P, ctypes.c_int, _I, _F, _P],
     "qia_adaln_modulation": [_P, _P, _P, _P, _I, _I, _I, _I, _P],
     "qia_cfg_euler": [_P, _P, _P, _P, _I, _I, _F, _F, _P],
+    "qia_cfg_euler_sched": [_P, _P, _P, _P, _I, _I, _F, _P, _P],
+    "qia_rope21_table": [_P, _I, _P, _I, _P, _P, _P, _I, _I, _I, _I, _I, _P, _P],
+    "qia_proj_out_cfg_euler": [_P, _P, _P, _P, _P, _I, _I, _I, _F, _P, _P],
     "qia_ln_mod": [_P, _P, _P, _P, _I, _I, _I, _F, _P],
     "qia_ln_mod_quant": [_P, _P, _P, _P, _P, _I, _I, _I, _F, _P],
     "qia_gated_residual": [_P, _P, _P, _P, _I, _I, _I, _P],

@@ -31,13 +31,6 @@ def gelu_tanh(x: torch.Tensor) -> torch.Tensor:
     return out
 
 
-def install_swiglu(transformer):
-    for block in transformer.transformer_blocks:
-        def forward(self, hidden_states):
-            return self.out(swiglu(self.gate_layer(hidden_states), self.proj(hidden_states)))
-        block.img_mlp.forward = types.MethodType(forward, block.img_mlp)
-
-
 def rms_norm(x: torch.Tensor, weight: torch.Tensor, eps: float) -> torch.Tensor:
     _lib.require_cuda(x, weight)
     if (x.dtype != torch.bfloat16 or not x.is_contiguous() or x.shape[-1] != 128
@@ -49,16 +42,37 @@ def rms_norm(x: torch.Tensor, weight: torch.Tensor, eps: float) -> torch.Tensor:
     return out
 
 
-def install_qk_norm(transformer):
+def _qk_norm_kernel_ok(norm, x) -> bool:
+    """An input the qia_rms_norm kernel takes: contiguous CUDA bf16 rows of 128
+    and a bf16 weight without bias."""
+    w = getattr(norm, "weight", None)
+    return (x.is_cuda and x.dtype == torch.bfloat16 and x.is_contiguous() and x.shape[-1] == 128
+            and w is not None and w.dtype == torch.bfloat16 and w.is_contiguous()
+            and getattr(norm, "bias", None) is None)
+
+
+def install_qk_norm(transformer) -> None:
+    """Give every block's per-head Q/K RMSNorm (attn.norm_q / attn.norm_k) the
+    qia_rms_norm kernel (Diffusers RMSNorm's two roundings) for the inputs it
+    takes; other inputs keep the module's own forward (the reference's
+    install_qk_norm contract, src/qwen_image_accel/kernels/bf16.py:66-77)."""
     for block in transformer.transformer_blocks:
         for norm in (block.attn.norm_q, block.attn.norm_k):
-            eager = norm.forward
+            native = norm.forward
+            norm.forward = types.MethodType(
+                lambda mod, x, _native=native: rms_norm(x, mod.weight, mod.eps) if _qk_norm_kernel_ok(mod, x)
+                else _native(x), norm)
 
-            def forward(self, x, _eager=eager):
-                if (x.is_cuda and x.dtype == torch.bfloat16 and x.is_contiguous()
-                        and x.shape[-1] == 128 and self.weight is not None
-                        and self.weight.dtype == torch.bfloat16 and self.weight.is_contiguous()
-                        and self.bias is None):
-                    return rms_norm(x, self.weight, self.eps)
-                return _eager(x)
-            norm.forward = types.MethodType(forward, norm)
+
+def install_swiglu(transformer) -> None:
+    """Give every block's SwiGLU MLP (img_mlp: gate_layer, proj, out) the
+    qia_swiglu kernel between its projections (the reference's install_swiglu
+    contract, src/qwen_image_accel/kernels/bf16.py:39-43). Blocks whose decode
+    is routed (optimizations/decode.py) already run this MLP and are left
+    alone."""
+    routed = getattr(transformer, "_qia_decode", None)
+    for block in transformer.transformer_blocks:
+        if routed is not None:
+            continue
+        block.img_mlp.forward = types.MethodType(
+            lambda mlp, x: mlp.out(swiglu(mlp.gate_layer(x).contiguous(), mlp.proj(x).contiguous())), block.img_mlp)

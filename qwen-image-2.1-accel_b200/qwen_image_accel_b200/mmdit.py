@@ -43,9 +43,9 @@ from .kernels.elementwise import residual
 from .kernels.epilogue import layer_norm_scale_quantize_grouped
 from .kernels.layernorm import layer_norm_scale
 from .kernels.mxfp8 import quantize
-from .kernels.scheduler import cfg_euler
+from .kernels.scheduler import cfg_euler, proj_out_cfg_euler
 from .optimizations.mxfp8 import (MXFP8Linear, matmul_gate_residual_grouped, matmul_gelu_quantize_grouped,
-                                  matmul_grouped)
+                                  matmul_grouped, skip_block_indices)
 from .optimizations.sage_attention import (sage_attention_joint_quantized, sage_attention_split,
                                            sage_attention_split_quantized, workspace_bytes)
 from .kernels.bf16 import gelu_tanh
@@ -190,6 +190,7 @@ class _Linear:
 
 class DualStreamBlock:
     def __init__(self, params: dict, prefix: str, cfg: MMDiTConfig, quantized: bool, device):
+        self.quantized = quantized    # MXFP8 linears; False: bf16 (a skip block of the MXFP8 profiles)
         P = lambda n: params[prefix + n].to(device)  # noqa: E731
         cat = lambda names, suffix: torch.cat([P(f"attn.{n}.{suffix}") for n in names])  # noqa: E731
         self.img_qkv = _Linear(cat(("to_q", "to_k", "to_v"), "weight"), cat(("to_q", "to_k", "to_v"), "bias"), quantized)
@@ -209,12 +210,16 @@ class DualStreamBlock:
 class MMDiT:
     """Qwen-Image v1 dual-stream MMDiT on the libqia_b200 kernels."""
 
-    def __init__(self, cfg: MMDiTConfig, params, device="cuda", profile: str = "mxfp8_sage"):
+    def __init__(self, cfg: MMDiTConfig, params, device="cuda", profile: str = "mxfp8_sage", skip_blocks=None):
+        """skip_blocks: blocks whose linears stay bf16 in the MXFP8 profiles
+        (default: QW21_MXFP8_SKIP_BLOCKS, else the profile's list, else
+        "0,31", as the reference's quantize_transformer applies it)."""
         self.cfg, self.device = cfg, torch.device(device)
         prof = get_profile(profile)
         if not prof.fused:
             raise ValueError(f"profile {profile!r} has no fused path")
         self.quantized, self.sage = prof.quantized, prof.sage
+        self.skip_blocks = skip_block_indices(skip_blocks, prof.skip_blocks) if prof.quantized else set()
         get = params if callable(params) else (lambda n: params[n])
         dev = self.device
         G = lambda n: get(n).to(dev)  # noqa: E731
@@ -232,7 +237,7 @@ class MMDiT:
             pre = f"transformer_blocks.{i}."
             names = [pre + n for n in parameter_shapes_block_names()]
             local = {n: get(n) for n in names}
-            self.blocks.append(DualStreamBlock(local, pre, cfg, self.quantized, dev))
+            self.blocks.append(DualStreamBlock(local, pre, cfg, self.quantized and i not in self.skip_blocks, dev))
             for m in ("img_mod.1", "txt_mod.1"):
                 mod_w.append(local[pre + m + ".weight"].to(dev))
                 mod_b.append(local[pre + m + ".bias"].to(dev))
@@ -293,7 +298,8 @@ class MMDiT:
         sh1_i, s1_i, g1_i, sh2_i, s2_i, g2_i = mod_img
         sh1_t, s1_t, g1_t, sh2_t, s2_t, g2_t = mod_txt
         # ---- norm1 + modulation + Q|K|V projections
-        if self.quantized:
+        mx = blk.quantized
+        if mx:
             # image and text projections share N and K: one grouped launch
             a_i, a_t = layer_norm_scale_quantize_grouped([(x, s1_i, sh1_i), (c, s1_t, sh1_t)], self.ln)
             qkv_i, qkv_t = matmul_grouped([(blk.img_qkv.mx, a_i), (blk.txt_qkv.mx, a_t)])
@@ -302,7 +308,7 @@ class MMDiT:
             qkv_i = F.linear(layer_norm_scale(x, s1_i, self.ln, shift=sh1_i), blk.img_qkv.w, blk.img_qkv.b)
             qkv_t = F.linear(layer_norm_scale(c, s1_t, self.ln, shift=sh1_t), blk.txt_qkv.w, blk.txt_qkv.b)
         S = Lt + Li
-        if self.quantized and self.sage:
+        if mx and self.sage:
             # ---- QK-RMSNorm + RoPE + Sage quantization straight from the two
             # projections, joint attention, per-stream MXFP8 outputs for the
             # output projections (no bf16 Q/K/V or attention output in memory)
@@ -326,16 +332,16 @@ class MMDiT:
             self._attention(q, k, v, Lt, a_t, a_i)
             del q, k, v
         # ---- output projections + gated residual (in place on the streams)
-        if self.quantized and self.sage:
+        if mx and self.sage:
             pass
-        elif self.quantized:
+        elif mx:
             matmul_gate_residual_grouped([(blk.img_out.mx, quantize(a_i.view(B * Li, D)), g1_i, x),
                                           (blk.txt_out.mx, quantize(a_t.view(B * Lt, D)), g1_t, c)])
         else:
             x = residual(x, F.linear(a_i.view(B, Li, D), blk.img_out.w, blk.img_out.b), g1_i)
             c = residual(c, F.linear(a_t.view(B, Lt, D), blk.txt_out.w, blk.txt_out.b), g1_t)
         # ---- norm2 + modulation + GELU-tanh MLP + gated residual
-        if self.quantized:
+        if mx:
             n_i, n_t = layer_norm_scale_quantize_grouped([(x, s2_i, sh2_i), (c, s2_t, sh2_t)], self.ln)
             hi, ht = matmul_gelu_quantize_grouped([(blk.img_up.mx, n_i), (blk.txt_up.mx, n_t)])
             del n_i, n_t
@@ -363,11 +369,14 @@ class MMDiT:
         Hl, h0 = H // U, plan.u * (H // U)
         sh1_i, s1_i, g1_i, sh2_i, s2_i, g2_i = mod_img
         sh1_t, s1_t, g1_t, sh2_t, s2_t, g2_t = mod_txt
-        if not self.quantized:
-            raise NotImplementedError("the sharded step runs the MXFP8 profiles")
-        a_i, a_t = layer_norm_scale_quantize_grouped([(x, s1_i, sh1_i), (c, s1_t, sh1_t)], self.ln)
-        qkv_i, qkv_t = matmul_grouped([(blk.img_qkv.mx, a_i), (blk.txt_qkv.mx, a_t)])
-        del a_i, a_t
+        mx = blk.quantized
+        if mx:
+            a_i, a_t = layer_norm_scale_quantize_grouped([(x, s1_i, sh1_i), (c, s1_t, sh1_t)], self.ln)
+            qkv_i, qkv_t = matmul_grouped([(blk.img_qkv.mx, a_i), (blk.txt_qkv.mx, a_t)])
+            del a_i, a_t
+        else:
+            qkv_i = F.linear(layer_norm_scale(x, s1_i, self.ln, shift=sh1_i), blk.img_qkv.w, blk.img_qkv.b)
+            qkv_t = F.linear(layer_norm_scale(c, s1_t, self.ln, shift=sh1_t), blk.txt_qkv.w, blk.txt_qkv.b)
         # local Q/K/V: image tokens (all heads), text tokens (all heads)
         qi, ki, vi = (torch.empty(B, Sl, H, hd, device=x.device, dtype=torch.bfloat16) for _ in range(3))
         qt, kt, vt = (torch.empty(B, Lt, H, hd, device=x.device, dtype=torch.bfloat16) for _ in range(3))
@@ -390,6 +399,14 @@ class MMDiT:
             a_i[b] = head_to_seq(o_i[0], plan)
             a_t[b] = gather_heads(o_t[0], plan)
         del qi, ki, vi, qt, kt, vt
+        if not mx:
+            x = residual(x, F.linear(a_i.view(B, Sl, D), blk.img_out.w, blk.img_out.b), g1_i)
+            c = residual(c, F.linear(a_t.view(B, Lt, D), blk.txt_out.w, blk.txt_out.b), g1_t)
+            hi = gelu_tanh(F.linear(layer_norm_scale(x, s2_i, self.ln, shift=sh2_i), blk.img_up.w, blk.img_up.b))
+            x = residual(x, F.linear(hi, blk.img_down.w, blk.img_down.b), g2_i)
+            ht = gelu_tanh(F.linear(layer_norm_scale(c, s2_t, self.ln, shift=sh2_t), blk.txt_up.w, blk.txt_up.b))
+            c = residual(c, F.linear(ht, blk.txt_down.w, blk.txt_down.b), g2_t)
+            return x, c
         matmul_gate_residual_grouped([(blk.img_out.mx, quantize(a_i.view(B * Sl, D)), g1_i, x),
                                       (blk.txt_out.mx, quantize(a_t.view(B * Lt, D)), g1_t, c)])
         n_i, n_t = layer_norm_scale_quantize_grouped([(x, s2_i, sh2_i), (c, s2_t, sh2_t)], self.ln)
@@ -466,6 +483,12 @@ class MMDiT:
 
         shared_timestep: every batch row has the same timestep (the CFG
         batch), so the timestep embedding and modulation are computed once."""
+        y = self.forward_hidden(hidden_states, encoder_hidden_states, timestep, img_shape, shared_timestep)
+        return F.linear(y, *self.proj_out)
+
+    def forward_hidden(self, hidden_states: torch.Tensor, encoder_hidden_states: torch.Tensor,
+                       timestep: torch.Tensor, img_shape, shared_timestep: bool = False) -> torch.Tensor:
+        """forward() up to proj_out: the norm_out output [B, Li, D] bf16."""
         cfg = self.cfg
         x = F.linear(hidden_states, *self.img_in)
         t = timestep.to(torch.bfloat16)
@@ -484,21 +507,36 @@ class MMDiT:
             x, c = self.block_forward(blk, x, c, m_img, m_txt, freqs_img, freqs_txt)
         emb = F.linear(F.silu(temb), *self.norm_out)
         scale, shift = emb.chunk(2, dim=1)
-        y = layer_norm_scale(x, (1 + scale)[:, None].contiguous(), self.ln, shift=shift[:, None].contiguous())
-        return F.linear(y, *self.proj_out)
+        return layer_norm_scale(x, (1 + scale)[:, None].contiguous(), self.ln, shift=shift[:, None].contiguous())
+
+    @staticmethod
+    def schedule(sigma, sigma_next, device) -> torch.Tensor:
+        """The step's (sigma, sigma_next) as the device float32 pair the step
+        kernels read (a tensor given as `sigma` is taken as that pair)."""
+        if isinstance(sigma, torch.Tensor):
+            return sigma
+        return torch.tensor([sigma, sigma_next], dtype=torch.float32).to(device, non_blocking=True)
 
     def denoise_step(self, latents: torch.Tensor, prompt_embeds: torch.Tensor, negative_embeds: torch.Tensor,
-                     sigma: float, sigma_next: float, img_shape, cfg_scale: float = 4.0) -> torch.Tensor:
+                     sigma, sigma_next, img_shape, cfg_scale: float = 4.0,
+                     out: torch.Tensor | None = None) -> torch.Tensor:
         """One flow-matching Euler step with true CFG batched as B = 2
         (WHL:diffusers/pipelines/qwenimage/pipeline_qwenimage.py:643-681;
-        schedulers/scheduling_flow_match_euler_discrete.py:483-517)."""
+        schedulers/scheduling_flow_match_euler_discrete.py:483-517): the
+        transformer on [latents, latents] with [prompt, negative] embeddings,
+        then proj_out, the CFG combine and the Euler update in one kernel
+        (qia_proj_out_cfg_euler). sigma, sigma_next: host floats, or `sigma`
+        a device float32 tensor holding both (what a captured step reads; see
+        optimizations/cuda_graph.DenoiseStepGraph). out: the updated latents'
+        buffer (may be latents)."""
         b = latents.shape[0]
+        sig = self.schedule(sigma, sigma_next, latents.device)
         x_in = torch.cat([latents, latents])
         enc = torch.cat([prompt_embeds, negative_embeds])
-        t = torch.full((2 * b,), sigma, device=latents.device, dtype=latents.dtype)
-        v = self.forward(x_in, enc, t, img_shape, shared_timestep=True)
-        cond, neg = v[:b], v[b:]
-        return cfg_euler(cond.contiguous(), neg.contiguous(), latents.contiguous(), cfg_scale, sigma_next - sigma)
+        t = sig[:1].to(latents.dtype).expand(2 * b)
+        y = self.forward_hidden(x_in, enc, t, img_shape, shared_timestep=True)
+        w, bias = self.proj_out
+        return proj_out_cfg_euler(y, w, bias, latents.contiguous(), cfg_scale, sig, out=out)
 
 
     def forward_sharded(self, hidden_local: torch.Tensor, encoder_hidden_states: torch.Tensor,
@@ -542,12 +580,12 @@ class MMDiT:
         if not plan.cfg_split:
             raise ValueError("denoise_step_sharded needs a plan with a CFG split")
         b = latents_local.shape[0]
+        sig = self.schedule(sigma, sigma_next, latents_local.device)
         enc = prompt_embeds if plan.half == 0 else negative_embeds
-        t = torch.full((b,), sigma, device=latents_local.device, dtype=latents_local.dtype)
+        t = sig[:1].to(latents_local.dtype).expand(b)
         v = self.forward_sharded(latents_local, enc, t, img_shape, plan)
         cond, neg = exchange_cfg(v, plan)
-        return cfg_euler(cond.contiguous(), neg.contiguous(), latents_local.contiguous(), cfg_scale,
-                         sigma_next - sigma)
+        return cfg_euler(cond.contiguous(), neg.contiguous(), latents_local.contiguous(), cfg_scale, sigmas=sig)
 
 
 def parameter_shapes_block_names() -> list[str]:

@@ -38,6 +38,22 @@ class MXFP8Linear(nn.Module):
         b = linear.bias
         self.register_buffer("bias", None if b is None else b.detach().to(torch.bfloat16).contiguous())
 
+    @classmethod
+    def from_parts(cls, values: torch.Tensor, scales: torch.Tensor, bias: torch.Tensor | None = None):
+        """An MXFP8Linear over already quantized weights: values E4M3 [N, K]
+        row-major, scales the E8M0 128x4 layout of N rows (no copy)."""
+        self = cls.__new__(cls)
+        nn.Module.__init__(self)
+        self.out_features, self.in_features = values.shape
+        if not _supported(self.in_features, self.out_features):
+            raise ValueError("MXFP8Linear needs in/out features that are multiples of 128")
+        if scales.numel() != values.numel() // 32:
+            raise ValueError("scales must hold one E8M0 per 32 weights")
+        self.register_buffer("weight_fp8", values.t())
+        self.register_buffer("weight_scale", scales)
+        self.register_buffer("bias", bias)
+        return self
+
     # the [N, K] row-major view the kernels consume
     def _w(self):
         return self.weight_fp8.t()
@@ -178,54 +194,120 @@ def matmul_gate_residual_grouped(items) -> None:
     _grouped(_lib.EPI_GATE_RESIDUAL, problems)
 
 
-# Which of a block's linears each selection converts. `attention` covers the
-# projections around attention, `mlp` the feed-forward projections; names of
-# both the single-stream 2.1 block and the dual-stream v1 block are listed
-# (absent names are skipped).
-LAYER_GROUPS = {
-    "attention": ("attn.to_q", "attn.to_k", "attn.to_v", "attn.to_out.0",
-                  "attn.add_q_proj", "attn.add_k_proj", "attn.add_v_proj", "attn.to_add_out"),
-    "mlp": ("img_mlp.gate_layer", "img_mlp.proj", "img_mlp.out",
-            "img_mlp.net.0.proj", "img_mlp.net.2", "txt_mlp.net.0.proj", "txt_mlp.net.2"),
-}
-LAYER_GROUPS["all"] = LAYER_GROUPS["attention"] + LAYER_GROUPS["mlp"]
+# The linears a layer selection names, per group, over both block layouts this
+# package serves (the 2.1 single-stream block and the v1 dual-stream block); a
+# name a block does not have is passed over. The group and environment names
+# are the reference's interface (src/qwen_image_accel/optimizations/mxfp8.py:
+# 46-50); the v1 names are additions.
+_ATTENTION_LINEARS = ("attn.to_q", "attn.to_k", "attn.to_v", "attn.to_out.0",
+                      "attn.add_q_proj", "attn.add_k_proj", "attn.add_v_proj", "attn.to_add_out")
+_MLP_LINEARS = ("img_mlp.gate_layer", "img_mlp.proj", "img_mlp.out",
+                "img_mlp.net.0.proj", "img_mlp.net.2", "txt_mlp.net.0.proj", "txt_mlp.net.2")
+LAYER_GROUPS = {"attention": _ATTENTION_LINEARS, "mlp": _MLP_LINEARS, "all": _ATTENTION_LINEARS + _MLP_LINEARS}
 
 
-def selected_layers(selection=None):
-    """Resolve QW21_MXFP8_LAYERS: a group name or an explicit comma-separated list."""
-    raw = (selection if selection is not None else os.environ.get("QW21_MXFP8_LAYERS", "all")).strip()
-    if raw in LAYER_GROUPS:
-        return set(LAYER_GROUPS[raw])
-    names = {n.strip() for n in raw.split(",") if n.strip()}
-    unknown = names - set(LAYER_GROUPS["all"])
+def selected_layers(selection: str | None = None) -> set:
+    """The linear names a selection converts. `selection` (default: the
+    QW21_MXFP8_LAYERS environment variable, else "all") is a group name of
+    LAYER_GROUPS or a comma-separated list of linear names; an unknown name is
+    a ValueError."""
+    spec = (os.environ.get("QW21_MXFP8_LAYERS", "all") if selection is None else selection).strip()
+    if spec in LAYER_GROUPS:
+        return set(LAYER_GROUPS[spec])
+    chosen = {part.strip() for part in spec.split(",")} - {""}
+    unknown = chosen.difference(LAYER_GROUPS["all"])
     if unknown:
-        raise ValueError(f"Unknown MXFP8 layer names {sorted(unknown)}; "
-                         f"choose from {sorted(LAYER_GROUPS['all'])} or {sorted(LAYER_GROUPS)}")
-    return names
+        raise ValueError(f"QW21_MXFP8_LAYERS: {sorted(unknown)} are not block linears; give a group "
+                         f"({', '.join(LAYER_GROUPS)}) or names from {sorted(LAYER_GROUPS['all'])}")
+    return chosen
 
 
-def quantize_transformer(transformer, skip_blocks=None, layers=None):
-    """Replace selected block linears with MXFP8Linear; everything else stays BF16.
+def skip_block_indices(skip_blocks=None, profile_default: str | None = None) -> set:
+    """Block indices that keep every linear in bf16: `skip_blocks` (a
+    comma-separated string or an iterable of ints), else the
+    QW21_MXFP8_SKIP_BLOCKS environment variable, else the profile's own list
+    (`profile_default`, e.g. the balanced profiles' "0,1,2,29,30,31"), else
+    "0,31" -- the reference's default (src/qwen_image_accel/pipeline.py:133),
+    taken literally whatever the depth of the stack."""
+    if skip_blocks is None:
+        skip_blocks = os.environ.get("QW21_MXFP8_SKIP_BLOCKS", profile_default or "0,31")
+    if isinstance(skip_blocks, str):
+        return {int(tok) for tok in skip_blocks.split(",") if tok.strip()}
+    return {int(i) for i in skip_blocks}
 
-    Blocks listed in skip_blocks (default QW21_MXFP8_SKIP_BLOCKS or "0,31")
-    keep every linear in BF16. Returns the converted module names."""
-    raw = skip_blocks if skip_blocks is not None else os.environ.get("QW21_MXFP8_SKIP_BLOCKS", "0,31")
-    skip = {int(i) for i in str(raw).split(",") if i.strip()}
-    wanted = selected_layers(layers)
+
+def _owner(module: nn.Module, dotted: str):
+    """(parent module, attribute name) of a dotted child path, or None."""
+    parent_path, _, leaf = dotted.rpartition(".")
+    try:
+        parent = module.get_submodule(parent_path) if parent_path else module
+    except AttributeError:
+        return None
+    return (parent, leaf) if isinstance(getattr(parent, leaf, None), nn.Module) else None
+
+
+def quantize_transformer(transformer, skip_blocks=None, layers=None) -> list:
+    """Swap the selected bf16 linears of every block outside skip_blocks for
+    MXFP8Linear (weights quantized once, here); norms, modulation,
+    embeddings, the output projection and every non-block module stay as
+    they are. Returns the converted modules' names
+    ("transformer_blocks.<i>.<linear>")."""
+    keep_bf16 = skip_block_indices(skip_blocks)
+    names = sorted(selected_layers(layers))
     converted = []
     with torch.no_grad():
         for index, block in enumerate(transformer.transformer_blocks):
-            if index in skip:
+            if index in keep_bf16:
                 continue
-            for name in sorted(wanted):
-                try:
-                    child = block.get_submodule(name)
-                except AttributeError:
+            for name in names:
+                found = _owner(block, name)
+                if found is None:
                     continue
-                if not isinstance(child, nn.Linear) or not _supported(child.in_features, child.out_features):
+                parent, leaf = found
+                lin = getattr(parent, leaf)
+                if type(lin) is not nn.Linear or not _supported(lin.in_features, lin.out_features):
                     continue
-                parent_name, _, leaf = name.rpartition(".")
-                parent = block.get_submodule(parent_name) if parent_name else block
-                setattr(parent, leaf, MXFP8Linear(child))
+                setattr(parent, leaf, MXFP8Linear(lin))
                 converted.append(f"transformer_blocks.{index}.{name}")
     return converted
+
+
+def stack_linears(linears) -> nn.Module:
+    """One linear whose output rows are those of `linears` in order (all
+    MXFP8Linear or all bias-free bf16 nn.Linear, same in_features), whose
+    storage the given modules then share: each of them is left holding views
+    into the stacked weight, so nothing is duplicated and each still computes
+    its own rows. (MXFP8 scales stack by concatenation: the 128x4 layout
+    orders whole 128-row tiles, and every out_features is a multiple of 128.)"""
+    linears = list(linears)
+    k = linears[0].in_features
+    if any(l.in_features != k for l in linears):
+        raise ValueError("stacked linears must share in_features")
+    if all(isinstance(l, MXFP8Linear) for l in linears):
+        values = torch.cat([l._w() for l in linears])
+        scales = torch.cat([l.weight_scale for l in linears])
+        has_bias = [l.bias is not None for l in linears]
+        if any(has_bias) and not all(has_bias):
+            raise ValueError("stacked MXFP8 linears must all have a bias or none")
+        bias = torch.cat([l.bias for l in linears]) if all(has_bias) else None
+        stacked = MXFP8Linear.from_parts(values, scales, bias)
+        r = c = 0
+        for l in linears:
+            n, ns = l.out_features, l.weight_scale.numel()
+            l.weight_fp8 = values[r:r + n].t()
+            l.weight_scale = scales[c:c + ns]
+            if bias is not None:
+                l.bias = bias[r:r + n]
+            r, c = r + n, c + ns
+        return stacked
+    if all(type(l) is nn.Linear and l.bias is None for l in linears):
+        weight = torch.cat([l.weight.detach() for l in linears])
+        stacked = nn.Linear(k, weight.shape[0], bias=False, device=weight.device, dtype=weight.dtype)
+        stacked.weight = nn.Parameter(weight, requires_grad=False)
+        r = 0
+        for l in linears:
+            n = l.out_features
+            l.weight = nn.Parameter(weight[r:r + n], requires_grad=False)
+            r += n
+        return stacked
+    raise ValueError("stack_linears takes all-MXFP8 or all bias-free bf16 linears")

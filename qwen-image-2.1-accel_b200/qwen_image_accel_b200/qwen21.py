@@ -128,16 +128,26 @@ class _Norm:
 
 class Block21:
     """One 2.1 block (params: a name -> tensor mapping or callable with the
-    Diffusers names of block21_parameter_shapes)."""
+    Diffusers names of block21_parameter_shapes).
+
+    Each linear is an MXFP8Linear (tcgen05 block-scaled GEMM) or a bf16
+    nn.Linear, chosen per linear: the profile's `quantized` flag sets all of
+    them, `quantized=False` keeps a block in bf16 (the profile's skip_blocks),
+    and Block21.bind takes whatever modules a caller's model already holds.
+    Every fused step is chosen from the types it finds: MXFP8 straight out of
+    the LayerNorm when all of its consumers are MXFP8, the attention output as
+    MXFP8 into the output projection's gate-residual epilogue when that
+    projection is MXFP8, the SwiGLU fused with the quantization of the down
+    projection's operand when gate, value and down projections are MXFP8."""
 
     def __init__(self, params: Callable[[str], torch.Tensor] | dict, cfg: Block21Config = Block21Config(),
-                 device="cuda", profile: str = "mxfp8_sage", sage_prefill: bool = False):
+                 device="cuda", profile: str = "mxfp8_sage", sage_prefill: bool = False,
+                 quantized: bool | None = None):
         prof = get_profile(profile)
         if not prof.fused:
             raise ValueError(f"profile {profile!r} has no fused decode path")
         get = params if callable(params) else params.__getitem__
-        self.cfg = cfg
-        self.quantized, self.sage, self.sage_prefill = prof.quantized, prof.sage, sage_prefill
+        mx = prof.quantized if quantized is None else quantized
         dev = torch.device(device)
 
         def linear(name_or_weight):
@@ -146,35 +156,73 @@ class Block21:
             lin = nn.Linear(w.shape[1], w.shape[0], bias=False, device=dev, dtype=torch.bfloat16)
             with torch.no_grad():
                 lin.weight.copy_(w)
-            return MXFP8Linear(lin) if self.quantized else lin
+            return MXFP8Linear(lin) if mx else lin
 
-        self.qkv = linear(torch.cat([get(f"attn.to_{n}.weight") for n in "qkv"]))
-        self.to_out = linear("attn.to_out.0.weight")
-        self.gate_layer, self.proj, self.out = (linear(f"img_mlp.{n}.weight") for n in ("gate_layer", "proj", "out"))
-        self.norm_q = _Norm(get("attn.norm_q.weight").to(dev, torch.bfloat16).contiguous(), cfg.eps)
-        self.norm_k = _Norm(get("attn.norm_k.weight").to(dev, torch.bfloat16).contiguous(), cfg.eps)
+        self._setup(cfg, prof.sage, sage_prefill,
+                    qkv=linear(torch.cat([get(f"attn.to_{n}.weight") for n in "qkv"])),
+                    to_out=linear("attn.to_out.0.weight"),
+                    mlp=tuple(linear(f"img_mlp.{n}.weight") for n in ("gate_layer", "proj", "out")),
+                    norm_q=get("attn.norm_q.weight").to(dev, torch.bfloat16).contiguous(),
+                    norm_k=get("attn.norm_k.weight").to(dev, torch.bfloat16).contiguous())
+
+    @classmethod
+    def bind(cls, qkv, to_out, mlp, norm_q: torch.Tensor, norm_k: torch.Tensor, cfg: Block21Config, sage: bool,
+             sage_prefill: bool = False) -> "Block21":
+        """A Block21 over modules a caller already holds, sharing their
+        weights: qkv is one linear over the stacked [W_q; W_k; W_v] rows or a
+        (to_q, to_k, to_v) tuple; to_out, mlp = (gate_layer, proj, out) are
+        nn.Linear (bf16, no bias) or MXFP8Linear modules."""
+        self = cls.__new__(cls)
+        self._setup(cfg, sage, sage_prefill, qkv=qkv, to_out=to_out, mlp=tuple(mlp), norm_q=norm_q, norm_k=norm_k)
+        return self
+
+    def _setup(self, cfg, sage, sage_prefill, qkv, to_out, mlp, norm_q, norm_k):
+        self.cfg = cfg
+        self.sage, self.sage_prefill = sage, sage_prefill
+        self.qkv, self.to_out = qkv, to_out
+        self.gate_layer, self.proj, self.out = mlp
+        self.norm_q = _Norm(norm_q, cfg.eps)
+        self.norm_k = _Norm(norm_k, cfg.eps)
         self.norm = _Norm(None, cfg.eps, (cfg.dim,))          # img_norm1 / img_norm2: no affine
+        parts = qkv if isinstance(qkv, tuple) else (qkv,)
+        self.qkv_mx = all(isinstance(p, MXFP8Linear) for p in parts)
+        self.out_mx = isinstance(to_out, MXFP8Linear)
+        self.gv_mx = isinstance(self.gate_layer, MXFP8Linear) and isinstance(self.proj, MXFP8Linear)
+        self.down_mx = isinstance(self.out, MXFP8Linear)
+
+    @property
+    def quantized(self) -> bool:
+        """Every linear of the block is MXFP8."""
+        return self.qkv_mx and self.out_mx and self.gv_mx and self.down_mx
 
     # ------------------------------------------------------------------ helpers
-    def _normalized(self, h, scale):
-        """LN(h) x scale, as MXFP8 straight out of the LN when the consumers
-        are MXFP8 linears (quantized_decode.py:99-105)."""
-        if not self.quantized:
+    def _normalized(self, h, scale, mx: bool):
+        """LN(h) x scale, as MXFP8 straight out of the LN when its consumers
+        are MXFP8 linears (mx), else bf16."""
+        if not mx:
             return layer_norm_scale(h, scale, self.norm)
         x = layer_norm_scale_quantize(h, scale, self.norm)
         if x is None:
             raise NotImplementedError(f"LN + MXFP8: unsupported input {tuple(h.shape)}")
         return x
 
+    @staticmethod
+    def _apply(lin, x):
+        """One linear on x: an MXFP8 activation (Quantized) or a bf16 tensor."""
+        if isinstance(lin, MXFP8Linear):
+            if isinstance(x, torch.Tensor):
+                x = quantize(x.reshape(-1, x.shape[-1]).contiguous())
+            return lin.matmul(x)
+        return F.linear(x, lin.weight)
+
     def _qkv_into(self, x, b, s, freqs, oq, ok, ov, offset):
         """q|k|v projection of the LN output x (bf16 tensor, or MXFP8 Quantized
-        in the quantized profiles) for s tokens per sample, RMS-normalised and
-        rotated into rows [offset, offset + s) of the joint NHD buffers."""
-        if self.quantized:
-            a = x if not isinstance(x, torch.Tensor) else quantize(x.reshape(-1, x.shape[-1]))
-            qkv = self.qkv.matmul(a).view(b, s, -1)
+        when the projections are MXFP8) for s tokens per sample, RMS-normalised
+        and rotated into rows [offset, offset + s) of the joint NHD buffers."""
+        if isinstance(self.qkv, tuple):
+            qkv = torch.cat([self._apply(p, x).view(b, s, -1) for p in self.qkv], dim=-1)
         else:
-            qkv = F.linear(x, self.qkv.weight).view(b, s, -1)
+            qkv = self._apply(self.qkv, x).view(b, s, -1)
         joint_qk_norm_rope(qkv, self.norm_q.weight, self.norm_k.weight, torch.view_as_real(freqs).contiguous(),
                            oq, ok, ov, offset, eps=self.cfg.eps)
 
@@ -183,28 +231,33 @@ class Block21:
         return tuple(torch.empty(shape, device=device, dtype=torch.bfloat16) for _ in range(3))
 
     def _out_proj(self, attn):
-        flat = attn.flatten(2, 3)
-        if self.quantized:
-            return self.to_out(flat.contiguous())
-        return F.linear(flat, self.to_out.weight)
+        return self._apply(self.to_out, attn.flatten(2, 3).contiguous()).view(*attn.shape[:2], -1)
 
     def _swiglu_act(self, x):
-        """MXFP8 SwiGLU activation of the MLP (quantized profiles): the gate and
-        value projections of one shared activation in one grouped launch, then
-        SwiGLU + quantization in one pass. (The single-GEMM form with the
-        SwiGLU in the epilogue, MXFP8Linear.matmul_swiglu_quantize, gives the
-        same bytes but measured slower here: its per-element IEEE divide and
-        exp hold the accumulator hand-off of the GEMM.)"""
-        a = x if not isinstance(x, torch.Tensor) else quantize(x.reshape(-1, x.shape[-1]))
+        """MXFP8 SwiGLU activation of the MLP (gate, value and down projections
+        MXFP8): the gate and value projections of one shared activation in one
+        grouped launch, then SwiGLU + quantization in one pass. (The
+        single-GEMM form with the SwiGLU in the epilogue,
+        MXFP8Linear.matmul_swiglu_quantize, gives the same bytes but measured
+        slower here: its per-element IEEE divide and exp hold the accumulator
+        hand-off of the GEMM.)"""
+        a = x if not isinstance(x, torch.Tensor) else quantize(x.reshape(-1, x.shape[-1]).contiguous())
         gate, value = matmul_grouped([(self.gate_layer, a), (self.proj, a)])
         return swiglu_quantize(gate, value)
 
+    def _gate_value(self, x):
+        if self.gv_mx:
+            a = x if not isinstance(x, torch.Tensor) else quantize(x.reshape(-1, x.shape[-1]).contiguous())
+            return matmul_grouped([(self.gate_layer, a), (self.proj, a)])
+        return self._apply(self.gate_layer, x), self._apply(self.proj, x)
+
     def _mlp(self, x, lead):
-        """SwiGLU MLP; x is the LN output (bf16) or its MXFP8 quantization."""
-        if self.quantized:
+        """SwiGLU MLP; x is the LN output (bf16, or its MXFP8 quantization when
+        the gate and value projections are MXFP8)."""
+        if self.gv_mx and self.down_mx:
             return self.out.matmul(self._swiglu_act(x)).view(*lead, -1)
-        return F.linear(swiglu(F.linear(x, self.gate_layer.weight), F.linear(x, self.proj.weight)),
-                        self.out.weight)
+        gate, value = self._gate_value(x)
+        return self._apply(self.out, swiglu(gate.contiguous(), value.contiguous())).view(*lead, -1)
 
     def _rows(self, name, x, vectors, prefix_len, other=None):
         """LN x (1+s) (name "ln") or the gated residual (name "res") with the
@@ -246,9 +299,9 @@ class Block21:
         oq, ok, ov = self._joint(b, p + st, h.device)
         ok[:, :p].copy_(cached_k)
         ov[:, :p].copy_(cached_v)
-        self._qkv_into(self._normalized(h, s1), b, st, freqs, oq, ok, ov, p)
+        self._qkv_into(self._normalized(h, s1, self.qkv_mx), b, st, freqs, oq, ok, ov, p)
         q = oq[:, p:]
-        if self.sage and key_valid is None and self.quantized:
+        if self.sage and key_valid is None and self.out_mx:
             h = self.to_out.matmul_gate_residual(sage_attention_quantized(q, ok, ov), g1, h)
         else:
             if self.sage and key_valid is None:
@@ -258,10 +311,33 @@ class Block21:
                 attn = F.scaled_dot_product_attention(q.transpose(1, 2), ok.transpose(1, 2), ov.transpose(1, 2),
                                                       attn_mask=mask).transpose(1, 2)
             h = residual(h, self._out_proj(attn).contiguous(), g1)
-        x = self._normalized(h, s2)
-        if self.quantized:
+        x = self._normalized(h, s2, self.gv_mx)
+        if self.gv_mx and self.down_mx:
             return self.out.matmul_gate_residual(self._swiglu_act(x), g2, h)
         return residual(h, self._mlp(x, (b, st)).contiguous(), g2)
+
+    def attention_cached(self, x, freqs: torch.Tensor, layer_cache: KVLayerCache,
+                         key_valid: torch.Tensor | None = None) -> torch.Tensor:
+        """The attention half of the cached decode on an already modulated
+        input x [B, St, D] bf16: Q/K/V projections, QK-RMSNorm + RoPE behind the
+        cached prefix K/V, attention over [prefix, target] (Sage when the block
+        has it and nothing is masked, else SDPA), output projection -> bf16
+        [B, St, D]."""
+        b, st, _ = x.shape
+        cached_k, cached_v = layer_cache.get()
+        p = cached_k.shape[1]
+        oq, ok, ov = self._joint(b, p + st, x.device)
+        ok[:, :p].copy_(cached_k)
+        ov[:, :p].copy_(cached_v)
+        self._qkv_into(x.contiguous(), b, st, freqs, oq, ok, ov, p)
+        q = oq[:, p:]
+        if self.sage and key_valid is None:
+            attn = sage_attention(q, ok, ov)
+        else:
+            mask = None if key_valid is None else key_valid[:, None, None, :]
+            attn = F.scaled_dot_product_attention(q.transpose(1, 2), ok.transpose(1, 2), ov.transpose(1, 2),
+                                                  attn_mask=mask).transpose(1, 2)
+        return self._out_proj(attn)
 
     def forward_prefill(self, h: torch.Tensor, modulation: torch.Tensor, freqs: torch.Tensor,
                         image_ids: torch.Tensor, prefix_len: int, layer_cache: KVLayerCache | None = None,

@@ -17,6 +17,7 @@ the reference's own ops; the per-token work is in the blocks.
 """
 from __future__ import annotations
 
+import ctypes
 import math
 
 import torch
@@ -24,6 +25,8 @@ import torch.nn.functional as F
 
 from . import _lib
 from .kernels.layernorm import layer_norm_scale
+from .optimizations.mxfp8 import skip_block_indices
+from .profiles import get_profile
 from .qwen21 import Block21, Block21Config, KVCache, _Norm, block21_parameter_shapes, modulation_values
 
 
@@ -109,6 +112,35 @@ def rope_table(img_shapes, image_pad_mask: torch.Tensor, axes_dim=(16, 56, 56), 
     return torch.cat([tabs[0][frame_index], tabs[1][h_index], tabs[2][w_index]], dim=-1)
 
 
+_DEVICE_AXES: dict = {}
+
+
+def rope_table_device(img_shapes, image_pad_mask: torch.Tensor, axes_dim=(16, 56, 56),
+                      theta: int = 10000) -> torch.Tensor:
+    """rope_table built on the device (qia_rope21_table): the same integer
+    positions, taken with prefix sums over the image mask instead of the
+    reference's host loop, and the same per-axis complex64 rows gathered --
+    bit-identical to rope_table. image_pad_mask: bool [S] on the GPU; the
+    result is complex64 [S, sum(axes_dim)/2] on the same device."""
+    dev = image_pad_mask.device
+    _lib.require_cuda(image_pad_mask)
+    key = (tuple(axes_dim), theta, str(dev))
+    tabs = _DEVICE_AXES.get(key)
+    if tabs is None:
+        tabs = _DEVICE_AXES[key] = [torch.view_as_real(_axis_table(d, theta)).to(dev).contiguous()
+                                    for d in axes_dim]
+    hw = (ctypes.c_int32 * (2 * max(1, len(img_shapes))))()
+    for i, (_, h, w) in enumerate(img_shapes):
+        hw[2 * i], hw[2 * i + 1] = int(h), int(w)
+    mask = image_pad_mask.to(torch.uint8).contiguous()
+    s = mask.shape[0]
+    out = torch.empty(s, sum(axes_dim) // 2, 2, device=dev, dtype=torch.float32)
+    _lib.call("qia_rope21_table", _lib.ptr(mask), s, ctypes.cast(hw, ctypes.c_void_p), len(img_shapes),
+              _lib.ptr(tabs[0]), _lib.ptr(tabs[1]), _lib.ptr(tabs[2]), axes_dim[0] // 2, axes_dim[1] // 2,
+              axes_dim[2] // 2, 8192, 1024, _lib.ptr(out), _lib.stream(dev))
+    return torch.view_as_complex(out)
+
+
 class Qwen21Transformer:
     """QwenImage21Transformer2DModel on the sm_100a kernels (causal_condition,
     patch size 1). params: name -> tensor mapping or callable with the
@@ -116,9 +148,14 @@ class Qwen21Transformer:
 
     def __init__(self, params, num_layers: int = 32, cfg: Block21Config = Block21Config(),
                  context_in_dim: int = 4096, device="cuda", profile: str = "mxfp8_sage", sage_prefill: bool = False,
-                 axes_dims_rope=(16, 56, 56)):
+                 axes_dims_rope=(16, 56, 56), skip_blocks=None):
         get = params if callable(params) else params.__getitem__
         dev = torch.device(device)
+        prof = get_profile(profile)
+        # blocks that keep bf16 linears in the MXFP8 profiles (default: the
+        # QW21_MXFP8_SKIP_BLOCKS environment variable, else the profile's list,
+        # else "0,31", as configure_pipeline / quantize_transformer)
+        self.skip_blocks = skip_block_indices(skip_blocks, prof.skip_blocks) if prof.quantized else set()
         self.cfg, self.axes = cfg, tuple(axes_dims_rope)
         w = lambda n: get(n).to(dev, torch.bfloat16).contiguous()
         self.w = {n: w(n) for n in ("img_in.weight", "modulation.1.weight", "norm_out.linear.weight",
@@ -126,7 +163,8 @@ class Qwen21Transformer:
                                     "time_text_embed.timestep_embedder.linear_2.weight", "txt_in.text_norm.weight",
                                     "txt_in.in_layer.weight", "txt_in.out_layer.weight")}
         self.blocks = [Block21(lambda n, i=i: get(f"transformer_blocks.{i}.{n}"), cfg, device=dev, profile=profile,
-                               sage_prefill=sage_prefill) for i in range(num_layers)]
+                               sage_prefill=sage_prefill, quantized=prof.quantized and i not in self.skip_blocks)
+                       for i in range(num_layers)]
         self.ln = _Norm(None, cfg.eps, (cfg.dim,))
         self._layouts: dict = {}
         # QwenImage21TemporalTimesteps(256): frequencies built once in fp32 on the CPU
@@ -166,7 +204,7 @@ class Qwen21Transformer:
         image_pad_mask = torch.repeat_interleave(img_mask[0], repeats)
         image_ids, target = token_metadata(image_pad_mask.to(device), img_shapes[0])
         lay = {"repeats": repeats.to(device), "pad": image_pad_mask.to(device), "pad_cpu": image_pad_mask.cpu(),
-               "rope": rope_table(img_shapes[0], image_pad_mask, self.axes).to(device), "image_ids": image_ids,
+               "rope": rope_table_device(img_shapes[0], image_pad_mask.to(device), self.axes), "image_ids": image_ids,
                "target": target, "prefix_len": int((~target).sum())}
         if len(self._layouts) >= 8:
             self._layouts.pop(next(iter(self._layouts)))

@@ -103,3 +103,37 @@ def test_shared_timestep_modulation_matches_per_row():
     a = model.forward(x, enc, t, shape).float()
     b = model.forward(x, enc, t, shape, shared_timestep=True).float()
     assert psnr(b.cpu(), a.cpu()) >= 60.0
+
+
+def test_overlapped_modulation_survives_allocator_churn():
+    """The side-stream modulation launches read SiLU(temb) and write the
+    vectors buffer, both allocated on the main stream: main-stream
+    allocations made meanwhile must not reuse their memory. The vectors are
+    compared bit for bit with a run without that churn."""
+    from qwen_image_accel_b200.mmdit import MMDiT, MMDiTConfig, random_parameters
+    cfg = MMDiTConfig(num_layers=6, num_attention_heads=4, joint_attention_dim=512)
+    model = MMDiT(cfg, random_parameters(cfg, 7, "cpu"), device="cuda", profile="mxfp8_sage")
+    g = torch.Generator(device="cuda").manual_seed(3)
+    temb = torch.randn(1, cfg.dim, device="cuda", dtype=torch.bfloat16, generator=g)
+    main = torch.cuda.current_stream()
+
+    def collect(churn: bool):
+        mods, events = model.modulations_overlapped(temb.clone())
+        junk = []
+        if churn:
+            for i in range(64):           # reuse freed blocks of every size class on the main stream
+                t = torch.full((1 << (8 + i % 12),), float(i), device="cuda", dtype=torch.bfloat16)
+                junk.append(t * 2)
+                del t
+        out = []
+        for m, ev in zip(mods, events):
+            if ev is not None:
+                main.wait_event(ev)
+            out.append(torch.cat([v.reshape(-1) for s in m for v in s]).clone())
+        del junk
+        return torch.stack(out)
+
+    clean = collect(False)
+    torch.cuda.synchronize()
+    for _ in range(3):
+        assert torch.equal(collect(True), clean)

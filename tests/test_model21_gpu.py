@@ -67,3 +67,34 @@ def test_prefill_extract_then_cached_step(profile, sage_prefill, min_psnr, min_c
         assert a.shape == b.shape and torch.isfinite(a).all(), name
     for name, (pv, cv) in report.items():
         assert pv >= min_psnr and cv >= min_cos, (name, pv, cv)
+
+
+ROPE_LAYOUTS = {
+    "golden": ([("t", 20), ("i", 48), ("t", 6), ("i", 64)], [(1, 6, 8), (1, 8, 8)]),
+    "adjacent": ([("t", 4), ("i", 4), ("i", 6), ("t", 2), ("i", 12)], [(1, 2, 2), (1, 2, 3), (1, 3, 4)]),
+    "edit_1024": ([("t", 113), ("i", 4096), ("t", 20), ("i", 4096)], [(1, 64, 64), (1, 64, 64)]),
+    "t2i_2048_odd": ([("t", 97), ("i", 128 * 96)], [(1, 128, 96)]),
+    "trailing_text": ([("t", 3), ("i", 15), ("t", 300)], [(1, 3, 5)]),
+}
+
+
+@pytest.mark.parametrize("name", list(ROPE_LAYOUTS))
+def test_rope_table_on_device_is_bit_identical(name):
+    """qia_rope21_table (positions by prefix sums on the GPU, then the exact
+    per-axis gather) against the host table of the reference's loop
+    (rope_table, itself pinned to QwenImage21Rope's output)."""
+    from qwen_image_accel_b200.qwen21_model import rope_table, rope_table_device
+    runs, shapes = ROPE_LAYOUTS[name]
+    mask = torch.cat([torch.full((n,), kind == "i") for kind, n in runs])
+    host = rope_table(shapes, mask)
+    dev = rope_table_device(shapes, mask.cuda())
+    assert dev.shape == host.shape
+    assert torch.equal(torch.view_as_real(dev).cpu(), torch.view_as_real(host))
+
+
+def test_rope_table_device_rejects_positions_past_the_tables():
+    from qwen_image_accel_b200 import _lib
+    from qwen_image_accel_b200.qwen21_model import rope_table_device
+    mask = torch.ones(2 * 4100, dtype=torch.bool, device="cuda")
+    with pytest.raises(_lib.QiaError):
+        rope_table_device([(1, 2, 4100)], mask)        # a 4100-wide grid needs 2050 negative rows (1024 held)

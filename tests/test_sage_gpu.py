@@ -1,8 +1,8 @@
 """GPU parity of the Sage-style INT8/FP8 attention (tcgen05).
 
 * quantization half: the bf16 K mean is bit-exact against the CPU oracle
-  (oracle.sage_quant_*), INT8 Q/K and FP8 V codes within one step in at most
-  1 in 1000 elements and scales within 2 ulp (the kernels use the reference's
+  (oracle.sage_quant_*), INT8 Q/K and FP8 V codes within one step (at
+  rounding ties) in at most 1 in 100 elements and scales within 2 ulp (the kernels use the reference's
   fast-math divide, the oracle IEEE; test_sage_ref_gpu.py pins the kernels bit
   for bit against the built reference);
 * attention: cosine >= 0.999 (BASELINE north_star gate) against the oracle's
@@ -57,16 +57,19 @@ def test_quantization_bit_exact(b, sq, skv, h):
     assert np.array_equal(ws["k_mean"].float().view(b, h, 128).cpu().numpy(), km)
     # the kernels divide as the reference's fast-math build does (pinned bit for
     # bit against it in test_sage_ref_gpu.py); the oracle's IEEE divides may
-    # move a code by one or a scale by an ulp or two
+    # move a scale by an ulp or two, and a code by one where x * 127/amax (or
+    # v * 448/amax) sits exactly on a rounding tie -- frequent with bf16 data,
+    # whose values and block maxima share few significant bits (e.g. v = 0.539,
+    # amax = 2.875: v * 448/amax = 84.0 exactly, the tie between E4M3 80 and 88)
     for got, want in ((got_q8, q8), (got_k8, k8)):
         diff = np.abs(got.astype(np.int32) - want.astype(np.int32))
-        assert diff.max() <= 1 and np.count_nonzero(diff) * 1000 <= diff.size
+        assert diff.max() <= 1 and np.count_nonzero(diff) * 100 <= diff.size
     for got, want in ((ws["q_scale"].view(b, h, -1)[:, :, : qs.shape[-1]].cpu().numpy(), qs),
                       (ws["k_scale"].view(b, h, -1)[:, :, : ks.shape[-1]].cpu().numpy(), ks),
                       (ws["v_scale"].view(b, h, 128).cpu().numpy(), vs)):
         assert np.abs(got.view(np.int32) - want.view(np.int32)).max() <= 2
     vdiff = np.abs(got_v8.astype(np.int32) - v8.astype(np.int32))
-    assert vdiff.max() <= 1 and np.count_nonzero(vdiff) * 1000 <= vdiff.size
+    assert vdiff.max() <= 1 and np.count_nonzero(vdiff) * 100 <= vdiff.size
     # padding rows are zero
     assert int(ws["q8"].view(bh, -1, 128)[:, sq:].abs().sum()) == 0
     assert int(ws["k8"].view(bh, -1, 128)[:, skv:].abs().sum()) == 0

@@ -1,0 +1,96 @@
+"""The denoise step's tail and its graph replay on the GPU:
+
+* qia_proj_out_cfg_euler (proj_out GEMM on tcgen05 + CFG combine + Euler
+  update in one kernel) against the eager sequence it replaces -- F.linear
+  (cuBLAS), the pipeline's CFG combine with norm rescale, the scheduler's
+  fp32 Euler step (WHL:diffusers/pipelines/qwenimage/pipeline_qwenimage.py:
+  643-681; schedulers/scheduling_flow_match_euler_discrete.py:483-517). The
+  GEMM sums in another order than cuBLAS, so a proj_out value can land one
+  bf16 ulp apart at a rounding boundary: the updated latents must be equal
+  for >= 99 % of elements and within 2 bf16 ulp of the larger of the result
+  and the step's update everywhere;
+* qia_cfg_euler_sched (dt read on the device) bit-identical to qia_cfg_euler
+  with the same dt;
+* DenoiseStepGraph (the whole step in one CUDA graph) bit-identical to the
+  eager denoise_step over several steps of a schedule.
+"""
+import pytest
+import torch
+import torch.nn.functional as F
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(autouse=True)
+def _cuda():
+    if not torch.cuda.is_available():
+        pytest.skip("needs a CUDA device")
+
+
+def eager_tail(y, w, b, lat, s, sigmas):
+    rows = lat.shape[0] * lat.shape[1]
+    v = F.linear(y, w, b).view(2, rows, 64)
+    cond, neg = v[0].view_as(lat), v[1].view_as(lat)
+    comb = neg + s * (cond - neg)
+    noise = comb * (torch.norm(cond, dim=-1, keepdim=True) / torch.norm(comb, dim=-1, keepdim=True))
+    dt = sigmas[1] - sigmas[0]
+    return (lat.to(torch.float32) + dt * noise).to(lat.dtype)
+
+
+@pytest.mark.parametrize("rows,k,with_bias,in_place", [(4096, 3072, True, False), (1000, 3072, True, True),
+                                                         (200, 512, False, False), (64, 64, True, False)])
+def test_proj_out_cfg_euler_vs_eager(rows, k, with_bias, in_place):
+    from qwen_image_accel_b200 import _lib
+    from qwen_image_accel_b200.kernels.scheduler import proj_out_cfg_euler
+    g = torch.Generator(device="cuda").manual_seed(rows + k)
+    y = torch.randn(2 * rows, k, device="cuda", generator=g).to(torch.bfloat16)
+    w = (0.02 * torch.randn(64, k, device="cuda", generator=g)).to(torch.bfloat16)
+    b = (0.01 * torch.randn(64, device="cuda", generator=g)).to(torch.bfloat16) if with_bias else None
+    lat = torch.randn(1, rows, 64, device="cuda", generator=g).to(torch.bfloat16)
+    sigmas = torch.tensor([0.9, 0.875], device="cuda", dtype=torch.float32)
+    ref = eager_tail(y, w, b, lat, 4.0, sigmas)
+    src = lat.clone()
+    got = proj_out_cfg_euler(y, w, b, src, 4.0, sigmas, out=src if in_place else None)
+    torch.cuda.synchronize()
+    assert _lib.device_error() == 0
+    assert got.shape == lat.shape and torch.isfinite(got.float()).all()
+    # a proj_out value one bf16 ulp apart moves the update dt * v by its own
+    # ulp: bound the difference by 2 ulp of the larger of the result and the
+    # update (ref - latents)
+    diff = (got.float() - ref.float()).abs()
+    scale = torch.maximum(ref.float().abs(), (ref.float() - lat.float()).abs())
+    assert bool((diff <= scale * 2.0 ** -6 + 1e-30).all()), float(diff.max())
+    assert (got == ref).float().mean().item() >= 0.99
+
+
+def test_cfg_euler_sched_equals_host_dt():
+    from qwen_image_accel_b200.kernels.scheduler import cfg_euler
+    g = torch.Generator(device="cuda").manual_seed(5)
+    cond, neg, lat = (torch.randn(2, 777, 64, device="cuda", generator=g).to(torch.bfloat16) for _ in range(3))
+    sigmas = torch.tensor([0.875, 0.75], device="cuda", dtype=torch.float32)   # dt exactly -0.125
+    a = cfg_euler(cond, neg, lat, 4.0, dt=-0.125)
+    b = cfg_euler(cond, neg, lat, 4.0, sigmas=sigmas)
+    assert torch.equal(a, b)
+
+
+def test_denoise_step_graph_equals_eager():
+    from qwen_image_accel_b200.mmdit import MMDiT, MMDiTConfig, random_parameters
+    from qwen_image_accel_b200.optimizations.cuda_graph import DenoiseStepGraph
+    cfg = MMDiTConfig(num_layers=3, num_attention_heads=4, joint_attention_dim=512)
+    model = MMDiT(cfg, random_parameters(cfg, 7, "cpu"), device="cuda", profile="mxfp8_sage")
+    g = torch.Generator(device="cuda").manual_seed(11)
+    lat = torch.randn(1, 12 * 16, 64, device="cuda", generator=g).to(torch.bfloat16)
+    pe = torch.randn(1, 40, 512, device="cuda", generator=g).to(torch.bfloat16)
+    ne = torch.randn(1, 40, 512, device="cuda", generator=g).to(torch.bfloat16)
+    schedule = torch.tensor([1.0, 0.9, 0.7, 0.45, 0.2], device="cuda", dtype=torch.float32)
+    eager = lat
+    for i in range(4):
+        eager = model.denoise_step(eager, pe, ne, schedule[i:i + 2], None, (1, 12, 16))
+    graph = DenoiseStepGraph(model, lat, pe, ne, (1, 12, 16))
+    replayed = graph.denoise(lat, schedule).clone()
+    assert torch.equal(replayed, eager)
+    # host inputs and host schedule floats through the same public step()
+    x = lat.cpu()
+    for i in range(4):
+        x = graph.step(x, (float(schedule[i]), float(schedule[i + 1])))
+    assert torch.equal(x, eager)
