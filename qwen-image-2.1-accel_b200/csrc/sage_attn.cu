@@ -559,6 +559,114 @@ __device__ __forceinline__ void tc_st_32x32b_x16(uint32_t taddr, const uint32_t 
       : "memory");
 }
 
+// P of one 64-key half for one query row: P = 2^(S * sc - m) (S the int32
+// scores of the half, m the row max offset by log2(448), so P <= 448) as E4M3
+// codes four per word into w, the fp32 P added to the row sum (lane pairs
+// ds01 / ds23 on the full path, ds[] on a ragged last half of `valid` keys).
+__device__ __forceinline__ void p_half(const uint32_t (&sv)[64], int valid, float sc, float m, uint64_t& ds01,
+                                       uint64_t& ds23, float (&ds)[4], uint32_t (&w)[16]) {
+  if (valid >= kHalf) {
+    // s*sc - m = X*sc - (2^23+2^22)*sc - m with X = float(2^23+2^22+s)
+    // exactly (|s| < 2^22): one FMA per score after an integer add
+    const float bias = fmaf(12582912.0f, sc, m);
+    const uint64_t sc2 = f2_pack(sc, sc), nb2 = f2_pack(-bias, -bias);
+#pragma unroll
+    for (int t4 = 0; t4 < 64; t4 += 4) {
+      float a[4], pv[4];
+      f2_unpack(f2_fma(f2_pack(__int_as_float(int(sv[t4]) + 0x4B400000), __int_as_float(int(sv[t4 + 1]) + 0x4B400000)),
+                       sc2, nb2), a[0], a[1]);
+      f2_unpack(f2_fma(f2_pack(__int_as_float(int(sv[t4 + 2]) + 0x4B400000), __int_as_float(int(sv[t4 + 3]) + 0x4B400000)),
+                       sc2, nb2), a[2], a[3]);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) pv[e] = ex2_approx(a[e]);
+      ds01 = f2_add(ds01, f2_pack(pv[0], pv[1]));
+      ds23 = f2_add(ds23, f2_pack(pv[2], pv[3]));
+      w[t4 / 4] = cvt_e4m3x4(pv[0], pv[1], pv[2], pv[3]);
+    }
+  } else {
+#pragma unroll
+    for (int t4 = 0; t4 < 64; t4 += 4) {
+      float pv[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        pv[e] = t4 + e < valid ? ex2_approx(fmaf(i2f_small(sv[t4 + e]), sc, -m)) : 0.0f;
+        ds[e] += pv[e];
+      }
+      w[t4 / 4] = cvt_e4m3x4(pv[0], pv[1], pv[2], pv[3]);
+    }
+  }
+}
+
+// The epilogue of one query row (one thread, its TMEM lane): O (128 fp32
+// columns from o_col) / rowsum * v_scale -> the bf16 output row (stream a or
+// b of the joint sequence) or, with MXFP8 outputs, its E4M3 codes and E8M0
+// scales. A row that saw no key (rowsum 0) writes zeros.
+__device__ __forceinline__ void attn_store_row(const AttnParams& p, uint32_t tmem, uint32_t t_lane, uint32_t o_col,
+                                               int bh, int q_tok, float dsum) {
+  // a row that may see no key at all (a key limit of 0) writes zeros
+  const float rinv = dsum > 0.0f ? 1.0f / dsum : 0.0f;
+  const float* vs = p.v_scale + int64_t(bh) * kD;
+  const int b = bh / p.H, h = bh % p.H;
+  if (p.qa_values) {
+    // bf16(O * rinv * v_scale) quantized to MXFP8 in place of the bf16 store:
+    // this thread's 128 channels of head h are four 32-wide MX blocks of row
+    // `row` of its stream, K index 128 h .. 128 h + 127 of the next GEMM
+    const bool in_a = q_tok < p.split;
+    const int64_t len = in_a ? p.split : p.Sq - p.split;
+    const int64_t row = int64_t(b) * len + (in_a ? q_tok : q_tok - p.split);
+    uint8_t* qv = (in_a ? p.qa_values : p.qb_values) + row * int64_t(p.H * kD) + h * kD;
+    uint8_t* qsc = in_a ? p.qa_scales : p.qb_scales;
+    uint32_t e4 = 0;
+#pragma unroll 1
+    for (int c = 0; c < 4; ++c) {
+      uint32_t ov[32];
+      tc_ld_32x32b_x32(tmem + t_lane + o_col + uint32_t(c * 32), ov);
+      tc_wait_ld();
+      float f[32];
+      float amax = 0.0f;
+#pragma unroll
+      for (int e = 0; e < 32; ++e) {
+        f[e] = round_bf16(__uint_as_float(ov[e]) * rinv * __ldg(vs + c * 32 + e));
+        amax = fmaxf(amax, fabsf(f[e]));
+      }
+      const int ex = mx_exponent(amax);
+      const float inv = mx_inverse_scale(ex);
+      uint32_t w[8];
+#pragma unroll
+      for (int q4 = 0; q4 < 8; ++q4)
+        w[q4] = cvt_e4m3x4(f[4 * q4] * inv, f[4 * q4 + 1] * inv, f[4 * q4 + 2] * inv, f[4 * q4 + 3] * inv);
+      if (q_tok < p.Sq)
+        st_global_v8(qv + c * 32, make_uint4(w[0], w[1], w[2], w[3]), make_uint4(w[4], w[5], w[6], w[7]));
+      e4 |= uint32_t(ex) << (8 * c);
+    }
+    // the four scale bytes (K blocks 4h .. 4h+3) are adjacent in the blocked layout
+    if (q_tok < p.Sq) *reinterpret_cast<uint32_t*>(qsc + mx_scale_offset(row, 4 * h, p.H)) = e4;
+  } else {
+  // the joint [text, image] sequence can be written back as two streams
+  uint4* dst = q_tok < p.split
+                   ? reinterpret_cast<uint4*>(p.out + b * p.out_stride_b + int64_t(q_tok) * p.out_stride_s +
+                                              h * p.out_stride_h)
+                   : reinterpret_cast<uint4*>(p.out2 + b * p.out2_stride_b +
+                                              int64_t(q_tok - p.split) * p.out2_stride_s + h * p.out2_stride_h);
+#pragma unroll 1
+  for (int c = 0; c < 4; ++c) {
+    uint32_t ov[32];
+    tc_ld_32x32b_x32(tmem + t_lane + o_col + uint32_t(c * 32), ov);
+    tc_wait_ld();
+    if (q_tok < p.Sq) {
+#pragma unroll
+      for (int c8 = 0; c8 < 4; ++c8) {
+        float f[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e)
+          f[e] = __uint_as_float(ov[c8 * 8 + e]) * rinv * __ldg(vs + c * 32 + c8 * 8 + e);
+        dst[c * 4 + c8] = pack8(f);
+      }
+    }
+  }
+  }
+}
+
 __global__ void __launch_bounds__(192, 2)
 sage_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                  const __grid_constant__ CUtensorMap tm_v, AttnParams p, int* err) {
@@ -810,36 +918,7 @@ sage_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
       tc_ld_32x32b_x32(tmem + t_lane + uint32_t(h * kHalf + 32), *reinterpret_cast<uint32_t(*)[32]>(&sv[32]));
       tc_wait_ld();
       uint32_t w[16];
-      if (valid >= kHalf) {
-        // s*sc - m = X*sc - (2^23+2^22)*sc - m with X = float(2^23+2^22+s)
-        // exactly (|s| < 2^22): one FMA per score after an integer add
-        const float bias = fmaf(12582912.0f, sc, m);
-        const uint64_t sc2 = f2_pack(sc, sc), nb2 = f2_pack(-bias, -bias);
-#pragma unroll
-        for (int t4 = 0; t4 < 64; t4 += 4) {
-          float a[4], pv[4];
-          f2_unpack(f2_fma(f2_pack(__int_as_float(int(sv[t4]) + 0x4B400000), __int_as_float(int(sv[t4 + 1]) + 0x4B400000)),
-                           sc2, nb2), a[0], a[1]);
-          f2_unpack(f2_fma(f2_pack(__int_as_float(int(sv[t4 + 2]) + 0x4B400000), __int_as_float(int(sv[t4 + 3]) + 0x4B400000)),
-                           sc2, nb2), a[2], a[3]);
-#pragma unroll
-          for (int e = 0; e < 4; ++e) pv[e] = ex2_approx(a[e]);
-          ds01 = f2_add(ds01, f2_pack(pv[0], pv[1]));
-          ds23 = f2_add(ds23, f2_pack(pv[2], pv[3]));
-          w[t4 / 4] = cvt_e4m3x4(pv[0], pv[1], pv[2], pv[3]);
-        }
-      } else {
-#pragma unroll
-        for (int t4 = 0; t4 < 64; t4 += 4) {
-          float pv[4];
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            pv[e] = t4 + e < valid ? ex2_approx(fmaf(i2f_small(sv[t4 + e]), sc, -m)) : 0.0f;
-            ds[e] += pv[e];
-          }
-          w[t4 / 4] = cvt_e4m3x4(pv[0], pv[1], pv[2], pv[3]);
-        }
-      }
+      p_half(sv, valid, sc, m, ds01, ds23, ds, w);
       tc_st_32x32b_x16(tmem + t_lane + uint32_t(h * kHalf), w);
       tc_wait_st();
       tc_fence_before();
@@ -858,68 +937,7 @@ sage_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
     const float dsum = (ds[0] + ds[1]) + (ds[2] + ds[3]);
     if (ok && __all_sync(0xffffffffu, mbar_wait(smem_u32(o_full), 0, err))) {
       tc_fence_after();
-      // a row that may see no key at all (a key limit of 0) writes zeros
-      const float rinv = dsum > 0.0f ? 1.0f / dsum : 0.0f;
-      const float* vs = p.v_scale + int64_t(bh) * kD;
-      const int b = bh / p.H, h = bh % p.H;
-      if (p.qa_values) {
-        // bf16(O * rinv * v_scale) quantized to MXFP8 in place of the bf16 store:
-        // this thread's 128 channels of head h are four 32-wide MX blocks of row
-        // `row` of its stream, K index 128 h .. 128 h + 127 of the next GEMM
-        const bool in_a = q_tok < p.split;
-        const int64_t len = in_a ? p.split : p.Sq - p.split;
-        const int64_t row = int64_t(b) * len + (in_a ? q_tok : q_tok - p.split);
-        uint8_t* qv = (in_a ? p.qa_values : p.qb_values) + row * int64_t(p.H * kD) + h * kD;
-        uint8_t* qsc = in_a ? p.qa_scales : p.qb_scales;
-        uint32_t e4 = 0;
-#pragma unroll 1
-        for (int c = 0; c < 4; ++c) {
-          uint32_t ov[32];
-          tc_ld_32x32b_x32(tmem + t_lane + kTmemO + uint32_t(c * 32), ov);
-          tc_wait_ld();
-          float f[32];
-          float amax = 0.0f;
-#pragma unroll
-          for (int e = 0; e < 32; ++e) {
-            f[e] = round_bf16(__uint_as_float(ov[e]) * rinv * __ldg(vs + c * 32 + e));
-            amax = fmaxf(amax, fabsf(f[e]));
-          }
-          const int ex = mx_exponent(amax);
-          const float inv = mx_inverse_scale(ex);
-          uint32_t w[8];
-#pragma unroll
-          for (int q4 = 0; q4 < 8; ++q4)
-            w[q4] = cvt_e4m3x4(f[4 * q4] * inv, f[4 * q4 + 1] * inv, f[4 * q4 + 2] * inv, f[4 * q4 + 3] * inv);
-          if (q_tok < p.Sq)
-            st_global_v8(qv + c * 32, make_uint4(w[0], w[1], w[2], w[3]), make_uint4(w[4], w[5], w[6], w[7]));
-          e4 |= uint32_t(ex) << (8 * c);
-        }
-        // the four scale bytes (K blocks 4h .. 4h+3) are adjacent in the blocked layout
-        if (q_tok < p.Sq) *reinterpret_cast<uint32_t*>(qsc + mx_scale_offset(row, 4 * h, p.H)) = e4;
-      } else {
-      // the joint [text, image] sequence can be written back as two streams
-      uint4* dst = q_tok < p.split
-                       ? reinterpret_cast<uint4*>(p.out + b * p.out_stride_b + int64_t(q_tok) * p.out_stride_s +
-                                                  h * p.out_stride_h)
-                       : reinterpret_cast<uint4*>(p.out2 + b * p.out2_stride_b +
-                                                  int64_t(q_tok - p.split) * p.out2_stride_s + h * p.out2_stride_h);
-#pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
-        uint32_t ov[32];
-        tc_ld_32x32b_x32(tmem + t_lane + kTmemO + uint32_t(c * 32), ov);
-        tc_wait_ld();
-        if (q_tok < p.Sq) {
-#pragma unroll
-          for (int c8 = 0; c8 < 4; ++c8) {
-            float f[8];
-#pragma unroll
-            for (int e = 0; e < 8; ++e)
-              f[e] = __uint_as_float(ov[c8 * 8 + e]) * rinv * __ldg(vs + c * 32 + c8 * 8 + e);
-            dst[c * 4 + c8] = pack8(f);
-          }
-        }
-      }
-      }
+      attn_store_row(p, tmem, t_lane, kTmemO, bh, q_tok, dsum);
     }
   }
 
