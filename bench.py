@@ -267,10 +267,11 @@ def ncu_traffic(kernel: str, shape: str):
     p = ROOT / "profiles" / "roofline_traffic.json"
     if not p.exists():
         return None, None
-    rec = json.loads(p.read_text()).get(kernel)
-    if not rec or rec.get("shape") != shape:
-        return None, None
-    return int(rec["dram_read_bytes"]) + int(rec["dram_write_bytes"]), rec.get("source")
+    recs = json.loads(p.read_text()).get(kernel) or []
+    for rec in recs if isinstance(recs, list) else [recs]:
+        if rec.get("shape") == shape:
+            return int(rec["dram_read_bytes"]) + int(rec["dram_write_bytes"]), rec.get("source")
+    return None, None
 
 
 # ----------------------------------------------------------------------------- our arm: the denoise step

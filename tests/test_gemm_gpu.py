@@ -179,6 +179,36 @@ def test_full_size_bf16_contract():
     assert rel_fro(y.float(), ref.float()) < 1e-2
 
 
+# BASELINE config 2, every shape of the sweep: M in {4352, 16640} x (QKV
+# 3072->9216, out 3072->3072, FFN up 3072->12288 with the GELU-tanh epilogue,
+# FFN down 12288->3072), activations ~N(0, 1), weights ~N(0, 0.02), bias
+# ~N(0, 0.01), seed 1; the launch picks its tile width as in the model.
+@pytest.mark.parametrize("m", [4352, 16640])
+@pytest.mark.parametrize("n,k,gelu", [(9216, 3072, False), (3072, 3072, False), (12288, 3072, True),
+                                      (3072, 12288, False)])
+def test_config2_sweep_shapes(m, n, k, gelu):
+    from qwen_image_accel_b200 import _lib
+    from qwen_image_accel_b200.kernels.mxfp8 import quantize
+    from qwen_image_accel_b200.optimizations.mxfp8 import MXFP8Linear
+    lin = make_linear(n, k, 1)
+    mx = MXFP8Linear(lin)
+    a = quantize(make_x(m, k, 1))
+    y = mx.matmul_gelu(a) if gelu else mx.matmul(a)
+    torch.cuda.synchronize()
+    assert _lib.device_error() == 0
+    assert y.shape == (m, n)
+    wq = type(a)(mx.weight_fp8.t(), mx.weight_scale, n, torch.Size((n, k)))
+    da, dw = dequant(a), dequant(wq)
+    bf16_ref = F.linear(da.to(torch.bfloat16), dw.to(torch.bfloat16), lin.bias)
+    exact = da @ dw.T + lin.bias.float()
+    if gelu:
+        bf16_ref = F.gelu(bf16_ref, approximate="tanh")
+        exact = F.gelu(exact, approximate="tanh")
+    del da, dw
+    assert rel_fro(y.float(), bf16_ref.float()) < 1e-2   # north_star contract
+    assert rel_fro(y.float(), exact) < 4e-3              # accumulation order + bf16 roundings only
+
+
 @pytest.mark.parametrize("m,n,k", [(4352, 9216, 3072), (300, 1536, 384)])
 def test_pair_and_single_kernels_agree(monkeypatch, m, n, k):
     """Both kernels sum each output over the same 32-wide K blocks; their
