@@ -46,8 +46,9 @@ from .kernels.mxfp8 import quantize
 from .kernels.scheduler import cfg_euler, proj_out_cfg_euler
 from .optimizations.mxfp8 import (MXFP8Linear, matmul_gate_residual_grouped, matmul_gelu_quantize_grouped,
                                   matmul_grouped, skip_block_indices)
-from .optimizations.sage_attention import (sage_attention_joint_quantized, sage_attention_split,
-                                           sage_attention_split_quantized, workspace_bytes)
+from .optimizations.sage_attention import (sage_attention_from_workspace, sage_attention_joint_quantized,
+                                           sage_attention_split, sage_attention_split_quantized, sage_quantize_joint,
+                                           workspace_bytes)
 from .kernels.bf16 import gelu_tanh
 from .profiles import get_profile
 
@@ -357,10 +358,17 @@ class MMDiT:
     def block_forward_sharded(self, blk: DualStreamBlock, x: torch.Tensor, c: torch.Tensor, mod_img, mod_txt,
                               freqs_img, freqs_txt, plan):
         """block_forward for one rank of a Ulysses group (see ulysses.py): x is
-        this rank's image tokens [B, S_loc, D] (freqs_img sliced to them), c the
-        replicated text stream [B, Lt, D]. Joint attention runs on this rank's
-        H/U heads over every token; the results are the unsharded block's."""
-        from .ulysses import gather_heads, head_to_seq, seq_to_head
+        this rank's image tokens [B, S_loc, D], c the replicated text stream
+        [B, Lt, D], freqs_img the RoPE table of every image token of the half.
+        Joint attention runs on this rank's H/U heads over every token; the
+        results are the unsharded block's.
+
+        With MXFP8 projections and Sage attention, the image tokens' q|k|v
+        projection rows of this rank's heads cross in one all-to-all before any
+        QK-norm/RoPE, and the fused QK-norm + RoPE + Sage quantizer reads them
+        (and the text rows of the same heads) in the projection layout: the
+        bf16 Q/K/V never exist in memory, as on one GPU."""
+        from .ulysses import gather_heads, head_to_seq, projection_heads, projection_to_heads, seq_to_head
         cfg = self.cfg
         B, Sl, D = x.shape
         Lt = c.shape[1]
@@ -377,28 +385,46 @@ class MMDiT:
         else:
             qkv_i = F.linear(layer_norm_scale(x, s1_i, self.ln, shift=sh1_i), blk.img_qkv.w, blk.img_qkv.b)
             qkv_t = F.linear(layer_norm_scale(c, s1_t, self.ln, shift=sh1_t), blk.txt_qkv.w, blk.txt_qkv.b)
-        # local Q/K/V: image tokens (all heads), text tokens (all heads)
-        qi, ki, vi = (torch.empty(B, Sl, H, hd, device=x.device, dtype=torch.bfloat16) for _ in range(3))
-        qt, kt, vt = (torch.empty(B, Lt, H, hd, device=x.device, dtype=torch.bfloat16) for _ in range(3))
-        joint_qk_norm_rope(qkv_i.view(B, Sl, 3 * D), blk.norm_q, blk.norm_k, freqs_img, qi, ki, vi, 0, cfg.eps)
-        joint_qk_norm_rope(qkv_t.view(B, Lt, 3 * D), blk.norm_added_q, blk.norm_added_k, freqs_txt, qt, kt, vt, 0,
-                           cfg.eps)
-        # joint [text, image] sequence of this rank's heads
         S = Lt + U * Sl
         a_t = torch.empty(B, Lt, H, hd, device=x.device, dtype=torch.bfloat16)
         a_i = torch.empty(B, Sl, H, hd, device=x.device, dtype=torch.bfloat16)
-        for b in range(B):
-            qj, kj, vj = (torch.empty(1, S, Hl, hd, device=x.device, dtype=torch.bfloat16) for _ in range(3))
-            for dst, src_t, src_i in ((qj, qt, qi), (kj, kt, ki), (vj, vt, vi)):
-                dst[0, :Lt].copy_(src_t[b, :, h0:h0 + Hl])
-                seq_to_head(src_i[b], plan, out=dst[0, Lt:])
-            o_t = torch.empty(1, Lt, Hl, hd, device=x.device, dtype=torch.bfloat16)
-            o_i = torch.empty(1, U * Sl, Hl, hd, device=x.device, dtype=torch.bfloat16)
-            self._attention(qj, kj, vj, Lt, o_t, o_i)
-            del qj, kj, vj
-            a_i[b] = head_to_seq(o_i[0], plan)
-            a_t[b] = gather_heads(o_t[0], plan)
-        del qi, ki, vi, qt, kt, vt
+        if mx and self.sage:
+            qkv_i, qkv_t = qkv_i.view(B, Sl, 3 * D), qkv_t.view(B, Lt, 3 * D)
+            for b in range(B):
+                qkv_ih = projection_to_heads(qkv_i[b], H, plan)       # [U * S_loc, 3 * Hl * hd]
+                qkv_th = projection_heads(qkv_t[b], H, plan)          # [Lt, 3 * Hl * hd]
+                ws = sage_quantize_joint(qkv_th[None], qkv_ih[None], (blk.norm_added_q, blk.norm_added_k),
+                                         (blk.norm_q, blk.norm_k), freqs_txt, freqs_img, Hl, cfg.eps)
+                del qkv_ih, qkv_th
+                o = torch.empty(1, S, Hl, hd, device=x.device, dtype=torch.bfloat16)
+                sage_attention_from_workspace(ws["_workspace"], o)
+                del ws
+                a_i[b] = head_to_seq(o[0, Lt:], plan)
+                a_t[b] = gather_heads(o[0, :Lt], plan)
+                del o
+            del qkv_i, qkv_t
+        else:
+            # local Q/K/V: image tokens (all heads), text tokens (all heads)
+            lo, hi = plan.image_slice(U * Sl)
+            qi, ki, vi = (torch.empty(B, Sl, H, hd, device=x.device, dtype=torch.bfloat16) for _ in range(3))
+            qt, kt, vt = (torch.empty(B, Lt, H, hd, device=x.device, dtype=torch.bfloat16) for _ in range(3))
+            joint_qk_norm_rope(qkv_i.view(B, Sl, 3 * D), blk.norm_q, blk.norm_k, freqs_img[lo:hi].contiguous(),
+                               qi, ki, vi, 0, cfg.eps)
+            joint_qk_norm_rope(qkv_t.view(B, Lt, 3 * D), blk.norm_added_q, blk.norm_added_k, freqs_txt, qt, kt, vt,
+                               0, cfg.eps)
+            # joint [text, image] sequence of this rank's heads
+            for b in range(B):
+                qj, kj, vj = (torch.empty(1, S, Hl, hd, device=x.device, dtype=torch.bfloat16) for _ in range(3))
+                for dst, src_t, src_i in ((qj, qt, qi), (kj, kt, ki), (vj, vt, vi)):
+                    dst[0, :Lt].copy_(src_t[b, :, h0:h0 + Hl])
+                    seq_to_head(src_i[b], plan, out=dst[0, Lt:])
+                o_t = torch.empty(1, Lt, Hl, hd, device=x.device, dtype=torch.bfloat16)
+                o_i = torch.empty(1, U * Sl, Hl, hd, device=x.device, dtype=torch.bfloat16)
+                self._attention(qj, kj, vj, Lt, o_t, o_i)
+                del qj, kj, vj
+                a_i[b] = head_to_seq(o_i[0], plan)
+                a_t[b] = gather_heads(o_t[0], plan)
+            del qi, ki, vi, qt, kt, vt
         if not mx:
             x = residual(x, F.linear(a_i.view(B, Sl, D), blk.img_out.w, blk.img_out.b), g1_i)
             c = residual(c, F.linear(a_t.view(B, Lt, D), blk.txt_out.w, blk.txt_out.b), g1_t)
@@ -564,7 +590,7 @@ class MMDiT:
                 # the fused single-GPU block applies unchanged
                 x, c = self.block_forward(blk, x, c, m_img, m_txt, freqs_loc, freqs_txt)
             else:
-                x, c = self.block_forward_sharded(blk, x, c, m_img, m_txt, freqs_loc, freqs_txt, plan)
+                x, c = self.block_forward_sharded(blk, x, c, m_img, m_txt, freqs_img, freqs_txt, plan)
         emb = F.linear(F.silu(temb), *self.norm_out)
         scale, shift = emb.chunk(2, dim=1)
         y = layer_norm_scale(x, (1 + scale)[:, None].contiguous(), self.ln, shift=shift[:, None].contiguous())

@@ -253,6 +253,25 @@ def sage_attention_joint_quantized(qkv0: torch.Tensor, qkv1: torch.Tensor, weigh
     return qa, qb
 
 
+def sage_attention_from_workspace(workspace: torch.Tensor, out: torch.Tensor,
+                                  sm_scale: float | None = None) -> torch.Tensor:
+    """The attention half alone (qia_sage_attn_quantized) on a workspace that
+    sage_quantize or sage_quantize_joint filled for out's (B, S, H) with
+    S = Sq = Skv: out (B, S, H, 128) bf16, any strides with a contiguous
+    head_dim; returns out."""
+    _check_settings()
+    _lib.require_cuda(workspace, out)
+    if out.ndim != 4 or out.shape[-1] != 128 or out.dtype != torch.bfloat16:
+        raise NotImplementedError("out must be (B, S, H, 128) bf16")
+    b, s, h, d = out.shape
+    need = workspace_bytes(b, h, s, s)
+    if workspace.dtype != torch.uint8 or workspace.numel() < need:
+        raise ValueError(f"workspace holds {workspace.numel()} bytes, the attention needs {need}")
+    _lib.call("qia_sage_attn_quantized", _lib.ptr(workspace), _lib.ptr(out), b, s, s, h, d, _strides(out),
+              float(sm_scale or 0.0), _lib.stream(out.device))
+    return out
+
+
 def sage_quantize(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor) -> dict:
     """Run only the quantization half; returns the workspace views."""
     _validate(q, k, v)

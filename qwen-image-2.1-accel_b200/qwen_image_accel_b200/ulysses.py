@@ -82,6 +82,38 @@ def seq_to_head(x_local: torch.Tensor, plan: ShardPlan, out: torch.Tensor | None
     return out
 
 
+def projection_to_heads(qkv_local: torch.Tensor, heads: int, plan: ShardPlan) -> torch.Tensor:
+    """[S_loc, 3*H*d] fused q|k|v projection rows of this rank's tokens (q at
+    column 0, k at H*d, v at 2*H*d) -> [U * S_loc, 3*(H/U)*d]: every token of
+    the half (rank order), the q|k|v of this rank's H/U heads laid out the same
+    way with H/U heads (q at 0, k at (H/U)*d, v at 2*(H/U)*d). One all-to-all
+    moves Q, K and V together, before any QK-norm/RoPE (both are per token and
+    per head, so they can run after the exchange)."""
+    U = plan.ulysses
+    S_loc, width = qkv_local.shape
+    if heads % U or width % (3 * heads):
+        raise ValueError(f"a {width}-wide q|k|v projection of {heads} heads does not split over U={U}")
+    if U == 1:
+        return qkv_local
+    Hl, d = heads // U, width // (3 * heads)
+    send = qkv_local.view(S_loc, 3, U, Hl, d).permute(2, 0, 1, 3, 4).contiguous()   # [dest, S_loc, 3, H/U, d]
+    out = torch.empty(U * S_loc, 3 * Hl * d, device=qkv_local.device, dtype=qkv_local.dtype)
+    dist.all_to_all_single(out.view(U, S_loc, 3, Hl, d), send, group=plan.group)
+    return out
+
+
+def projection_heads(qkv: torch.Tensor, heads: int, plan: ShardPlan) -> torch.Tensor:
+    """[S, 3*H*d] q|k|v projection rows (replicated on every rank of the half)
+    -> [S, 3*(H/U)*d]: this rank's H/U heads in the projection_to_heads layout."""
+    U = plan.ulysses
+    S, width = qkv.shape
+    if U == 1:
+        return qkv
+    Hl, d = heads // U, width // (3 * heads)
+    h0 = plan.u * Hl
+    return qkv.view(S, 3, heads, d)[:, :, h0:h0 + Hl].reshape(S, 3 * Hl * d)
+
+
 def head_to_seq(o_heads: torch.Tensor, plan: ShardPlan) -> torch.Tensor:
     """[U * S_loc, H / U, d] (every token, this rank's heads) -> [S_loc, H, d]."""
     U = plan.ulysses

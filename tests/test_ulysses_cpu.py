@@ -1,7 +1,8 @@
 """CFG split + Ulysses collectives (qwen_image_accel_b200/ulysses.py) on gloo
-CPU ranks: the sequence<->head all-to-alls, the head all-gather of the text
-stream and the CFG velocity swap equal their single-process definitions, and a
-head-sharded attention equals the unsharded one."""
+CPU ranks: the sequence<->head all-to-alls (of Q/K/V and of the fused q|k|v
+projection rows), the head all-gather of the text stream and the CFG velocity
+swap equal their single-process definitions, and a head-sharded attention
+equals the unsharded one."""
 import os
 import socket
 from datetime import timedelta
@@ -28,7 +29,8 @@ def _worker(rank, world, port, cfg_split, results):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=60))
     try:
-        from qwen_image_accel_b200.ulysses import exchange_cfg, gather_heads, head_to_seq, make_plan, seq_to_head
+        from qwen_image_accel_b200.ulysses import (exchange_cfg, gather_heads, head_to_seq, make_plan,
+                                                    projection_heads, projection_to_heads, seq_to_head)
         plan = make_plan(cfg_split)
         U = plan.ulysses
         S, H, d = 6 * U, 3 * U, 8
@@ -40,6 +42,12 @@ def _worker(rank, world, port, cfg_split, results):
         assert torch.equal(got, full[:, heads]), "seq_to_head"
         assert torch.equal(head_to_seq(got, plan), full[lo:hi]), "head_to_seq"
         assert torch.equal(gather_heads(full[:, heads].contiguous(), plan), full), "gather_heads"
+        # the fused q|k|v projection rows: this rank's heads of every token, in
+        # the layout the joint quantizer reads (q, k, v sections of H/U heads)
+        qkv = torch.randn(S, 3 * H * d, generator=g, dtype=torch.float64)
+        want = qkv.view(S, 3, H, d)[:, :, heads].reshape(S, 3 * (H // U) * d)
+        assert torch.equal(projection_to_heads(qkv[lo:hi].contiguous(), H, plan), want), "projection_to_heads"
+        assert torch.equal(projection_heads(qkv, H, plan), want), "projection_heads"
         q, k, v = (torch.randn(S, H, d, generator=g, dtype=torch.float64) for _ in range(3))
         local = _attention(*(seq_to_head(t[lo:hi].contiguous(), plan) for t in (q, k, v)))
         assert torch.allclose(head_to_seq(local, plan), _attention(q, k, v)[lo:hi], atol=1e-12), "attention"
