@@ -478,6 +478,70 @@ int qia_sage_attn_quantized(const void* workspace, void* out, int64_t batch,
                             int64_t head_dim, const int64_t* out_strides,
                             float sm_scale, void* stream);
 
+/* ---- Ulysses exchanges over NVLink peer memory (CFG split x Ulysses) ----
+ * The sharded dual-stream block moves each block's image q|k|v projection
+ * rows from the rank that owns the tokens to the ranks that own the heads,
+ * and the attention output back, by storing into the other ranks' device
+ * buffers mapped with CUDA IPC. Each producing kernel's CTAs signal every
+ * rank after their stores (system-scope fence, then a system-scope atomic add
+ * on the receiving rank's 64-bit counter for this rank); qia_ulysses_wait
+ * waits, with a time limit, for a round's signals.
+ * Replaces: torch.distributed.all_to_all_single / all_gather under the
+ * Ulysses helpers of the reference's dependency
+ * (WHL:diffusers/models/attention_dispatch.py:2099-2182, 2510-2606). */
+
+/* Size of an IPC handle (cudaIpcMemHandle_t). */
+int64_t qia_ipc_handle_bytes(void);
+/* A zeroed device buffer of `bytes` and its IPC handle (qia_ipc_handle_bytes
+ * bytes at `handle`), for the other ranks to map. */
+int qia_ipc_alloc(int64_t bytes, void** ptr, void* handle);
+/* Map another process's buffer from its handle (peer access enabled lazily). */
+int qia_ipc_open(const void* handle, void** ptr);
+int qia_ipc_close(void* ptr);
+int qia_ipc_free(void* ptr);
+
+/* CTAs qia_ulysses_scatter_qkv launches (each signals every rank once). */
+int64_t qia_ulysses_scatter_ctas(int64_t s_loc, int64_t heads);
+/* Rows s of this rank's fused q|k|v projection ([s_loc, ld] bf16: q, k, v of
+ * `heads` heads of 128) -> every rank r's receive buffer recv_peers[r]
+ * ([U * s_loc, 3 * (heads/U) * 128] bf16): row rank * s_loc + s, the q, k and
+ * v of r's heads [r * heads/U, (r + 1) * heads/U) -- the layout
+ * qia_sage_quantize_joint reads with heads/U heads. recv_peers and
+ * signal_peers are device arrays of U pointers (this rank's own buffers at
+ * index `rank`); each CTA adds 1 to signal_peers[r][rank] for every r. */
+int qia_ulysses_scatter_qkv(const void* qkv, int64_t ld, int64_t s_loc,
+                            int64_t heads, int64_t head_dim,
+                            void* const* recv_peers, void* const* signal_peers,
+                            int64_t ulysses, int64_t rank, void* stream);
+/* Wait for the next round of a wait site: *round (uint64, device, only this
+ * entry updates it) += 1, then wait until counters[s] >= round * per_round
+ * for s < sources. A wait longer than timeout_ns records QIA_ERR_TIMEOUT in
+ * the device error word (qia_device_error) and returns. */
+int qia_ulysses_wait(const void* counters, void* round, int64_t sources,
+                     int64_t per_round, int64_t timeout_ns, void* stream);
+/* CTAs of one unmasked attention launch (each signals every rank once in
+ * qia_sage_attn_quantized_peers). */
+int64_t qia_sage_attn_ctas(int64_t batch, int64_t heads, int64_t seq_q);
+/* The attention half on a workspace filled by qia_sage_quantize_joint (batch
+ * 1, `heads` heads, joint sequence of `seq` = split text + image tokens),
+ * writing its output straight to the ranks that need it: image token j
+ * (query split + j) to row j % peer_rows of img_peers[j / peer_rows], every
+ * text token to each txt_peers[r], both [rows, heads_total * 128] bf16 at
+ * head columns head0 .. head0 + heads - 1; then each CTA adds 1 to
+ * signal_peers[r][slot] for every rank r. img_peers, txt_peers and
+ * signal_peers are device arrays of peer_count pointers.
+ * Replaces: the Ulysses attention's output all-to-all and the text all-gather
+ * (WHL:diffusers/models/attention_dispatch.py:2510-2606) fused into the
+ * reference's decode attention epilogue (src/qwen_image_accel/optimizations/
+ * sage_attention.py:19-25). */
+int qia_sage_attn_quantized_peers(const void* workspace, int64_t seq,
+                                  int64_t heads, int64_t head_dim,
+                                  int64_t split, void* const* img_peers,
+                                  void* const* txt_peers, int64_t peer_rows,
+                                  int64_t peer_count, int64_t head0,
+                                  int64_t heads_total, void* const* signal_peers,
+                                  int64_t slot, float sm_scale, void* stream);
+
 /* Allocation-free variant of qia_sage_attention (no counterpart in the
  * reference): identical arguments minus the workspace. Some callers cannot
  * allocate device memory when they need attention -- a host that reaches the

@@ -518,6 +518,18 @@ struct AttnParams {
   // clamped to [0, Skv]. Null: every query sees all Skv keys.
   const int* kv_limit;
   int64_t kv_limit_stride_b;
+  // Ulysses output exchange (null img_peers: the outputs above). Batch 1: the
+  // image row j of the joint sequence (query token split + j) goes straight to
+  // the rank that owns the token -- row j % peer_rows of img_peers[j /
+  // peer_rows] -- and every text row to each rank's txt_peers buffer, both
+  // [rows, peer_ld] bf16 at columns (peer_head0 + h) * 128. After its stores
+  // every CTA adds 1 to counter peer_slot of each rank (signal_peers), after a
+  // system-scope fence.
+  __nv_bfloat16* const* img_peers;
+  __nv_bfloat16* const* txt_peers;
+  unsigned long long* const* signal_peers;
+  int peer_count, peer_rows, peer_head0, peer_slot;
+  int64_t peer_ld;
 };
 
 // Two CTAs share an SM (98 KB of shared memory and 256 TMEM columns each), so
@@ -641,6 +653,41 @@ __device__ __forceinline__ void attn_store_row(const AttnParams& p, uint32_t tme
     }
     // the four scale bytes (K blocks 4h .. 4h+3) are adjacent in the blocked layout
     if (q_tok < p.Sq) *reinterpret_cast<uint32_t*>(qsc + mx_scale_offset(row, 4 * h, p.H)) = e4;
+  } else if (p.img_peers) {
+    // Ulysses: an image row to the rank that owns its token, a text row to
+    // every rank (NVLink stores into the peers' buffers)
+    const int64_t col = int64_t(p.peer_head0 + h) * kD;
+    const bool txt = q_tok < p.split;
+    const int j = q_tok - p.split;
+#pragma unroll 1
+    for (int c = 0; c < 4; ++c) {
+      uint32_t ov[32];
+      tc_ld_32x32b_x32(tmem + t_lane + o_col + uint32_t(c * 32), ov);
+      tc_wait_ld();
+      if (q_tok < p.Sq) {
+        uint4 pk[4];
+#pragma unroll
+        for (int c8 = 0; c8 < 4; ++c8) {
+          float f[8];
+#pragma unroll
+          for (int e = 0; e < 8; ++e)
+            f[e] = __uint_as_float(ov[c8 * 8 + e]) * rinv * __ldg(vs + c * 32 + c8 * 8 + e);
+          pk[c8] = pack8(f);
+        }
+        if (txt) {
+          for (int r = 0; r < p.peer_count; ++r) {
+            uint4* dst = reinterpret_cast<uint4*>(p.txt_peers[r] + int64_t(q_tok) * p.peer_ld + col) + c * 4;
+#pragma unroll
+            for (int c8 = 0; c8 < 4; ++c8) dst[c8] = pk[c8];
+          }
+        } else {
+          uint4* dst = reinterpret_cast<uint4*>(p.img_peers[j / p.peer_rows] + int64_t(j % p.peer_rows) * p.peer_ld +
+                                                col) + c * 4;
+#pragma unroll
+          for (int c8 = 0; c8 < 4; ++c8) dst[c8] = pk[c8];
+        }
+      }
+    }
   } else {
   // the joint [text, image] sequence can be written back as two streams
   uint4* dst = q_tok < p.split
@@ -941,8 +988,11 @@ sage_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
     }
   }
 
+  if (p.signal_peers) __threadfence_system();   // this CTA's peer stores before its signals
   tc_fence_before();
   __syncthreads();
+  if (p.signal_peers && int(threadIdx.x) < p.peer_count)
+    atomicAdd_system(p.signal_peers[threadIdx.x] + p.peer_slot, 1ull);
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem, kAttnTmemCols);
@@ -1102,9 +1152,17 @@ struct MxOut {
   void* b_scales = nullptr;
 };
 
+struct PeerOut {
+  void* const* img = nullptr;
+  void* const* txt = nullptr;
+  void* const* signal = nullptr;
+  int count = 0, rows = 0, head0 = 0, slot = 0;
+  int64_t ld = 0;
+};
+
 int launch_attn(const Workspace& ws, void* out, Strides os, void* out2, Strides os2, int64_t split, int64_t B,
                 int64_t H, int64_t Sq, int64_t Skv, float sm_scale, cudaStream_t st, const MxOut& mx = MxOut(),
-                const int* kv_limit = nullptr, int64_t kv_limit_stride_b = 0) {
+                const int* kv_limit = nullptr, int64_t kv_limit_stride_b = 0, const PeerOut& peers = PeerOut()) {
   static bool attr_done[64] = {false};
   static std::mutex mu;
   int dev = 0;
@@ -1137,7 +1195,7 @@ int launch_attn(const Workspace& ws, void* out, Strides os, void* out2, Strides 
   p.out2_stride_b = os2.b;
   p.out2_stride_s = os2.s;
   p.out2_stride_h = os2.h;
-  p.split = (out2 || mx.a_values) ? int(split) : int(Sq);
+  p.split = (out2 || mx.a_values || peers.img) ? int(split) : int(Sq);
   p.B = int(B);
   p.H = int(H);
   p.Sq = int(Sq);
@@ -1151,6 +1209,14 @@ int launch_attn(const Workspace& ws, void* out, Strides os, void* out2, Strides 
   p.qb_scales = (uint8_t*)mx.b_scales;
   p.kv_limit = kv_limit;
   p.kv_limit_stride_b = kv_limit_stride_b;
+  p.img_peers = (__nv_bfloat16* const*)peers.img;
+  p.txt_peers = (__nv_bfloat16* const*)peers.txt;
+  p.signal_peers = (unsigned long long* const*)peers.signal;
+  p.peer_count = peers.count;
+  p.peer_rows = peers.rows;
+  p.peer_head0 = peers.head0;
+  p.peer_slot = peers.slot;
+  p.peer_ld = peers.ld;
   const dim3 grid = kv_limit ? dim3(unsigned(B * H), unsigned(sqp / 128)) : dim3(unsigned(sqp / 128), unsigned(B * H));
   sage_attn_kernel<<<grid, 192, kAttnSmem, st>>>(tq, tk, tv, p, device_error_word());
   return check_launch("sage_attn_kernel");
@@ -1460,6 +1526,43 @@ extern "C" int qia_sage_attn_quantized(const void* workspace, void* out, int64_t
   workspace_layout(batch, heads, seq_q, seq_kv, (uint8_t*)const_cast<void*>(workspace), &ws);
   const float scale = sm_scale > 0.0f ? sm_scale : 1.0f / sqrtf(float(head_dim));
   return launch_attn(ws, out, so, nullptr, so, 0, batch, heads, seq_q, seq_kv, scale, as_stream(stream));
+}
+
+extern "C" int64_t qia_sage_attn_ctas(int64_t batch, int64_t heads, int64_t seq_q) {
+  if (batch <= 0 || heads <= 0 || seq_q <= 0) return -1;
+  return batch * heads * (pad128(seq_q) / 128);
+}
+
+extern "C" int qia_sage_attn_quantized_peers(const void* workspace, int64_t seq, int64_t heads, int64_t head_dim,
+                                             int64_t split, void* const* img_peers, void* const* txt_peers,
+                                             int64_t peer_rows, int64_t peer_count, int64_t head0,
+                                             int64_t heads_total, void* const* signal_peers, int64_t slot,
+                                             float sm_scale, void* stream) {
+  int rc = check_sizes(1, heads, seq, seq, head_dim, "qia_sage_attn_quantized_peers");
+  if (rc) return rc;
+  if (!workspace || !aligned(workspace, 256) || !img_peers || !txt_peers || !signal_peers)
+    return set_error(QIA_ERR_INVALID, "qia_sage_attn_quantized_peers: null pointer");
+  if (peer_count <= 0 || peer_count > 64 || slot < 0 || slot >= peer_count || split <= 0 || split >= seq ||
+      peer_rows <= 0 || (seq - split) != peer_rows * peer_count || head0 < 0 || head0 + heads > heads_total)
+    return set_error(QIA_ERR_INVALID,
+                     "qia_sage_attn_quantized_peers: seq=%lld split=%lld rows=%lld ranks=%lld heads %lld+%lld of %lld",
+                     (long long)seq, (long long)split, (long long)peer_rows, (long long)peer_count, (long long)head0,
+                     (long long)heads, (long long)heads_total);
+  Workspace ws;
+  workspace_layout(1, heads, seq, seq, (uint8_t*)const_cast<void*>(workspace), &ws);
+  const float scale = sm_scale > 0.0f ? sm_scale : 1.0f / sqrtf(float(head_dim));
+  PeerOut po;
+  po.img = img_peers;
+  po.txt = txt_peers;
+  po.signal = signal_peers;
+  po.count = int(peer_count);
+  po.rows = int(peer_rows);
+  po.head0 = int(head0);
+  po.slot = int(slot);
+  po.ld = heads_total * kD;
+  const Strides none{0, 0, 0};
+  return launch_attn(ws, nullptr, none, nullptr, none, split, 1, heads, seq, seq, scale, as_stream(stream), MxOut(),
+                     nullptr, 0, po);
 }
 
 // Same computation as qia_sage_attention, with the library's built-in scratch

@@ -221,6 +221,7 @@ class MMDiT:
             raise ValueError(f"profile {profile!r} has no fused path")
         self.quantized, self.sage = prof.quantized, prof.sage
         self.skip_blocks = skip_block_indices(skip_blocks, prof.skip_blocks) if prof.quantized else set()
+        self._peer_exchanges: dict = {}
         get = params if callable(params) else (lambda n: params[n])
         dev = self.device
         G = lambda n: get(n).to(dev)  # noqa: E731
@@ -277,6 +278,18 @@ class MMDiT:
             o = F.scaled_dot_product_attention(q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2)).transpose(1, 2)
             out_txt.copy_(o[:, :split])
             out_img.copy_(o[:, split:])
+
+    def _peer_exchange(self, plan, s_loc: int, txt_len: int):
+        """The PeerExchange of this plan's Ulysses group for these sizes,
+        built on first use by every rank of the group together (outside CUDA
+        graph capture: the first step runs eagerly)."""
+        from .ulysses import PeerExchange
+        key = (id(plan.group), s_loc, txt_len)
+        px = self._peer_exchanges.get(key)
+        if px is None:
+            px = self._peer_exchanges[key] = PeerExchange(plan, s_loc, txt_len, self.cfg.num_attention_heads,
+                                                          self.device)
+        return px
 
     def _attn_ws(self, q, k):
         need = workspace_bytes(q.shape[0], q.shape[2], q.shape[1], k.shape[1])
@@ -364,11 +377,16 @@ class MMDiT:
         results are the unsharded block's.
 
         With MXFP8 projections and Sage attention, the image tokens' q|k|v
-        projection rows of this rank's heads cross in one all-to-all before any
-        QK-norm/RoPE, and the fused QK-norm + RoPE + Sage quantizer reads them
-        (and the text rows of the same heads) in the projection layout: the
-        bf16 Q/K/V never exist in memory, as on one GPU."""
-        from .ulysses import gather_heads, head_to_seq, projection_heads, projection_to_heads, seq_to_head
+        projection rows of this rank's heads cross before any QK-norm/RoPE, and
+        the fused QK-norm + RoPE + Sage quantizer reads them (and the text rows
+        of the same heads) in the projection layout: the bf16 Q/K/V never exist
+        in memory, as on one GPU. With one CFG row per rank (B = 1) the rows
+        cross through NVLink peer memory (ulysses.PeerExchange: a scatter
+        kernel into the heads' owners, and the attention kernel storing its
+        output straight into the tokens' owners); otherwise, or with
+        QIA_ULYSSES_P2P=0, through torch.distributed all-to-alls."""
+        from .ulysses import (gather_heads, gather_heads_into, head_to_seq, head_to_seq_into, peer_exchange_enabled,
+                              projection_heads, projection_to_heads, seq_to_head)
         cfg = self.cfg
         B, Sl, D = x.shape
         Lt = c.shape[1]
@@ -386,9 +404,24 @@ class MMDiT:
             qkv_i = F.linear(layer_norm_scale(x, s1_i, self.ln, shift=sh1_i), blk.img_qkv.w, blk.img_qkv.b)
             qkv_t = F.linear(layer_norm_scale(c, s1_t, self.ln, shift=sh1_t), blk.txt_qkv.w, blk.txt_qkv.b)
         S = Lt + U * Sl
-        a_t = torch.empty(B, Lt, H, hd, device=x.device, dtype=torch.bfloat16)
-        a_i = torch.empty(B, Sl, H, hd, device=x.device, dtype=torch.bfloat16)
-        if mx and self.sage:
+        px = self._peer_exchange(plan, Sl, Lt) if (mx and self.sage and B == 1 and peer_exchange_enabled()) \
+            else None
+        if px is None:
+            a_t = torch.empty(B, Lt, H, hd, device=x.device, dtype=torch.bfloat16)
+            a_i = torch.empty(B, Sl, H, hd, device=x.device, dtype=torch.bfloat16)
+        if px is not None:
+            # NVLink peer-memory exchanges: the q|k|v rows scattered to the
+            # heads' owners, the attention output stored by the attention
+            # kernel into the tokens' owners
+            recv = px.scatter_qkv(qkv_i.view(Sl, 3 * D))
+            qkv_th = projection_heads(qkv_t.view(Lt, 3 * D), H, plan)
+            ws = sage_quantize_joint(qkv_th[None], recv[None], (blk.norm_added_q, blk.norm_added_k),
+                                     (blk.norm_q, blk.norm_k), freqs_txt, freqs_img, Hl, cfg.eps)
+            del qkv_i, qkv_t, qkv_th
+            img_out, txt_out = px.attention(ws["_workspace"])
+            del ws
+            a_i, a_t = img_out.view(1, Sl, H, hd), txt_out.view(1, Lt, H, hd)
+        elif mx and self.sage:
             qkv_i, qkv_t = qkv_i.view(B, Sl, 3 * D), qkv_t.view(B, Lt, 3 * D)
             for b in range(B):
                 qkv_ih = projection_to_heads(qkv_i[b], H, plan)       # [U * S_loc, 3 * Hl * hd]
@@ -399,8 +432,8 @@ class MMDiT:
                 o = torch.empty(1, S, Hl, hd, device=x.device, dtype=torch.bfloat16)
                 sage_attention_from_workspace(ws["_workspace"], o)
                 del ws
-                a_i[b] = head_to_seq(o[0, Lt:], plan)
-                a_t[b] = gather_heads(o[0, :Lt], plan)
+                head_to_seq_into(o[0, Lt:], a_i[b], plan)
+                gather_heads_into(o[0, :Lt], a_t[b], plan)
                 del o
             del qkv_i, qkv_t
         else:

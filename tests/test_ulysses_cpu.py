@@ -29,8 +29,9 @@ def _worker(rank, world, port, cfg_split, results):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=60))
     try:
-        from qwen_image_accel_b200.ulysses import (exchange_cfg, gather_heads, head_to_seq, make_plan,
-                                                    projection_heads, projection_to_heads, seq_to_head)
+        from qwen_image_accel_b200.ulysses import (exchange_cfg, gather_heads, gather_heads_into, head_to_seq,
+                                                    head_to_seq_into, make_plan, projection_heads,
+                                                    projection_to_heads, seq_to_head)
         plan = make_plan(cfg_split)
         U = plan.ulysses
         S, H, d = 6 * U, 3 * U, 8
@@ -48,6 +49,19 @@ def _worker(rank, world, port, cfg_split, results):
         want = qkv.view(S, 3, H, d)[:, :, heads].reshape(S, 3 * (H // U) * d)
         assert torch.equal(projection_to_heads(qkv[lo:hi].contiguous(), H, plan), want), "projection_to_heads"
         assert torch.equal(projection_heads(qkv, H, plan), want), "projection_heads"
+        # head chunks of this rank's heads, and the outputs scattered back by chunk
+        Hl = H // U
+        o_img = torch.zeros(hi - lo, H, d, dtype=torch.float64)
+        o_txt = torch.zeros(S, H, d, dtype=torch.float64)
+        for ci in range(3):
+            hs = slice(plan.u * Hl + ci * Hl // 3, plan.u * Hl + (ci + 1) * Hl // 3)
+            want_c = qkv.view(S, 3, H, d)[:, :, hs].reshape(S, -1)
+            assert torch.equal(projection_to_heads(qkv[lo:hi].contiguous(), H, plan, (ci, 3)), want_c), "chunk in"
+            assert torch.equal(projection_heads(qkv, H, plan, (ci, 3)), want_c), "chunk text"
+            head_to_seq_into(full[:, hs].contiguous(), o_img, plan, (ci, 3))
+            gather_heads_into(full[:, hs].contiguous(), o_txt, plan, (ci, 3))
+        assert torch.equal(o_img, full[lo:hi]), "head_to_seq_into"
+        assert torch.equal(o_txt, full), "gather_heads_into"
         q, k, v = (torch.randn(S, H, d, generator=g, dtype=torch.float64) for _ in range(3))
         local = _attention(*(seq_to_head(t[lo:hi].contiguous(), plan) for t in (q, k, v)))
         assert torch.allclose(head_to_seq(local, plan), _attention(q, k, v)[lo:hi], atol=1e-12), "attention"
