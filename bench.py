@@ -20,7 +20,8 @@ product API (optimizations/cuda_graph.DenoiseStepGraph), K replays bracketed
 by barrier + synchronize and timed with CUDA events on the launching stream,
 max over ranks. The step streams ~27 GB of weights (far above the 126 MB L2),
 so no flush is needed between steps; the kernel-level measurements of configs
-1-3 flush L2 (a 256 MiB write) before every timed launch. `e2e`: K steps of
+1-3 flush L2 (a 256 MiB write, then a 256 MiB read that evicts its dirty
+lines) before every timed launch. `e2e`: K steps of
 DenoiseStepGraph.step() with the latents and both prompt embeddings copied in
 from pinned host memory and the new latents copied back, every step.
 
@@ -227,13 +228,19 @@ def reference_arm(args, rank, world):
 
 # ----------------------------------------------------------------------------- kernel timing helpers
 class L2Flush:
-    """Writes 256 MiB (twice the 126 MB L2) so the next launch reads cold."""
+    """Writes 256 MiB (twice the 126 MB L2), then reads another 256 MiB, so
+    the next launch reads cold and starts with no dirty lines in L2: after
+    the write alone, the timed kernel would pay for writing the flush's own
+    dirty lines back to DRAM."""
 
     def __init__(self, device):
         self.buf = torch.empty(256 << 20, dtype=torch.uint8, device=device)
+        self.clean = torch.ones(32 << 20, dtype=torch.int64, device=device)
+        self.sink = torch.empty((), dtype=torch.int64, device=device)
 
     def __call__(self):
         self.buf.fill_(1)
+        torch.amax(self.clean, dim=0, out=self.sink)
 
 
 def time_launches(fn, flush: L2Flush, n: int = 20, warmup: int = 3) -> float:
@@ -629,7 +636,7 @@ def step_arm(args, rank, world, local_rank):
                 "config": {"workload": workload, "global_batch": 2, "seq_len": img + TXT_LEN,
                            "parallelism": parallelism, "cuda_graph": "DenoiseStepGraph (whole step)",
                            "l2": "step working set (27 GB weights) >> L2, no flush; kernel lines flush L2 (256 MiB "
-                                 "write) before each timed launch"},
+                                 "write, then a 256 MiB read that evicts its dirty lines) before each timed launch"},
                 "e2e": {"value": round(head["e2e_ms"] / (world if c4_only else 1), 3), "unit": "ms/step",
                         "h2d_bytes_per_step": head["h2d"], "d2h_bytes_per_step": head["d2h"]},
                 "gpu_launches": head["launches_per_step"] * args.steps,

@@ -24,8 +24,6 @@
 //               two-MUFU sigmoid form of GELU-tanh (gelu_tanh_fast) and run on
 //               BN=192 tiles, whose double-buffered accumulators let the
 //               epilogue of one tile overlap the main loop of the next.
-// A second kernel (mxfp8_gemm_pair_kernel, below) runs the same roles on a
-// cluster of two CTAs sharing each MMA (cta_group::2); QIA_GEMM_PAIR=1 selects it.
 //
 // TMEM columns: NACC accumulators of BN columns (double-buffered when they
 // fit, so the epilogue of tile i overlaps the MMAs of tile i+1; with the one
@@ -505,255 +503,6 @@ mxfp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a0, const __grid_cons
   }
 }
 
-// ------------------------------------------------------------------ CTA-pair kernel
-// The same GEMM with one tcgen05 MMA shared by a cluster of two CTAs on two
-// SMs (cta_group::2): an output tile is 256 x BN; each CTA loads its own 128
-// rows of A and half (BN/2 rows) of B into its shared memory, so per SM the
-// tensor cores read half the B bytes of the single-CTA kernel and shared
-// memory bandwidth stops being the bound. Each CTA also loads its 128 rows of
-// A scales and all BN columns of B scales. Rank 0 issues the scale copies and
-// MMAs for both; every CTA's TMA loads count on rank 0's `full` barrier, rank
-// 0's commits arrive on both CTAs' `empty` / `acc_full` barriers, and both
-// CTAs' epilogue warps release the accumulator on rank 0's `acc_empty`.
-// Every load is a plain (non-multicast) TMA into the loading CTA's own memory.
-template <int BN>
-struct PairCfg {
-  static constexpr int BM = 128, BK = 128;   // rows of A per CTA
-  static constexpr int A_BYTES = BM * BK;
-  static constexpr int B_BYTES = BN / 2 * BK;  // this CTA's half of the B tile
-  static constexpr int SFB_CHUNKS = (BN + 127) / 128;  // BN=192 tiles at odd multiples of 64 span two
-  static constexpr int SF_BYTES = 512 + 512 * SFB_CHUNKS;
-  static constexpr int STAGE_BYTES = (A_BYTES + B_BYTES + SF_BYTES + 1023) / 1024 * 1024;
-  static constexpr int BAR_BYTES = 1024;
-  static constexpr int STAGES = (232448 - BAR_BYTES - 1024) / STAGE_BYTES > 8 ? 8
-                                                                            : (232448 - BAR_BYTES - 1024) / STAGE_BYTES;
-  static constexpr int TX_BYTES = 2 * (A_BYTES + B_BYTES + SF_BYTES);  // both CTAs, counted on rank 0
-  static constexpr int NACC = BN <= 192 ? 2 : 1;
-  static constexpr int SF_SLOTS = 4;
-  static constexpr int SF_COLS = 16;       // A scales at +0, B scales at +8 (8-column aligned)
-  static constexpr int SFB_OFF = 8;
-  static constexpr int SFA_COL = NACC * BN;
-  static constexpr int TMEM_COLS = 512;
-  static constexpr int SMEM = STAGES * STAGE_BYTES + BAR_BYTES + 1024;
-  static_assert(SFA_COL + SF_SLOTS * SF_COLS <= TMEM_COLS, "TMEM budget");
-  static_assert(SMEM <= 232448, "shared memory budget");
-  static_assert(STAGES >= 4, "pipeline depth");
-};
-
-template <int BN>
-__host__ __device__ constexpr uint32_t mxf8_idesc_pair() {
-  return (uint32_t(BN >> 3) << 17) | (1u << 23) | (uint32_t(256 >> 4) << 24);
-}
-
-template <int BN, int EPI>
-__global__ void __launch_bounds__(kGemmThreads, 1)
-mxfp8_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
-                       const __grid_constant__ CUtensorMap tmap_sfa, const __grid_constant__ CUtensorMap tmap_sfb,
-                       EpiParams ep, int M, int N, int K, int* err) {
-  using C = PairCfg<BN>;
-  extern __shared__ __align__(1024) uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* bar_area = smem + C::STAGES * C::STAGE_BYTES;
-  uint64_t* full = reinterpret_cast<uint64_t*>(bar_area);   // used on rank 0 only
-  uint64_t* empty = full + C::STAGES;
-  uint64_t* acc_full = empty + C::STAGES;
-  uint64_t* acc_empty = acc_full + 2;                        // used on rank 0 only
-  uint64_t* drain = acc_empty + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
-
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const uint32_t rank = cluster_ctarank();
-  const int pair = blockIdx.x >> 1, num_pairs = gridDim.x >> 1;
-  const int m_blocks = (M + 127) / 128, m_pairs = (m_blocks + 1) / 2;
-  const int n_tiles = N / BN, k_blocks = K / 128;
-  const int num_tiles = m_pairs * n_tiles;
-  const int kb_tiles = K / 128;
-
-  if (threadIdx.x == 0) {
-    for (int s = 0; s < C::STAGES; ++s) {
-      mbar_init(smem_u32(&full[s]), 1);
-      mbar_init(smem_u32(&empty[s]), 1);
-    }
-    for (int a = 0; a < 2; ++a) {
-      mbar_init(smem_u32(&acc_full[a]), 1);
-      mbar_init(smem_u32(&acc_empty[a]), 2 * kEpiWarps);
-    }
-    mbar_init(smem_u32(drain), 1);
-    fence_barrier_init();
-    prefetch_tmap(&tmap_a);
-    prefetch_tmap(&tmap_b);
-    prefetch_tmap(&tmap_sfa);
-    prefetch_tmap(&tmap_sfb);
-  }
-  if (warp == 1) tmem_alloc_pair(smem_u32(tmem_slot), C::TMEM_COLS);
-  tc_fence_before();
-  __syncthreads();
-  cluster_sync();  // both CTAs' barriers initialised before any cross-CTA arrive
-  tc_fence_after();
-  const uint32_t tmem_base = *tmem_slot;
-
-  if (warp == 0) {
-    // ------------------------------------------------------------ producer (both CTAs)
-    if (lane == 0) {
-      int s = 0;
-      uint32_t phase = 0;
-      int issued = 0;
-      bool ok = true;
-      for (int tile = pair; tile < num_tiles && ok; tile += num_pairs) {
-        const int m_pair = tile / n_tiles, n_blk = tile % n_tiles;
-        const int m_blk = m_pair * 2 + int(rank);
-        const int m0 = m_blk * 128, n0 = n_blk * BN;
-        const int nb0 = n0 + int(rank) * (BN / 2);
-        const int c0 = n0 >> 7;
-        for (int kb = 0; kb < k_blocks; ++kb) {
-          if (!mbar_wait(smem_u32(&empty[s]), phase ^ 1, err)) { ok = false; break; }
-          uint8_t* st = smem + s * C::STAGE_BYTES;
-          if (rank == 0) mbar_arrive_expect_tx(smem_u32(&full[s]), C::TX_BYTES);
-          const uint32_t fb = map_to_rank(smem_u32(&full[s]), 0);
-          tma_load_2d_pair(smem_u32(st), &tmap_a, fb, kb * 128, m0);
-          tma_load_2d_pair(smem_u32(st + C::A_BYTES), &tmap_b, fb, kb * 128, nb0);
-          // scale chunks: 512 B = rows {2i, 2i+1} of the [*, 256] byte views
-          tma_load_2d_pair(smem_u32(st + C::A_BYTES + C::B_BYTES), &tmap_sfa, fb, 0, (m_blk * kb_tiles + kb) * 2);
-#pragma unroll
-          for (int c = 0; c < C::SFB_CHUNKS; ++c)
-            tma_load_2d_pair(smem_u32(st + C::A_BYTES + C::B_BYTES + 512 + 512 * c), &tmap_sfb, fb, 0,
-                             ((c0 + c) * kb_tiles + kb) * 2);
-          ++issued;
-          if (++s == C::STAGES) { s = 0; phase ^= 1; }
-        }
-      }
-      if (!ok && rank == 0) {
-        // Let the copies already queued land before shared memory goes away
-        // (rank 0's full barriers count both CTAs' bytes).
-        for (int i = 0; i < C::STAGES && i < issued; ++i) {
-          if (--s < 0) { s = C::STAGES - 1; phase ^= 1; }
-          mbar_wait(smem_u32(&full[s]), phase, nullptr, 100000000ull);
-        }
-      }
-    }
-  } else if (warp == 1) {
-    // ------------------------------------------------------------ MMA issuer (rank 0)
-    if (lane == 0) {
-      bool ok = true;
-      if (rank == 0) {
-        int s = 0, sf_slot = 0;
-        uint32_t phase = 0;
-        int it = 0;
-        for (int tile = pair; tile < num_tiles && ok; tile += num_pairs, ++it) {
-          const int a = (C::NACC == 2) ? (it & 1) : 0;
-          const uint32_t acc_phase = (C::NACC == 2) ? ((it >> 1) & 1) : (it & 1);
-          if (!mbar_wait(smem_u32(&acc_empty[a]), acc_phase ^ 1, err)) { ok = false; break; }
-          tc_fence_after();
-          const int n0 = (tile % n_tiles) * BN;
-          const uint32_t d_tmem = tmem_base + uint32_t(a * BN);
-          for (int kb = 0; kb < k_blocks; ++kb) {
-            if (!mbar_wait(smem_u32(&full[s]), phase, err)) { ok = false; break; }
-            const uint32_t st = smem_u32(smem + s * C::STAGE_BYTES);
-            const uint32_t sfa_tmem = tmem_base + uint32_t(C::SFA_COL + sf_slot * C::SF_COLS);
-            const uint32_t sfb_base = sfa_tmem + C::SFB_OFF;
-            const uint32_t sfb_tmem = sfb_base + uint32_t((n0 & 127) >> 5);
-            if (++sf_slot == C::SF_SLOTS) sf_slot = 0;
-            tc_cp_32x128b_warpx4_pair(sfa_tmem, smem_desc_sf(st + C::A_BYTES + C::B_BYTES));
-#pragma unroll
-            for (int c = 0; c < C::SFB_CHUNKS; ++c)
-              tc_cp_32x128b_warpx4_pair(sfb_base + 4 * c, smem_desc_sf(st + C::A_BYTES + C::B_BYTES + 512 + 512 * c));
-            const uint64_t adesc = smem_desc_k_sw128(st);
-            const uint64_t bdesc = smem_desc_k_sw128(st + C::A_BYTES);
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              const uint32_t idesc = mxf8_idesc_pair<BN>() | (uint32_t(j) << 4) | (uint32_t(j) << 29);
-              tc_mma_mxf8_pair(d_tmem, adesc + uint64_t(2 * j), bdesc + uint64_t(2 * j), idesc, sfa_tmem, sfb_tmem,
-                               (kb | j) != 0);
-            }
-            tc_commit_pair(smem_u32(&empty[s]), 0x3);
-            if (++s == C::STAGES) { s = 0; phase ^= 1; }
-          }
-          if (ok) tc_commit_pair(smem_u32(&acc_full[a]), 0x3);
-        }
-        // drain: every MMA has finished reading both CTAs' shared memory and
-        // writing both CTAs' TMEM (arrives on both CTAs' drain barriers)
-        tc_commit_pair(smem_u32(drain), 0x3);
-      }
-      mbar_wait(smem_u32(drain), 0, ok ? err : nullptr, 100000000ull);
-    }
-  } else {
-    // ------------------------------------------------------------ epilogue (both CTAs)
-    const int sub = warp & 3;
-    const int half = (warp - 2) / 4;
-    const int row_in_tile = sub * 32 + lane;
-    constexpr int kChunks = BN / 64;
-    const uint32_t release_bar_local = smem_u32(&acc_empty[0]);
-    int it = 0;
-    for (int tile = pair; tile < num_tiles; tile += num_pairs, ++it) {
-      const int a = (C::NACC == 2) ? (it & 1) : 0;
-      const uint32_t acc_phase = (C::NACC == 2) ? ((it >> 1) & 1) : (it & 1);
-      const bool got = __all_sync(0xffffffffu, mbar_wait(smem_u32(&acc_full[a]), acc_phase, err));
-      if (!got) break;
-      tc_fence_after();
-      const int m_blk = (tile / n_tiles) * 2 + int(rank);
-      const int n0 = (tile % n_tiles) * BN;
-      const int64_t row = int64_t(m_blk) * 128 + row_in_tile;
-      const bool live = row < M;
-      const bool in_pad = m_blk < m_blocks;   // rows of the padded [m_blocks*128, N] outputs
-      const uint32_t t_row = tmem_base + (uint32_t(sub * 32) << 16) + uint32_t(a * BN);
-      const uint32_t bar = release_bar_local + uint32_t(a * 8);
-      if constexpr (C::NACC == 1) {
-        // one accumulator: release it before the math (see the single-CTA kernel)
-        uint32_t r[kChunks][32];
-#pragma unroll
-        for (int jj = 0; jj < kChunks; ++jj) tc_ld_32x32b_x32(t_row + uint32_t((half * kChunks + jj) * 32), r[jj]);
-        tc_wait_ld();
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) {
-          if (rank == 0) mbar_arrive(bar);
-          else mbar_arrive_cluster(map_to_rank(bar, 0));
-        }
-        if (in_pad) {
-#pragma unroll
-          for (int jj = 0; jj < kChunks; ++jj) {
-            float v[32];
-#pragma unroll
-            for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[jj][i]);
-            epilogue_chunk<EPI>(v, ep, row, n0 + (half * kChunks + jj) * 32, live, N);
-          }
-        }
-      } else {
-#pragma unroll 1
-        for (int jj = 0; jj < kChunks; ++jj) {
-          const int j = half * kChunks + jj;
-          uint32_t r[32];
-          tc_ld_32x32b_x32(t_row + uint32_t(j * 32), r);
-          tc_wait_ld();
-          if (jj == kChunks - 1) {
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) {
-              if (rank == 0) mbar_arrive(bar);
-              else mbar_arrive_cluster(map_to_rank(bar, 0));
-            }
-          }
-          if (in_pad) {
-            const int col = n0 + j * 32;
-            float v[32];
-#pragma unroll
-            for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
-            epilogue_chunk<EPI>(v, ep, row, col, live, N);
-          }
-        }
-      }
-    }
-  }
-
-  tc_fence_before();
-  __syncthreads();
-  cluster_sync();  // both CTAs finished with TMEM and with each other's barriers
-  if (warp == 1) {
-    tc_fence_after();
-    tmem_dealloc_pair(tmem_base, C::TMEM_COLS);
-  }
-}
-
 // ------------------------------------------------------------------ host side
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
@@ -859,81 +608,6 @@ int make_sf_tmap(CUtensorMap* map, const void* base, int64_t bytes) {
   return QIA_OK;
 }
 
-// Clusters of two that can be resident at once (1 CTA per SM), per device and
-// tile width; the persistent grid never exceeds it so that no pair waits for
-// another to finish.
-template <int BN, int EPI>
-int pair_clusters() {
-  using C = PairCfg<BN>;
-  static int cached[64] = {0};
-  static std::mutex mu;
-  int dev = 0;
-  cudaGetDevice(&dev);
-  std::lock_guard<std::mutex> lock(mu);
-  if (dev < 0 || dev >= 64) return 0;
-  if (cached[dev] == 0) {
-    cudaError_t e = cudaFuncSetAttribute(mxfp8_gemm_pair_kernel<BN, EPI>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
-    if (e != cudaSuccess) { set_error(QIA_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e)); return 0; }
-    cudaLaunchConfig_t cfg = {};
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = 2;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
-    cfg.gridDim = dim3(2 * unsigned(sm_count() / 2));
-    cfg.blockDim = dim3(kGemmThreads);
-    cfg.dynamicSmemBytes = C::SMEM;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    int n = 0;
-    e = cudaOccupancyMaxActiveClusters(&n, mxfp8_gemm_pair_kernel<BN, EPI>, &cfg);
-    if (e != cudaSuccess || n <= 0) {
-      set_error(QIA_ERR_CUDA, "cudaOccupancyMaxActiveClusters: %s", cudaGetErrorString(e));
-      return 0;
-    }
-    cached[dev] = n;
-  }
-  return cached[dev];
-}
-
-template <int BN, int EPI>
-int launch_gemm_pair(const void* a, const void* sa, const void* b, const void* sb, const EpiParams& ep, int64_t M,
-                     int64_t N, int64_t K, cudaStream_t st) {
-  using C = PairCfg<BN>;
-  const int clusters_max = pair_clusters<BN, EPI>();
-  if (clusters_max <= 0) return QIA_ERR_CUDA;
-  const int64_t m_blocks = (M + 127) / 128, m_pad = m_blocks * 128, kb_tiles = K / 128;
-  CUtensorMap ta, tb, tsa, tsb;
-  int rc = make_tmap(&ta, a, m_pad, K, 128);
-  if (rc) return rc;
-  rc = make_tmap(&tb, b, N, K, BN / 2);
-  if (rc) return rc;
-  rc = make_sf_tmap(&tsa, sa, m_blocks * kb_tiles * 512);
-  if (rc) return rc;
-  rc = make_sf_tmap(&tsb, sb, (N / 128) * kb_tiles * 512);
-  if (rc) return rc;
-  const int64_t tiles = ((m_blocks + 1) / 2) * (N / BN);
-  int64_t clusters = clusters_max;
-  if (clusters > tiles) clusters = tiles;
-  cudaLaunchConfig_t cfg = {};
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = 2;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  cfg.gridDim = dim3(unsigned(2 * clusters));
-  cfg.blockDim = dim3(kGemmThreads);
-  cfg.dynamicSmemBytes = C::SMEM;
-  cfg.stream = st;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, mxfp8_gemm_pair_kernel<BN, EPI>, ta, tb, tsa, tsb, ep, int(M), int(N),
-                                     int(K), device_error_word());
-  if (e != cudaSuccess) return set_error(QIA_ERR_CUDA, "mxfp8_gemm_pair_kernel launch: %s", cudaGetErrorString(e));
-  return check_launch("mxfp8_gemm_pair_kernel");
-}
-
 int pick_bn(int64_t M, int64_t N, bool heavy_epilogue, bool even_chunks = false) {
   // QIA_GEMM_BN (128, 192 or 256) pins the tile width, for tuning and tests.
   const char* env = getenv("QIA_GEMM_BN");
@@ -952,34 +626,6 @@ int pick_bn(int64_t M, int64_t N, bool heavy_epilogue, bool even_chunks = false)
     // measured per-tile efficiency on B200: BN=256 (one accumulator, released
     // before the epilogue math) > 192 > 128
     const double eff = double(tiles) / double(waves * sms) * (bn == 192 ? 0.8 : 1.0) * (bn == 128 ? 0.7 : 1.0);
-    if (eff > best_eff + 1e-9) { best_eff = eff; best = bn; }
-  }
-  return best;
-}
-
-// The CTA-pair kernel is opt-in: QIA_GEMM_PAIR=1 selects it (measured on
-// B200 it reads less L2 per output but issues its MMAs no faster than the
-// single-CTA kernel with BN=256, which stays the default).
-bool use_pair(int64_t M) {
-  const char* env = getenv("QIA_GEMM_PAIR");
-  return env && env[0] == '1' && M > 0;
-}
-
-int pick_bn_pair(int64_t M, int64_t N) {
-  const char* env = getenv("QIA_GEMM_BN");
-  const int forced = env ? atoi(env) : 0;
-  if ((forced == 128 || forced == 192 || forced == 256) && N % forced == 0) return forced;
-  const int64_t m_pairs = ((M + 127) / 128 + 1) / 2;
-  const int pairs = sm_count() / 2;
-  int best = 0;
-  double best_eff = -1.0;
-  for (int bn : {192, 256, 128}) {
-    if (N % bn) continue;
-    const int64_t tiles = m_pairs * (N / bn);
-    const int64_t waves = (tiles + pairs - 1) / pairs;
-    // BN=256 has one accumulator (epilogue not overlapped); BN=128 reads the
-    // most shared memory per MMA
-    const double eff = double(tiles) / double(waves * pairs) * (bn == 256 ? 0.93 : 1.0) * (bn == 128 ? 0.9 : 1.0);
     if (eff > best_eff + 1e-9) { best_eff = eff; best = bn; }
   }
   return best;
@@ -1007,17 +653,6 @@ int dispatch(const Problem* in, int count, int64_t N, int64_t K, void* stream, c
   }
   if (m_tiles * 128 > (1LL << 30)) return set_error(QIA_ERR_UNSUPPORTED, "%s: too large", who);
   cudaStream_t st = as_stream(stream);
-  if constexpr (EPI != kEpiSwigluQuant) {   // the CTA-pair kernel has no SwiGLU epilogue
-    if (count == 1 && use_pair(pr[0].M)) {
-      const Problem& p = pr[0];
-      switch (pick_bn_pair(p.M, N)) {
-        case 128: return launch_gemm_pair<128, EPI>(p.a, p.sa, p.b, p.sb, p.ep, p.M, N, K, st);
-        case 192: return launch_gemm_pair<192, EPI>(p.a, p.sa, p.b, p.sb, p.ep, p.M, N, K, st);
-        case 256: return launch_gemm_pair<256, EPI>(p.a, p.sa, p.b, p.sb, p.ep, p.M, N, K, st);
-        default: return set_error(QIA_ERR_UNSUPPORTED, "%s: N=%lld has no supported tile width", who, (long long)N);
-      }
-    }
-  }
   // the tile width is chosen for the group's total M tiles
   const int bn = pick_bn(m_tiles * 128, N, EPI == kEpiGeluQuant || EPI == kEpiGeluBf16, EPI == kEpiSwigluQuant);
   switch (bn) {

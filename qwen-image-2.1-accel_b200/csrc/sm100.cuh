@@ -179,86 +179,6 @@ __device__ __forceinline__ void tc_st_32x32b_x32(uint32_t taddr, const uint32_t 
 
 __device__ __forceinline__ void tc_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
-// ----------------------------------------------------------------- CTA pairs
-// A cluster of two CTAs on two SMs shares one tcgen05 MMA (cta_group::2): the
-// even CTA (rank 0) issues the MMAs, each CTA holds half of the operands in its
-// own shared memory and its half of the accumulator rows in its own TMEM. Every
-// tcgen05 instruction of such a kernel uses cta_group::2. No TMA multicast.
-__device__ __forceinline__ uint32_t cluster_ctarank() {
-  uint32_t r;
-  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
-  return r;
-}
-
-// All threads of both CTAs; release/acquire orders shared-memory and barrier
-// state across the pair.
-__device__ __forceinline__ void cluster_sync() {
-  asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
-  asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
-}
-
-// The shared::cluster address of the same shared variable in CTA `rank`.
-__device__ __forceinline__ uint32_t map_to_rank(uint32_t saddr, uint32_t rank) {
-  uint32_t r;
-  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
-  return r;
-}
-
-// Arrive on an mbarrier of either CTA of the cluster (shared::cluster address).
-__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_bar) {
-  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_bar) : "memory");
-}
-
-// TMA tile load into this CTA's shared memory whose completion (bytes) is
-// counted on `cluster_bar`, an mbarrier of either CTA of the pair.
-__device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const CUtensorMap* map, uint32_t cluster_bar, int x,
-                                                 int y) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], "
-      "[%2];" ::"r"(dst),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(cluster_bar), "r"(x), "r"(y)
-      : "memory");
-}
-
-// Executed by one warp of EACH CTA of the pair (same warp index, same slot
-// offset): allocates `ncols` columns at the same address in both SMs' TMEM.
-__device__ __forceinline__ void tmem_alloc_pair(uint32_t dst_smem, uint32_t ncols) {
-  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dst_smem), "r"(ncols)
-               : "memory");
-  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
-}
-
-__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
-  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
-}
-
-// Arrive once on the mbarrier at offset `bar` in every CTA of `cta_mask` when
-// all prior tcgen05 operations of this thread finish.
-__device__ __forceinline__ void tc_commit_pair(uint32_t bar, uint16_t cta_mask) {
-  asm volatile(
-      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(bar),
-      "h"(cta_mask)
-      : "memory");
-}
-
-// Each CTA's shared memory at `sdesc` -> its own TMEM at `taddr` (issued once,
-// by the MMA thread of rank 0).
-__device__ __forceinline__ void tc_cp_32x128b_warpx4_pair(uint32_t taddr, uint64_t sdesc) {
-  asm volatile("tcgen05.cp.cta_group::2.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(sdesc) : "memory");
-}
-
-// D (256 x N over the pair) (+)= A (128 rows per CTA) * B^T (N/2 rows per CTA),
-// E4M3 with E8M0 1x32 block scales (A scales per CTA, all N B scales per CTA).
-__device__ __forceinline__ void tc_mma_mxf8_pair(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
-                                                 uint32_t sfa_tmem, uint32_t sfb_tmem, uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::2.kind::mxf8f6f4.block_scale [%0], %1, %2, %3, [%5], [%6], p;\n\t}" ::"r"(d_tmem),
-      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(sfa_tmem), "r"(sfb_tmem)
-      : "memory");
-}
-
 // Shared-memory matrix descriptor, K-major, 128-byte swizzle: 8-row core
 // groups 1024 B apart (SBO), leading offset unused (16 B), sm_100 version bit.
 __device__ __forceinline__ uint64_t smem_desc_k_sw128(uint32_t saddr) {
