@@ -381,10 +381,11 @@ class MMDiT:
         the fused QK-norm + RoPE + Sage quantizer reads them (and the text rows
         of the same heads) in the projection layout: the bf16 Q/K/V never exist
         in memory, as on one GPU. With one CFG row per rank (B = 1) the rows
-        cross through NVLink peer memory (ulysses.PeerExchange: a scatter
-        kernel into the heads' owners, and the attention kernel storing its
-        output straight into the tokens' owners); otherwise, or with
-        QIA_ULYSSES_P2P=0, through torch.distributed all-to-alls."""
+        of every Sage block (MXFP8 or bf16 projections) cross through NVLink
+        peer memory (ulysses.PeerExchange: a scatter kernel into the heads'
+        owners, and the attention kernel storing its output straight into the
+        tokens' owners); otherwise, or with QIA_ULYSSES_P2P=0, through
+        torch.distributed all-to-alls."""
         from .ulysses import (gather_heads, gather_heads_into, head_to_seq, head_to_seq_into, peer_exchange_enabled,
                               projection_heads, projection_to_heads, seq_to_head)
         cfg = self.cfg
@@ -404,8 +405,7 @@ class MMDiT:
             qkv_i = F.linear(layer_norm_scale(x, s1_i, self.ln, shift=sh1_i), blk.img_qkv.w, blk.img_qkv.b)
             qkv_t = F.linear(layer_norm_scale(c, s1_t, self.ln, shift=sh1_t), blk.txt_qkv.w, blk.txt_qkv.b)
         S = Lt + U * Sl
-        px = self._peer_exchange(plan, Sl, Lt) if (mx and self.sage and B == 1 and peer_exchange_enabled()) \
-            else None
+        px = self._peer_exchange(plan, Sl, Lt) if (self.sage and B == 1 and peer_exchange_enabled()) else None
         if px is None:
             a_t = torch.empty(B, Lt, H, hd, device=x.device, dtype=torch.bfloat16)
             a_i = torch.empty(B, Sl, H, hd, device=x.device, dtype=torch.bfloat16)
@@ -413,8 +413,8 @@ class MMDiT:
             # NVLink peer-memory exchanges: the q|k|v rows scattered to the
             # heads' owners, the attention output stored by the attention
             # kernel into the tokens' owners
-            recv = px.scatter_qkv(qkv_i.view(Sl, 3 * D))
-            qkv_th = projection_heads(qkv_t.view(Lt, 3 * D), H, plan)
+            recv = px.scatter_qkv(qkv_i.reshape(Sl, 3 * D))
+            qkv_th = projection_heads(qkv_t.reshape(Lt, 3 * D), H, plan)
             ws = sage_quantize_joint(qkv_th[None], recv[None], (blk.norm_added_q, blk.norm_added_k),
                                      (blk.norm_q, blk.norm_k), freqs_txt, freqs_img, Hl, cfg.eps)
             del qkv_i, qkv_t, qkv_th
