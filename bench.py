@@ -950,6 +950,11 @@ def profile_case(name: str):
     q21step - the `--config q21` denoiser: prefill, two decode steps, then one
               decode step inside an NVTX range named `step`.
     ffn_up_c5 - the FFN-up GEMM (GELU+MXFP8 epilogue) at config 5's M=32768.
+    exchange - the config-5 Ulysses exchange kernels at one rank's sizes of the
+              4-GPU layout (U=2: 8192 image tokens per rank, 24 heads, 256 text
+              tokens), two ranks emulated on one GPU as two launches into two
+              buffer sets: the q|k|v scatter (twice), the wait, the fused
+              quantizer and the attention with its peer-store epilogue (twice).
     kernels - one launch each of the memory-bound kernels at the step's
               shapes: LN + modulation -> MXFP8 (image + text rows, grouped),
               the AdaLN modulation GEMV (one block), the config-1 AdaLN
@@ -975,6 +980,8 @@ def profile_case(name: str):
         MXFP8Linear(lin).matmul_gelu_quantize(a)
     elif name == "kernels":
         profile_kernels(device, g)
+    elif name == "exchange":
+        profile_exchange(device, g)
     elif name == "attn":
         from qwen_image_accel_b200.optimizations.sage_attention import sage_attention
         q, k, v = (torch.randn(1, IMG_LEN + TXT_LEN, HEADS, 128, device=device, dtype=torch.bfloat16, generator=g)
@@ -1030,6 +1037,41 @@ def profile_case(name: str):
     log(f"profile case {name}: done")
 
 
+def profile_exchange(device, g):
+    """The `exchange` profile case (see profile_case)."""
+    from qwen_image_accel_b200 import _lib
+    from qwen_image_accel_b200.mmdit import rope_tables
+    from qwen_image_accel_b200.optimizations.sage_attention import sage_quantize_joint
+    U, s_loc, H = 2, IMG_LEN_C5 // 2, HEADS
+    hl, S = H // U, TXT_LEN + IMG_LEN_C5
+    bf = torch.bfloat16
+    qkv = torch.randn(U * s_loc, 3 * H * 128, device=device, dtype=bf, generator=g)
+    qkv_t = torch.randn(TXT_LEN, 3 * H * 128, device=device, dtype=bf, generator=g)
+    recv = [torch.empty(U * s_loc, 3 * hl * 128, device=device, dtype=bf) for _ in range(U)]
+    img = [torch.empty(s_loc, H, 128, device=device, dtype=bf) for _ in range(U)]
+    txt = [torch.empty(TXT_LEN, H, 128, device=device, dtype=bf) for _ in range(U)]
+    sig = [torch.zeros(2 * U + 2, dtype=torch.int64, device=device) for _ in range(U)]
+    table = lambda ts, off=0: torch.tensor([t.data_ptr() + off for t in ts], dtype=torch.int64, device=device)  # noqa: E731
+    rt, it, tt, sq, so = table(recv), table(img), table(txt), table(sig), table(sig, 8 * U)
+    st = _lib.stream(device)
+    for u in range(U):
+        rows = qkv[u * s_loc:(u + 1) * s_loc]
+        _lib.call("qia_ulysses_scatter_qkv", _lib.ptr(rows), rows.stride(0), s_loc, H, 128, _lib.ptr(rt),
+                  _lib.ptr(sq), U, u, st)
+    ctas = int(_lib.load().qia_ulysses_scatter_ctas(s_loc, H))
+    _lib.call("qia_ulysses_wait", _lib.ptr(sig[0]), _lib.ptr(sig[0][2 * U:]), U, ctas, 10_000_000_000, st)
+    w = tuple(torch.ones(128, device=device, dtype=bf) for _ in range(2))
+    fi, ft = (torch.view_as_real(t).to(device).contiguous() for t in rope_tables(*GRID_C5, TXT_LEN))
+    for u in range(U):
+        heads_u = qkv_t.view(TXT_LEN, 3, U, hl, 128)[:, :, u].reshape(TXT_LEN, 3 * hl * 128)
+        ws = sage_quantize_joint(heads_u[None], recv[u][None], w, w, ft, fi, hl)
+        _lib.call("qia_sage_attn_quantized_peers", _lib.ptr(ws["_workspace"]), S, hl, 128, TXT_LEN, _lib.ptr(it),
+                  _lib.ptr(tt), s_loc, U, u * hl, H, _lib.ptr(so), u, 0.0, st)
+    torch.cuda.synchronize()
+    if _lib.device_error():
+        raise SystemExit("exchange profile case: a device-side wait timed out")
+
+
 def profile_kernels(device, g):
     """The `kernels` profile case (see profile_case)."""
     from qwen_image_accel_b200.kernels.adaln import adaln_residual
@@ -1079,7 +1121,7 @@ def main():
                     help="c5 (default): the 2048^2 step (CFG split x Ulysses for N>1), with config 4 and the "
                          "configs 1-3 kernel lines at N=1; c4: the 1024^2 step (replicas for N>1); prefill: the "
                          "2.1 block-causal prefill attention; q21: the 2.1 cached-decode step")
-    ap.add_argument("--profile-case", choices=["ffn_up", "ffn_up_c5", "kernels", "attn", "step8", "step8_c5",
+    ap.add_argument("--profile-case", choices=["ffn_up", "ffn_up_c5", "kernels", "exchange", "attn", "step8", "step8_c5",
                                                "quant", "prefill", "q21step"],
                     help="run one small fixed case for an ncu capture and exit")
     args = ap.parse_args()
