@@ -1050,16 +1050,15 @@ def profile_exchange(device, g):
     recv = [torch.empty(U * s_loc, 3 * hl * 128, device=device, dtype=bf) for _ in range(U)]
     img = [torch.empty(s_loc, H, 128, device=device, dtype=bf) for _ in range(U)]
     txt = [torch.empty(TXT_LEN, H, 128, device=device, dtype=bf) for _ in range(U)]
-    sig = [torch.zeros(2 * U + 2, dtype=torch.int64, device=device) for _ in range(U)]
+    sig = [torch.zeros(2 * U + 4, dtype=torch.int64, device=device) for _ in range(U)]
     table = lambda ts, off=0: torch.tensor([t.data_ptr() + off for t in ts], dtype=torch.int64, device=device)  # noqa: E731
     rt, it, tt, sq, so = table(recv), table(img), table(txt), table(sig), table(sig, 8 * U)
     st = _lib.stream(device)
     for u in range(U):
         rows = qkv[u * s_loc:(u + 1) * s_loc]
         _lib.call("qia_ulysses_scatter_qkv", _lib.ptr(rows), rows.stride(0), s_loc, H, 128, _lib.ptr(rt),
-                  _lib.ptr(sq), U, u, st)
-    ctas = int(_lib.load().qia_ulysses_scatter_ctas(s_loc, H))
-    _lib.call("qia_ulysses_wait", _lib.ptr(sig[0]), _lib.ptr(sig[0][2 * U:]), U, ctas, 10_000_000_000, st)
+                  _lib.ptr(sq), _lib.ptr(sig[u][2 * U + 2:]), U, u, st)
+    _lib.call("qia_ulysses_wait", _lib.ptr(sig[0]), _lib.ptr(sig[0][2 * U:]), U, 1, 10_000_000_000, st)
     w = tuple(torch.ones(128, device=device, dtype=bf) for _ in range(2))
     fi, ft = (torch.view_as_real(t).to(device).contiguous() for t in rope_tables(*GRID_C5, TXT_LEN))
     for u in range(U):

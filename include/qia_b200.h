@@ -500,19 +500,20 @@ int qia_ipc_open(const void* handle, void** ptr);
 int qia_ipc_close(void* ptr);
 int qia_ipc_free(void* ptr);
 
-/* CTAs qia_ulysses_scatter_qkv launches (each signals every rank once). */
-int64_t qia_ulysses_scatter_ctas(int64_t s_loc, int64_t heads);
 /* Rows s of this rank's fused q|k|v projection ([s_loc, ld] bf16: q, k, v of
  * `heads` heads of 128) -> every rank r's receive buffer recv_peers[r]
  * ([U * s_loc, 3 * (heads/U) * 128] bf16): row rank * s_loc + s, the q, k and
  * v of r's heads [r * heads/U, (r + 1) * heads/U) -- the layout
  * qia_sage_quantize_joint reads with heads/U heads. recv_peers and
  * signal_peers are device arrays of U pointers (this rank's own buffers at
- * index `rank`); each CTA adds 1 to signal_peers[r][rank] for every r. */
+ * index `rank`); the CTAs count themselves on `done` (uint64 in this rank's
+ * memory, used by this entry only) and the launch's last CTA adds 1 to
+ * signal_peers[r][rank] for every r. */
 int qia_ulysses_scatter_qkv(const void* qkv, int64_t ld, int64_t s_loc,
                             int64_t heads, int64_t head_dim,
                             void* const* recv_peers, void* const* signal_peers,
-                            int64_t ulysses, int64_t rank, void* stream);
+                            void* done, int64_t ulysses, int64_t rank,
+                            void* stream);
 /* Wait for the next round of a wait site: *round (uint64, device, only this
  * entry updates it) += 1, then wait until counters[s] >= round * per_round
  * for s < sources. A wait longer than timeout_ns records QIA_ERR_TIMEOUT in

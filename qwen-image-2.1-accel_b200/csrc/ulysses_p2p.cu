@@ -11,13 +11,16 @@
 // kernel's own epilogue (sage_attn.cu, qia_sage_attn_quantized_peers).
 //
 // Completion protocol: every thread of a producing CTA issues a system-scope
-// fence after its stores; after a CTA barrier, thread r adds 1 to rank r's
-// 64-bit counter of this rank (a system-scope atomic through the peer
-// mapping). Counters only grow, across calls and CUDA graph replays. The
-// consuming rank's wait kernel keeps its own round number in device memory
-// (so a replayed graph waits for the next round, not the one it was captured
-// in) and waits, with a time limit, until every source's counter reaches
-// round x (CTAs per round); on timeout it records QIA_ERR_TIMEOUT and returns.
+// fence after its stores. The q|k|v producers (this scatter, or the QKV
+// GEMM's scatter epilogue) then count their CTAs on a counter in this rank's
+// memory, and the launch's last CTA adds 1 to every rank's 64-bit counter of
+// this rank (a system-scope atomic through the peer mapping): one signal per
+// launch, whichever producer ran. The attention signals from every CTA. The
+// counters only grow, across calls and CUDA graph replays. The consuming
+// rank's wait kernel keeps its own round number in device memory (so a
+// replayed graph waits for the next round, not the one it was captured in)
+// and waits, with a time limit, until every source's counter reaches round x
+// (signals per round); on timeout it records QIA_ERR_TIMEOUT and returns.
 // No TMA, no multicast, no library kernel touches peer memory.
 #include <cstring>
 
@@ -35,6 +38,7 @@ struct ScatterArgs {
   int64_t ld_chunks;                   // row stride in 16-byte chunks
   uint4* const* recv;                  // [U] each rank's receive buffer [U * s_loc, 3 * Hl * 128]
   unsigned long long* const* signal;   // [U] each rank's counters (this rank's slot u)
+  unsigned long long* done;            // this rank's count of finished CTAs of this kernel
   int64_t s_loc;
   int heads, ulysses, u;
 };
@@ -61,7 +65,14 @@ __global__ void __launch_bounds__(kScatterThreads) ulysses_scatter_qkv_kernel(Sc
   }
   __threadfence_system();
   __syncthreads();
-  if (threadIdx.x < a.ulysses) atomicAdd_system(a.signal[threadIdx.x] + a.u, 1ull);
+  if (threadIdx.x == 0) {
+    // the launch's last CTA to finish signals every rank once
+    const unsigned long long n = atomicAdd(a.done, 1ull) + 1ull;
+    if (n % gridDim.x == 0) {
+      __threadfence_system();
+      for (int r = 0; r < a.ulysses; ++r) atomicAdd_system(a.signal[r] + a.u, 1ull);
+    }
+  }
 }
 
 __device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long long* p) {
@@ -142,15 +153,12 @@ extern "C" int qia_ipc_free(void* ptr) {
   return QIA_OK;
 }
 
-extern "C" int64_t qia_ulysses_scatter_ctas(int64_t s_loc, int64_t heads) {
-  if (s_loc <= 0 || heads <= 0) return -1;
-  return scatter_grid(s_loc, heads);
-}
-
 extern "C" int qia_ulysses_scatter_qkv(const void* qkv, int64_t ld, int64_t s_loc, int64_t heads, int64_t head_dim,
-                                       void* const* recv_peers, void* const* signal_peers, int64_t ulysses,
-                                       int64_t rank, void* stream) {
-  if (!qkv || !recv_peers || !signal_peers) return set_error(QIA_ERR_INVALID, "qia_ulysses_scatter_qkv: null pointer");
+                                       void* const* recv_peers, void* const* signal_peers, void* done,
+                                       int64_t ulysses, int64_t rank, void* stream) {
+  if (!qkv || !recv_peers || !signal_peers || !done)
+    return set_error(QIA_ERR_INVALID, "qia_ulysses_scatter_qkv: null pointer");
+  if (!aligned(done, 8)) return set_error(QIA_ERR_ALIGNMENT, "qia_ulysses_scatter_qkv: done alignment");
   if (head_dim != kHeadDim) return set_error(QIA_ERR_UNSUPPORTED, "qia_ulysses_scatter_qkv: head_dim must be 128");
   if (s_loc <= 0 || heads <= 0 || ulysses <= 0 || ulysses > 64 || heads % ulysses || rank < 0 || rank >= ulysses)
     return set_error(QIA_ERR_INVALID, "qia_ulysses_scatter_qkv: s_loc=%lld heads=%lld U=%lld rank=%lld",
@@ -162,6 +170,7 @@ extern "C" int qia_ulysses_scatter_qkv(const void* qkv, int64_t ld, int64_t s_lo
   a.ld_chunks = ld / 8;
   a.recv = (uint4* const*)recv_peers;
   a.signal = (unsigned long long* const*)signal_peers;
+  a.done = (unsigned long long*)done;
   a.s_loc = s_loc;
   a.heads = int(heads);
   a.ulysses = int(ulysses);

@@ -78,7 +78,7 @@ SIGNATURES.update({
     "qia_ipc_open": [_P, ctypes.POINTER(ctypes.c_void_p)],
     "qia_ipc_close": [_P],
     "qia_ipc_free": [_P],
-    "qia_ulysses_scatter_qkv": [_P, _I, _I, _I, _I, _P, _P, _I, _I, _P],
+    "qia_ulysses_scatter_qkv": [_P, _I, _I, _I, _I, _P, _P, _P, _I, _I, _P],
     "qia_ulysses_wait": [_P, _P, _I, _I, _I, _P],
     "qia_sage_attn_quantized_peers": [_P, _I, _I, _I, _I, _P, _P, _I, _I, _I, _I, _P, _I, _F, _P],
 })
@@ -87,7 +87,6 @@ SIGNATURES.update({
 RAW_SIGNATURES: dict[str, tuple] = {
     "qia_sage_workspace_bytes": (ctypes.c_int64, [_I, _I, _I, _I]),
     "qia_ipc_handle_bytes": (ctypes.c_int64, []),
-    "qia_ulysses_scatter_ctas": (ctypes.c_int64, [_I, _I]),
     "qia_sage_attn_ctas": (ctypes.c_int64, [_I, _I, _I]),
 }
 

@@ -397,6 +397,8 @@ class MMDiT:
         sh1_i, s1_i, g1_i, sh2_i, s2_i, g2_i = mod_img
         sh1_t, s1_t, g1_t, sh2_t, s2_t, g2_t = mod_txt
         mx = blk.quantized
+        S = Lt + U * Sl
+        px = self._peer_exchange(plan, Sl, Lt) if (self.sage and B == 1 and peer_exchange_enabled()) else None
         if mx:
             a_i, a_t = layer_norm_scale_quantize_grouped([(x, s1_i, sh1_i), (c, s1_t, sh1_t)], self.ln)
             qkv_i, qkv_t = matmul_grouped([(blk.img_qkv.mx, a_i), (blk.txt_qkv.mx, a_t)])
@@ -404,8 +406,6 @@ class MMDiT:
         else:
             qkv_i = F.linear(layer_norm_scale(x, s1_i, self.ln, shift=sh1_i), blk.img_qkv.w, blk.img_qkv.b)
             qkv_t = F.linear(layer_norm_scale(c, s1_t, self.ln, shift=sh1_t), blk.txt_qkv.w, blk.txt_qkv.b)
-        S = Lt + U * Sl
-        px = self._peer_exchange(plan, Sl, Lt) if (self.sage and B == 1 and peer_exchange_enabled()) else None
         if px is None:
             a_t = torch.empty(B, Lt, H, hd, device=x.device, dtype=torch.bfloat16)
             a_i = torch.empty(B, Sl, H, hd, device=x.device, dtype=torch.bfloat16)

@@ -227,7 +227,8 @@ class PeerExchange:
       tokens, every head;
     * txt_out [L_txt, H, 128] bf16: the text tokens' attention output;
     * uint64 counters: [U] q|k|v signals, [U] output signals (one slot per
-      source rank), then the two wait sites' round numbers.
+      source rank), the two wait sites' round numbers, and the scatter
+      kernel's CTA count (it signals once per launch).
 
     Per block: scatter_qkv (qia_ulysses_scatter_qkv into every rank's recv,
     then a wait for the other ranks' rows) and attention (the attention kernel
@@ -247,7 +248,7 @@ class PeerExchange:
         hl = heads // U
         self.plan, self.s_loc, self.txt_len, self.heads, self.device = plan, s_loc, txt_len, heads, device
         sizes = {"recv": U * s_loc * 3 * hl * 128 * 2, "img": s_loc * heads * 128 * 2,
-                 "txt": txt_len * heads * 128 * 2, "sig": (2 * U + 2) * 8}
+                 "txt": txt_len * heads * 128 * 2, "sig": (2 * U + 3) * 8}
         lib = _lib.load()
         hb = int(lib.qia_ipc_handle_bytes())
         self._own, self._mapped, handles = {}, [], {}
@@ -278,7 +279,7 @@ class PeerExchange:
         sig = self._own["sig"]
         self._sig_qkv, self._sig_out = sig, sig + 8 * U
         self._round_qkv, self._round_out = sig + 16 * U, sig + 16 * U + 8
-        self.scatter_ctas = int(lib.qia_ulysses_scatter_ctas(s_loc, heads))
+        self._done_scatter = sig + 16 * U + 16
         self.attn_ctas = int(lib.qia_sage_attn_ctas(1, hl, txt_len + U * s_loc))
 
     def scatter_qkv(self, qkv_local: torch.Tensor) -> torch.Tensor:
@@ -291,8 +292,14 @@ class PeerExchange:
             raise ValueError("qkv rows must be [S_loc, 3*H*128] bf16 with contiguous rows")
         st = _lib.stream(qkv_local.device)
         _lib.call("qia_ulysses_scatter_qkv", _lib.ptr(qkv_local), qkv_local.stride(0), self.s_loc, self.heads, 128,
-                  _lib.ptr(self.recv_peers), _lib.ptr(self.sig_qkv_peers), U, self.plan.u, st)
-        _lib.call("qia_ulysses_wait", self._sig_qkv, self._round_qkv, U, self.scatter_ctas, self.TIMEOUT_NS, st)
+                  _lib.ptr(self.recv_peers), _lib.ptr(self.sig_qkv_peers), self._done_scatter, U, self.plan.u, st)
+        return self.wait_qkv()
+
+    def wait_qkv(self) -> torch.Tensor:
+        """Wait until every rank's q|k|v rows of this round are in recv; returns recv."""
+        from . import _lib
+        _lib.call("qia_ulysses_wait", self._sig_qkv, self._round_qkv, self.plan.ulysses, 1, self.TIMEOUT_NS,
+                  _lib.stream(self.device))
         return self.recv
 
     def attention(self, workspace: torch.Tensor, sm_scale: float | None = None):

@@ -8,7 +8,8 @@ tests/test_ulysses_gpu.py runs the real exchange between GPUs.
   reports QIA_ERR_TIMEOUT through the device error word (no GPU fault, the
   context stays usable), and passes rounds whose signals are all present;
 * qia_ulysses_scatter_qkv puts every rank's q|k|v rows where the fused
-  quantizer of the heads' owner reads them, and signals each rank once per CTA;
+  quantizer of the heads' owner reads them, and signals each rank once per
+  launch;
 * qia_sage_attn_quantized_peers writes each image row to the token's owner and
   the text rows to every rank, byte-identical to the single-GPU split
   attention of the same heads, and signals each rank once per CTA.
@@ -68,19 +69,20 @@ def test_scatter_layout_and_signals(U, s_loc, heads):
     qkv = torch.randn(U * s_loc, 3 * heads * 128, device=DEV, generator=g).to(torch.bfloat16)
     recv = [torch.zeros(U * s_loc, 3 * hl * 128, device=DEV, dtype=torch.bfloat16) for _ in range(U)]
     sig = [torch.zeros(2 * U + 2, dtype=torch.int64, device=DEV) for _ in range(U)]
+    done = torch.zeros(U, dtype=torch.int64, device=DEV)
     rt, sg = _table(recv), _table(sig)
     st = L.stream(qkv.device)
-    for u in range(U):                                   # rank u's rows
+    for u in range(U):                                   # rank u's rows, twice (two rounds)
         rows = qkv[u * s_loc:(u + 1) * s_loc]
-        L.call("qia_ulysses_scatter_qkv", L.ptr(rows), rows.stride(0), s_loc, heads, 128, L.ptr(rt), L.ptr(sg), U, u,
-               st)
+        for _ in range(2):
+            L.call("qia_ulysses_scatter_qkv", L.ptr(rows), rows.stride(0), s_loc, heads, 128, L.ptr(rt), L.ptr(sg),
+                   L.ptr(done[u:]), U, u, st)
     torch.cuda.synchronize()
     assert L.device_error() == 0
-    ctas = L.load().qia_ulysses_scatter_ctas(s_loc, heads)
     for r in range(U):
         want = qkv.view(U * s_loc, 3, U, hl, 128)[:, :, r].reshape(U * s_loc, 3 * hl * 128)
         assert torch.equal(recv[r], want)
-        assert sig[r][:U].tolist() == [ctas] * U
+        assert sig[r][:U].tolist() == [2] * U          # one signal per launch
         assert int(sig[r][U:].abs().sum()) == 0
 
 
