@@ -625,7 +625,7 @@ def step_arm(args, rank, world, local_rank):
                                         "txt tokens), CFG batch 2, profile mxfp8_sage")
             parallelism = ("single GPU (CFG batch 2)" if plan is None else
                            (f"CFG split x Ulysses {plan.ulysses} (q|k|v rows and attention output over NVLink "
-                            "peer memory; NCCL for the bf16 blocks and the per-step CFG exchange)" if plan.ulysses > 1
+                            "peer memory; NCCL for the per-step CFG exchange)" if plan.ulysses > 1
                             else "CFG split (one NCCL exchange per step)"))
             value, scaling = head["ms"], "strong"
         line = {"metric": metric, "value": round(value, 3), "unit": "ms/step", "n_gpus": world,
