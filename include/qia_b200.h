@@ -3,9 +3,11 @@
  *
  * Every function takes plain device pointers, int64 sizes and the caller's
  * cudaStream_t (passed as void*), queues its kernel(s) on that stream and
- * returns a status code (QIA_OK == 0). Nothing here allocates device memory,
- * synchronises the device or aborts the process; the text of the last failure
- * on the calling host thread is returned by qia_last_error_string().
+ * returns a status code (QIA_OK == 0). No compute entry point allocates device
+ * memory, synchronises the device or aborts the process (the qia_ipc_* set-up
+ * entries of the multi-GPU exchange allocate, map and synchronise by design);
+ * the text of the last failure on the calling host thread is returned by
+ * qia_last_error_string().
  *
  * Tensor conventions (all contiguous unless a leading dimension is given):
  *   bf16       : __nv_bfloat16 / torch.bfloat16, row-major.
