@@ -1,7 +1,11 @@
-"""Sharded MMDiT step (CFG split + Ulysses over NCCL) against the single-GPU
-step, on a tiny model: every per-row and per-head computation is the same
-kernel on the same inputs, so the results are bit-identical. Needs >= 2 GPUs
-(skipped otherwise); run as `pytest -m gpu` on a multi-GPU box."""
+"""Sharded MMDiT step (CFG split + Ulysses) against the single-GPU step, on a
+tiny model: every per-row and per-head computation is the same kernel on the
+same inputs, so the results are bit-identical. With one CFG row per rank the
+Ulysses exchanges go through NVLink peer memory (ulysses.PeerExchange: the
+q|k|v scatter kernel and the attention's peer-store epilogue, for the MXFP8
+blocks and the bf16 block 0 alike); the CFG swap of the velocities goes
+through NCCL. Needs >= 2 GPUs (skipped otherwise); run as `pytest -m gpu` on a
+multi-GPU box."""
 import os
 import socket
 from datetime import timedelta
