@@ -536,6 +536,8 @@ def measure_c3(device, peak_fp8, peak_kind, flush):
            "ms": round(ms, 4), "fused_norm_rope_quantizers_ms": round(ms_quant, 4),
            "roofline": roofline_entry("sage_quant_* + sage_attn_kernel", ops / (ms * 1e-3) / 1e12, peak_fp8,
                                       "TOP/s", "tensor", peak_kind, algorithmic_ops=ops)}
+    traffic, source = ncu_traffic("sage_quant_* + sage_attn_kernel", f"B={b} H={h} S={s}")
+    out["roofline"].update(traffic=traffic, traffic_source=source)
     if sage_ref.available():
         ref = sage_ref.attention(q, k, v)
         ms_ref = time_launches(lambda: sage_ref.attention(q, k, v), flush)
