@@ -24,8 +24,8 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-def _worker(rank, world, port, cfg_split, results):
-    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+def _worker(rank, world, port, cfg_split, p2p, results):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), QIA_ULYSSES_P2P="1" if p2p else "0")
     torch.cuda.set_device(rank)
     dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=120),
                             device_id=torch.device("cuda", rank))
@@ -59,14 +59,16 @@ def _worker(rank, world, port, cfg_split, results):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world,cfg_split", [(2, False), (2, True), (4, True), (8, True)])
-def test_sharded_step_matches_single_gpu(world, cfg_split):
+# p2p=False: the torch.distributed exchanges (the path of B > 1 per rank)
+@pytest.mark.parametrize("world,cfg_split,p2p", [(2, False, True), (2, False, False), (2, True, True),
+                                                 (4, True, True), (8, True, True)])
+def test_sharded_step_matches_single_gpu(world, cfg_split, p2p):
     if torch.cuda.device_count() < world:
         pytest.skip(f"needs {world} GPUs")
     ctx = mp.get_context("spawn")
     results = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, cfg_split, results)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, cfg_split, p2p, results)) for r in range(world)]
     for p in procs:
         p.start()
     out = {}
