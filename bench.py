@@ -475,9 +475,11 @@ def measure_c2(device, peak_fp8, hbm, peak_kind, hbm_kind, flush):
         xq = torch.randn(m, DIM, device=device, dtype=torch.bfloat16, generator=g)
         ms_q = time_launches(lambda: quantize(xq), flush)
         nbytes = m * DIM * (2 + 1 + 1 / 32)
+        traffic, source = ncu_traffic("mx_quantize_kernel", f"[{m},{DIM}]")
         out.setdefault("quantizer", []).append(
             roofline_entry(f"mx_quantize_kernel [{m},{DIM}]", nbytes / (ms_q * 1e-3) / 1e9, hbm, "GB/s", "hbm",
-                           hbm_kind, algorithmic_bytes=int(nbytes), ms=round(ms_q, 4)))
+                           hbm_kind, traffic=traffic, traffic_source=source, algorithmic_bytes=int(nbytes),
+                           ms=round(ms_q, 4)))
     fr = [s["frac"] for s in out["shapes"]]
     out["frac_min"], out["frac_mean"] = round(min(fr), 3), round(statistics.mean(fr), 3)
     out["vs_scaled_mm_min"] = round(min(s["vs_scaled_mm"] for s in out["shapes"]), 3)
